@@ -1,0 +1,768 @@
+// Aggregator side of the slot protocol: the slot pool (per-slot cudaMalloc +
+// CUDA IPC handles), the fused frozen base weights, one round over pool slots,
+// and the barrier-driven main loop. Mirrors the reference module
+// ext_aggregator (src/cpp_extensions/ext_aggregator.cpp); each entry point
+// cites the function whose behaviour it keeps.
+//
+// Differences by design:
+//  * a round is one kernel (slot_round.cu) reading the slot buffers through a
+//    slot table; no concatenated input or staging output exists;
+//  * commands naming a bad slot, a non-owner or an oversized shape are
+//    dropped and that slot is evicted, instead of ending the main loop;
+//  * o_proj / down_proj / embed / lm_head weights are borrowed (the caller
+//    keeps them alive), q|k|v and gate|up are fused into library-owned copies,
+//    the same memory behaviour as the reference's detach()/cat().
+#include <cuda_bf16.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <unistd.h>
+
+#include <chrono>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "common.h"
+#include "shm_abi.h"
+#include "slot_round.h"
+#include "vocab_ops.h"
+
+using namespace swl;
+
+namespace {
+
+struct Slot {
+  std::atomic<int> owner{-1};
+  void* in = nullptr;
+  void* out = nullptr;
+  cudaIpcMemHandle_t in_handle;
+  cudaIpcMemHandle_t out_handle;
+};
+
+struct Pool {
+  Slot slots[kMaxSlots];
+  std::atomic<uint64_t> free_w[kMaskWords];
+  std::atomic<uint64_t> active_w[kMaskWords];
+  std::atomic<int> active_slot_count{0};
+  int num_slots = 0;
+  int device = 0;
+  int hidden = 0, inter = 0, qkv = 0;
+  size_t in_bytes = 0, out_bytes = 0;
+  int max_seq_per_step = 0;
+  bool initialized = false;
+};
+
+struct Layer {
+  void* qkv = nullptr;  // owned [q+k+v, hidden]
+  void* gu = nullptr;   // owned [gate+up, hidden]
+  const void* o = nullptr;     // borrowed [hidden_out, hidden]
+  const void* down = nullptr;  // borrowed [hidden, inter]
+  const void* o_bias = nullptr;
+  const void* down_bias = nullptr;
+  int64_t q_dim = 0, k_dim = 0, v_dim = 0, gate_dim = 0, up_dim = 0;
+  int64_t hidden = 0, inter = 0, o_out = 0, down_out = 0;
+  CUtensorMap tm_qkv, tm_o, tm_gu, tm_down;
+};
+
+struct SamplingState {
+  bool do_sample = false;
+  float temperature = 1.0f;
+  int top_k = 0;
+  float top_p = 1.0f;
+};
+
+Pool g_pool;
+std::vector<Layer> g_layers;
+int g_num_layers = 0;
+bool g_weights_ready = false;
+int g_device = 0;
+
+const void* g_embed = nullptr;    // borrowed [vocab, hidden]
+const void* g_lm_head = nullptr;  // borrowed [vocab, hidden]
+CUtensorMap g_tm_lm;
+int64_t g_vocab = 0, g_embed_hidden = 0;
+bool g_vocab_ready = false;
+void* g_logits = nullptr;  // [kMaxSlots, vocab] bf16 LM-head scratch
+
+ControlBlock* g_ctrl = nullptr;
+Command* g_ring = nullptr;
+int g_capacity = 0;
+size_t g_map_bytes = 0;
+
+cudaStream_t g_stream = nullptr;
+int g_round_algo = kAlgoTensorCore;
+int g_round_splits = 0;
+std::map<int, SamplingState> g_sampling;  // worker_id -> params (main-loop thread only)
+
+Mask128 load_mask(const std::atomic<uint64_t>* w) {
+  return {w[0].load(std::memory_order_acquire), w[1].load(std::memory_order_acquire)};
+}
+void store_mask(std::atomic<uint64_t>* w, const Mask128& m) {
+  w[0].store(m.w[0], std::memory_order_release);
+  w[1].store(m.w[1], std::memory_order_release);
+}
+
+int ensure_stream() {
+  if (!g_stream) SWL_CUDA_TRY(cudaStreamCreateWithFlags(&g_stream, cudaStreamNonBlocking));
+  return SWL_OK;
+}
+
+// One validated command of a round.
+struct RoundCmd {
+  int slot_id;
+  int worker_id;
+  int64_t rows;
+};
+
+// Checks slot id, ownership and shape of each command against the pool; bad
+// ones are reported in *bad (slot ids) and left out of *good.
+void validate(const RoundCmd* cmds, int n, int64_t in_row_bytes, int64_t out_row_bytes,
+              std::vector<RoundCmd>* good, std::vector<int>* bad, std::string* why) {
+  good->clear();
+  bad->clear();
+  for (int i = 0; i < n; ++i) {
+    const RoundCmd& c = cmds[i];
+    char buf[256];
+    if (c.slot_id < 0 || c.slot_id >= g_pool.num_slots) {
+      snprintf(buf, sizeof(buf), "invalid slot_id %d; ", c.slot_id);
+      *why += buf;
+      continue;  // cannot evict an out-of-range id
+    }
+    int owner = g_pool.slots[c.slot_id].owner.load(std::memory_order_acquire);
+    if (owner != c.worker_id) {
+      snprintf(buf, sizeof(buf), "worker %d does not own slot %d (owner=%d); ", c.worker_id,
+               c.slot_id, owner);
+      *why += buf;
+      bad->push_back(c.slot_id);
+      continue;
+    }
+    if (c.rows <= 0 || c.rows * in_row_bytes > static_cast<int64_t>(g_pool.in_bytes) ||
+        c.rows * out_row_bytes > static_cast<int64_t>(g_pool.out_bytes)) {
+      snprintf(buf, sizeof(buf), "slot %d: %lld rows exceed the slot buffers; ", c.slot_id,
+               static_cast<long long>(c.rows));
+      *why += buf;
+      bad->push_back(c.slot_id);
+      continue;
+    }
+    good->push_back(c);
+  }
+}
+
+// Runs one round over validated commands on `stream` (no synchronisation).
+int run_round(int op, int layer, const std::vector<RoundCmd>& cmds, cudaStream_t stream) {
+  if (cmds.empty()) return SWL_OK;
+  const int n = static_cast<int>(cmds.size());
+  if (op == kOpEmbed) {
+    if (!g_vocab_ready) return set_error(SWL_ERR_STATE, "embed: weights not initialized");
+    TokenTable tab;
+    tab.nslots = n;
+    int acc = 0;
+    for (int i = 0; i < n; ++i) {
+      const Slot& s = g_pool.slots[cmds[i].slot_id];
+      tab.row_start[i] = acc;
+      tab.tokens[i] = static_cast<const int64_t*>(s.in);
+      tab.out[i] = static_cast<__nv_bfloat16*>(s.out);
+      acc += static_cast<int>(cmds[i].rows);
+    }
+    tab.row_start[n] = acc;
+    tab.total_rows = acc;
+    return launch_embed_gather(tab, g_embed, g_vocab, g_embed_hidden, stream);
+  }
+  if (op == kOpLmHead) {
+    if (!g_vocab_ready) return set_error(SWL_ERR_STATE, "lm_head: weights not initialized");
+    SlotTable tab;
+    TokenOuts outs;
+    tab.nslots = n;
+    for (int i = 0; i < n; ++i) {
+      const Slot& s = g_pool.slots[cmds[i].slot_id];
+      tab.row_start[i] = i;
+      tab.in[i] = static_cast<const __nv_bfloat16*>(s.in) + (cmds[i].rows - 1) * g_embed_hidden;
+      tab.out[i] = static_cast<__nv_bfloat16*>(g_logits) + static_cast<int64_t>(i) * g_vocab;
+      outs.p[i] = static_cast<int64_t*>(s.out);
+    }
+    tab.row_start[n] = n;
+    tab.total_rows = n;
+    RoundShape shape{g_vocab, g_embed_hidden, g_embed_hidden, g_vocab, nullptr};
+    SWL_TRY(launch_slot_round(tab, shape, g_lm_head, &g_tm_lm, g_round_algo, g_round_splits, stream));
+    return launch_argmax_rows(g_logits, n, g_vocab, g_vocab, outs, stream);
+  }
+  if (layer < 0 || layer >= g_num_layers)
+    return set_error(SWL_ERR_ARG, "round: layer_idx %d out of range [0, %d)", layer, g_num_layers);
+  const Layer& L = g_layers[layer];
+  const void* W;
+  const CUtensorMap* tm;
+  RoundShape shape;
+  switch (op) {
+    case kOpQkvFused:
+      W = L.qkv; tm = &L.tm_qkv;
+      shape = {L.q_dim + L.k_dim + L.v_dim, L.hidden, 0, 0, nullptr};
+      break;
+    case kOpOProj:
+      W = L.o; tm = &L.tm_o;
+      shape = {L.o_out, L.hidden, 0, 0, static_cast<const __nv_bfloat16*>(L.o_bias)};
+      break;
+    case kOpGateUpFused:
+      W = L.gu; tm = &L.tm_gu;
+      shape = {L.gate_dim + L.up_dim, L.hidden, 0, 0, nullptr};
+      break;
+    case kOpDownProj:
+      W = L.down; tm = &L.tm_down;
+      shape = {L.down_out, L.inter, 0, 0, static_cast<const __nv_bfloat16*>(L.down_bias)};
+      break;
+    default:
+      return set_error(SWL_ERR_ARG, "round: unknown op %d", op);
+  }
+  shape.in_stride = shape.K;
+  shape.out_stride = shape.N;
+  SlotTable tab;
+  tab.nslots = n;
+  int acc = 0;
+  for (int i = 0; i < n; ++i) {
+    const Slot& s = g_pool.slots[cmds[i].slot_id];
+    tab.row_start[i] = acc;
+    tab.in[i] = static_cast<const __nv_bfloat16*>(s.in);
+    tab.out[i] = static_cast<__nv_bfloat16*>(s.out);
+    acc += static_cast<int>(cmds[i].rows);
+  }
+  tab.row_start[n] = acc;
+  tab.total_rows = acc;
+  return launch_slot_round(tab, shape, W, tm, g_round_algo, g_round_splits, stream);
+}
+
+void row_bytes_for(int op, int layer, int64_t* in_row, int64_t* out_row) {
+  int64_t H = g_pool.hidden, I = g_pool.inter;
+  *in_row = 2 * H;
+  *out_row = 2 * H;
+  if (op == kOpEmbed) { *in_row = 8; *out_row = 2 * H; return; }
+  if (op == kOpLmHead) { *in_row = 2 * H; *out_row = 0; return; }
+  if (layer >= 0 && layer < g_num_layers) {
+    const Layer& L = g_layers[layer];
+    if (op == kOpQkvFused) *out_row = 2 * (L.q_dim + L.k_dim + L.v_dim);
+    if (op == kOpGateUpFused) *out_row = 2 * (L.gate_dim + L.up_dim);
+    if (op == kOpDownProj) *in_row = 2 * I;
+  }
+}
+
+}  // namespace
+
+// ===== slot pool ============================================================
+
+// ext_aggregator.cpp:138-187 init_slot_pool. Per-slot buffers: input
+// max_seq_per_step * max(inter, hidden) * dtype_size bytes, output
+// max_seq_per_step * max(2 * inter, qkv) * dtype_size bytes, each its own
+// cudaMalloc with its own IPC handle (a worker can map only its own slot).
+SWL_EXPORT int swl_agg_init_slot_pool(int num_slots, int device_index, int hidden_dim,
+                                      int intermediate_dim, int num_kv_heads, int head_dim,
+                                      int max_seq_per_step, int dtype_size, size_t* in_bytes,
+                                      size_t* out_bytes) {
+  if (num_slots <= 0 || num_slots > kMaxSlots)
+    return set_error(SWL_ERR_ARG, "num_slots must be between 1 and %d", kMaxSlots);
+  if (hidden_dim <= 0 || intermediate_dim <= 0 || max_seq_per_step <= 0 || dtype_size <= 0)
+    return set_error(SWL_ERR_ARG, "init_slot_pool: dimensions must be positive");
+  if (g_pool.initialized) return set_error(SWL_ERR_STATE, "init_slot_pool: already initialized");
+  SWL_CUDA_TRY(cudaSetDevice(device_index));
+  Pool& p = g_pool;
+  p.num_slots = num_slots;
+  p.device = device_index;
+  p.hidden = hidden_dim;
+  p.inter = intermediate_dim;
+  p.qkv = hidden_dim + num_kv_heads * head_dim * 2;
+  p.max_seq_per_step = max_seq_per_step;
+  p.in_bytes = static_cast<size_t>(max_seq_per_step) * std::max(intermediate_dim, hidden_dim) * dtype_size;
+  p.out_bytes = static_cast<size_t>(max_seq_per_step) * std::max(intermediate_dim * 2, p.qkv) * dtype_size;
+  store_mask(p.free_w, Mask128::first_n(num_slots));
+  store_mask(p.active_w, Mask128());
+  p.active_slot_count.store(0);
+  for (int i = 0; i < num_slots; ++i) {
+    Slot& s = p.slots[i];
+    s.owner.store(-1);
+    SWL_CUDA_TRY(cudaMalloc(&s.in, p.in_bytes));
+    SWL_CUDA_TRY(cudaMemset(s.in, 0, p.in_bytes));
+    SWL_CUDA_TRY(cudaIpcGetMemHandle(&s.in_handle, s.in));
+    SWL_CUDA_TRY(cudaMalloc(&s.out, p.out_bytes));
+    SWL_CUDA_TRY(cudaMemset(s.out, 0, p.out_bytes));
+    SWL_CUDA_TRY(cudaIpcGetMemHandle(&s.out_handle, s.out));
+  }
+  p.initialized = true;
+  if (in_bytes) *in_bytes = p.in_bytes;
+  if (out_bytes) *out_bytes = p.out_bytes;
+  return SWL_OK;
+}
+
+// ext_aggregator.cpp:190-245 claim_slot: lowest free slot by CAS on its mask
+// word; scrubs stale ready / evicted bits of the previous tenant.
+SWL_EXPORT int swl_agg_claim_slot(int worker_id, int* slot_id, unsigned char* in_handle,
+                                  unsigned char* out_handle, size_t* in_bytes, size_t* out_bytes) {
+  if (!g_pool.initialized) return set_error(SWL_ERR_STATE, "claim_slot: slot pool not initialized");
+  for (;;) {
+    Mask128 freem = load_mask(g_pool.free_w);
+    if (freem.empty()) return set_error(SWL_ERR_FULL, "No free slots available");
+    int sid = freem.lowest();
+    int k = sid >> 6;
+    uint64_t expect = freem.w[k];
+    if (g_pool.free_w[k].compare_exchange_weak(expect, expect & ~(1ull << (sid & 63)),
+                                               std::memory_order_acq_rel,
+                                               std::memory_order_acquire)) {
+      Slot& s = g_pool.slots[sid];
+      s.owner.store(worker_id, std::memory_order_release);
+      if (g_ctrl) {
+        g_ctrl->per_slot_ready_mask.clear_bit(sid);
+        g_ctrl->evicted_slot_mask.clear_bit(sid);
+      }
+      if (slot_id) *slot_id = sid;
+      if (in_handle) std::memcpy(in_handle, &s.in_handle, sizeof(cudaIpcMemHandle_t));
+      if (out_handle) std::memcpy(out_handle, &s.out_handle, sizeof(cudaIpcMemHandle_t));
+      if (in_bytes) *in_bytes = g_pool.in_bytes;
+      if (out_bytes) *out_bytes = g_pool.out_bytes;
+      return SWL_OK;
+    }
+  }
+}
+
+// ext_aggregator.cpp:248-296 release_slot: owner CAS, zero both buffers and
+// wait for the zeroing before the slot becomes claimable again.
+SWL_EXPORT int swl_agg_release_slot(int slot_id, int worker_id) {
+  if (!g_pool.initialized) return set_error(SWL_ERR_STATE, "release_slot: slot pool not initialized");
+  if (slot_id < 0 || slot_id >= g_pool.num_slots)
+    return set_error(SWL_ERR_ARG, "release_slot: invalid slot_id");
+  Slot& s = g_pool.slots[slot_id];
+  int expect = worker_id;
+  if (!s.owner.compare_exchange_strong(expect, -1, std::memory_order_acq_rel,
+                                       std::memory_order_acquire))
+    return set_error(SWL_ERR_OWNER, "release_slot: worker does not own slot %d", slot_id);
+  SWL_CUDA_TRY(cudaSetDevice(g_pool.device));
+  cudaStream_t st;
+  SWL_CUDA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  cudaMemsetAsync(s.in, 0, g_pool.in_bytes, st);
+  cudaMemsetAsync(s.out, 0, g_pool.out_bytes, st);
+  cudaError_t e = cudaStreamSynchronize(st);
+  cudaStreamDestroy(st);
+  if (e != cudaSuccess) return set_error(SWL_ERR_CUDA, "release_slot: %s", cudaGetErrorString(e));
+  g_pool.free_w[slot_id >> 6].fetch_or(1ull << (slot_id & 63), std::memory_order_release);
+  g_pool.active_w[slot_id >> 6].fetch_and(~(1ull << (slot_id & 63)), std::memory_order_release);
+  return SWL_OK;
+}
+
+// ext_aggregator.cpp:299-304 get_slot_owner (-1 if free or invalid).
+SWL_EXPORT int swl_agg_get_slot_owner(int slot_id) {
+  if (!g_pool.initialized || slot_id < 0 || slot_id >= g_pool.num_slots) return -1;
+  return g_pool.slots[slot_id].owner.load(std::memory_order_acquire);
+}
+
+// ext_aggregator.cpp:307-328 get_slot_pool_status. masks = {free_lo, free_hi,
+// active_lo, active_hi}; owners receives num_slots entries (cap kMaxSlots).
+SWL_EXPORT int swl_agg_get_slot_pool_status(int* initialized, int* num_slots, uint64_t* masks,
+                                            int* active_slot_count, int* owners) {
+  if (initialized) *initialized = g_pool.initialized ? 1 : 0;
+  if (num_slots) *num_slots = g_pool.num_slots;
+  Mask128 f = load_mask(g_pool.free_w), a = load_mask(g_pool.active_w);
+  if (masks) {
+    masks[0] = f.w[0];
+    masks[1] = f.w[1];
+    masks[2] = a.w[0];
+    masks[3] = a.w[1];
+  }
+  if (active_slot_count) *active_slot_count = g_pool.active_slot_count.load();
+  if (owners)
+    for (int i = 0; i < g_pool.num_slots; ++i) owners[i] = g_pool.slots[i].owner.load();
+  return SWL_OK;
+}
+
+// Aggregator-local device addresses of a slot's buffers (for in-process
+// drivers such as tests and the benchmark; workers use the IPC handles).
+SWL_EXPORT int swl_agg_slot_buffers(int slot_id, void** in, void** out) {
+  if (!g_pool.initialized || slot_id < 0 || slot_id >= g_pool.num_slots)
+    return set_error(SWL_ERR_ARG, "slot_buffers: invalid slot %d", slot_id);
+  if (in) *in = g_pool.slots[slot_id].in;
+  if (out) *out = g_pool.slots[slot_id].out;
+  return SWL_OK;
+}
+
+// ext_aggregator.cpp:1410-1431 cleanup_slot_pool.
+SWL_EXPORT int swl_agg_cleanup_slot_pool(void) {
+  if (!g_pool.initialized) return SWL_OK;
+  SWL_CUDA_TRY(cudaSetDevice(g_pool.device));
+  SWL_CUDA_TRY(cudaDeviceSynchronize());
+  for (int i = 0; i < g_pool.num_slots; ++i) {
+    Slot& s = g_pool.slots[i];
+    if (s.in) cudaFree(s.in);
+    if (s.out) cudaFree(s.out);
+    s.in = s.out = nullptr;
+    s.owner.store(-1);
+  }
+  g_pool.initialized = false;
+  g_pool.num_slots = 0;
+  return SWL_OK;
+}
+
+// ===== weights ===============================================================
+
+// ext_aggregator.cpp:338-345 init_aggregator_begin.
+SWL_EXPORT int swl_agg_init_begin(int num_layers, int device_index) {
+  if (num_layers <= 0) return set_error(SWL_ERR_ARG, "init_aggregator_begin: num_layers must be > 0");
+  SWL_CUDA_TRY(cudaSetDevice(device_index));
+  for (Layer& L : g_layers) {
+    if (L.qkv) cudaFree(L.qkv);
+    if (L.gu) cudaFree(L.gu);
+  }
+  g_layers.assign(num_layers, Layer());
+  g_num_layers = num_layers;
+  g_device = device_index;
+  g_weights_ready = false;
+  return ensure_stream();
+}
+
+// ext_aggregator.cpp:347-376 init_aggregator_layer: W_qkv = cat(q, k, v) and
+// W_gu = cat(gate, up) along the output dimension into library-owned
+// buffers; o / down (and optional biases, NULL = none) are borrowed. All
+// weights are row-major [out, in] bf16 on the aggregator device.
+SWL_EXPORT int swl_agg_init_layer(int layer_idx, const void* q, int64_t q_rows, const void* k,
+                                  int64_t k_rows, const void* v, int64_t v_rows, const void* o,
+                                  int64_t o_rows, const void* o_bias, const void* gate,
+                                  int64_t gate_rows, const void* up, int64_t up_rows,
+                                  const void* down, int64_t down_rows, const void* down_bias,
+                                  int64_t hidden, int64_t inter) {
+  if (layer_idx < 0 || layer_idx >= g_num_layers)
+    return set_error(SWL_ERR_ARG, "init_aggregator_layer: layer_idx %d out of range [0, %d)",
+                     layer_idx, g_num_layers);
+  if (!q || !k || !v || !o || !gate || !up || !down)
+    return set_error(SWL_ERR_ARG, "init_aggregator_layer: null weight");
+  Layer& L = g_layers[layer_idx];
+  if (L.qkv) cudaFree(L.qkv);
+  if (L.gu) cudaFree(L.gu);
+  L = Layer();
+  L.q_dim = q_rows; L.k_dim = k_rows; L.v_dim = v_rows;
+  L.gate_dim = gate_rows; L.up_dim = up_rows;
+  L.hidden = hidden; L.inter = inter; L.o_out = o_rows; L.down_out = down_rows;
+  const size_t row_h = static_cast<size_t>(hidden) * 2;
+  SWL_CUDA_TRY(cudaSetDevice(g_device));
+  SWL_CUDA_TRY(cudaMalloc(&L.qkv, (q_rows + k_rows + v_rows) * row_h));
+  SWL_CUDA_TRY(cudaMalloc(&L.gu, (gate_rows + up_rows) * row_h));
+  char* dq = static_cast<char*>(L.qkv);
+  SWL_CUDA_TRY(cudaMemcpyAsync(dq, q, q_rows * row_h, cudaMemcpyDeviceToDevice, g_stream));
+  SWL_CUDA_TRY(cudaMemcpyAsync(dq + q_rows * row_h, k, k_rows * row_h, cudaMemcpyDeviceToDevice, g_stream));
+  SWL_CUDA_TRY(cudaMemcpyAsync(dq + (q_rows + k_rows) * row_h, v, v_rows * row_h,
+                               cudaMemcpyDeviceToDevice, g_stream));
+  char* dg = static_cast<char*>(L.gu);
+  SWL_CUDA_TRY(cudaMemcpyAsync(dg, gate, gate_rows * row_h, cudaMemcpyDeviceToDevice, g_stream));
+  SWL_CUDA_TRY(cudaMemcpyAsync(dg + gate_rows * row_h, up, up_rows * row_h, cudaMemcpyDeviceToDevice,
+                               g_stream));
+  SWL_CUDA_TRY(cudaStreamSynchronize(g_stream));
+  L.o = o;
+  L.down = down;
+  L.o_bias = o_bias;
+  L.down_bias = down_bias;
+  SWL_TRY(encode_weight_tmap(&L.tm_qkv, L.qkv, q_rows + k_rows + v_rows, hidden));
+  SWL_TRY(encode_weight_tmap(&L.tm_o, L.o, o_rows, hidden));
+  SWL_TRY(encode_weight_tmap(&L.tm_gu, L.gu, gate_rows + up_rows, hidden));
+  SWL_TRY(encode_weight_tmap(&L.tm_down, L.down, down_rows, inter));
+  return SWL_OK;
+}
+
+// ext_aggregator.cpp:378-410 init_aggregator_finalize. No staging buffers are
+// needed: the round kernel writes straight into the slot outputs.
+SWL_EXPORT int swl_agg_init_finalize(void) {
+  for (int i = 0; i < g_num_layers; ++i)
+    if (!g_layers[i].qkv) return set_error(SWL_ERR_STATE, "init_aggregator_finalize: layer %d missing", i);
+  g_weights_ready = true;
+  return SWL_OK;
+}
+
+// ext_aggregator.cpp:413-424 init_embed_lm_head_weights (both borrowed).
+SWL_EXPORT int swl_agg_init_embed_lm_head(const void* embed, const void* lm_head, int64_t vocab,
+                                          int64_t hidden) {
+  if (!embed || !lm_head || vocab <= 0 || hidden <= 0)
+    return set_error(SWL_ERR_ARG, "init_embed_lm_head_weights: invalid arguments");
+  SWL_CUDA_TRY(cudaSetDevice(g_device));
+  SWL_TRY(ensure_stream());
+  g_embed = embed;
+  g_lm_head = lm_head;
+  g_vocab = vocab;
+  g_embed_hidden = hidden;
+  SWL_TRY(encode_weight_tmap(&g_tm_lm, lm_head, vocab, hidden));
+  if (g_logits) cudaFree(g_logits);
+  SWL_CUDA_TRY(cudaMalloc(&g_logits, static_cast<size_t>(kMaxSlots) * vocab * 2));
+  g_vocab_ready = true;
+  return SWL_OK;
+}
+
+// ext_aggregator.cpp:427-459 init_aggregator_queue: map the queue segment
+// created by ext_ipc_queue.create_queue (this module's own view).
+SWL_EXPORT int swl_agg_init_queue(const char* shm_name, int capacity) {
+  if (capacity <= 0) return set_error(SWL_ERR_ARG, "init_aggregator_queue: capacity must be positive");
+  if (!shm_name || !shm_name[0]) return set_error(SWL_ERR_ARG, "init_aggregator_queue: shm_name cannot be empty");
+  int fd = shm_open(shm_name, O_RDWR, 0600);
+  if (fd < 0) return set_error(SWL_ERR_SYS, "Failed to open shared memory: %s", shm_name);
+  size_t bytes = shm_bytes(capacity);
+  void* p = mmap(nullptr, bytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+  close(fd);
+  if (p == MAP_FAILED) return set_error(SWL_ERR_SYS, "Failed to mmap shared memory");
+  if (g_ctrl) munmap(g_ctrl, g_map_bytes);
+  g_ctrl = static_cast<ControlBlock*>(p);
+  g_ring = reinterpret_cast<Command*>(static_cast<char*>(p) + sizeof(ControlBlock));
+  g_capacity = capacity;
+  g_map_bytes = bytes;
+  return SWL_OK;
+}
+
+// Round kernel selection: algo 0/1 = tensor cores, 2 = CUDA cores;
+// splits <= 0 = automatic K split.
+SWL_EXPORT int swl_agg_set_round_algo(int algo, int splits) {
+  if (algo < 0 || algo > 2) return set_error(SWL_ERR_ARG, "unknown round algo %d", algo);
+  g_round_algo = algo == kAlgoSimt ? kAlgoSimt : kAlgoTensorCore;
+  g_round_splits = splits;
+  return SWL_OK;
+}
+
+// The fused weight of (layer, op) and its [N, K] shape, for callers that
+// check a round against their own reference.
+SWL_EXPORT int swl_agg_weight(int layer, int op, const void** W, int64_t* N, int64_t* K) {
+  if (layer < 0 || layer >= g_num_layers) return set_error(SWL_ERR_ARG, "weight: bad layer");
+  const Layer& L = g_layers[layer];
+  switch (op) {
+    case kOpQkvFused: *W = L.qkv; *N = L.q_dim + L.k_dim + L.v_dim; *K = L.hidden; break;
+    case kOpOProj: *W = L.o; *N = L.o_out; *K = L.hidden; break;
+    case kOpGateUpFused: *W = L.gu; *N = L.gate_dim + L.up_dim; *K = L.hidden; break;
+    case kOpDownProj: *W = L.down; *N = L.down_out; *K = L.inter; break;
+    default: return set_error(SWL_ERR_ARG, "weight: bad op");
+  }
+  return SWL_OK;
+}
+
+// One round over pool slots, asynchronously on `stream` (NULL = the
+// library's own stream, then synchronised). Slot i of the round has
+// bx[i] * tx[i] token rows in its input buffer. Ownership and buffer bounds
+// are checked first; any failure rejects the whole call with an error. This
+// is the unit the main loop runs per op (ext_aggregator.cpp:1187-1193).
+SWL_EXPORT int swl_agg_execute_round(int op, int layer, int n, const int* slot_ids,
+                                     const int* worker_ids, const int64_t* bx, const int64_t* tx,
+                                     void* stream) {
+  if (!g_pool.initialized) return set_error(SWL_ERR_STATE, "execute_round: slot pool not initialized");
+  if (op != kOpEmbed && op != kOpLmHead && !g_weights_ready)
+    return set_error(SWL_ERR_STATE, "execute_round: weights not initialized");
+  if (n < 0 || n > g_pool.num_slots) return set_error(SWL_ERR_ARG, "execute_round: bad slot count %d", n);
+  std::vector<RoundCmd> cmds(n);
+  for (int i = 0; i < n; ++i) {
+    if (bx[i] <= 0 || tx[i] <= 0 || bx[i] > 65536 || tx[i] > 65536)
+      return set_error(SWL_ERR_ARG, "execute_round: invalid bx/tx dimensions");
+    cmds[i] = {slot_ids[i], worker_ids[i], bx[i] * tx[i]};
+  }
+  int64_t in_row, out_row;
+  row_bytes_for(op, layer, &in_row, &out_row);
+  std::vector<RoundCmd> good;
+  std::vector<int> bad;
+  std::string why;
+  validate(cmds.data(), n, in_row, out_row, &good, &bad, &why);
+  if (static_cast<int>(good.size()) != n) return set_error(SWL_ERR_OWNER, "execute_round: %s", why.c_str());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bool own = st == nullptr;
+  if (own) {
+    SWL_TRY(ensure_stream());
+    st = g_stream;
+  }
+  SWL_TRY(run_round(op, layer, good, st));
+  if (own) SWL_CUDA_TRY(cudaStreamSynchronize(st));
+  return SWL_OK;
+}
+
+// ===== main loop ===============================================================
+
+namespace {
+
+// ext_aggregator.cpp:879-978 aggregator_wait_for_slots: wait until every
+// active slot has set its ready bit; drop slots that signal leave mid-op
+// (checked every 10 ms) and evict slots not ready within 500 ms. Returns the
+// remaining slot count, or -1 when the quit flag is raised.
+int wait_for_slots(Mask128& active) {
+  using clk = std::chrono::steady_clock;
+  auto start = clk::now(), last_leave = start;
+  const auto kEvictAfter = std::chrono::milliseconds(500);
+  const auto kLeaveEvery = std::chrono::milliseconds(10);
+  long spins = 0;
+  for (;;) {
+    Mask128 ready = g_ctrl->per_slot_ready_mask.load();
+    Mask128 missing = active & ~ready;
+    if (missing.empty()) return active.count();
+    if (g_ctrl->quit_flag.load(std::memory_order_acquire)) return -1;
+    ++spins;
+    if (spins < kSpinTight) continue;
+    if (spins < kSpinYield) { cpu_relax(); continue; }
+    auto now = clk::now();
+    if (now - last_leave > kLeaveEvery) {
+      last_leave = now;
+      Mask128 leaving = g_ctrl->pending_slot_leaves.load() & active;
+      if (!leaving.empty()) {
+        active = active & ~leaving;
+        g_ctrl->pending_slot_leaves.and_with(~leaving);
+        g_ctrl->active_slot_mask.store(active);
+        g_ctrl->active_slot_count.store(active.count());
+        if (active.empty()) return 0;
+      }
+    }
+    if (now - start > kEvictAfter) {
+      Mask128 stuck = active & ~g_ctrl->per_slot_ready_mask.load();
+      if (!stuck.empty()) {
+        active = active & ~stuck;
+        g_ctrl->active_slot_mask.store(active);
+        g_ctrl->active_slot_count.store(active.count());
+        for (Mask128 r = stuck; !r.empty();) {
+          int sid = r.lowest();
+          r.clear(sid);
+          g_ctrl->evicted_slot_mask.set_bit(sid);
+        }
+        fprintf(stderr, "[swl aggregator] evicting stuck slot(s) mask=0x%llx:%llx; %d continue\n",
+                (unsigned long long)stuck.w[1], (unsigned long long)stuck.w[0], active.count());
+        if (active.empty()) return 0;
+        start = clk::now();
+        spins = 0;
+      }
+    }
+    cpu_relax();
+    cpu_relax();
+  }
+}
+
+// ext_aggregator.cpp:981-987 aggregator_signal_done_slots.
+void signal_done() {
+  g_ctrl->slot_ready_count.store(0, std::memory_order_release);
+  Mask128 active = g_ctrl->active_slot_mask.load();
+  g_ctrl->per_slot_ready_mask.and_with(~active);
+  g_ctrl->barrier_done_epoch.fetch_add(1, std::memory_order_release);
+}
+
+// ext_aggregator.cpp:991-1020 apply_pending_sampling_states.
+void apply_pending_sampling(const Mask128& joins) {
+  Mask128 todo = g_ctrl->pending_sampling_mask.load() & joins;
+  for (Mask128 r = todo; !r.empty();) {
+    int sid = r.lowest();
+    r.clear(sid);
+    int wid = g_pool.slots[sid].owner.load(std::memory_order_acquire);
+    if (wid >= 0) {
+      const PendingSampling& p = g_ctrl->pending_sampling[sid];
+      g_sampling[wid] = {p.do_sample, p.temperature, p.top_k, p.top_p};
+    }
+  }
+  g_ctrl->pending_sampling_mask.and_with(~todo);
+}
+
+void evict(const std::vector<int>& slots, Mask128& active) {
+  for (int sid : slots) {
+    active.clear(sid);
+    g_ctrl->evicted_slot_mask.set_bit(sid);
+  }
+  g_ctrl->active_slot_mask.store(active);
+  g_ctrl->active_slot_count.store(active.count());
+}
+
+}  // namespace
+
+// ext_aggregator.cpp:1024-1210 aggregator_main_loop_slots. Blocking; the
+// Python binding calls it without the GIL. Joins/leaves are applied at token
+// boundaries; each token is 1 + 4 * num_layers + 1 rounds.
+SWL_EXPORT int swl_agg_main_loop_slots(int num_slots, int dtype_code) {
+  (void)num_slots;
+  if (!g_ctrl || !g_ring) return set_error(SWL_ERR_STATE, "Aggregator queue not initialized");
+  if (!g_weights_ready) return set_error(SWL_ERR_STATE, "Aggregator weights not initialized");
+  if (!g_pool.initialized) return set_error(SWL_ERR_STATE, "Slot pool not initialized");
+  if (dtype_code != 15) return set_error(SWL_ERR_ARG, "only bf16 (dtype_code 15) is supported");
+  SWL_CUDA_TRY(cudaSetDevice(g_device));
+  SWL_TRY(ensure_stream());
+  Mask128 active;
+  std::vector<RoundCmd> cmds, good;
+  std::vector<int> bad;
+  cmds.reserve(kMaxSlots);
+  while (g_ctrl->quit_flag.load(std::memory_order_acquire) == 0) {
+    Mask128 leaves, joins;
+    if (!g_ctrl->pending_slot_leaves.load().empty()) leaves = g_ctrl->pending_slot_leaves.take_all();
+    if (!leaves.empty()) active = active & ~leaves;
+    if (!g_ctrl->pending_slot_joins.load().empty()) joins = g_ctrl->pending_slot_joins.take_all();
+    if (!joins.empty()) {
+      apply_pending_sampling(joins);
+      active = active | joins;
+    }
+    int N = active.count();
+    g_ctrl->active_slot_mask.store(active);
+    g_ctrl->active_slot_count.store(N);
+    store_mask(g_pool.active_w, active);
+    g_pool.active_slot_count.store(N);
+    if (N == 0) {
+      std::this_thread::sleep_for(std::chrono::milliseconds(1));
+      continue;
+    }
+    const int ops_per_token = 1 + g_num_layers * 4 + 1;
+    for (int op_idx = 0; op_idx < ops_per_token; ++op_idx) {
+      int got = wait_for_slots(active);
+      if (got < 0) {
+        signal_done();
+        break;
+      }
+      if (got == 0) break;
+      N = got;
+      // Drain N commands, discarding entries of slots evicted meanwhile.
+      cmds.clear();
+      int tail = g_ctrl->tail.load(std::memory_order_acquire);
+      int drained = 0, op = -1, layer = -1;
+      bool quit = false;
+      while (static_cast<int>(cmds.size()) < N && drained < kMaxSlots + 8) {
+        Command* c = &g_ring[tail];
+        long spin = 0;
+        while (c->ready.load(std::memory_order_acquire) != 1) {
+          if (g_ctrl->quit_flag.load(std::memory_order_acquire)) { quit = true; break; }
+          if (++spin > 10000000) {
+            fprintf(stderr, "[swl aggregator] command not ready after drain wait; quitting\n");
+            g_ctrl->quit_flag.store(1, std::memory_order_release);
+            quit = true;
+            break;
+          }
+          if (spin > kSpinYield) cpu_relax();
+        }
+        if (quit) break;
+        c->ready.store(0, std::memory_order_release);
+        tail = (tail + 1) % g_capacity;
+        ++drained;
+        if (c->slot_id >= 0 && c->slot_id < kMaxSlots && active.test(c->slot_id)) {
+          if (op < 0) { op = c->op_type; layer = c->layer_idx; }
+          cmds.push_back({c->slot_id, c->worker_id, c->bx * c->tx});
+          if (c->op_type == kOpSetSampling) {
+            SamplingState s;
+            s.do_sample = (c->x_key & 1) != 0;
+            s.temperature = static_cast<float>(c->x_key >> 1) / 10000.0f;
+            s.top_k = static_cast<int>(c->y0_key);
+            s.top_p = static_cast<float>(c->y1_key) / 10000.0f;
+            g_sampling[c->worker_id] = s;
+          }
+        }
+      }
+      g_ctrl->tail.store(tail, std::memory_order_release);
+      if (quit || g_ctrl->quit_flag.load(std::memory_order_acquire)) {
+        signal_done();
+        break;
+      }
+      if (cmds.empty()) continue;
+      if (op == kOpSetSampling) {
+        signal_done();
+        continue;
+      }
+      int64_t in_row, out_row;
+      row_bytes_for(op, layer, &in_row, &out_row);
+      std::string why;
+      validate(cmds.data(), static_cast<int>(cmds.size()), in_row, out_row, &good, &bad, &why);
+      if (!why.empty()) fprintf(stderr, "[swl aggregator] dropping commands: %s\n", why.c_str());
+      if (!bad.empty()) evict(bad, active);
+      int st = run_round(op, layer, good, g_stream);
+      if (st == SWL_OK) {
+        cudaError_t e = cudaStreamSynchronize(g_stream);
+        if (e != cudaSuccess) st = set_error(SWL_ERR_CUDA, "round: %s", cudaGetErrorString(e));
+      }
+      if (st != SWL_OK) {
+        fprintf(stderr, "[swl aggregator] round op=%d layer=%d failed: %s\n", op, layer, last_error());
+        signal_done();
+        return st;  // device state is unknown; stop like the reference does
+      }
+      signal_done();
+    }
+  }
+  return SWL_OK;
+}

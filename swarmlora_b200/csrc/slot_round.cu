@@ -1,0 +1,454 @@
+// Slot-round kernels: gather -> frozen-base GEMM -> scatter in one launch.
+//
+// Product path (kAlgoTensorCore), one CTA of 4 warps per (128 weight rows,
+// token chunk, K split):
+//   warp 0      TMA producer: streams 128x64 bf16 tiles of W (HBM, evict-first)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-3   gather producers: cp.async the chunk's token rows straight from
+//               each slot's input buffer into the 128B-swizzled B operand
+//   all warps   epilogue: TMEM -> shared memory (f32), reduce the K splits of
+//               the cluster through distributed shared memory, add bias, write
+//               bf16 rows directly into each slot's output buffer.
+// The MMA is "swap-AB": the 128 weight rows are the MMA M dimension and the
+// (few) decode tokens the N dimension, so a decode round of 28 tokens is a
+// 128 x 32 x 64 MMA stream whose speed is set by the W stream from HBM.
+//
+// Reference behaviour replaced: ext_aggregator.cpp:470-626
+// (execute_batched_gemm_slots: torch::cat gather, matmul_out, per-slot copy_).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.h"
+#include "ptx.cuh"
+#include "slot_round.h"
+
+namespace swl {
+
+__device__ unsigned int g_round_error_word = 0;
+
+namespace {
+
+constexpr int kBlockW = 128;                          // weight rows per CTA (MMA M)
+constexpr int kBlockK = 64;                           // K elements per stage (128 bytes)
+constexpr int kWStageBytes = kBlockW * kBlockK * 2;   // 16 KB
+constexpr int kThreads = 128;
+constexpr int kGatherThreads = 64;                    // warps 2-3
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;    // 2 s of device time
+
+enum ErrCode : unsigned int {
+  kErrWaitEmptyW = 1,
+  kErrWaitFull = 2,
+  kErrWaitEmptyX = 3,
+  kErrWaitAcc = 4,
+};
+
+template <int BN>
+struct TcCfg {
+  static constexpr int kStages = BN == 32 ? 5 : (BN == 64 ? 4 : (BN == 128 ? 6 : 4));
+  static constexpr int kXStageBytes = BN * 128;
+  static constexpr int kPipeBytes = kStages * (kWStageBytes + kXStageBytes);
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kPipeBytes + 256 + BN * 16;
+  static constexpr int kTmemCols = BN;
+  static_assert(BN * kBlockW * 4 <= kPipeBytes, "epilogue tile must fit in pipeline smem");
+};
+
+// Slot of global row `gr`: the largest s with row_start[s] <= gr.
+__device__ __forceinline__ int slot_of_row(const SlotTable& tab, int gr) {
+  int lo = 0, hi = tab.nslots - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (tab.row_start[mid] <= gr) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    slot_round_tc_kernel(const __grid_constant__ CUtensorMap wmap,
+                         const __grid_constant__ SlotTable tab, const RoundShape shape,
+                         int splits) {
+  using Cfg = TcCfg<BN>;
+  constexpr int STAGES = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* w_st = smem;
+  uint8_t* x_st = smem + STAGES * kWStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(x_st + STAGES * Cfg::kXStageBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accf + 1);
+  const __nv_bfloat16** row_in = reinterpret_cast<const __nv_bfloat16**>(tmem_holder + 2);
+  __nv_bfloat16** row_out = reinterpret_cast<__nv_bfloat16**>(tmem_holder + 2 + 2 * BN);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rank = splits > 1 ? static_cast<int>(ptx::cluster_rank()) : 0;
+  const int n0 = (blockIdx.x / splits) * kBlockW;
+  const int chunk_row0 = blockIdx.y * BN;
+  const int chunk_rows = min(BN, tab.total_rows - chunk_row0);
+  const int nkb = static_cast<int>((shape.K + kBlockK - 1) / kBlockK);
+  const int kb_begin = static_cast<int>(static_cast<int64_t>(rank) * nkb / splits);
+  const int kb_end = static_cast<int>(static_cast<int64_t>(rank + 1) * nkb / splits);
+  const int nk = kb_end - kb_begin;
+  unsigned int* err = &g_round_error_word;
+
+  // Row table for this token chunk: where each gathered row comes from and goes to.
+  for (int r = tid; r < BN; r += kThreads) {
+    const __nv_bfloat16* pin = nullptr;
+    __nv_bfloat16* pout = nullptr;
+    if (r < chunk_rows) {
+      int gr = chunk_row0 + r;
+      int s = slot_of_row(tab, gr);
+      int64_t local = gr - tab.row_start[s];
+      pin = tab.in[s] + local * shape.in_stride;
+      pout = tab.out[s] + local * shape.out_stride;
+    }
+    row_in[r] = pin;
+    row_out[r] = pout;
+  }
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&full[s], 1 + kGatherThreads);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    ptx::mbar_init(accf, 1);
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&wmap);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_holder, Cfg::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = ptx::policy_evict_first();
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (!ptx::mbar_wait(&empty[s], ph ^ 1, err, kErrWaitEmptyW, kWaitTimeoutNs)) break;
+        ptx::mbar_arrive_expect_tx(&full[s], kWStageBytes);
+        ptx::tma_load_2d(w_st + s * kWStageBytes, &wmap, &full[s], (kb_begin + i) * kBlockK, n0,
+                         pol);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::idesc_bf16_f32(kBlockW, BN);
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (!ptx::mbar_wait(&full[s], ph, err, kErrWaitFull, kWaitTimeoutNs)) break;
+        ptx::tc_fence_after();
+        const uint32_t wa = ptx::smem_addr(w_st + s * kWStageBytes);
+        const uint32_t xa = ptx::smem_addr(x_st + s * Cfg::kXStageBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBlockK / 16; ++kk) {
+          ptx::mma_bf16_ss(tmem, ptx::sw128_kmajor_desc(wa + kk * 32),
+                           ptx::sw128_kmajor_desc(xa + kk * 32), idesc,
+                           (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        ptx::tc_commit(&empty[s]);
+      }
+      ptx::tc_commit(accf);
+    }
+  } else {
+    // Gather producers. Row r of the B tile holds token row r of the chunk;
+    // its eight 16-byte pieces are stored XOR-swizzled by (r & 7) as the
+    // 128B-swizzle canonical layout requires. Rows past the chunk are zeros.
+    const int t = tid - 2 * 32;
+    bool ok = true;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1;
+      if (!ptx::mbar_wait(&empty[s], ph ^ 1, err, kErrWaitEmptyX, kWaitTimeoutNs)) {
+        ok = false;
+        break;
+      }
+      const int64_t k0 = static_cast<int64_t>(kb_begin + i) * kBlockK;
+      const uint32_t xs = ptx::smem_addr(x_st + s * Cfg::kXStageBytes);
+      for (int c = t; c < BN * 8; c += kGatherThreads) {
+        const int r = c >> 3, j = c & 7;
+        const __nv_bfloat16* src = row_in[r];
+        const int64_t kcol = k0 + j * 8;
+        const bool live = src != nullptr && kcol < shape.K;
+        ptx::cp_async_16(xs + r * 128 + ((j ^ (r & 7)) << 4),
+                         live ? static_cast<const void*>(src + kcol) : static_cast<const void*>(tab.in[0]),
+                         live ? 16u : 0u);
+      }
+      ptx::cp_async_commit();
+      if (i >= 1) {
+        ptx::cp_async_wait<1>();
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(&full[(i - 1) % STAGES]);
+      }
+    }
+    ptx::cp_async_wait<0>();
+    if (ok && nk >= 1) {
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive(&full[(nk - 1) % STAGES]);
+    }
+  }
+  __syncwarp();
+
+  // ---- epilogue ------------------------------------------------------------
+  const bool acc_ok = ptx::mbar_wait(accf, 0, err, kErrWaitAcc, kWaitTimeoutNs);
+  __syncwarp();
+  ptx::tc_fence_after();
+  float* P = reinterpret_cast<float*>(smem);  // [BN tokens][128 weight rows] f32
+  if (acc_ok && nk > 0) {
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t v[32];
+      ptx::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, v);
+      ptx::tc_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) P[(c0 + j) * kBlockW + q * 32 + lane] = __uint_as_float(v[j]);
+    }
+  } else {
+    for (int e = tid; e < BN * kBlockW; e += kThreads) P[e] = 0.f;
+  }
+  ptx::tc_fence_before();
+  if (splits > 1) ptx::cluster_sync();
+  else __syncthreads();
+
+  // Each CTA of the cluster reduces an equal share of the tile's 4-float groups.
+  const int groups = chunk_rows * (kBlockW / 4);
+  const int g_begin = static_cast<int>(static_cast<int64_t>(rank) * groups / splits);
+  const int g_end = static_cast<int>(static_cast<int64_t>(rank + 1) * groups / splits);
+  const uint32_t pbase = ptx::smem_addr(P);
+  for (int g = g_begin + tid; g < g_end; g += kThreads) {
+    const int r = g >> 5;
+    const int c = (g & 31) * 4;
+    const int64_t n = n0 + c;
+    if (n >= shape.N) continue;
+    const uint32_t off = static_cast<uint32_t>((r * kBlockW + c) * 4);
+    float4 acc;
+    if (splits > 1) {
+      acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < splits; ++p) {
+        const float4 v = ptx::ld_cluster_f4(ptx::map_peer(pbase + off, p));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+    } else {
+      acc = *reinterpret_cast<const float4*>(P + r * kBlockW + c);
+    }
+    if (shape.bias) {
+      acc.x += __bfloat162float(shape.bias[n]);
+      acc.y += __bfloat162float(shape.bias[n + 1]);
+      acc.z += __bfloat162float(shape.bias[n + 2]);
+      acc.w += __bfloat162float(shape.bias[n + 3]);
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 packed;
+    packed.x = *reinterpret_cast<uint32_t*>(&lo);
+    packed.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(row_out[r] + n) = packed;
+  }
+
+  if (splits > 1) ptx::cluster_sync();  // peers may still read our P
+  else __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+}
+
+// Plain CUDA-core round: one warp per (output feature, token row). Slow but
+// independent of the tensor-core machinery; used to cross-check on device.
+__global__ void slot_round_simt_kernel(const __nv_bfloat16* __restrict__ W,
+                                       const __grid_constant__ SlotTable tab,
+                                       const RoundShape shape) {
+  const int64_t n = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int gr = blockIdx.y;
+  if (n >= shape.N || gr >= tab.total_rows) return;
+  const int s = slot_of_row(tab, gr);
+  const int64_t local = gr - tab.row_start[s];
+  const __nv_bfloat16* x = tab.in[s] + local * shape.in_stride;
+  const __nv_bfloat16* w = W + n * shape.K;
+  float acc = 0.f;
+  for (int64_t k = lane; k < shape.K; k += 32)
+    acc += __bfloat162float(x[k]) * __bfloat162float(w[k]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) {
+    if (shape.bias) acc += __bfloat162float(shape.bias[n]);
+    tab.out[s][local * shape.out_stride + n] = __float2bfloat16_rn(acc);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int BN>
+int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& map, int splits,
+              cudaStream_t stream) {
+  using Cfg = TcCfg<BN>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(slot_round_tc_kernel<BN>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess)
+    return set_error(SWL_ERR_CUDA, "slot round: smem attribute: %s", cudaGetErrorString(attr_err));
+
+  const int n_tiles = static_cast<int>((shape.N + kBlockW - 1) / kBlockW);
+  const int m_chunks = (tab.total_rows + BN - 1) / BN;
+  const int nkb = static_cast<int>((shape.K + kBlockK - 1) / kBlockK);
+  if (splits <= 0) {
+    const int per_sm = BN <= 64 ? 2 : 1;
+    const int cap = sm_count() * per_sm;
+    splits = cap / std::max(1, n_tiles * m_chunks);
+    splits = std::min(splits, nkb / 4);
+  }
+  splits = std::max(1, std::min(splits, std::min(8, nkb)));
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * splits), static_cast<unsigned>(m_chunks), 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SWL_CUDA_TRY(cudaLaunchKernelEx(&cfg, slot_round_tc_kernel<BN>, map, tab, shape, splits));
+  return SWL_OK;
+}
+
+}  // namespace
+
+int encode_weight_tmap(CUtensorMap* map, const void* W, int64_t N, int64_t K) {
+  auto enc = tmap_encoder();
+  if (!enc) return set_error(SWL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(W) & 15) != 0 || (K * 2) % 16 != 0)
+    return set_error(SWL_ERR_ARG, "weight must be 16-byte aligned with K*2 a multiple of 16");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(kBlockW)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(W), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(SWL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return SWL_OK;
+}
+
+int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void* W,
+                      const CUtensorMap* tmap, int algo, int splits, cudaStream_t stream) {
+  if (tab.nslots <= 0 || tab.total_rows <= 0) return SWL_OK;  // nothing to do
+  if (tab.nslots > kMaxSlots) return set_error(SWL_ERR_ARG, "too many slots (%d)", tab.nslots);
+  if (shape.N <= 0 || shape.K <= 0 || (shape.N % 8) != 0 || (shape.K % 8) != 0)
+    return set_error(SWL_ERR_ARG, "round shape N=%lld K=%lld must be positive multiples of 8",
+                     (long long)shape.N, (long long)shape.K);
+  if (algo == kAlgoSimt) {
+    if (tab.total_rows > 65535) return set_error(SWL_ERR_ARG, "simt round: too many rows");
+    dim3 grid(static_cast<unsigned>((shape.N + 7) / 8), static_cast<unsigned>(tab.total_rows));
+    slot_round_simt_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(W), tab,
+                                                     shape);
+    SWL_CUDA_TRY(cudaGetLastError());
+    return SWL_OK;
+  }
+  CUtensorMap local;
+  if (!tmap) {
+    SWL_TRY(encode_weight_tmap(&local, W, shape.N, shape.K));
+    tmap = &local;
+  }
+  const int m = tab.total_rows;
+  if (m <= 32) return launch_tc<32>(tab, shape, *tmap, splits, stream);
+  if (m <= 64) return launch_tc<64>(tab, shape, *tmap, splits, stream);
+  if (m <= 128) return launch_tc<128>(tab, shape, *tmap, splits, stream);
+  return launch_tc<256>(tab, shape, *tmap, splits, stream);
+}
+
+int read_and_clear_device_error(unsigned int* code) {
+  unsigned int v = 0, zero = 0;
+  SWL_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_round_error_word, sizeof(v)));
+  if (v) SWL_CUDA_TRY(cudaMemcpyToSymbol(g_round_error_word, &zero, sizeof(zero)));
+  *code = v;
+  return SWL_OK;
+}
+
+}  // namespace swl
+
+using namespace swl;
+
+// Raw C-ABI round over caller-provided slot buffers (no pool): slot i reads
+// rows[i] rows of K bf16 from in_ptrs[i] (row stride in_stride elements) and
+// writes rows[i] rows of N bf16 to out_ptrs[i] (row stride out_stride).
+// W is [N, K] row-major bf16 on the current device; bias is [N] or NULL.
+// algo: 0 auto (tensor cores), 1 tensor cores, 2 CUDA cores.
+// splits: K-split factor (cluster size) for the tensor-core path; <= 0 = auto.
+SWL_EXPORT int swl_slot_gemm(const void* W, int64_t N, int64_t K, const void* bias, int nslots,
+                             const void* const* in_ptrs, void* const* out_ptrs, const int* rows,
+                             int64_t in_stride, int64_t out_stride, int algo, int splits,
+                             void* stream) {
+  if (!W || nslots < 0 || nslots > kMaxSlots || (nslots > 0 && (!in_ptrs || !out_ptrs || !rows)))
+    return set_error(SWL_ERR_ARG, "swl_slot_gemm: invalid arguments");
+  SlotTable tab;
+  tab.nslots = nslots;
+  int acc = 0;
+  for (int i = 0; i < nslots; ++i) {
+    if (rows[i] < 0) return set_error(SWL_ERR_ARG, "swl_slot_gemm: negative row count");
+    if (rows[i] > 0 && (!in_ptrs[i] || !out_ptrs[i]))
+      return set_error(SWL_ERR_ARG, "swl_slot_gemm: null slot buffer");
+    tab.row_start[i] = acc;
+    tab.in[i] = static_cast<const __nv_bfloat16*>(in_ptrs[i]);
+    tab.out[i] = static_cast<__nv_bfloat16*>(out_ptrs[i]);
+    acc += rows[i];
+  }
+  tab.row_start[nslots] = acc;
+  tab.total_rows = acc;
+  RoundShape shape{N, K, in_stride > 0 ? in_stride : K, out_stride > 0 ? out_stride : N,
+                   static_cast<const __nv_bfloat16*>(bias)};
+  for (int i = 0; i < nslots; ++i) {
+    if ((reinterpret_cast<uintptr_t>(tab.in[i]) & 15) || (reinterpret_cast<uintptr_t>(tab.out[i]) & 7))
+      return set_error(SWL_ERR_ARG, "swl_slot_gemm: slot buffers must be 16-byte (in) / 8-byte (out) aligned");
+  }
+  if ((shape.in_stride % 8) || (shape.out_stride % 4))
+    return set_error(SWL_ERR_ARG, "swl_slot_gemm: row strides must keep rows aligned");
+  return launch_slot_round(tab, shape, W, nullptr, algo == kAlgoSimt ? kAlgoSimt : kAlgoTensorCore,
+                           splits, static_cast<cudaStream_t>(stream));
+}
+
+// Reads (and clears) the device error word set by bounded waits in the round
+// kernels; synchronous. *code = 0 means no wait ran out.
+SWL_EXPORT int swl_round_device_error(unsigned int* code) {
+  if (!code) return set_error(SWL_ERR_ARG, "null code pointer");
+  return read_and_clear_device_error(code);
+}

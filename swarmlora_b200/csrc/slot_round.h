@@ -1,0 +1,57 @@
+// Gather -> frozen-base GEMM -> scatter over the slot pool, as one kernel.
+//
+// A round computes, for every active slot s with rows_s tokens,
+//   out_s[r, :] = in_s[r, :] @ W^T (+ bias)   for r in [0, rows_s)
+// where in_s is the slot's [rows_s, K] bf16 input buffer and out_s its
+// [rows_s, N] bf16 output buffer, W is the fused [N, K] weight. This is
+// the reference's execute_batched_gemm_slots (ext_aggregator.cpp:470-626:
+// torch::cat of the slot inputs, matmul_out against W.t(), copy_ back per
+// slot) without the concatenated or staged intermediate.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "shm_abi.h"
+
+namespace swl {
+
+// Slot table handed to the kernel by value (kernel parameter space): the
+// rows of slot i are global rows [row_start[i], row_start[i+1]).
+struct SlotTable {
+  int nslots;
+  int total_rows;
+  int row_start[kMaxSlots + 1];
+  const __nv_bfloat16* in[kMaxSlots];
+  __nv_bfloat16* out[kMaxSlots];
+};
+
+struct RoundShape {
+  int64_t N;            // output features (rows of W)
+  int64_t K;            // input features
+  int64_t in_stride;    // elements between consecutive rows of a slot input
+  int64_t out_stride;   // elements between consecutive rows of a slot output
+  const __nv_bfloat16* bias;  // [N] or nullptr
+};
+
+enum RoundAlgo : int {
+  kAlgoAuto = 0,
+  kAlgoTensorCore = 1,  // tcgen05 + TMA weight stream (the product path)
+  kAlgoSimt = 2,        // plain CUDA-core kernel, used as an on-device cross-check
+};
+
+// Encodes the TMA descriptor for a row-major [N, K] bf16 weight (box 64 x 128,
+// 128-byte swizzle). Returns SWL_OK or an error status.
+int encode_weight_tmap(CUtensorMap* map, const void* W, int64_t N, int64_t K);
+
+// Launches one round on `stream`. `tmap` may be nullptr (encoded on the fly).
+// `splits` <= 0 picks the split-K factor automatically.
+int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void* W,
+                      const CUtensorMap* tmap, int algo, int splits, cudaStream_t stream);
+
+// Device error word written by bounded waits inside round kernels (0 = ok).
+int read_and_clear_device_error(unsigned int* code);
+
+}  // namespace swl
