@@ -81,6 +81,16 @@ SIGNATURES: dict[str, tuple] = {
     # ---- kernels callable directly
     "swl_slot_gemm": (_i32, [_p, _i64, _i64, _p, _i32, _pp, _pp, _pi32, _i64, _i64, _i32, _i32, _p]),
     "swl_round_device_error": (_i32, [_pu32]),
+    # ---- worker kernels
+    "swl_lora_shrink": (_i32, [_i32, _pi32, _pp, _i64, _pp, _i64, _i32, _i32, _p, _p]),
+    "swl_lora_expand": (_i32, [_i32, _pi32, _pp, _i64, _pp, _pp, _i64, _pp, _i64, _i64, _i32,
+                               _i32, _pi64, _f32, _i32, _i32, _p, _p]),
+    "swl_rope_append": (_i32, [_i32, _pi32, _pp, _i64, _pp, _pp, _pp, _pp, _i32, _i32, _i32, _i32,
+                               _p, _i32, _p, _p]),
+    "swl_attention_part_floats": (_i64, [_i32, _i32, _i32, _i32]),
+    "swl_paged_attention": (_i32, [_i32, _pi32, _pp, _pp, _pp, _pp, _pp, _i64, _i32, _i32, _i32,
+                                   _i32, _f32, _i32, _p, _p, _p]),
+    "swl_rms_norm": (_i32, [_i32, _pi32, _pp, _i64, _pp, _i64, _p, _i64, _f32, _p]),
 }
 
 _lib = None

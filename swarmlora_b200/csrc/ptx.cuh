@@ -106,6 +106,15 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+// Arrives on `bar` (counted in its expected arrivals) once every cp.async this
+// thread issued so far has landed; the thread itself does not wait.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
 // Makes this thread's generic-proxy shared-memory writes visible to the
 // async proxy (the tensor core reads operands through it).
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -147,6 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (i / STAGES) & 1;
         if (!ptx::mbar_wait(&full[s], ph, err, kErrWaitFull, kWaitTimeoutNs)) break;
         ptx::tc_fence_after();
+        ptx::fence_proxy_async_smem();  // gathered rows were written by cp.async
         const uint32_t wa = ptx::smem_addr(w_st + s * kWStageBytes);
         const uint32_t xa = ptx::smem_addr(x_st + s * Cfg::kXStageBytes);
 #pragma unroll
@@ -164,14 +165,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // its eight 16-byte pieces are stored XOR-swizzled by (r & 7) as the
     // 128B-swizzle canonical layout requires. Rows past the chunk are zeros.
     const int t = tid - 2 * 32;
-    bool ok = true;
     for (int i = 0; i < nk; ++i) {
       const int s = i % STAGES;
       const uint32_t ph = (i / STAGES) & 1;
-      if (!ptx::mbar_wait(&empty[s], ph ^ 1, err, kErrWaitEmptyX, kWaitTimeoutNs)) {
-        ok = false;
-        break;
-      }
+      if (!ptx::mbar_wait(&empty[s], ph ^ 1, err, kErrWaitEmptyX, kWaitTimeoutNs)) break;
       const int64_t k0 = static_cast<int64_t>(kb_begin + i) * kBlockK;
       const uint32_t xs = ptx::smem_addr(x_st + s * Cfg::kXStageBytes);
       for (int c = t; c < BN * 8; c += kGatherThreads) {
@@ -183,18 +180,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                          live ? static_cast<const void*>(src + kcol) : static_cast<const void*>(tab.in[0]),
                          live ? 16u : 0u);
       }
-      ptx::cp_async_commit();
-      if (i >= 1) {
-        ptx::cp_async_wait<1>();
-        ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(&full[(i - 1) % STAGES]);
-      }
+      // The arrival lands when this thread's copies have; no blocking here.
+      ptx::cp_async_arrive_noinc(&full[s]);
     }
-    ptx::cp_async_wait<0>();
-    if (ok && nk >= 1) {
-      ptx::fence_proxy_async_smem();
-      ptx::mbar_arrive(&full[(nk - 1) % STAGES]);
-    }
+    ptx::cp_async_wait_all();  // never leave copies in flight into freed smem
   }
   __syncwarp();
 
@@ -328,10 +317,15 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
   const int m_chunks = (tab.total_rows + BN - 1) / BN;
   const int nkb = static_cast<int>((shape.K + kBlockK - 1) / kBlockK);
   if (splits <= 0) {
+    // Largest power-of-two cluster (<= 8) that keeps the grid within the
+    // resident CTA capacity and at least 8 K-blocks per split. Clusters whose
+    // size does not divide the SMs of a GPC (3, 5, 6) schedule poorly.
     const int per_sm = BN <= 64 ? 2 : 1;
     const int cap = sm_count() * per_sm;
-    splits = cap / std::max(1, n_tiles * m_chunks);
-    splits = std::min(splits, nkb / 4);
+    const int base = std::max(1, n_tiles * m_chunks);
+    splits = 1;
+    for (int s = 2; s <= 8; s *= 2)
+      if (base * s <= cap && nkb / s >= 8) splits = s;
   }
   splits = std::max(1, std::min(splits, std::min(8, nkb)));
 

@@ -1,0 +1,164 @@
+// C-ABI entry points for the worker-side kernels (worker_ops.cu). Every
+// argument is a plain pointer, size or array of per-slot device pointers;
+// segment i of a call covers rows[i] token rows of slot i.
+#include "common.h"
+#include "worker_ops.h"
+
+using namespace swl;
+
+namespace {
+
+int fill_segments(RowSegments* s, int nseg, const int* rows) {
+  if (nseg < 0 || nseg > kMaxSlots) return set_error(SWL_ERR_ARG, "segment count %d out of range", nseg);
+  if (nseg > 0 && !rows) return set_error(SWL_ERR_ARG, "null rows array");
+  s->nseg = nseg;
+  int acc = 0;
+  for (int i = 0; i < nseg; ++i) {
+    if (rows[i] < 0) return set_error(SWL_ERR_ARG, "negative row count");
+    s->row_start[i] = acc;
+    acc += rows[i];
+  }
+  s->row_start[nseg] = acc;
+  s->total_rows = acc;
+  return SWL_OK;
+}
+
+template <class T>
+T* cast(const void* p) {
+  return static_cast<T*>(const_cast<void*>(p));
+}
+
+}  // namespace
+
+// LoRA shrink (model_builder.py:258-262 first GEMM, worker_sync.py:305/:375
+// lora_A): ws[split][row][R] = partial sums of x[row] @ A over a K split.
+// A[i] is [K, R] row-major (NULL: slot has no adapter, nothing written).
+SWL_EXPORT int swl_lora_shrink(int nseg, const int* rows, const void* const* x, int64_t x_stride,
+                               const void* const* A, int64_t K, int R, int splits, float* ws,
+                               void* stream) {
+  LoraShrinkTable t;
+  SWL_TRY(fill_segments(&t.seg, nseg, rows));
+  for (int i = 0; i < nseg; ++i) {
+    t.x[i] = cast<const __nv_bfloat16>(x[i]);
+    t.A[i] = cast<const __nv_bfloat16>(A[i]);
+  }
+  return launch_lora_shrink(t, K, R, x_stride, splits, ws, static_cast<cudaStream_t>(stream));
+}
+
+// LoRA expand fused with the round epilogue. mode 0: out = base + d (QKV);
+// mode 1: out = resid + (base + d) (O / Down, d scaled by post_scale after
+// the expand); mode 2: out = silu(gate + dg) * (up + du) over the Gate+Up
+// output (out has n_total / 2 columns). block_end[nblocks] gives the fused
+// projections' column ends; B[i] is [n_total, r] (lora_B rows), NULL = none.
+SWL_EXPORT int swl_lora_expand(int nseg, const int* rows, const void* const* base,
+                               int64_t base_stride, const void* const* B, const void* const* resid,
+                               int64_t resid_stride, void* const* out, int64_t out_stride,
+                               int64_t n_total, int r, int nblocks, const int64_t* block_end,
+                               float post_scale, int mode, int splits, const float* ws,
+                               void* stream) {
+  if (nblocks < 1 || nblocks > 3 || !block_end) return set_error(SWL_ERR_ARG, "lora_expand: bad block layout");
+  if (mode < 0 || mode > 2) return set_error(SWL_ERR_ARG, "lora_expand: bad mode");
+  if (mode == kExpandResidual && !resid) return set_error(SWL_ERR_ARG, "lora_expand: residual mode needs resid");
+  LoraExpandTable t;
+  SWL_TRY(fill_segments(&t.seg, nseg, rows));
+  for (int i = 0; i < nseg; ++i) {
+    t.base[i] = cast<const __nv_bfloat16>(base[i]);
+    t.B[i] = B ? cast<const __nv_bfloat16>(B[i]) : nullptr;
+    t.resid[i] = resid ? cast<const __nv_bfloat16>(resid[i]) : nullptr;
+    t.out[i] = cast<__nv_bfloat16>(out[i]);
+  }
+  ExpandParams p;
+  p.n_total = n_total;
+  p.r = r;
+  p.nblocks = nblocks;
+  for (int b = 0; b < 3; ++b) p.block_end[b] = b < nblocks ? block_end[b] : n_total;
+  p.post_scale = post_scale;
+  p.mode = mode;
+  p.base_stride = base_stride;
+  p.out_stride = out_stride;
+  p.resid_stride = resid_stride;
+  p.splits = splits;
+  return launch_lora_expand(t, p, ws, static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+int fill_attn(AttnTable* t, int nseg, const int* rows, const void* const* qkv,
+              const void* const* block_tables, void* const* k_cache, void* const* v_cache,
+              const void* const* seqlens, void* const* out) {
+  SWL_TRY(fill_segments(&t->seg, nseg, rows));
+  for (int i = 0; i < nseg; ++i) {
+    t->qkv[i] = qkv ? cast<const __nv_bfloat16>(qkv[i]) : nullptr;
+    t->block_table[i] = cast<const int>(block_tables[i]);
+    t->k_cache[i] = cast<__nv_bfloat16>(k_cache[i]);
+    t->v_cache[i] = cast<__nv_bfloat16>(v_cache[i]);
+    t->seqlen[i] = cast<const int>(seqlens[i]);
+    t->out[i] = out ? cast<__nv_bfloat16>(out[i]) : nullptr;
+    if (!t->block_table[i] || !t->k_cache[i] || !t->v_cache[i] || !t->seqlen[i])
+      return set_error(SWL_ERR_ARG, "attention: null per-slot pointer");
+  }
+  return SWL_OK;
+}
+}  // namespace
+
+// NeoX rotary embedding of q and k (vLLM rotary_embedding, is_neox=True, as
+// called at worker_sync.py:192-193) and the paged KV append done inside
+// flash_attn_with_kvcache (worker_sync.py:196-203): token t of slot i sits at
+// position *seqlens[i] + t; rotated q goes to q_rot [total_rows, hq*D].
+SWL_EXPORT int swl_rope_append(int nseg, const int* rows, const void* const* qkv,
+                               int64_t qkv_stride, const void* const* block_tables,
+                               void* const* k_cache, void* const* v_cache,
+                               const void* const* seqlens, int hq, int hkv, int head_dim, int page,
+                               const void* cos_sin, int max_pos, void* q_rot, void* stream) {
+  AttnTable t;
+  SWL_TRY(fill_attn(&t, nseg, rows, qkv, block_tables, k_cache, v_cache, seqlens, nullptr));
+  AttnParams p = {};
+  p.hq = hq; p.hkv = hkv; p.head_dim = head_dim; p.page = page;
+  p.qkv_stride = qkv_stride;
+  p.cos_sin = cast<const __nv_bfloat16>(cos_sin);
+  p.max_pos = max_pos;
+  p.q_rot = cast<__nv_bfloat16>(q_rot);
+  return launch_rope_append(t, p, static_cast<cudaStream_t>(stream));
+}
+
+// Number of fp32 scratch floats swl_paged_attention needs in `part` for this
+// launch shape (0 when the context is not split).
+SWL_EXPORT int64_t swl_attention_part_floats(int total_rows, int hq, int hkv, int max_len) {
+  return attention_part_floats(total_rows, hq, attention_splits(total_rows, hkv, max_len));
+}
+
+// Causal GQA attention of each new token over its slot's paged cache
+// (flash_attn_with_kvcache semantics, worker_sync.py:196-203): token t of
+// slot i attends to cache positions 0 .. *seqlens[i] + t. max_len bounds
+// every slot's *seqlens + rows (it sizes the context split). out[i] rows get
+// [hq * D] bf16 (row stride out_stride).
+SWL_EXPORT int swl_paged_attention(int nseg, const int* rows, const void* const* block_tables,
+                                   const void* const* k_cache, const void* const* v_cache,
+                                   const void* const* seqlens, void* const* out, int64_t out_stride,
+                                   int hq, int hkv, int head_dim, int page, float scale, int max_len,
+                                   const void* q_rot, float* part, void* stream) {
+  AttnTable t;
+  SWL_TRY(fill_attn(&t, nseg, rows, nullptr, block_tables, const_cast<void* const*>(k_cache),
+                    const_cast<void* const*>(v_cache), seqlens, out));
+  AttnParams p = {};
+  p.hq = hq; p.hkv = hkv; p.head_dim = head_dim; p.page = page;
+  p.out_stride = out_stride;
+  p.scale = scale;
+  p.max_len = max_len;
+  p.q_rot = cast<__nv_bfloat16>(q_rot);
+  p.part = part;
+  return launch_paged_attention(t, p, static_cast<cudaStream_t>(stream));
+}
+
+// LlamaRMSNorm over rows: out = w * bf16(x * rsqrt(mean(x^2) + eps)).
+SWL_EXPORT int swl_rms_norm(int nseg, const int* rows, const void* const* x, int64_t x_stride,
+                            void* const* out, int64_t out_stride, const void* w, int64_t hidden,
+                            float eps, void* stream) {
+  NormTable t;
+  SWL_TRY(fill_segments(&t.seg, nseg, rows));
+  for (int i = 0; i < nseg; ++i) {
+    t.x[i] = cast<const __nv_bfloat16>(x[i]);
+    t.out[i] = cast<__nv_bfloat16>(out[i]);
+  }
+  return launch_rms_norm(t, cast<const __nv_bfloat16>(w), hidden, eps, x_stride, out_stride,
+                         static_cast<cudaStream_t>(stream));
+}

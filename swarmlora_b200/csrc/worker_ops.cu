@@ -1,0 +1,482 @@
+// Worker-side kernels around each round, batched over slots.
+//
+//  * lora_shrink   t = x @ A (A = [K, R], R = rank * fused projections),
+//                  split over K into fp32 partials.
+//  * lora_expand   d = bf16(t) @ B^T per fused projection, then the
+//                  epilogue of the round read in place from the slot output:
+//                  QKV: base + d; O/Down: resid + (base + bf16(d * s));
+//                  Gate+Up: silu(gate + dg) * (up + du).
+//  * rope_append   NeoX RoPE on q and k, k/v appended to the paged cache.
+//  * paged_attention  causal GQA attention of each new token over its slot's
+//                  pages (split over the context, partials combined).
+//  * rms_norm      LlamaRMSNorm.
+//
+// Rounding follows the reference's bf16 tensors: the LoRA intermediate t and
+// delta d are bf16 (model_builder.py:258-262, worker_sync.py:305/:375), the
+// adds are bf16 adds (worker_sync.py:270-389), RoPE arithmetic is per-op bf16
+// (vLLM rotary_embedding), RMSNorm rounds the normalised row before the weight
+// multiply (HF LlamaRMSNorm), silu(g) is rounded before the multiply by up.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+
+#include "common.h"
+#include "worker_ops.h"
+
+namespace swl {
+
+namespace {
+
+__device__ __forceinline__ float bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ int seg_of_row(const RowSegments& s, int gr) {
+  int lo = 0, hi = s.nseg - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (s.row_start[mid] <= gr) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// ---- LoRA shrink ---------------------------------------------------------------
+// CTA = (segment, K split). Threads are (column group cg of 8 columns, k lane
+// kg); each accumulates ROWS rows x 8 columns over its k values, then the k
+// lanes are summed through shared memory. Output: ws[split][row][R] fp32.
+template <int ROWS>
+__global__ void __launch_bounds__(256) lora_shrink_kernel(const __grid_constant__ LoraShrinkTable tab,
+                                                          int64_t K, int R, int64_t x_stride,
+                                                          int splits, float* __restrict__ ws) {
+  extern __shared__ float red[];  // [256][ROWS * 8]
+  const int seg = blockIdx.x / splits, split = blockIdx.x % splits;
+  const __nv_bfloat16* A = tab.A[seg];
+  if (!A) return;
+  const int G = R / 8;
+  const int kgroups = 256 / G;
+  const int t = threadIdx.x;
+  const bool active = t < kgroups * G;
+  const int cg = t % G, kg = t / G;
+  const int64_t kb = (K * split / splits) & ~int64_t(7);
+  const int64_t ke = split == splits - 1 ? K : ((K * (split + 1) / splits) & ~int64_t(7));
+  const int row0 = tab.seg.row_start[seg], rows = tab.seg.row_start[seg + 1] - row0;
+  const int total = tab.seg.total_rows;
+  for (int r0 = 0; r0 < rows; r0 += ROWS) {
+    float acc[ROWS][8];
+#pragma unroll
+    for (int rr = 0; rr < ROWS; ++rr)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[rr][j] = 0.f;
+    if (active) {
+      const __nv_bfloat16* xr[ROWS];
+#pragma unroll
+      for (int rr = 0; rr < ROWS; ++rr)
+        xr[rr] = tab.x[seg] + static_cast<int64_t>(min(r0 + rr, rows - 1)) * x_stride;
+      for (int64_t k = kb + kg; k < ke; k += kgroups) {
+        float a[8];
+        load8(A + k * R + cg * 8, a);
+#pragma unroll
+        for (int rr = 0; rr < ROWS; ++rr) {
+          const float xv = __bfloat162float(xr[rr][k]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[rr][j] = fmaf(xv, a[j], acc[rr][j]);
+        }
+      }
+    }
+#pragma unroll
+    for (int rr = 0; rr < ROWS; ++rr)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) red[t * (ROWS * 8) + rr * 8 + j] = acc[rr][j];
+    __syncthreads();
+    for (int o = t; o < ROWS * R; o += 256) {
+      const int rr = o / R, c = o % R;
+      if (r0 + rr < rows) {
+        float s = 0.f;
+        for (int g = 0; g < kgroups; ++g) s += red[(g * G + c / 8) * (ROWS * 8) + rr * 8 + (c & 7)];
+        ws[(static_cast<int64_t>(split) * total + row0 + r0 + rr) * R + c] = s;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---- LoRA expand + round epilogue ---------------------------------------------------
+// CTA = (segment, column tile of 256 outputs), one thread per output column;
+// the bf16 shrink result t of the segment's rows is rebuilt in shared memory
+// from the fp32 partials.
+template <int RANK>
+__global__ void __launch_bounds__(256) lora_expand_kernel(const __grid_constant__ LoraExpandTable tab,
+                                                          const ExpandParams p,
+                                                          const float* __restrict__ ws) {
+  extern __shared__ float tsm[];  // [rows_chunk][R]
+  constexpr int kRowsChunk = 16;
+  const int seg = blockIdx.x;
+  const int R = RANK * p.nblocks;
+  const int64_t n_out = p.mode == kExpandSiluMul ? p.n_total / 2 : p.n_total;
+  const int64_t n = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
+  const __nv_bfloat16* B = tab.B[seg];
+  const int row0 = tab.seg.row_start[seg], rows = tab.seg.row_start[seg + 1] - row0;
+  const int total = tab.seg.total_rows;
+  // This thread's B rows (one, or gate+up for the SwiGLU epilogue), kept in registers.
+  float b0[RANK], b1[RANK];
+  int blk0 = 0, blk1 = 1;
+  const bool live = n < n_out;
+  if (B && live) {
+    const int64_t c0 = n;
+    blk0 = c0 < p.block_end[0] ? 0 : (c0 < p.block_end[1] ? 1 : 2);
+#pragma unroll
+    for (int j = 0; j < RANK; j += 8) {
+      float v[8];
+      load8(B + c0 * RANK + j, v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) b0[j + q] = v[q];
+    }
+    if (p.mode == kExpandSiluMul) {
+      const int64_t c1 = n + n_out;
+      blk1 = c1 < p.block_end[0] ? 0 : (c1 < p.block_end[1] ? 1 : 2);
+#pragma unroll
+      for (int j = 0; j < RANK; j += 8) {
+        float v[8];
+        load8(B + c1 * RANK + j, v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) b1[j + q] = v[q];
+      }
+    }
+  }
+  for (int r0 = 0; r0 < rows; r0 += kRowsChunk) {
+    const int nr = min(kRowsChunk, rows - r0);
+    if (B) {
+      __syncthreads();
+      for (int o = threadIdx.x; o < nr * R; o += blockDim.x) {
+        const int rr = o / R, c = o % R;
+        float s = 0.f;
+        for (int sp = 0; sp < p.splits; ++sp)
+          s += ws[(static_cast<int64_t>(sp) * total + row0 + r0 + rr) * R + c];
+        tsm[rr * R + c] = bf(s);  // t is a bf16 tensor in the reference
+      }
+      __syncthreads();
+    }
+    if (!live) continue;
+    for (int rr = 0; rr < nr; ++rr) {
+      const int64_t lr = r0 + rr;
+      const __nv_bfloat16* base = tab.base[seg] + lr * p.base_stride;
+      __nv_bfloat16* out = tab.out[seg] + lr * p.out_stride;
+      float d0 = 0.f, d1 = 0.f;
+      if (B) {
+        const float* t = tsm + rr * R;
+#pragma unroll
+        for (int j = 0; j < RANK; ++j) d0 = fmaf(t[blk0 * RANK + j], b0[j], d0);
+        d0 = bf(d0);
+        if (p.post_scale != 0.f) d0 = bf(d0 * p.post_scale);
+        if (p.mode == kExpandSiluMul) {
+#pragma unroll
+          for (int j = 0; j < RANK; ++j) d1 = fmaf(t[blk1 * RANK + j], b1[j], d1);
+          d1 = bf(d1);
+        }
+      }
+      if (p.mode == kExpandSiluMul) {
+        const float g = B ? bf(__bfloat162float(base[n]) + d0) : __bfloat162float(base[n]);
+        const float u = B ? bf(__bfloat162float(base[n + n_out]) + d1) : __bfloat162float(base[n + n_out]);
+        const float sg = bf(g / (1.f + __expf(-g)));
+        out[n] = __float2bfloat16_rn(sg * u);
+      } else {
+        float v = B ? bf(__bfloat162float(base[n]) + d0) : __bfloat162float(base[n]);
+        if (p.mode == kExpandResidual) v = __bfloat162float(tab.resid[seg][lr * p.resid_stride + n]) + v;
+        out[n] = __float2bfloat16_rn(v);
+      }
+    }
+  }
+}
+
+// ---- RoPE + KV append ----------------------------------------------------------------
+__global__ void __launch_bounds__(256) rope_append_kernel(const __grid_constant__ AttnTable tab,
+                                                          const AttnParams p) {
+  const int gr = blockIdx.x;
+  const int s = seg_of_row(tab.seg, gr);
+  const int local = gr - tab.seg.row_start[s];
+  const int pos = *tab.seqlen[s] + local;
+  const int D = p.head_dim, half = D / 2;
+  const __nv_bfloat16* row = tab.qkv[s] + static_cast<int64_t>(local) * p.qkv_stride;
+  const __nv_bfloat16* cs = p.cos_sin + static_cast<int64_t>(pos) * D;
+  const int page = tab.block_table[s][pos / p.page];
+  const int off = pos % p.page;
+  const int64_t kv_row = (static_cast<int64_t>(page) * p.page + off) * p.hkv;
+  const int q_pairs = p.hq * half, k_pairs = p.hkv * half;
+  for (int i = threadIdx.x; i < q_pairs + k_pairs; i += blockDim.x) {
+    const bool is_q = i < q_pairs;
+    const int ii = is_q ? i : i - q_pairs;
+    const int h = ii / half, d = ii % half;
+    const __nv_bfloat16* src = row + (is_q ? 0 : p.hq * D) + h * D;
+    const float x = __bfloat162float(src[d]), y = __bfloat162float(src[d + half]);
+    const float c = __bfloat162float(cs[d]), sn = __bfloat162float(cs[half + d]);
+    const float o1 = bf(bf(x * c) - bf(y * sn));
+    const float o2 = bf(bf(y * c) + bf(x * sn));
+    __nv_bfloat16* dst = is_q ? p.q_rot + static_cast<int64_t>(gr) * p.hq * D + h * D
+                              : tab.k_cache[s] + (kv_row + h) * D;
+    dst[d] = __float2bfloat16_rn(o1);
+    dst[d + half] = __float2bfloat16_rn(o2);
+  }
+  const __nv_bfloat16* vsrc = row + (p.hq + p.hkv) * D;
+  for (int i = threadIdx.x; i < p.hkv * D; i += blockDim.x)
+    tab.v_cache[s][kv_row * D + i] = vsrc[i];
+}
+
+// ---- paged attention -------------------------------------------------------------------
+// CTA = (token row, kv head, context split); warp w = query head kvh*G + w.
+// Lanes: grp = lane / 4 picks one of 8 keys per step, sub = lane % 4 holds
+// 32 of the 128 head dims. Online softmax in the log2 domain.
+constexpr int kD = 128;
+__global__ void __launch_bounds__(256) paged_attention_kernel(const __grid_constant__ AttnTable tab,
+                                                              const AttnParams p, int splits,
+                                                              float* __restrict__ part) {
+  const int gr = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.hq / p.hkv;
+  if (w >= G) return;
+  const int h = kvh * G + w;
+  const int s = seg_of_row(tab.seg, gr);
+  const int local = gr - tab.seg.row_start[s];
+  const int L = *tab.seqlen[s] + local + 1;  // causal: keys 0 .. pos
+  const int jb = static_cast<int>(static_cast<int64_t>(L) * split / splits);
+  const int je = static_cast<int>(static_cast<int64_t>(L) * (split + 1) / splits);
+  const int grp = lane >> 2, sub = lane & 3;
+  const float qscale = p.scale * 1.4426950408889634f;
+  float q[32];
+  {
+    const __nv_bfloat16* qp = p.q_rot + (static_cast<int64_t>(gr) * p.hq + h) * kD + sub * 32;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float v[8];
+      load8(qp + c * 8, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[c * 8 + i] = v[i] * qscale;
+    }
+  }
+  const int* bt = tab.block_table[s];
+  const __nv_bfloat16* kc = tab.k_cache[s];
+  const __nv_bfloat16* vc = tab.v_cache[s];
+  float m = -INFINITY, l = 0.f, o[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) o[i] = 0.f;
+  for (int j0 = jb; j0 < je; j0 += 8) {
+    const int j = j0 + grp;
+    const bool valid = j < je;
+    float kv[32], vv[32];
+    if (valid) {
+      const int64_t base = ((static_cast<int64_t>(bt[j / p.page]) * p.page + j % p.page) * p.hkv + kvh) * kD + sub * 32;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float t8[8];
+        load8(kc + base + c * 8, t8);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) kv[c * 8 + i] = t8[i];
+        load8(vc + base + c * 8, t8);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vv[c * 8 + i] = t8[i];
+      }
+    }
+    float sc = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) sc = fmaf(q[i], kv[i], sc);
+    }
+    sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+    if (!valid) sc = -INFINITY;
+    float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float mn = fmaxf(m, mx);
+    const float corr = exp2f(m - mn);
+    const float pr = valid ? exp2f(sc - mn) : 0.f;
+    float ps = pr + __shfl_xor_sync(0xffffffffu, pr, 4);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+    l = l * corr + ps;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = o[i] * corr + (valid ? pr * vv[i] : 0.f);
+    m = mn;
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 4);
+    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 8);
+    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
+  }
+  if (grp != 0) return;
+  if (splits == 1) {
+    __nv_bfloat16* op = tab.out[s] + static_cast<int64_t>(local) * p.out_stride + h * kD + sub * 32;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) op[i] = __float2bfloat16_rn(o[i] * inv);
+  } else {
+    // partial record: [m, l, o[128]] per (row, head, split)
+    float* rec = part + ((static_cast<int64_t>(gr) * p.hq + h) * splits + split) * (kD + 2);
+    if (sub == 0) {
+      rec[0] = m;
+      rec[1] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) rec[2 + sub * 32 + i] = o[i];
+  }
+}
+
+// Combines the context splits: O = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s.
+__global__ void __launch_bounds__(128) attention_combine_kernel(const __grid_constant__ AttnTable tab,
+                                                                const AttnParams p, int splits,
+                                                                const float* __restrict__ part) {
+  const int gr = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int s = seg_of_row(tab.seg, gr);
+  const int local = gr - tab.seg.row_start[s];
+  const float* rec = part + (static_cast<int64_t>(gr) * p.hq + h) * splits * (kD + 2);
+  float M = -INFINITY;
+  for (int i = 0; i < splits; ++i) M = fmaxf(M, rec[i * (kD + 2)]);
+  float lsum = 0.f, acc = 0.f;
+  for (int i = 0; i < splits; ++i) {
+    const float mi = rec[i * (kD + 2)];
+    const float wgt = mi == -INFINITY ? 0.f : exp2f(mi - M);
+    lsum += wgt * rec[i * (kD + 2) + 1];
+    acc += wgt * rec[i * (kD + 2) + 2 + d];
+  }
+  tab.out[s][static_cast<int64_t>(local) * p.out_stride + h * kD + d] =
+      __float2bfloat16_rn(lsum > 0.f ? acc / lsum : 0.f);
+}
+
+// ---- RMSNorm ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rms_norm_kernel(const __grid_constant__ NormTable tab,
+                                                       const __nv_bfloat16* __restrict__ w,
+                                                       int64_t hidden, float eps, int64_t x_stride,
+                                                       int64_t out_stride) {
+  const int gr = blockIdx.x;
+  const int s = seg_of_row(tab.seg, gr);
+  const int64_t local = gr - tab.seg.row_start[s];
+  const __nv_bfloat16* x = tab.x[s] + local * x_stride;
+  __nv_bfloat16* y = tab.out[s] + local * out_stride;
+  float ss = 0.f;
+  for (int64_t i = threadIdx.x * 8; i < hidden; i += blockDim.x * 8) {
+    float v[8];
+    load8(x + i, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+  }
+  __shared__ float red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / static_cast<float>(hidden) + eps);
+  for (int64_t i = threadIdx.x * 8; i < hidden; i += blockDim.x * 8) {
+    float v[8], g[8];
+    load8(x + i, v);
+    load8(w + i, g);
+    __align__(16) __nv_bfloat162 o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      o[j] = __floats2bfloat162_rn(g[2 * j] * bf(v[2 * j] * inv), g[2 * j + 1] * bf(v[2 * j + 1] * inv));
+    *reinterpret_cast<uint4*>(y + i) = *reinterpret_cast<uint4*>(o);
+  }
+}
+
+}  // namespace
+
+int launch_lora_shrink(const LoraShrinkTable& tab, int64_t K, int R, int64_t x_stride, int splits,
+                       float* ws, cudaStream_t stream) {
+  if (tab.seg.nseg <= 0 || tab.seg.total_rows <= 0) return SWL_OK;
+  if (R % 8 || R <= 0 || R > 256 || K % 8) return set_error(SWL_ERR_ARG, "lora_shrink: R must be a multiple of 8 (<= 256), K of 8");
+  if (splits <= 0) return set_error(SWL_ERR_ARG, "lora_shrink: splits must be positive");
+  const int rows_max = [&] {
+    int m = 0;
+    for (int i = 0; i < tab.seg.nseg; ++i) m = std::max(m, tab.seg.row_start[i + 1] - tab.seg.row_start[i]);
+    return m;
+  }();
+  dim3 grid(tab.seg.nseg * splits);
+  if (rows_max <= 1) {
+    lora_shrink_kernel<1><<<grid, 256, 256 * 8 * sizeof(float), stream>>>(tab, K, R, x_stride, splits, ws);
+  } else {
+    lora_shrink_kernel<4><<<grid, 256, 256 * 32 * sizeof(float), stream>>>(tab, K, R, x_stride, splits, ws);
+  }
+  SWL_CUDA_TRY(cudaGetLastError());
+  return SWL_OK;
+}
+
+int launch_lora_expand(const LoraExpandTable& tab, const ExpandParams& p, const float* ws,
+                       cudaStream_t stream) {
+  if (tab.seg.nseg <= 0 || tab.seg.total_rows <= 0) return SWL_OK;
+  if (p.r % 8 || p.r <= 0 || p.r > 32) return set_error(SWL_ERR_ARG, "lora_expand: rank must be 8, 16, 24 or 32");
+  if (p.nblocks < 1 || p.nblocks > 3) return set_error(SWL_ERR_ARG, "lora_expand: 1..3 fused projections");
+  const int64_t n_out = p.mode == kExpandSiluMul ? p.n_total / 2 : p.n_total;
+  dim3 grid(tab.seg.nseg, static_cast<unsigned>((n_out + 255) / 256));
+  const size_t smem = 16 * p.r * p.nblocks * sizeof(float);
+  switch (p.r) {
+    case 8: lora_expand_kernel<8><<<grid, 256, smem, stream>>>(tab, p, ws); break;
+    case 16: lora_expand_kernel<16><<<grid, 256, smem, stream>>>(tab, p, ws); break;
+    case 24: lora_expand_kernel<24><<<grid, 256, smem, stream>>>(tab, p, ws); break;
+    default: lora_expand_kernel<32><<<grid, 256, smem, stream>>>(tab, p, ws); break;
+  }
+  SWL_CUDA_TRY(cudaGetLastError());
+  return SWL_OK;
+}
+
+int launch_rope_append(const AttnTable& tab, const AttnParams& p, cudaStream_t stream) {
+  if (tab.seg.total_rows <= 0) return SWL_OK;
+  if (p.head_dim != kD) return set_error(SWL_ERR_ARG, "rope: head_dim must be 128");
+  rope_append_kernel<<<tab.seg.total_rows, 256, 0, stream>>>(tab, p);
+  SWL_CUDA_TRY(cudaGetLastError());
+  return SWL_OK;
+}
+
+int attention_splits(int total_rows, int hkv, int max_len) {
+  // Enough context splits to give every SM a few CTAs, >= 64 keys per split.
+  const int base = std::max(1, total_rows * hkv);
+  int splits = std::max(1, std::min((4 * 148 + base - 1) / base, max_len / 64));
+  return std::min(splits, 32);
+}
+
+int64_t attention_part_floats(int total_rows, int hq, int splits) {
+  return splits > 1 ? static_cast<int64_t>(total_rows) * hq * splits * (kD + 2) : 0;
+}
+
+int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream_t stream) {
+  if (tab.seg.total_rows <= 0) return SWL_OK;
+  if (p.head_dim != kD || p.hq % p.hkv || p.hq / p.hkv > 8)
+    return set_error(SWL_ERR_ARG, "attention: head_dim 128 and at most 8 query heads per kv head");
+  const int splits = attention_splits(tab.seg.total_rows, p.hkv, p.max_len);
+  if (splits > 1 && !p.part) return set_error(SWL_ERR_ARG, "attention: missing partial scratch");
+  const int G = p.hq / p.hkv;
+  dim3 grid(tab.seg.total_rows, p.hkv, splits);
+  paged_attention_kernel<<<grid, 32 * G, 0, stream>>>(tab, p, splits, p.part);
+  SWL_CUDA_TRY(cudaGetLastError());
+  if (splits > 1) {
+    attention_combine_kernel<<<dim3(tab.seg.total_rows, p.hq), kD, 0, stream>>>(tab, p, splits, p.part);
+    SWL_CUDA_TRY(cudaGetLastError());
+  }
+  return SWL_OK;
+}
+
+int launch_rms_norm(const NormTable& tab, const __nv_bfloat16* w, int64_t hidden, float eps,
+                    int64_t x_stride, int64_t out_stride, cudaStream_t stream) {
+  if (tab.seg.total_rows <= 0) return SWL_OK;
+  if (hidden % 8) return set_error(SWL_ERR_ARG, "rms_norm: hidden must be a multiple of 8");
+  rms_norm_kernel<<<tab.seg.total_rows, 256, 0, stream>>>(tab, w, hidden, eps, x_stride, out_stride);
+  SWL_CUDA_TRY(cudaGetLastError());
+  return SWL_OK;
+}
+
+}  // namespace swl

@@ -1,0 +1,97 @@
+// Worker-side kernels around each aggregator round, batched over slots: each
+// slot (worker) brings its own adapter, residual and KV-cache pointers
+// through a by-value table, so one launch serves one worker or many.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "shm_abi.h"
+
+namespace swl {
+
+// Rows of slot i are global rows [row_start[i], row_start[i+1]).
+struct RowSegments {
+  int nseg;
+  int total_rows;
+  int row_start[kMaxSlots + 1];
+};
+
+// LoRA shrink: t[rows, R] = x[rows, K] @ A[K, R] (A row-major, R contiguous).
+struct LoraShrinkTable {
+  RowSegments seg;
+  const __nv_bfloat16* x[kMaxSlots];  // slot activations, row stride x_stride
+  const __nv_bfloat16* A[kMaxSlots];  // [K, R] or nullptr (no adapter)
+};
+
+// LoRA expand + epilogue over the fused output of a round.
+struct LoraExpandTable {
+  RowSegments seg;
+  const __nv_bfloat16* base[kMaxSlots];   // round output rows [rows, n_total] (row stride base_stride)
+  const __nv_bfloat16* B[kMaxSlots];      // [n_total, r] lora_B rows, or nullptr
+  const __nv_bfloat16* resid[kMaxSlots];  // [rows, n_out] residual (mode kResidual) or nullptr
+  __nv_bfloat16* out[kMaxSlots];          // destination rows (row stride out_stride)
+};
+
+enum ExpandMode : int {
+  kExpandAdd = 0,       // out = base + delta                              (QKV)
+  kExpandResidual = 1,  // out = resid + (base + delta)                    (O, Down)
+  kExpandSiluMul = 2,   // out = silu(gate + dg) * (up + du), n_out = n/2 (Gate+Up)
+};
+
+struct ExpandParams {
+  int64_t n_total;      // columns of the round output
+  int r;                // rank
+  int nblocks;          // fused projections (1, 2 or 3)
+  int64_t block_end[3]; // exclusive column end of each projection
+  float post_scale;     // delta scale applied after the expand (O/Down), 0 = none
+  int mode;
+  int64_t base_stride, out_stride, resid_stride;
+  int splits;           // shrink partial count
+};
+
+// RoPE + paged KV append + attention tables.
+struct AttnTable {
+  RowSegments seg;
+  const __nv_bfloat16* qkv[kMaxSlots];  // [rows, (Hq + 2 Hkv) * D] (LoRA already added)
+  const int* block_table[kMaxSlots];    // device int32 page ids of the slot
+  __nv_bfloat16* k_cache[kMaxSlots];    // [pages, page, Hkv, D] of this layer
+  __nv_bfloat16* v_cache[kMaxSlots];
+  __nv_bfloat16* out[kMaxSlots];        // [rows, Hq * D] attention output
+  const int* seqlen[kMaxSlots];         // device int: cached tokens before this step
+};
+
+struct AttnParams {
+  int hq, hkv, head_dim, page;
+  int64_t qkv_stride, out_stride;
+  float scale;
+  const __nv_bfloat16* cos_sin;  // [max_pos, D]: cos (D/2) | sin (D/2)
+  int max_pos;
+  int max_len;                   // upper bound of any slot's context after this step
+  __nv_bfloat16* q_rot;          // [total_rows, Hq * D] scratch for rotated q
+  float* part;                   // split partials, attention_scratch_floats() floats
+};
+
+// Context splits the attention launch will use, and the fp32 partial-record
+// scratch it needs (0 when unsplit).
+int attention_splits(int total_rows, int hkv, int max_len);
+int64_t attention_part_floats(int total_rows, int hq, int splits);
+
+// RMSNorm over rows.
+struct NormTable {
+  RowSegments seg;
+  const __nv_bfloat16* x[kMaxSlots];
+  __nv_bfloat16* out[kMaxSlots];
+};
+
+int launch_lora_shrink(const LoraShrinkTable& tab, int64_t K, int R, int64_t x_stride, int splits,
+                       float* ws, cudaStream_t stream);
+int launch_lora_expand(const LoraExpandTable& tab, const ExpandParams& p, const float* ws,
+                       cudaStream_t stream);
+int launch_rope_append(const AttnTable& tab, const AttnParams& p, cudaStream_t stream);
+int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream_t stream);
+int launch_rms_norm(const NormTable& tab, const __nv_bfloat16* w, int64_t hidden, float eps,
+                    int64_t x_stride, int64_t out_stride, cudaStream_t stream);
+
+}  // namespace swl

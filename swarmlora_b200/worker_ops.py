@@ -1,0 +1,122 @@
+"""Worker-side kernels (LoRA delta, RoPE + paged KV append, paged attention,
+RMSNorm) over one or many slots, through libswarmlora_b200.so.
+
+A worker process normally calls these for its single slot; the benchmark
+calls them for all slots at once. Adapter weights are packed once into the
+layouts the kernels read (`pack_lora_layer`), following the reference's
+FusedLoRA packing (model_builder.py:217-262): the fused QKV / Gate+Up A
+matrices are pre-scaled by alpha/r in bf16, O / Down scale after the expand
+(worker_sync.py:305, :375).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from ._native import check, i32_array, lib, ptr_array
+
+EXPAND_ADD, EXPAND_RESIDUAL, EXPAND_SILU_MUL = 0, 1, 2
+
+
+def _stream(stream):
+    return (stream if stream is not None else torch.cuda.current_stream()).cuda_stream
+
+
+def _ptrs(ts):
+    return ptr_array([t.data_ptr() if t is not None else None for t in ts])
+
+
+@dataclass
+class LoraLayer:
+    """One layer of one adapter, in kernel layout (all bf16, on device)."""
+    A_qkv: torch.Tensor   # [H, 3r]  = cat(Aq^T s, Ak^T s, Av^T s)
+    B_qkv: torch.Tensor   # [q+k+v, r] = cat(Bq, Bk, Bv)
+    A_o: torch.Tensor     # [H, r]   = Ao^T
+    B_o: torch.Tensor     # [H, r]
+    A_gu: torch.Tensor    # [H, 2r]  = cat(Ag^T s, Au^T s)
+    B_gu: torch.Tensor    # [2I, r]  = cat(Bg, Bu)
+    A_down: torch.Tensor  # [I, r]   = Ad^T
+    B_down: torch.Tensor  # [H, r]
+    rank: int
+    scaling: float
+
+
+def pack_lora_layer(w: dict, scaling: float) -> LoraLayer:
+    """w maps 'q','k','v','o','gate','up','down' -> (lora_A [r, in], lora_B [out, r])."""
+    def a_scaled(name):
+        return (w[name][0].t() * scaling).to(torch.bfloat16)  # A.t() * s in bf16 (model_builder.py:237)
+    r = int(w["q"][0].shape[0])
+    return LoraLayer(
+        A_qkv=torch.cat([a_scaled("q"), a_scaled("k"), a_scaled("v")], 1).contiguous(),
+        B_qkv=torch.cat([w["q"][1], w["k"][1], w["v"][1]], 0).contiguous(),
+        A_o=w["o"][0].t().contiguous(),
+        B_o=w["o"][1].contiguous(),
+        A_gu=torch.cat([a_scaled("gate"), a_scaled("up")], 1).contiguous(),
+        B_gu=torch.cat([w["gate"][1], w["up"][1]], 0).contiguous(),
+        A_down=w["down"][0].t().contiguous(),
+        B_down=w["down"][1].contiguous(),
+        rank=r,
+        scaling=float(scaling),
+    )
+
+
+def lora_shrink(xs, As, K: int, R: int, splits: int, ws: torch.Tensor, x_stride: int | None = None,
+                rows=None, stream=None) -> None:
+    rows = rows if rows is not None else [int(x.shape[0]) for x in xs]
+    x_stride = x_stride if x_stride is not None else int(xs[0].stride(0))
+    check(lib().swl_lora_shrink(len(xs), i32_array(rows), _ptrs(xs), x_stride, _ptrs(As), K, R,
+                                splits, ws.data_ptr(), _stream(stream)))
+
+
+def lora_expand(bases, Bs, outs, n_total: int, r: int, block_ends, mode: int, splits: int,
+                ws: torch.Tensor, resids=None, post_scale: float = 0.0, rows=None,
+                base_stride: int | None = None, out_stride: int | None = None,
+                resid_stride: int = 0, stream=None) -> None:
+    rows = rows if rows is not None else [int(b.shape[0]) for b in bases]
+    base_stride = base_stride if base_stride is not None else int(bases[0].stride(0))
+    out_stride = out_stride if out_stride is not None else int(outs[0].stride(0))
+    be = (C.c_int64 * 3)(*[int(x) for x in block_ends] + [n_total] * (3 - len(block_ends)))
+    check(lib().swl_lora_expand(
+        len(bases), i32_array(rows), _ptrs(bases), base_stride,
+        _ptrs(Bs) if Bs is not None else None,
+        _ptrs(resids) if resids is not None else None, resid_stride,
+        _ptrs(outs), out_stride, n_total, r, len(block_ends), be, float(post_scale), mode, splits,
+        ws.data_ptr(), _stream(stream)))
+
+
+def rope_append(qkvs, block_tables, k_caches, v_caches, seqlens, q_rot, cos_sin, hq: int, hkv: int,
+                head_dim: int = 128, page: int = 16, rows=None, qkv_stride: int | None = None,
+                stream=None) -> None:
+    rows = rows if rows is not None else [int(q.shape[0]) for q in qkvs]
+    qkv_stride = qkv_stride if qkv_stride is not None else int(qkvs[0].stride(0))
+    check(lib().swl_rope_append(len(qkvs), i32_array(rows), _ptrs(qkvs), qkv_stride,
+                                _ptrs(block_tables), _ptrs(k_caches), _ptrs(v_caches),
+                                _ptrs(seqlens), hq, hkv, head_dim, page, cos_sin.data_ptr(),
+                                int(cos_sin.shape[0]), q_rot.data_ptr(), _stream(stream)))
+
+
+def attention_part_floats(total_rows: int, hq: int, hkv: int, max_len: int) -> int:
+    return int(lib().swl_attention_part_floats(total_rows, hq, hkv, max_len))
+
+
+def paged_attention(rows, block_tables, k_caches, v_caches, seqlens, outs, q_rot, part, hq: int,
+                    hkv: int, max_len: int, scale: float, head_dim: int = 128, page: int = 16,
+                    out_stride: int | None = None, stream=None) -> None:
+    out_stride = out_stride if out_stride is not None else int(outs[0].stride(0))
+    check(lib().swl_paged_attention(len(rows), i32_array(rows), _ptrs(block_tables),
+                                    _ptrs(k_caches), _ptrs(v_caches), _ptrs(seqlens), _ptrs(outs),
+                                    out_stride, hq, hkv, head_dim, page, float(scale), max_len,
+                                    q_rot.data_ptr(), part.data_ptr() if part is not None else None,
+                                    _stream(stream)))
+
+
+def rms_norm(xs, outs, w: torch.Tensor, eps: float, rows=None, x_stride: int | None = None,
+             out_stride: int | None = None, stream=None) -> None:
+    rows = rows if rows is not None else [int(x.shape[0]) for x in xs]
+    x_stride = x_stride if x_stride is not None else int(xs[0].stride(0))
+    out_stride = out_stride if out_stride is not None else int(outs[0].stride(0))
+    check(lib().swl_rms_norm(len(xs), i32_array(rows), _ptrs(xs), x_stride, _ptrs(outs),
+                             out_stride, w.data_ptr(), int(w.shape[0]), float(eps),
+                             _stream(stream)))
