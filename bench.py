@@ -1,0 +1,448 @@
+"""Decode benchmark of the SwarmLoRA aggregator hot path on B200.
+
+Workload: Llama-3.1-8B architecture (32 layers, hidden
+4096, 32/8 heads, intermediate 14336, vocab 128256), random-init bf16 weights
+~N(0, 0.02); 28 decode slots per GPU, each with its own r=16 / alpha=32
+adapter on all 7 projections (A, B ~ N(0, 0.02)); per-slot KV context
+~U[256, 1024] in pages of 16; one token per slot per step (greedy).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Our arm: every GPU runs its own aggregator group (adapter workers are
+partitioned per GPU, no collective on the data path). One step = one decode
+token for all slots of the group, replayed from a CUDA graph of the fixed
+launch sequence. `value` is device-timed (CUDA events, max over ranks);
+`e2e` re-times the step through the same API with the step's input token ids
+copied from pinned host memory and the next tokens read back every step.
+The per-round kernel times (the metric's "us per gather-GEMM-scatter round")
+and the roofline of the dominant kernel come from a second timed phase that
+replays each round kind over all 32 layers' weights.
+
+Reference arm (--impl reference): the reference path restated on the host
+CPU (oracle/, torch on CPU with all host threads), bounded to one decoder
+layer per step and extrapolated to the 32-layer token.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s/GPU (Llama-3.1-8B shape, N=28 slots)"
+UNIT = "tok/s"
+N_SLOTS = 28
+CTX_LO, CTX_HI = 256, 1024
+MAX_NEW = 160
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--slots", type=int, default=N_SLOTS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=None)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during a timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port of the reference path)
+# ---------------------------------------------------------------------------
+
+def cpu_layer_sample(n_slots, seed=0):
+    """Builds one decoder layer + N slots on the host and returns a callable
+    timing one layer step (all 4 rounds, LoRA, RoPE, attention, norms)."""
+    import math
+    import torch
+    from oracle import reference_math as ref
+
+    torch.manual_seed(seed)
+    H, I, HQ, HKV, D, r, s = 4096, 14336, 32, 8, 128, 16, 2.0
+    bf = torch.bfloat16
+    rnd = lambda *sh: (torch.randn(*sh) * 0.02).to(bf)
+    # weights pre-converted to fp32 once (the reference keeps its weights resident)
+    Wqkv = ref.fuse_qkv(rnd(HQ * D, H), rnd(HKV * D, H), rnd(HKV * D, H)).float()
+    Wo, Wgu, Wd = rnd(H, H).float(), ref.fuse_gate_up(rnd(I, H), rnd(I, H)).float(), rnd(H, I).float()
+    w_in = torch.ones(H, dtype=bf)
+    ads = []
+    for _ in range(n_slots):
+        A = {k: rnd(r, i) for k, i in (("q", H), ("k", H), ("v", H), ("o", H), ("g", H), ("u", H), ("d", I))}
+        B = {k: rnd(o, r) for k, o in (("q", HQ * D), ("k", HKV * D), ("v", HKV * D), ("o", H), ("g", I), ("u", I), ("d", H))}
+        fq = ref.pack_fused_lora([A["q"], A["k"], A["v"]], [B["q"], B["k"], B["v"]], s, [HQ * D, HKV * D, HKV * D])
+        fg = ref.pack_fused_lora([A["g"], A["u"]], [B["g"], B["u"]], s, [I, I])
+        ads.append((fq, fg, A, B))
+    ctx = [int(c) for c in torch.randint(CTX_LO, CTX_HI + 1, (n_slots,))]
+    pages_per = (CTX_HI + 16 + 15) // 16
+    kc = torch.randn(n_slots * pages_per, 16, HKV, D).to(bf)
+    vc = torch.randn(n_slots * pages_per, 16, HKV, D).to(bf)
+    tables = [list(range(i * pages_per, (i + 1) * pages_per)) for i in range(n_slots)]
+    cs = ref.cos_sin_cache(ref.llama3_inv_freq(D), CTX_HI + 16)
+    xs = [torch.randn(1, H).to(bf) for _ in range(n_slots)]
+
+    def mm(xl, W):  # the round: cat -> x @ W^T -> split (ext_aggregator.cpp:545-625)
+        rows = [x.shape[0] for x in xl]
+        return list(torch.split((torch.cat(xl, 0).float() @ W.t()).to(bf), rows, 0))
+
+    def step():
+        h = xs
+        x = [ref.rms_norm(v, w_in) for v in h]
+        qkv = mm(x, Wqkv)
+        attn = []
+        for i in range(n_slots):
+            (fA, fB), _, A, B = ads[i]
+            parts = [ref.add_bf16(p, d) for p, d in zip(torch.split(qkv[i], [HQ * D, HKV * D, HKV * D], -1),
+                                                        ref.fused_lora_delta(x[i], fA, fB, [HQ * D, HKV * D, HKV * D]))]
+            pos = torch.tensor([ctx[i]])
+            q = ref.rope_neox(parts[0], pos, cs, D)
+            k = ref.rope_neox(parts[1], pos, cs, D)
+            attn.append(ref.attention_with_kvcache(q.reshape(1, HQ, D), k.reshape(1, HKV, D),
+                                                   parts[2].reshape(1, HKV, D), kc, vc, tables[i],
+                                                   ctx[i], 1.0 / math.sqrt(D)).reshape(1, HQ * D))
+        o = mm(attn, Wo)
+        h = [ref.add_bf16(h[i], ref.add_bf16(o[i], ref.lora_delta_scale_after(attn[i], ads[i][2]["o"], ads[i][3]["o"], s)))
+             for i in range(n_slots)]
+        x = [ref.rms_norm(v, w_in) for v in h]
+        gu = mm(x, Wgu)
+        act = []
+        for i in range(n_slots):
+            _, (gA, gB), _, _ = ads[i]
+            g, u = torch.split(gu[i], [I, I], -1)
+            dg, du = ref.fused_lora_delta(x[i], gA, gB, [I, I])
+            act.append(ref.silu_mul(ref.add_bf16(g, dg), ref.add_bf16(u, du)))
+        d = mm(act, Wd)
+        return [ref.add_bf16(h[i], ref.add_bf16(d[i], ref.lora_delta_scale_after(act[i], ads[i][2]["d"], ads[i][3]["d"], s)))
+                for i in range(n_slots)]
+
+    def lm_head_cost():
+        W = torch.randn(128256, H).float() * 0.02
+        x = torch.randn(n_slots, H)
+        t0 = time.perf_counter()
+        (x @ W.t()).argmax(-1)
+        dt = time.perf_counter() - t0
+        del W
+        return dt
+
+    return step, lm_head_cost
+
+
+def cpu_baseline(n_slots, seconds_budget=20.0):
+    import torch
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    step, lm_cost = cpu_layer_sample(n_slots)
+    step()  # warm-up
+    t_lm = lm_cost()
+    times = []
+    t_start = time.perf_counter()
+    while time.perf_counter() - t_start < seconds_budget and len(times) < 20:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    times.sort()
+    t_layer = times[len(times) // 2]
+    tok_s = n_slots / (32 * t_layer + t_lm)
+    return {"value": round(tok_s, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(times)} single-layer steps of {n_slots} decode slots (4 rounds + LoRA + RoPE + "
+                      f"paged attention + norms, median {t_layer*1e3:.1f} ms) x 32 layers + one LM-head "
+                      f"GEMV+argmax ({t_lm*1e3:.1f} ms); oracle/ on torch CPU, fp32 weights"}
+
+
+def reference_arm(args):
+    import torch
+    world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    step, lm_cost = cpu_layer_sample(args.slots)
+    t_lm = lm_cost()
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    t_layer = sum(times) / len(times)
+    ms_tok = (32 * t_layer + t_lm) * 1e3
+    value = args.slots / (ms_tok / 1e3)
+    line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_tok, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "BASELINE config 2: Llama-3.1-8B shape, 28 decode slots, r=16 adapters, "
+                                   "ctx U[256,1024]", "slots": args.slots, "layers": 32, "vocab": 128256,
+                       "sample": "one decoder layer per step, extrapolated x32 + LM head"},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} single-layer steps of {args.slots} slots on {threads} threads"},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def round_phase(grp, cfg, reps=3):
+    """Times each round kind over all layers' weights (> L2 in total) from a
+    CUDA graph; returns {op: us per launch} and the algorithmic bytes."""
+    import torch
+    from swarmlora_b200 import ext_aggregator as agg
+    ops = {"qkv": agg.OP_QKV_FUSED, "o": agg.OP_O_PROJ, "gate_up": agg.OP_GATE_UP_FUSED,
+           "down": agg.OP_DOWN_PROJ}
+    H, I, M = cfg.hidden, cfg.inter, grp.n
+    shapes = {"qkv": (cfg.qkv_n, H), "o": (H, cfg.hq * cfg.head_dim), "gate_up": (2 * I, H), "down": (H, I)}
+    s = torch.cuda.Stream()
+    out = {}
+    for name, op in ops.items():
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for l in range(cfg.layers):
+                grp._round(op, l, s.cuda_stream)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        with torch.cuda.stream(s):
+            for _ in range(reps):
+                g.replay()
+        b.record(s)
+        b.synchronize()
+        us = a.elapsed_time(b) * 1e3 / (reps * cfg.layers)
+        N, K = shapes[name]
+        byts = 2 * N * K + 2 * M * K + 2 * M * N
+        out[name] = {"us": round(us, 3), "bytes": byts, "gbs": round(byts / us / 1e3, 1)}
+        del g
+    return out
+
+
+def our_arm(args):
+    import torch
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from swarmlora_b200.engine import LLAMA_3_1_8B, SlotGroup, random_adapter, random_base
+
+    cfg = LLAMA_3_1_8B
+    n = args.slots
+    g = torch.Generator().manual_seed(1234 + rank)
+    ctx = [int(c) for c in torch.randint(CTX_LO, CTX_HI + 1, (n,), generator=g)]
+    base = random_base(cfg, seed=1, device=dev)
+    adapters = [random_adapter(cfg, seed=100 + rank * 1000 + i, device=dev) for i in range(n)]
+    total_new = args.warmup + args.steps + args.warmup + args.steps + 4
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=max(MAX_NEW, total_new), device=local, seed=rank)
+    start_tokens = torch.randint(0, cfg.vocab, (n,), generator=g)
+    grp.tokens.copy_(start_tokens)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        grp.enqueue_step(stream)  # eager warm-up (sets kernel attributes before capture)
+    torch.cuda.synchronize()
+    grp.reset_positions()
+    grp.tokens.copy_(start_tokens)
+    grp.capture(stream)
+
+    # ---- device-resident throughput -------------------------------------------
+    for _ in range(args.warmup):
+        grp.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.25)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            grp.replay()
+    ev1.record(stream)
+    ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    time.sleep(0.1)
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_max = max_over_ranks(ms, world, dev)
+    value = n * world * args.steps / (ms_max / 1e3)
+
+    # ---- end to end: host token ids in, next tokens out, every step --------------
+    grp.reset_positions()
+    h_in = torch.empty(n, dtype=torch.int64).pin_memory()
+    h_out = torch.empty(n, dtype=torch.int64).pin_memory()
+    h_in.copy_(grp.tokens.cpu())
+    for _ in range(args.warmup):
+        grp.tokens.copy_(h_in, non_blocking=True)
+        grp.replay()
+        h_out.copy_(grp.tokens, non_blocking=True)
+        torch.cuda.synchronize()
+        h_in.copy_(h_out)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            grp.tokens.copy_(h_in, non_blocking=True)
+            grp.replay()
+            h_out.copy_(grp.tokens, non_blocking=True)
+            stream.synchronize()
+            h_in.copy_(h_out)
+    e1.record(stream)
+    e1.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    e2e = n * world * args.steps / (e2e_ms / 1e3)
+
+    # ---- per-round kernel times (roofline of the dominant kernel) --------------
+    rounds = round_phase(grp, cfg)
+    peak, peak_kind = measured_peaks()
+    dom = max(rounds, key=lambda k: rounds[k]["us"])
+    achieved = rounds[dom]["bytes"] / rounds[dom]["us"] / 1e3
+    launches = grp.launches_per_step() * args.steps
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_baseline(n)
+        except Exception as e:  # report, do not fail the GPU number
+            cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"failed: {e}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights, adapters, KV contexts)",
+            "config": {"workload": "BASELINE config 2: Llama-3.1-8B shape (32 layers, vocab 128256), "
+                                   f"{n} decode slots/GPU, distinct r=16 adapters on 7 projections, "
+                                   f"ctx U[{CTX_LO},{CTX_HI}] paged 16, 1 token/slot/step, greedy",
+                       "slots_per_gpu": n, "parallelism": f"{world} independent aggregator groups",
+                       "l2": "weights (15 GB/step) far exceed L2; no flush needed",
+                       "us_per_round": {k: v["us"] for k, v in rounds.items()},
+                       "round_gbs": {k: v["gbs"] for k, v in rounds.items()}},
+            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 8 * n,
+                    "d2h_bytes_per_step": 8 * n},
+            "roofline": {"bound": "hbm", "kernel": f"slot_round_tc ({dom} round, M={n})",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": peak_kind},
+            "gpu_launches": launches,
+            "clocks": clk,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    grp.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    return our_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

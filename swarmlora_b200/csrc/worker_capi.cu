@@ -162,3 +162,27 @@ SWL_EXPORT int swl_rms_norm(int nseg, const int* rows, const void* const* x, int
   return launch_rms_norm(t, cast<const __nv_bfloat16>(w), hidden, eps, x_stride, out_stride,
                          static_cast<cudaStream_t>(stream));
 }
+
+// n device-to-device copies in one launch: bytes[i] from src[i] to dst[i]
+// (used to move tokens, embeddings and next-token ids between slot buffers
+// and worker buffers without one memcpy call per slot).
+SWL_EXPORT int swl_copy_rows(int n, const void* const* src, void* const* dst, const int64_t* bytes,
+                             void* stream) {
+  if (n < 0 || n > kMaxSlots || (n > 0 && (!src || !dst || !bytes)))
+    return set_error(SWL_ERR_ARG, "copy_rows: invalid arguments");
+  CopyTable t;
+  for (int i = 0; i < n; ++i) {
+    if (bytes[i] < 0 || (bytes[i] > 0 && (!src[i] || !dst[i])))
+      return set_error(SWL_ERR_ARG, "copy_rows: bad entry %d", i);
+    t.src[i] = src[i];
+    t.dst[i] = dst[i];
+    t.bytes[i] = bytes[i];
+  }
+  return launch_copy_rows(t, n, static_cast<cudaStream_t>(stream));
+}
+
+// p[0..n) += delta on the device (KV positions after a step).
+SWL_EXPORT int swl_advance_i32(int* p, int n, int delta, void* stream) {
+  if (n > 0 && !p) return set_error(SWL_ERR_ARG, "advance_i32: null pointer");
+  return launch_advance_i32(p, n, delta, static_cast<cudaStream_t>(stream));
+}

@@ -394,7 +394,43 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __grid_constant__ N
   }
 }
 
+// ---- batched copies / counters -------------------------------------------------------
+// One CTA per copy; 16-byte vectors when both ends and the size allow it.
+__global__ void copy_rows_kernel(const __grid_constant__ CopyTable tab) {
+  const int i = blockIdx.x;
+  const char* src = static_cast<const char*>(tab.src[i]);
+  char* dst = static_cast<char*>(tab.dst[i]);
+  const int64_t n = tab.bytes[i];
+  const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | n) & 15) == 0;
+  if (vec) {
+    for (int64_t k = threadIdx.x; k < n / 16; k += blockDim.x)
+      reinterpret_cast<uint4*>(dst)[k] = reinterpret_cast<const uint4*>(src)[k];
+  } else {
+    for (int64_t k = threadIdx.x; k < n; k += blockDim.x) dst[k] = src[k];
+  }
+}
+
+__global__ void advance_i32_kernel(int* p, int n, int delta) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] += delta;
+}
+
 }  // namespace
+
+int launch_copy_rows(const CopyTable& tab, int n, cudaStream_t stream) {
+  if (n <= 0) return SWL_OK;
+  if (n > kMaxSlots) return set_error(SWL_ERR_ARG, "copy_rows: at most %d copies per call", kMaxSlots);
+  copy_rows_kernel<<<n, 256, 0, stream>>>(tab);
+  SWL_CUDA_TRY(cudaGetLastError());
+  return SWL_OK;
+}
+
+int launch_advance_i32(int* p, int n, int delta, cudaStream_t stream) {
+  if (n <= 0) return SWL_OK;
+  advance_i32_kernel<<<(n + 255) / 256, 256, 0, stream>>>(p, n, delta);
+  SWL_CUDA_TRY(cudaGetLastError());
+  return SWL_OK;
+}
 
 int launch_lora_shrink(const LoraShrinkTable& tab, int64_t K, int R, int64_t x_stride, int splits,
                        float* ws, cudaStream_t stream) {

@@ -85,6 +85,15 @@ struct NormTable {
   __nv_bfloat16* out[kMaxSlots];
 };
 
+// Batched device copies (one per entry; at most kMaxSlots per launch).
+struct CopyTable {
+  const void* src[kMaxSlots];
+  void* dst[kMaxSlots];
+  int64_t bytes[kMaxSlots];
+};
+int launch_copy_rows(const CopyTable& tab, int n, cudaStream_t stream);
+int launch_advance_i32(int* p, int n, int delta, cudaStream_t stream);
+
 int launch_lora_shrink(const LoraShrinkTable& tab, int64_t K, int R, int64_t x_stride, int splits,
                        float* ws, cudaStream_t stream);
 int launch_lora_expand(const LoraExpandTable& tab, const ExpandParams& p, const float* ws,

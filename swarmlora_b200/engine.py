@@ -1,0 +1,312 @@
+"""One GPU's aggregator group stepped as a unit: the frozen base in the
+aggregator's slot pool plus N worker slots, each with its own LoRA adapter,
+RMSNorm weights and paged KV cache.
+
+`SlotGroup.step()` enqueues one decode token for every slot — the per-token
+loop of the reference's worker (worker_sync.py:1274-1425,
+_generate_one_token_all) with the aggregator's 1 + 4*L + 1 rounds
+(ext_aggregator.cpp:1095-1202) — as a fixed sequence of launches:
+
+  tokens -> slot inputs, EMBED round, embeddings -> hidden
+  per layer:
+    RMSNorm(h) -> slot input          LoRA shrink (x @ A_qkv)
+    QKV round (slot in -> slot out)   LoRA expand + add -> qkv
+    RoPE + paged KV append            attention -> slot input
+    LoRA shrink (attn @ A_o)          O round
+    LoRA expand, + residual -> h      RMSNorm(h) -> slot input
+    LoRA shrink (x @ A_gu)            Gate+Up round
+    LoRA expand, SiLU*mul -> slot in  LoRA shrink (act @ A_down)
+    Down round                        LoRA expand, + residual -> h
+  RMSNorm(h) -> slot input, LM_HEAD round (greedy), next token -> tokens,
+  KV positions += 1
+
+Every launch reads/writes the slot buffers in place, so the sequence has no
+host synchronisation and is captured once into a CUDA graph (`capture`) and
+replayed per token. Rounds go through the aggregator's C-ABI round entry
+(ownership and buffer bounds checked at capture time).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from . import ext_aggregator as agg
+from . import worker_ops as wo
+from ._native import check, i32_array, i64_array, lib, ptr_array
+
+BF16 = torch.bfloat16
+
+
+@dataclass
+class ModelConfig:
+    hidden: int = 4096
+    inter: int = 14336
+    layers: int = 32
+    hq: int = 32
+    hkv: int = 8
+    head_dim: int = 128
+    vocab: int = 128256
+    rank: int = 16
+    alpha: int = 32
+    eps: float = 1e-5
+    page: int = 16
+    max_seq_per_step: int = 16
+    rope_theta: float = 500000.0
+    rope_scaling: dict = field(default_factory=lambda: {
+        "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+        "original_max_position_embeddings": 8192, "rope_type": "llama3"})
+
+    @property
+    def qkv_n(self) -> int:
+        return (self.hq + 2 * self.hkv) * self.head_dim
+
+
+LLAMA_3_1_8B = ModelConfig()
+
+
+def cos_sin_cache(cfg: ModelConfig, max_pos: int, device) -> torch.Tensor:
+    """build_vllm_cos_sin_cache (paged_attention.py:131-142) from HF's
+    LlamaRotaryEmbedding inv_freq (model_builder.py:293-303)."""
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
+    hf = LlamaConfig(hidden_size=cfg.hidden, num_attention_heads=cfg.hq,
+                     num_key_value_heads=cfg.hkv, head_dim=cfg.head_dim,
+                     rope_theta=cfg.rope_theta, rope_scaling=dict(cfg.rope_scaling),
+                     max_position_embeddings=max(max_pos, 131072))
+    inv = LlamaRotaryEmbedding(config=hf).inv_freq.float().cpu()
+    t = torch.arange(max_pos, dtype=torch.float32)
+    f = torch.outer(t, inv)
+    return torch.cat([f.cos().to(BF16), f.sin().to(BF16)], -1).to(device)
+
+
+@dataclass
+class BaseWeights:
+    """Frozen base model in HF layout ([out, in], bf16) on the device."""
+    q: list
+    k: list
+    v: list
+    o: list
+    gate: list
+    up: list
+    down: list
+    in_norm: list
+    post_norm: list
+    final_norm: torch.Tensor
+    embed: torch.Tensor
+    lm_head: torch.Tensor
+
+
+def random_base(cfg: ModelConfig, seed: int, device, std: float = 0.02,
+                norm_noise: float = 0.0) -> BaseWeights:
+    """Seeded random-init base weights ~ N(0, std)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def w(*shape):
+        return (torch.randn(*shape, generator=g, device=device) * std).to(BF16)
+
+    def norm():
+        return (1.0 + norm_noise * torch.randn(cfg.hidden, generator=g, device=device)).to(BF16)
+
+    H, I, D = cfg.hidden, cfg.inter, cfg.head_dim
+    L = cfg.layers
+    return BaseWeights(
+        q=[w(cfg.hq * D, H) for _ in range(L)], k=[w(cfg.hkv * D, H) for _ in range(L)],
+        v=[w(cfg.hkv * D, H) for _ in range(L)], o=[w(H, cfg.hq * D) for _ in range(L)],
+        gate=[w(I, H) for _ in range(L)], up=[w(I, H) for _ in range(L)],
+        down=[w(H, I) for _ in range(L)],
+        in_norm=[norm() for _ in range(L)], post_norm=[norm() for _ in range(L)],
+        final_norm=norm(), embed=w(cfg.vocab, H), lm_head=w(cfg.vocab, H))
+
+
+def random_adapter(cfg: ModelConfig, seed: int, device, std: float = 0.02) -> list:
+    """Per layer: {'q': (A [r, in], B [out, r]), ...}, A, B ~ N(0, std)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    H, I, D, r = cfg.hidden, cfg.inter, cfg.head_dim, cfg.rank
+    dims = {"q": (H, cfg.hq * D), "k": (H, cfg.hkv * D), "v": (H, cfg.hkv * D),
+            "o": (cfg.hq * D, H), "gate": (H, I), "up": (H, I), "down": (I, H)}
+    out = []
+    for _ in range(cfg.layers):
+        layer = {}
+        for name, (i, o) in dims.items():
+            layer[name] = ((torch.randn(r, i, generator=g, device=device) * std).to(BF16),
+                           (torch.randn(o, r, generator=g, device=device) * std).to(BF16))
+        out.append(layer)
+    return out
+
+
+class SlotGroup:
+    """N decode slots on one aggregator (this process owns the pool)."""
+
+    def __init__(self, cfg: ModelConfig, base: BaseWeights, adapters: list, ctx_lens: list,
+                 max_new: int, device: int = 0, seed: int = 0, kv_std: float = 1.0,
+                 round_algo: int = 1, worker_id0: int = 1000):
+        self.cfg = cfg
+        self.dev = torch.device("cuda", device)
+        self.n = n = len(ctx_lens)
+        self.base = base
+        H, I, D = cfg.hidden, cfg.inter, cfg.head_dim
+        self.ctx0 = list(ctx_lens)
+        self.max_len = max(ctx_lens) + max_new
+        # --- aggregator: pool + fused weights ------------------------------------
+        agg.init_slot_pool(n, device, H, I, cfg.hkv, D, cfg.max_seq_per_step, 2)
+        agg.init_aggregator_begin(cfg.layers, device)
+        for l in range(cfg.layers):
+            agg.init_aggregator_layer(l, base.q[l], base.k[l], base.v[l], base.o[l],
+                                      torch.empty(0), base.gate[l], base.up[l], base.down[l],
+                                      torch.empty(0))
+        agg.init_aggregator_finalize()
+        agg.init_embed_lm_head_weights(base.embed, base.lm_head)
+        agg.set_round_algo(round_algo)
+        self.worker_ids = [worker_id0 + i for i in range(n)]
+        self.slot_ids = [agg.claim_slot(w)["slot_id"] for w in self.worker_ids]
+        bufs = [agg.slot_buffers(s) for s in self.slot_ids]
+        self.slot_in = [b[0] for b in bufs]
+        self.slot_out = [b[1] for b in bufs]
+        # --- workers: adapters, KV, buffers ---------------------------------------
+        self.lora = [None if ad is None else
+                     [wo.pack_lora_layer(ad[l], cfg.alpha / cfg.rank) for l in range(cfg.layers)]
+                     for ad in adapters]
+        pps = (self.max_len + cfg.page - 1) // cfg.page
+        g = torch.Generator(device=self.dev).manual_seed(seed + 7)
+        perm = torch.randperm(n * pps, generator=g, device=self.dev).to(torch.int32)
+        self.block_tables = [perm[i * pps:(i + 1) * pps].contiguous() for i in range(n)]
+        self.k_cache, self.v_cache = [], []
+        for _ in range(cfg.layers):
+            shape = (n * pps, cfg.page, cfg.hkv, D)
+            self.k_cache.append((torch.randn(shape, generator=g, device=self.dev) * kv_std).to(BF16))
+            self.v_cache.append((torch.randn(shape, generator=g, device=self.dev) * kv_std).to(BF16))
+        self.seqlens = torch.tensor(ctx_lens, dtype=torch.int32, device=self.dev)
+        self.cos_sin = cos_sin_cache(cfg, self.max_len + cfg.page, self.dev)
+        self.h = torch.empty(n, H, dtype=BF16, device=self.dev)
+        self.qkv = torch.empty(n, cfg.qkv_n, dtype=BF16, device=self.dev)
+        self.q_rot = torch.empty(n, cfg.hq * D, dtype=BF16, device=self.dev)
+        nparts = wo.attention_part_floats(n, cfg.hq, cfg.hkv, self.max_len)
+        self.part = torch.empty(max(1, nparts), dtype=torch.float32, device=self.dev)
+        self.splits = max(1, min(8, -(-296 // n)))
+        self.ws = torch.empty(self.splits * n * 3 * cfg.rank, dtype=torch.float32, device=self.dev)
+        self.tokens = torch.zeros(n, dtype=torch.int64, device=self.dev)
+        self._build_call_args()
+        self.graph = None
+
+    # ------------------------------------------------------------------------------
+    def _build_call_args(self):
+        cfg, n = self.cfg, self.n
+        H, I, D, r = cfg.hidden, cfg.inter, cfg.head_dim, cfg.rank
+        self.a_rows = i32_array([1] * n)
+        self.a_sids = i32_array(self.slot_ids)
+        self.a_wids = i32_array(self.worker_ids)
+        self.a_ones = i64_array([1] * n)
+        self.a_in = ptr_array(self.slot_in)
+        self.a_out = ptr_array(self.slot_out)
+        self.a_h = ptr_array([self.h[i].data_ptr() for i in range(n)])
+        self.a_qkv = ptr_array([self.qkv[i].data_ptr() for i in range(n)])
+        self.a_tok = ptr_array([self.tokens[i].data_ptr() for i in range(n)])
+        self.a_b8 = i64_array([8] * n)
+        self.a_bH = i64_array([2 * H] * n)
+        self.a_bt = ptr_array([t.data_ptr() for t in self.block_tables])
+        self.a_sl = ptr_array([self.seqlens[i].data_ptr() for i in range(n)])
+        self.a_kc = [ptr_array([k.data_ptr()] * n) for k in self.k_cache]
+        self.a_vc = [ptr_array([v.data_ptr()] * n) for v in self.v_cache]
+
+        def per_layer(attr):
+            return [ptr_array([None if self.lora[i] is None else
+                               getattr(self.lora[i][l], attr).data_ptr() for i in range(n)])
+                    for l in range(cfg.layers)]
+        self.A_qkv, self.B_qkv = per_layer("A_qkv"), per_layer("B_qkv")
+        self.A_o, self.B_o = per_layer("A_o"), per_layer("B_o")
+        self.A_gu, self.B_gu = per_layer("A_gu"), per_layer("B_gu")
+        self.A_dn, self.B_dn = per_layer("A_down"), per_layer("B_down")
+        self.ends_qkv = i64_array([cfg.hq * D, (cfg.hq + cfg.hkv) * D, cfg.qkv_n])
+        self.ends_gu = i64_array([I, 2 * I, 2 * I])
+        self.ends_h = i64_array([H, H, H])
+        self.scaling = cfg.alpha / r
+
+    def _round(self, op, layer, st):
+        check(lib().swl_agg_execute_round(op, layer, self.n, self.a_sids, self.a_wids, self.a_ones,
+                                          self.a_ones, st))
+
+    def enqueue_step(self, stream: torch.cuda.Stream) -> None:
+        """Queues one decode token for every slot on `stream` (no host sync)."""
+        L, cfg, n, st = lib(), self.cfg, self.n, stream.cuda_stream
+        H, I, D, r = cfg.hidden, cfg.inter, cfg.head_dim, cfg.rank
+        sp, ws = self.splits, self.ws.data_ptr()
+        rows = self.a_rows
+        check(L.swl_copy_rows(n, self.a_tok, self.a_in, self.a_b8, st))
+        self._round(agg.OP_EMBED, 0, st)
+        check(L.swl_copy_rows(n, self.a_out, self.a_h, self.a_bH, st))
+        for l in range(cfg.layers):
+            check(L.swl_rms_norm(n, rows, self.a_h, H, self.a_in, H, self.base.in_norm[l].data_ptr(),
+                                 H, cfg.eps, st))
+            check(L.swl_lora_shrink(n, rows, self.a_in, H, self.A_qkv[l], H, 3 * r, sp, ws, st))
+            self._round(agg.OP_QKV_FUSED, l, st)
+            check(L.swl_lora_expand(n, rows, self.a_out, cfg.qkv_n, self.B_qkv[l], None, 0, self.a_qkv,
+                                    cfg.qkv_n, cfg.qkv_n, r, 3, self.ends_qkv, 0.0, wo.EXPAND_ADD, sp,
+                                    ws, st))
+            check(L.swl_rope_append(n, rows, self.a_qkv, cfg.qkv_n, self.a_bt, self.a_kc[l],
+                                    self.a_vc[l], self.a_sl, cfg.hq, cfg.hkv, D, cfg.page,
+                                    self.cos_sin.data_ptr(), self.cos_sin.shape[0],
+                                    self.q_rot.data_ptr(), st))
+            check(L.swl_paged_attention(n, rows, self.a_bt, self.a_kc[l], self.a_vc[l], self.a_sl,
+                                        self.a_in, cfg.hq * D, cfg.hq, cfg.hkv, D, cfg.page,
+                                        1.0 / math.sqrt(D), self.max_len, self.q_rot.data_ptr(),
+                                        self.part.data_ptr(), st))
+            check(L.swl_lora_shrink(n, rows, self.a_in, cfg.hq * D, self.A_o[l], cfg.hq * D, r, sp,
+                                    ws, st))
+            self._round(agg.OP_O_PROJ, l, st)
+            check(L.swl_lora_expand(n, rows, self.a_out, H, self.B_o[l], self.a_h, H, self.a_h, H, H,
+                                    r, 1, self.ends_h, self.scaling, wo.EXPAND_RESIDUAL, sp, ws, st))
+            check(L.swl_rms_norm(n, rows, self.a_h, H, self.a_in, H, self.base.post_norm[l].data_ptr(),
+                                 H, cfg.eps, st))
+            check(L.swl_lora_shrink(n, rows, self.a_in, H, self.A_gu[l], H, 2 * r, sp, ws, st))
+            self._round(agg.OP_GATE_UP_FUSED, l, st)
+            check(L.swl_lora_expand(n, rows, self.a_out, 2 * I, self.B_gu[l], None, 0, self.a_in, I,
+                                    2 * I, r, 2, self.ends_gu, 0.0, wo.EXPAND_SILU_MUL, sp, ws, st))
+            check(L.swl_lora_shrink(n, rows, self.a_in, I, self.A_dn[l], I, r, sp, ws, st))
+            self._round(agg.OP_DOWN_PROJ, l, st)
+            check(L.swl_lora_expand(n, rows, self.a_out, H, self.B_dn[l], self.a_h, H, self.a_h, H, H,
+                                    r, 1, self.ends_h, self.scaling, wo.EXPAND_RESIDUAL, sp, ws, st))
+        check(L.swl_rms_norm(n, rows, self.a_h, H, self.a_in, H, self.base.final_norm.data_ptr(), H,
+                             cfg.eps, st))
+        self._round(agg.OP_LM_HEAD, 0, st)
+        check(L.swl_copy_rows(n, self.a_out, self.a_tok, self.a_b8, st))
+        check(L.swl_advance_i32(self.seqlens.data_ptr(), n, 1, st))
+
+    def launches_per_step(self) -> int:
+        """Kernel launches of one step (attention adds a combine launch when split)."""
+        attn = 2 if wo.attention_part_floats(self.n, self.cfg.hq, self.cfg.hkv, self.max_len) else 1
+        per_layer = 2 + 4 * 3 + 1 + attn  # norms, (shrink+round+expand)x4, rope, attention
+        return 3 + self.cfg.layers * per_layer + 1 + 2 + 1 + 1  # + LM head argmax
+
+    def capture(self, stream: torch.cuda.Stream | None = None) -> None:
+        """Captures one step into a CUDA graph (replayed by `replay`). Capture
+        does not execute the step, so the state is unchanged."""
+        s = stream or torch.cuda.Stream(self.dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            self.enqueue_step(s)
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def read_slot_rows(self, which: str, row_elems: int, dtype=BF16) -> torch.Tensor:
+        """Copies row 0 of every slot's input ('in') or output ('out') buffer
+        into a [n, row_elems] tensor (for checks; synchronises)."""
+        out = torch.empty(self.n, row_elems, dtype=dtype, device=self.dev)
+        src = self.a_in if which == "in" else self.a_out
+        nbytes = row_elems * out.element_size()
+        check(lib().swl_copy_rows(self.n, src, ptr_array([out[i].data_ptr() for i in range(self.n)]),
+                                  i64_array([nbytes] * self.n), torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        return out
+
+    def reset_positions(self) -> None:
+        self.seqlens.copy_(torch.tensor(self.ctx0, dtype=torch.int32))
+
+    def close(self) -> None:
+        self.graph = None
+        for s, w in zip(self.slot_ids, self.worker_ids):
+            agg.release_slot(s, w)
+        agg.cleanup_slot_pool()

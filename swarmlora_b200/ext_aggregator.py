@@ -1,0 +1,165 @@
+"""Drop-in for the reference's `ext_aggregator` module
+(src/cpp_extensions/ext_aggregator.cpp:1436-1517): slot pool, frozen base
+weights and the blocking main loop of the per-GPU aggregator.
+
+Same function names, argument names and return values; failures raise
+RuntimeError. Weight tensors are bf16 CUDA tensors with HF nn.Linear layout
+[out, in]; q|k|v and gate|up are fused into library-owned copies (so the
+caller may free its originals, as src/aggregator.py:351-356 does), while
+o / down / embed / lm_head are borrowed — this module keeps a reference so
+they stay alive, as the reference's detach() does.
+
+Additions (not in the reference): `execute_round` runs one round over pool
+slots on a given stream, `slot_buffers` returns a slot's device addresses
+for in-process drivers, `set_round_algo` selects the round kernel.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from ._native import check, i32_array, i64_array, lib
+
+OP_O_PROJ = 3
+OP_DOWN_PROJ = 6
+OP_QKV_FUSED = 9
+OP_GATE_UP_FUSED = 10
+OP_EMBED = 11
+OP_LM_HEAD = 12
+OP_SET_SAMPLING = 13
+MAX_SLOTS = 128
+
+_borrowed: dict = {}
+
+
+def _bf16_cuda(t: torch.Tensor, what: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.bfloat16:
+        raise RuntimeError(f"{what} must be a bf16 CUDA tensor")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{what} must be contiguous")
+    return t
+
+
+def init_slot_pool(num_slots: int, device_index: int, hidden_dim: int, intermediate_dim: int,
+                   num_kv_heads: int, head_dim: int, max_seq_per_step: int, dtype_size: int) -> dict:
+    """ext_aggregator.cpp:138-187."""
+    ib, ob = C.c_size_t(0), C.c_size_t(0)
+    check(lib().swl_agg_init_slot_pool(int(num_slots), int(device_index), int(hidden_dim),
+                                       int(intermediate_dim), int(num_kv_heads), int(head_dim),
+                                       int(max_seq_per_step), int(dtype_size), C.byref(ib), C.byref(ob)))
+    return {"num_slots": int(num_slots), "input_buffer_size": ib.value, "output_buffer_size": ob.value}
+
+
+def claim_slot(worker_id: int) -> dict:
+    """ext_aggregator.cpp:190-245."""
+    sid = C.c_int(-1)
+    hin, hout = C.create_string_buffer(64), C.create_string_buffer(64)
+    ib, ob = C.c_size_t(0), C.c_size_t(0)
+    check(lib().swl_agg_claim_slot(int(worker_id), C.byref(sid), hin, hout, C.byref(ib), C.byref(ob)))
+    return {"slot_id": sid.value, "worker_id": int(worker_id), "input_handle": hin.raw,
+            "output_handle": hout.raw, "input_buffer_size": ib.value, "output_buffer_size": ob.value}
+
+
+def release_slot(slot_id: int, worker_id: int) -> None:
+    """ext_aggregator.cpp:248-296."""
+    check(lib().swl_agg_release_slot(int(slot_id), int(worker_id)))
+
+
+def get_slot_owner(slot_id: int) -> int:
+    return int(lib().swl_agg_get_slot_owner(int(slot_id)))
+
+
+def get_slot_pool_status() -> dict:
+    """ext_aggregator.cpp:307-328."""
+    init, n, active = C.c_int(0), C.c_int(0), C.c_int(0)
+    masks = (C.c_uint64 * 4)()
+    owners = (C.c_int * MAX_SLOTS)()
+    check(lib().swl_agg_get_slot_pool_status(C.byref(init), C.byref(n), masks, C.byref(active), owners))
+    free_lo, free_hi, act_lo, act_hi = (int(m) for m in masks)
+    return {
+        "initialized": bool(init.value), "num_slots": n.value,
+        "free_mask_lo": free_lo, "free_mask_hi": free_hi,
+        "active_mask_lo": act_lo, "active_mask_hi": act_hi,
+        "free_count": bin(free_lo).count("1") + bin(free_hi).count("1"),
+        "active_count": bin(act_lo).count("1") + bin(act_hi).count("1"),
+        "active_slot_count": active.value,
+        "slot_owners": [int(owners[i]) for i in range(n.value)],
+    }
+
+
+def cleanup_slot_pool() -> None:
+    check(lib().swl_agg_cleanup_slot_pool())
+
+
+def init_aggregator_begin(num_layers: int, device_index: int) -> None:
+    check(lib().swl_agg_init_begin(int(num_layers), int(device_index)))
+    _borrowed.clear()
+
+
+def init_aggregator_layer(layer_idx: int, q_weight, k_weight, v_weight, o_weight, o_bias,
+                          gate_weight, up_weight, down_weight, down_bias) -> None:
+    """ext_aggregator.cpp:347-376 (an empty bias tensor means no bias)."""
+    q = _bf16_cuda(q_weight, "q_weight")
+    k = _bf16_cuda(k_weight, "k_weight")
+    v = _bf16_cuda(v_weight, "v_weight")
+    o = _bf16_cuda(o_weight, "o_weight")
+    g = _bf16_cuda(gate_weight, "gate_weight")
+    u = _bf16_cuda(up_weight, "up_weight")
+    d = _bf16_cuda(down_weight, "down_weight")
+    ob = _bf16_cuda(o_bias, "o_bias") if o_bias is not None and o_bias.numel() > 0 else None
+    db = _bf16_cuda(down_bias, "down_bias") if down_bias is not None and down_bias.numel() > 0 else None
+    hidden, inter = int(q.shape[1]), int(d.shape[1])
+    check(lib().swl_agg_init_layer(
+        int(layer_idx), q.data_ptr(), q.shape[0], k.data_ptr(), k.shape[0], v.data_ptr(), v.shape[0],
+        o.data_ptr(), o.shape[0], ob.data_ptr() if ob is not None else None,
+        g.data_ptr(), g.shape[0], u.data_ptr(), u.shape[0], d.data_ptr(), d.shape[0],
+        db.data_ptr() if db is not None else None, hidden, inter))
+    _borrowed[("layer", int(layer_idx))] = (o, d, ob, db)
+
+
+def init_aggregator_finalize() -> None:
+    check(lib().swl_agg_init_finalize())
+
+
+def init_embed_lm_head_weights(embed_weight, lm_head_weight) -> None:
+    """ext_aggregator.cpp:413-424."""
+    e = _bf16_cuda(embed_weight, "embed_weight")
+    h = _bf16_cuda(lm_head_weight, "lm_head_weight")
+    check(lib().swl_agg_init_embed_lm_head(e.data_ptr(), h.data_ptr(), int(e.shape[0]), int(e.shape[1])))
+    _borrowed["embed_lm_head"] = (e, h)
+
+
+def init_aggregator_queue(shm_name: str, capacity: int) -> None:
+    check(lib().swl_agg_init_queue(shm_name.encode(), int(capacity)))
+
+
+def aggregator_main_loop_slots(num_slots: int, dtype_code: int) -> None:
+    """ext_aggregator.cpp:1024-1210. Blocks until the quit flag is set; the
+    GIL is released for the duration (ctypes foreign call)."""
+    check(lib().swl_agg_main_loop_slots(int(num_slots), int(dtype_code)))
+
+
+# ---------------------------------------------------------------------------
+# additions
+# ---------------------------------------------------------------------------
+
+def execute_round(op: int, layer: int, slot_ids, worker_ids, bx, tx, stream=None) -> None:
+    """One round over pool slots (what the main loop runs per op), queued on
+    `stream` (a torch.cuda.Stream; None = the library's stream, synchronised)."""
+    n = len(slot_ids)
+    st = stream.cuda_stream if stream is not None else None
+    check(lib().swl_agg_execute_round(int(op), int(layer), n, i32_array(slot_ids), i32_array(worker_ids),
+                                      i64_array(bx), i64_array(tx), st))
+
+
+def slot_buffers(slot_id: int) -> tuple[int, int]:
+    """Aggregator-local device addresses (input, output) of a pool slot."""
+    a, b = C.c_void_p(), C.c_void_p()
+    check(lib().swl_agg_slot_buffers(int(slot_id), C.byref(a), C.byref(b)))
+    return int(a.value), int(b.value)
+
+
+def set_round_algo(algo: int, splits: int = 0) -> None:
+    """0/1: tensor-core round kernel (default); 2: CUDA-core cross-check kernel."""
+    check(lib().swl_agg_set_round_algo(int(algo), int(splits)))

@@ -12,6 +12,9 @@ import torch
 RTOL = 2e-2
 REL_FRO = 2e-2
 ATOL_RMS = 2e-2
+# Hidden states after several layers: bf16 residual adds of operands up to
+# ~4x the row rms cancel, so one ulp of an operand can be several % of rms.
+ATOL_RMS_MULTILAYER = 5e-2
 
 
 def assert_close(got: torch.Tensor, ref: torch.Tensor, what: str = "", rtol: float = RTOL,
@@ -31,5 +34,6 @@ def assert_close(got: torch.Tensor, ref: torch.Tensor, what: str = "", rtol: flo
     if bad.any():
         i = int(bad.flatten().nonzero()[0])
         raise AssertionError(
-            f"{what}: {int(bad.sum())} elements out of tolerance; first at flat index {i}: "
+            f"{what}: {int(bad.sum())} elements out of tolerance (rel Frobenius {fro:.3e}, "
+            f"max |diff|/rms {d.max().item() / max(rms, 1e-30):.3e}); first at flat index {i}: "
             f"got {g.flatten()[i].item():.6g} ref {r.flatten()[i].item():.6g}")
