@@ -51,6 +51,11 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--slots", type=int, default=N_SLOTS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="bracket the first timed step with cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off)")
+    ap.add_argument("--profile-round", choices=["qkv", "o", "gate_up", "down"], default=None,
+                    help="run only --steps launches of one round kind at M=--slots (small ncu case)")
     return ap.parse_args()
 
 
@@ -351,8 +356,13 @@ def our_arm(args):
     torch.cuda.synchronize()
     ev0.record(stream)
     with torch.cuda.stream(stream):
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            if args.profile_step and i == 0:
+                torch.cuda.profiler.start()
             grp.replay()
+            if args.profile_step and i == 0:
+                torch.cuda.synchronize()
+                torch.cuda.profiler.stop()
     ev1.record(stream)
     ev1.synchronize()
     ms = ev0.elapsed_time(ev1)
@@ -437,8 +447,36 @@ def our_arm(args):
     return 0
 
 
+def profile_round(args):
+    """Standalone round case for kernel captures: one weight of the named round
+    (> L2 for gate_up/down), --slots decode slots, --steps launches."""
+    import torch
+    from swarmlora_b200.rounds import slot_gemm
+    H, I = 4096, 14336
+    N, K = {"qkv": (6144, H), "o": (H, H), "gate_up": (2 * I, H), "down": (H, I)}[args.profile_round]
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+    W = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    ins = [torch.randn(16, K, generator=g, device=dev).to(torch.bfloat16)[:1] for _ in range(args.slots)]
+    outs = [torch.empty(16, N, dtype=torch.bfloat16, device=dev) for _ in range(args.slots)]
+    for _ in range(args.warmup):
+        slot_gemm(W, ins, outs)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        slot_gemm(W, ins, outs)
+    b.record()
+    b.synchronize()
+    print(json.dumps({"profile_round": args.profile_round, "M": args.slots, "N": N, "K": K,
+                      "launches": args.steps, "us_per_launch_incl_host": a.elapsed_time(b) * 1e3 / args.steps}))
+    return 0
+
+
 def main():
     args = parse()
+    if args.profile_round:
+        return profile_round(args)
     if args.impl == "reference":
         return reference_arm(args)
     return our_arm(args)

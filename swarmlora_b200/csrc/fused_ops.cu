@@ -1,0 +1,361 @@
+// Fused worker-side epilogues of the rounds (one launch between two rounds):
+//
+//  qkv_rope          after the QKV round: LoRA expand + add (q, k, v),
+//                    NeoX RoPE on q and k, k/v appended to the paged cache,
+//                    rotated q to the attention scratch.
+//  resid_norm_shrink after the O / Down round (and after the embedding):
+//                    LoRA expand (scaled after), + residual, RMSNorm of the
+//                    row (sum of squares reduced across a cluster of 8 CTAs
+//                    through distributed shared memory), normed row written
+//                    into the next round's slot input, and the next round's
+//                    LoRA shrink partials computed from it.
+//  gu_silu_shrink    after the Gate+Up round: LoRA expand + add on gate and
+//                    up, SiLU(gate) * up written into the Down round's slot
+//                    input, and the Down projection's LoRA shrink partials.
+//
+// The arithmetic (bf16 rounding points) is the same as the separate kernels
+// in worker_ops.cu and the reference's tensor ops (worker_sync.py:250-389,
+// model_builder.py:258-262, HF LlamaRMSNorm, vLLM rotary_embedding).
+#include <cuda_bf16.h>
+
+#include "common.h"
+#include "ptx.cuh"
+#include "worker_ops.h"
+
+namespace swl {
+
+namespace {
+
+constexpr int kCluster = 8;  // CTAs per row in resid_norm_shrink
+
+__device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ int seg_row(const RowSegments& s, int gr) {
+  int lo = 0, hi = s.nseg - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (s.row_start[mid] <= gr) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void ld8(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Rebuilds the bf16-rounded LoRA intermediate t[0..n) of global row gr from
+// `splits` fp32 partials ws[split][total_rows][n] into shared memory.
+__device__ __forceinline__ void rebuild_t(float* t, const float* ws, int splits, int total_rows,
+                                          int gr, int n) {
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    float s = 0.f;
+    for (int sp = 0; sp < splits; ++sp) s += ws[(static_cast<int64_t>(sp) * total_rows + gr) * n + j];
+    t[j] = bfr(s);
+  }
+}
+
+template <int RANK>
+__device__ __forceinline__ float lora_dot(const float* t, const __nv_bfloat16* brow) {
+  float d = 0.f;
+#pragma unroll
+  for (int j = 0; j < RANK; j += 8) {
+    float v[8];
+    ld8(brow + j, v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) d = fmaf(t[j + e], v[e], d);
+  }
+  return d;
+}
+
+// ---- after the QKV round -------------------------------------------------------------
+template <int RANK>
+__global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ QkvRopeTable tab,
+                                                       const QkvRopeParams p) {
+  __shared__ float t[3 * 32];
+  const int gr = blockIdx.x;
+  const int s = seg_row(tab.seg, gr);
+  const int64_t local = gr - tab.seg.row_start[s];
+  const __nv_bfloat16* B = tab.B[s];
+  if (B) rebuild_t(t, p.ws_in, p.splits_in, tab.seg.total_rows, gr, 3 * RANK);
+  __syncthreads();
+  const int pi = blockIdx.y * blockDim.x + threadIdx.x;
+  const int heads = p.hq + 2 * p.hkv;
+  const int half = p.head_dim / 2;
+  if (pi >= heads * half) return;
+  const int head = pi / half, d = pi % half;
+  const int blk = head < p.hq ? 0 : (head < p.hq + p.hkv ? 1 : 2);
+  const int64_t n1 = static_cast<int64_t>(head) * p.head_dim + d, n2 = n1 + half;
+  const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
+  float x1 = __bfloat162float(base[n1]), x2 = __bfloat162float(base[n2]);
+  if (B) {
+    x1 = bfr(x1 + bfr(lora_dot<RANK>(t + blk * RANK, B + n1 * RANK)));
+    x2 = bfr(x2 + bfr(lora_dot<RANK>(t + blk * RANK, B + n2 * RANK)));
+  }
+  const int pos = *tab.seqlen[s] + static_cast<int>(local);
+  if (blk == 2) {
+    const int page = tab.block_table[s][pos / p.page];
+    const int64_t row = ((static_cast<int64_t>(page) * p.page + pos % p.page) * p.hkv + (head - p.hq - p.hkv)) * p.head_dim;
+    tab.v_cache[s][row + d] = __float2bfloat16_rn(x1);
+    tab.v_cache[s][row + d + half] = __float2bfloat16_rn(x2);
+    return;
+  }
+  const __nv_bfloat16* cs = p.cos_sin + static_cast<int64_t>(pos) * p.head_dim;
+  const float c = __bfloat162float(cs[d]), sn = __bfloat162float(cs[half + d]);
+  const float o1 = bfr(bfr(x1 * c) - bfr(x2 * sn));
+  const float o2 = bfr(bfr(x2 * c) + bfr(x1 * sn));
+  __nv_bfloat16* dst;
+  if (blk == 0) {
+    dst = p.q_rot + (static_cast<int64_t>(gr) * p.hq + head) * p.head_dim;
+  } else {
+    const int page = tab.block_table[s][pos / p.page];
+    dst = tab.k_cache[s] + ((static_cast<int64_t>(page) * p.page + pos % p.page) * p.hkv + (head - p.hq)) * p.head_dim;
+  }
+  dst[d] = __float2bfloat16_rn(o1);
+  dst[d + half] = __float2bfloat16_rn(o2);
+}
+
+// ---- after the O / Down round (and the embedding) ------------------------------------
+// Cluster of kCluster CTAs per token row; CTA q owns columns [q*C, (q+1)*C).
+template <int RANK>
+__global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
+                                                                const ResidNormParams p) {
+  extern __shared__ float sm[];  // xs[C] | t[32] | red[...]
+  __shared__ float ss_part;
+  __shared__ float warp_ss[4];
+  const int q = static_cast<int>(ptx::cluster_rank());
+  const int gr = blockIdx.x / kCluster;
+  const int s = seg_row(tab.seg, gr);
+  const int64_t local = gr - tab.seg.row_start[s];
+  const int64_t C = p.hidden / kCluster;
+  const int64_t c0 = q * C;
+  float* xs = sm;
+  float* t = sm + C;
+  float* red = t + 32;
+  const __nv_bfloat16* B = tab.B[s];
+  if (RANK > 0 && B) rebuild_t(t, p.ws_in, p.splits_in, tab.seg.total_rows, gr, RANK);
+  __syncthreads();
+  const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
+  __nv_bfloat16* h = tab.h[s] + local * p.h_stride;
+  float ss = 0.f;
+  for (int64_t c = threadIdx.x * 4; c < C; c += blockDim.x * 4) {
+    const int64_t n = c0 + c;
+    const uint2 bu = *reinterpret_cast<const uint2*>(base + n);
+    const __nv_bfloat162* bv = reinterpret_cast<const __nv_bfloat162*>(&bu);
+    float v[4];
+    const float2 b01 = __bfloat1622float2(bv[0]), b23 = __bfloat1622float2(bv[1]);
+    v[0] = b01.x; v[1] = b01.y; v[2] = b23.x; v[3] = b23.y;
+    if (RANK > 0 && B) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float d = bfr(lora_dot<(RANK > 0 ? RANK : 8)>(t, B + (n + e) * RANK));
+        if (p.post_scale != 0.f) d = bfr(d * p.post_scale);
+        v[e] = bfr(v[e] + d);
+      }
+    }
+    if (p.has_resid) {
+      const uint2 ru = *reinterpret_cast<const uint2*>(h + n);
+      const __nv_bfloat162* rv = reinterpret_cast<const __nv_bfloat162*>(&ru);
+      const float2 r01 = __bfloat1622float2(rv[0]), r23 = __bfloat1622float2(rv[1]);
+      v[0] = bfr(r01.x + v[0]); v[1] = bfr(r01.y + v[1]);
+      v[2] = bfr(r23.x + v[2]); v[3] = bfr(r23.y + v[3]);
+    }
+    __align__(8) __nv_bfloat162 hv[2] = {__floats2bfloat162_rn(v[0], v[1]), __floats2bfloat162_rn(v[2], v[3])};
+    *reinterpret_cast<uint2*>(h + n) = *reinterpret_cast<uint2*>(hv);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      xs[c + e] = v[e];
+      ss = fmaf(v[e], v[e], ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) warp_ss[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) a += warp_ss[w];
+    ss_part = a;
+  }
+  ptx::cluster_sync();
+  float total = 0.f;
+  const uint32_t my = static_cast<uint32_t>(__cvta_generic_to_shared(&ss_part));
+  for (int r = 0; r < kCluster; ++r) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ptx::map_peer(my, r)) : "memory");
+    total += v;
+  }
+  const float inv = rsqrtf(total / static_cast<float>(p.hidden) + p.eps);
+  __nv_bfloat16* xo = tab.x_out[s] + local * p.x_stride;
+  for (int64_t c = threadIdx.x * 4; c < C; c += blockDim.x * 4) {
+    const int64_t n = c0 + c;
+    const uint2 wu = *reinterpret_cast<const uint2*>(p.w + n);
+    const __nv_bfloat162* wv = reinterpret_cast<const __nv_bfloat162*>(&wu);
+    const float2 w01 = __bfloat1622float2(wv[0]), w23 = __bfloat1622float2(wv[1]);
+    const float wf[4] = {w01.x, w01.y, w23.x, w23.y};
+    float x[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      x[e] = bfr(wf[e] * bfr(xs[c + e] * inv));
+      xs[c + e] = x[e];
+    }
+    __align__(8) __nv_bfloat162 xv[2] = {__floats2bfloat162_rn(x[0], x[1]), __floats2bfloat162_rn(x[2], x[3])};
+    *reinterpret_cast<uint2*>(xo + n) = *reinterpret_cast<uint2*>(xv);
+  }
+  __syncthreads();
+  // next round's LoRA shrink over this CTA's columns: ws_next[q][gr][j]
+  const __nv_bfloat16* A = tab.A_next[s];
+  if (A) {
+    const int R = p.r_next, G = R / 8;
+    const int kgroups = blockDim.x / G;
+    const int tid = threadIdx.x;
+    const bool active = tid < kgroups * G;
+    const int cg = tid % G, kg = tid / G;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (active) {
+      int64_t k = kg;
+#pragma unroll 4
+      for (; k < C; k += kgroups) {
+        float a[8];
+        ld8(A + (c0 + k) * R + cg * 8, a);
+        const float xv = xs[k];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(xv, a[e], acc[e]);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) red[tid * 8 + e] = acc[e];
+    __syncthreads();
+    for (int j = tid; j < R; j += blockDim.x) {
+      float v = 0.f;
+      for (int g = 0; g < kgroups; ++g) v += red[(g * G + j / 8) * 8 + (j & 7)];
+      p.ws_next[(static_cast<int64_t>(q) * tab.seg.total_rows + gr) * R + j] = v;
+    }
+  }
+  ptx::cluster_sync();  // peers may still read ss_part
+}
+
+// ---- after the Gate+Up round ----------------------------------------------------------
+template <int RANK>
+__global__ void __launch_bounds__(256) gu_silu_shrink_kernel(const __grid_constant__ GuSiluTable tab,
+                                                             const GuSiluParams p) {
+  __shared__ float t[2 * 32];
+  __shared__ float red[8][32];
+  const int gr = blockIdx.x;
+  const int s = seg_row(tab.seg, gr);
+  const int64_t local = gr - tab.seg.row_start[s];
+  const __nv_bfloat16* B = tab.B[s];
+  if (B) rebuild_t(t, p.ws_in, p.splits_in, tab.seg.total_rows, gr, 2 * RANK);
+  __syncthreads();
+  const int64_t n = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
+  float a = 0.f;
+  if (n < p.inter) {
+    const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
+    float g = __bfloat162float(base[n]), u = __bfloat162float(base[n + p.inter]);
+    if (B) {
+      g = bfr(g + bfr(lora_dot<RANK>(t, B + n * RANK)));
+      u = bfr(u + bfr(lora_dot<RANK>(t + RANK, B + (n + p.inter) * RANK)));
+    }
+    const float sg = bfr(g / (1.f + expf(-g)));
+    a = bfr(sg * u);
+    tab.act[s][local * p.act_stride + n] = __float2bfloat16_rn(a);
+  }
+  const __nv_bfloat16* A = tab.A_next[s];
+  if (!A) return;
+  const int R = p.r_next;
+  float part[32];
+  if (n < p.inter) {
+    for (int j = 0; j < R; j += 8) {
+      float v[8];
+      ld8(A + n * R + j, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) part[j + e] = a * v[e];
+    }
+  } else {
+    for (int j = 0; j < R; ++j) part[j] = 0.f;
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int j = 0; j < R; ++j) {
+    float v = part[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[w][j] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < R) {
+    float v = 0.f;
+    for (int ww = 0; ww < static_cast<int>(blockDim.x >> 5); ++ww) v += red[ww][threadIdx.x];
+    p.ws_next[(static_cast<int64_t>(blockIdx.y) * tab.seg.total_rows + gr) * R + threadIdx.x] = v;
+  }
+}
+
+}  // namespace
+
+int launch_qkv_rope(const QkvRopeTable& tab, const QkvRopeParams& p, int r, cudaStream_t stream) {
+  if (tab.seg.total_rows <= 0) return SWL_OK;
+  if (p.head_dim % 2 || p.head_dim > 256) return set_error(SWL_ERR_ARG, "qkv_rope: bad head_dim");
+  const int pairs = (p.hq + 2 * p.hkv) * (p.head_dim / 2);
+  dim3 grid(tab.seg.total_rows, (pairs + 255) / 256);
+  switch (r) {
+    case 8: qkv_rope_kernel<8><<<grid, 256, 0, stream>>>(tab, p); break;
+    case 16: qkv_rope_kernel<16><<<grid, 256, 0, stream>>>(tab, p); break;
+    case 32: qkv_rope_kernel<32><<<grid, 256, 0, stream>>>(tab, p); break;
+    default: return set_error(SWL_ERR_ARG, "qkv_rope: rank must be 8, 16 or 32");
+  }
+  SWL_CUDA_TRY(cudaGetLastError());
+  return SWL_OK;
+}
+
+int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p, int r_in,
+                             cudaStream_t stream) {
+  if (tab.seg.total_rows <= 0) return SWL_OK;
+  if (p.hidden % (kCluster * 4)) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be a multiple of 32");
+  if (p.r_next % 8 || p.r_next > 96) return set_error(SWL_ERR_ARG, "resid_norm: next rank layout must be 8..96 in steps of 8");
+  const int64_t C = p.hidden / kCluster;
+  const size_t smem = (C + 32 + 128 * 8) * sizeof(float);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tab.seg.total_rows * kCluster), 1, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  switch (r_in) {
+    case 0: SWL_CUDA_TRY(cudaLaunchKernelEx(&cfg, resid_norm_shrink_kernel<0>, tab, p)); break;
+    case 8: SWL_CUDA_TRY(cudaLaunchKernelEx(&cfg, resid_norm_shrink_kernel<8>, tab, p)); break;
+    case 16: SWL_CUDA_TRY(cudaLaunchKernelEx(&cfg, resid_norm_shrink_kernel<16>, tab, p)); break;
+    case 32: SWL_CUDA_TRY(cudaLaunchKernelEx(&cfg, resid_norm_shrink_kernel<32>, tab, p)); break;
+    default: return set_error(SWL_ERR_ARG, "resid_norm: input rank must be 0, 8, 16 or 32");
+  }
+  return SWL_OK;
+}
+
+int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, cudaStream_t stream) {
+  if (tab.seg.total_rows <= 0) return SWL_OK;
+  if (p.r_next % 8 || p.r_next > 32) return set_error(SWL_ERR_ARG, "gu_silu: next rank must be 8..32 in steps of 8");
+  dim3 grid(tab.seg.total_rows, static_cast<unsigned>((p.inter + 255) / 256));
+  switch (r) {
+    case 8: gu_silu_shrink_kernel<8><<<grid, 256, 0, stream>>>(tab, p); break;
+    case 16: gu_silu_shrink_kernel<16><<<grid, 256, 0, stream>>>(tab, p); break;
+    case 32: gu_silu_shrink_kernel<32><<<grid, 256, 0, stream>>>(tab, p); break;
+    default: return set_error(SWL_ERR_ARG, "gu_silu: rank must be 8, 16 or 32");
+  }
+  SWL_CUDA_TRY(cudaGetLastError());
+  return SWL_OK;
+}
+
+int resid_norm_splits() { return kCluster; }
+
+}  // namespace swl

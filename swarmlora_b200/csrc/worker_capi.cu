@@ -149,6 +149,133 @@ SWL_EXPORT int swl_paged_attention(int nseg, const int* rows, const void* const*
   return launch_paged_attention(t, p, static_cast<cudaStream_t>(stream));
 }
 
+// swl_paged_attention plus the O projection's LoRA shrink on its output:
+// ws_o[head][row][j] = sum_d out[row, head*D + d] * A_o[i][head*D + d, j]
+// (A_o[i] = lora_A(o_proj)^T, [hq*D, r]; NULL for a slot without adapter).
+SWL_EXPORT int swl_paged_attention_shrink(int nseg, const int* rows, const void* const* block_tables,
+                                          const void* const* k_cache, const void* const* v_cache,
+                                          const void* const* seqlens, void* const* out,
+                                          int64_t out_stride, int hq, int hkv, int head_dim, int page,
+                                          float scale, int max_len, const void* q_rot, float* part,
+                                          const void* const* A_o, int r, float* ws_o, void* stream) {
+  AttnTable t;
+  SWL_TRY(fill_attn(&t, nseg, rows, nullptr, block_tables, const_cast<void* const*>(k_cache),
+                    const_cast<void* const*>(v_cache), seqlens, out));
+  AttnParams p = {};
+  p.hq = hq; p.hkv = hkv; p.head_dim = head_dim; p.page = page;
+  p.out_stride = out_stride;
+  p.scale = scale;
+  p.max_len = max_len;
+  p.q_rot = cast<__nv_bfloat16>(q_rot);
+  p.part = part;
+  ShrinkSide sh;
+  for (int i = 0; i < kMaxSlots; ++i) sh.A[i] = (A_o && i < nseg) ? cast<const __nv_bfloat16>(A_o[i]) : nullptr;
+  sh.r = r;
+  sh.ws = ws_o;
+  if (!ws_o) return set_error(SWL_ERR_ARG, "attention shrink: null ws");
+  return launch_paged_attention(t, p, static_cast<cudaStream_t>(stream), &sh);
+}
+
+// Fused epilogue of the QKV round: q|k|v = round output + LoRA delta (shrink
+// partials ws_in [splits_in][rows][3r], lora_B rows B[i] [(hq+2hkv)*D, r]),
+// NeoX RoPE of q and k at position *seqlens[i] + t, k and v appended to the
+// paged cache, rotated q written to q_rot [total_rows, hq*D].
+SWL_EXPORT int swl_fused_qkv_rope(int nseg, const int* rows, const void* const* base,
+                                  int64_t base_stride, const void* const* B, int r,
+                                  const float* ws_in, int splits_in,
+                                  const void* const* block_tables, void* const* k_cache,
+                                  void* const* v_cache, const void* const* seqlens, int hq,
+                                  int hkv, int head_dim, int page, const void* cos_sin,
+                                  void* q_rot, void* stream) {
+  QkvRopeTable t;
+  SWL_TRY(fill_segments(&t.seg, nseg, rows));
+  for (int i = 0; i < nseg; ++i) {
+    t.base[i] = cast<const __nv_bfloat16>(base[i]);
+    t.B[i] = B ? cast<const __nv_bfloat16>(B[i]) : nullptr;
+    t.block_table[i] = cast<const int>(block_tables[i]);
+    t.k_cache[i] = cast<__nv_bfloat16>(k_cache[i]);
+    t.v_cache[i] = cast<__nv_bfloat16>(v_cache[i]);
+    t.seqlen[i] = cast<const int>(seqlens[i]);
+  }
+  QkvRopeParams p;
+  p.hq = hq; p.hkv = hkv; p.head_dim = head_dim; p.page = page;
+  p.base_stride = base_stride;
+  p.ws_in = ws_in;
+  p.splits_in = splits_in;
+  p.cos_sin = cast<const __nv_bfloat16>(cos_sin);
+  p.q_rot = cast<__nv_bfloat16>(q_rot);
+  return launch_qkv_rope(t, p, r, static_cast<cudaStream_t>(stream));
+}
+
+// Fused epilogue of the O / Down round (and of the embedding): h = [h +]
+// (base + bf16(bf16(t @ B^T) * post_scale)), then x = RMSNorm(h) * w written to
+// x_out (the next round's slot input) and the next round's LoRA shrink
+// partials ws_next[8][rows][r_next] = x @ A_next (A_next[i] NULL: none).
+SWL_EXPORT int swl_fused_resid_norm_shrink(int nseg, const int* rows, const void* const* base,
+                                           int64_t base_stride, const void* const* B, int r_in,
+                                           float post_scale, const float* ws_in, int splits_in,
+                                           int has_resid, void* const* h, int64_t h_stride,
+                                           const void* w, int64_t hidden, float eps,
+                                           void* const* x_out, int64_t x_stride,
+                                           const void* const* A_next, int r_next, float* ws_next,
+                                           void* stream) {
+  ResidNormTable t;
+  SWL_TRY(fill_segments(&t.seg, nseg, rows));
+  for (int i = 0; i < nseg; ++i) {
+    t.base[i] = cast<const __nv_bfloat16>(base[i]);
+    t.B[i] = B ? cast<const __nv_bfloat16>(B[i]) : nullptr;
+    t.h[i] = cast<__nv_bfloat16>(h[i]);
+    t.x_out[i] = cast<__nv_bfloat16>(x_out[i]);
+    t.A_next[i] = A_next ? cast<const __nv_bfloat16>(A_next[i]) : nullptr;
+  }
+  ResidNormParams p;
+  p.hidden = hidden;
+  p.post_scale = post_scale;
+  p.ws_in = ws_in;
+  p.splits_in = splits_in;
+  p.has_resid = has_resid;
+  p.w = cast<const __nv_bfloat16>(w);
+  p.eps = eps;
+  p.base_stride = base_stride;
+  p.h_stride = h_stride;
+  p.x_stride = x_stride;
+  p.r_next = A_next ? r_next : 0;
+  p.ws_next = ws_next;
+  return launch_resid_norm_shrink(t, p, B ? r_in : 0, static_cast<cudaStream_t>(stream));
+}
+
+// Fused epilogue of the Gate+Up round: gate/up = round output + LoRA delta
+// (partials ws_in [splits_in][rows][2r], lora_B rows B[i] [2*inter, r]),
+// act = SiLU(gate) * up written to act[i] (the Down round's slot input), and
+// the Down LoRA shrink partials ws_next[ceil(inter/256)][rows][r_next].
+SWL_EXPORT int swl_fused_gu_silu_shrink(int nseg, const int* rows, const void* const* base,
+                                        int64_t base_stride, const void* const* B, int r,
+                                        const float* ws_in, int splits_in, int64_t inter,
+                                        void* const* act, int64_t act_stride,
+                                        const void* const* A_next, int r_next, float* ws_next,
+                                        void* stream) {
+  GuSiluTable t;
+  SWL_TRY(fill_segments(&t.seg, nseg, rows));
+  for (int i = 0; i < nseg; ++i) {
+    t.base[i] = cast<const __nv_bfloat16>(base[i]);
+    t.B[i] = B ? cast<const __nv_bfloat16>(B[i]) : nullptr;
+    t.act[i] = cast<__nv_bfloat16>(act[i]);
+    t.A_next[i] = A_next ? cast<const __nv_bfloat16>(A_next[i]) : nullptr;
+  }
+  GuSiluParams p;
+  p.inter = inter;
+  p.base_stride = base_stride;
+  p.act_stride = act_stride;
+  p.ws_in = ws_in;
+  p.splits_in = splits_in;
+  p.r_next = r_next;
+  p.ws_next = ws_next;
+  return launch_gu_silu_shrink(t, p, r, static_cast<cudaStream_t>(stream));
+}
+
+// Number of shrink partials swl_fused_resid_norm_shrink writes (its cluster size).
+SWL_EXPORT int swl_fused_norm_splits(void) { return resid_norm_splits(); }
+
 // LlamaRMSNorm over rows: out = w * bf16(x * rsqrt(mean(x^2) + eps)).
 SWL_EXPORT int swl_rms_norm(int nseg, const int* rows, const void* const* x, int64_t x_stride,
                             void* const* out, int64_t out_stride, const void* w, int64_t hidden,

@@ -232,24 +232,62 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const __grid_constant_
 }
 
 // ---- paged attention -------------------------------------------------------------------
-// CTA = (token row, kv head, context split); warp w = query head kvh*G + w.
-// Lanes: grp = lane / 4 picks one of 8 keys per step, sub = lane % 4 holds
-// 32 of the 128 head dims. Online softmax in the log2 domain.
+// CTA = (token row, kv head, context split), one warp per query head of the
+// kv head's group. The split's pages stream through a 4-stage cp.async ring in
+// shared memory (one 16-token page of K and of V per stage; 16-byte pieces
+// XOR-swizzled by token so the warps' reads are conflict-free), shared by all
+// query heads of the group. Lanes: grp = lane / 4 takes one of 8 keys per step,
+// sub = lane % 4 holds 32 of the 128 dims. Online softmax in the log2 domain.
+// Every CTA writes a partial record [m, l, o[128]] per query head; the
+// combine kernel merges the splits.
 constexpr int kD = 128;
+constexpr int kPageTok = 16;
+constexpr int kAttnStages = 4;
+constexpr int kTileBytes = kPageTok * kD * 2;  // one page of K (or V) of one head
+
 __global__ void __launch_bounds__(256) paged_attention_kernel(const __grid_constant__ AttnTable tab,
                                                               const AttnParams p, int splits,
                                                               float* __restrict__ part) {
+  __shared__ __align__(128) uint8_t kv_sm[kAttnStages][2][kTileBytes];
   const int gr = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.hq / p.hkv;
-  if (w >= G) return;
+  const int nthreads = 32 * G;
   const int h = kvh * G + w;
   const int s = seg_of_row(tab.seg, gr);
   const int local = gr - tab.seg.row_start[s];
   const int L = *tab.seqlen[s] + local + 1;  // causal: keys 0 .. pos
-  const int jb = static_cast<int>(static_cast<int64_t>(L) * split / splits);
-  const int je = static_cast<int>(static_cast<int64_t>(L) * (split + 1) / splits);
+  const int ntiles = (L + kPageTok - 1) / kPageTok;
+  const int tb = static_cast<int>(static_cast<int64_t>(ntiles) * split / splits);
+  const int te = static_cast<int>(static_cast<int64_t>(ntiles) * (split + 1) / splits);
+  const int nt = te - tb;
   const int grp = lane >> 2, sub = lane & 3;
+  const int* bt = tab.block_table[s];
+  const __nv_bfloat16* kc = tab.k_cache[s];
+  const __nv_bfloat16* vc = tab.v_cache[s];
+
+  auto load_tile = [&](int i, int st) {
+    const int tile = tb + i;
+    const int64_t page = bt[tile];
+    for (int c = threadIdx.x; c < 2 * kPageTok * 16; c += nthreads) {
+      const int kv = c >> 8, cc = c & 255;
+      const int tok = cc >> 4, ch = cc & 15;
+      const bool live = tile * kPageTok + tok < L;
+      const __nv_bfloat16* src =
+          (kv ? vc : kc) + ((page * p.page + tok) * p.hkv + kvh) * kD + ch * 8;
+      const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(&kv_sm[st][kv][0])) +
+                           tok * 256 + ((ch ^ (tok & 7)) << 4);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
+                   "l"(live ? src : kc), "r"(live ? 16 : 0)
+                   : "memory");
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < kAttnStages - 1; ++i) {
+    if (i < nt) load_tile(i, i);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+
   const float qscale = p.scale * 1.4426950408889634f;
   float q[32];
   {
@@ -262,51 +300,62 @@ __global__ void __launch_bounds__(256) paged_attention_kernel(const __grid_const
       for (int i = 0; i < 8; ++i) q[c * 8 + i] = v[i] * qscale;
     }
   }
-  const int* bt = tab.block_table[s];
-  const __nv_bfloat16* kc = tab.k_cache[s];
-  const __nv_bfloat16* vc = tab.v_cache[s];
   float m = -INFINITY, l = 0.f, o[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) o[i] = 0.f;
-  for (int j0 = jb; j0 < je; j0 += 8) {
-    const int j = j0 + grp;
-    const bool valid = j < je;
-    float kv[32], vv[32];
-    if (valid) {
-      const int64_t base = ((static_cast<int64_t>(bt[j / p.page]) * p.page + j % p.page) * p.hkv + kvh) * kD + sub * 32;
+
+  for (int i = 0; i < nt; ++i) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kAttnStages - 2) : "memory");
+    __syncthreads();
+    const int nx = i + kAttnStages - 1;
+    if (nx < nt) load_tile(nx, nx % kAttnStages);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint8_t* ks = kv_sm[i % kAttnStages][0];
+    const uint8_t* vs = kv_sm[i % kAttnStages][1];
+#pragma unroll
+    for (int g8 = 0; g8 < kPageTok / 8; ++g8) {
+      const int tok = g8 * 8 + grp;
+      const bool valid = (tb + i) * kPageTok + tok < L;
+      float sc = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        float t8[8];
-        load8(kc + base + c * 8, t8);
+        const uint4 u = *reinterpret_cast<const uint4*>(ks + tok * 256 + (((4 * sub + c) ^ grp) << 4));
+        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) kv[c * 8 + i] = t8[i];
-        load8(vc + base + c * 8, t8);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) vv[c * 8 + i] = t8[i];
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(hv[e]);
+          sc = fmaf(q[c * 8 + 2 * e], f.x, sc);
+          sc = fmaf(q[c * 8 + 2 * e + 1], f.y, sc);
+        }
       }
-    }
-    float sc = 0.f;
-    if (valid) {
+      sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+      sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+      if (!valid) sc = -INFINITY;
+      float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mn = fmaxf(m, mx);
+      const float corr = mn == -INFINITY ? 1.f : exp2f(m - mn);
+      const float pr = valid ? exp2f(sc - mn) : 0.f;
+      float ps = pr + __shfl_xor_sync(0xffffffffu, pr, 4);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+      l = l * corr + ps;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) sc = fmaf(q[i], kv[i], sc);
-    }
-    sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-    sc += __shfl_xor_sync(0xffffffffu, sc, 2);
-    if (!valid) sc = -INFINITY;
-    float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 4));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-    const float mn = fmaxf(m, mx);
-    const float corr = exp2f(m - mn);
-    const float pr = valid ? exp2f(sc - mn) : 0.f;
-    float ps = pr + __shfl_xor_sync(0xffffffffu, pr, 4);
-    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-    l = l * corr + ps;
+      for (int c = 0; c < 4; ++c) {
+        const uint4 u = *reinterpret_cast<const uint4*>(vs + tok * 256 + (((4 * sub + c) ^ grp) << 4));
+        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) o[i] = o[i] * corr + (valid ? pr * vv[i] : 0.f);
-    m = mn;
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(hv[e]);
+          o[c * 8 + 2 * e] = o[c * 8 + 2 * e] * corr + pr * f.x;
+          o[c * 8 + 2 * e + 1] = o[c * 8 + 2 * e + 1] * corr + pr * f.y;
+        }
+      }
+      m = mn;
+    }
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     o[i] += __shfl_xor_sync(0xffffffffu, o[i], 4);
@@ -314,27 +363,23 @@ __global__ void __launch_bounds__(256) paged_attention_kernel(const __grid_const
     o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
   }
   if (grp != 0) return;
-  if (splits == 1) {
-    __nv_bfloat16* op = tab.out[s] + static_cast<int64_t>(local) * p.out_stride + h * kD + sub * 32;
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) op[i] = __float2bfloat16_rn(o[i] * inv);
-  } else {
-    // partial record: [m, l, o[128]] per (row, head, split)
-    float* rec = part + ((static_cast<int64_t>(gr) * p.hq + h) * splits + split) * (kD + 2);
-    if (sub == 0) {
-      rec[0] = m;
-      rec[1] = l;
-    }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) rec[2 + sub * 32 + i] = o[i];
+  float* rec = part + ((static_cast<int64_t>(gr) * p.hq + h) * splits + split) * (kD + 2);
+  if (sub == 0) {
+    rec[0] = m;
+    rec[1] = l;
   }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) rec[2 + sub * 32 + i] = o[i];
 }
 
-// Combines the context splits: O = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s.
+// Merges the context splits of one (row, head): O = sum_s 2^(m_s - M) o_s /
+// sum_s 2^(m_s - M) l_s, written as bf16 to the slot's attention output. With
+// a shrink side (A != nullptr) it also emits this head's share of the O
+// projection's LoRA shrink: ws[h][row][j] = sum_d out[d] * A[h*128 + d, j].
 __global__ void __launch_bounds__(128) attention_combine_kernel(const __grid_constant__ AttnTable tab,
                                                                 const AttnParams p, int splits,
-                                                                const float* __restrict__ part) {
+                                                                const float* __restrict__ part,
+                                                                const __grid_constant__ ShrinkSide sh) {
   const int gr = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int s = seg_of_row(tab.seg, gr);
   const int local = gr - tab.seg.row_start[s];
@@ -348,8 +393,33 @@ __global__ void __launch_bounds__(128) attention_combine_kernel(const __grid_con
     lsum += wgt * rec[i * (kD + 2) + 1];
     acc += wgt * rec[i * (kD + 2) + 2 + d];
   }
-  tab.out[s][static_cast<int64_t>(local) * p.out_stride + h * kD + d] =
-      __float2bfloat16_rn(lsum > 0.f ? acc / lsum : 0.f);
+  const __nv_bfloat16 ob = __float2bfloat16_rn(lsum > 0.f ? acc / lsum : 0.f);
+  tab.out[s][static_cast<int64_t>(local) * p.out_stride + h * kD + d] = ob;
+  const __nv_bfloat16* A = sh.A[s];
+  if (!A) return;
+  // shrink share of this head (r <= 32 columns)
+  __shared__ float red[4][32];
+  const float x = __bfloat162float(ob);
+  float t[32];
+  const __nv_bfloat16* ar = A + (static_cast<int64_t>(h) * kD + d) * sh.r;
+  for (int j = 0; j < sh.r; j += 8) {
+    float v[8];
+    load8(ar + j, v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t[j + e] = x * v[e];
+  }
+  const int w = d >> 5, lane = d & 31;
+  for (int j = 0; j < sh.r; ++j) {
+    float v = t[j];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0) red[w][j] = v;
+  }
+  __syncthreads();
+  if (d < sh.r) {
+    const float v = red[0][d] + red[1][d] + red[2][d] + red[3][d];
+    sh.ws[(static_cast<int64_t>(h) * tab.seg.total_rows + gr) * sh.r + d] = v;
+  }
 }
 
 // ---- RMSNorm ---------------------------------------------------------------------------
@@ -479,30 +549,38 @@ int launch_rope_append(const AttnTable& tab, const AttnParams& p, cudaStream_t s
 }
 
 int attention_splits(int total_rows, int hkv, int max_len) {
-  // Enough context splits to give every SM a few CTAs, >= 64 keys per split.
+  // Enough context splits for ~4 CTAs per SM, at least 4 pages per split.
   const int base = std::max(1, total_rows * hkv);
-  int splits = std::max(1, std::min((4 * 148 + base - 1) / base, max_len / 64));
+  int splits = std::max(1, std::min((4 * 148 + base - 1) / base, max_len / (4 * kPageTok)));
   return std::min(splits, 32);
 }
 
 int64_t attention_part_floats(int total_rows, int hq, int splits) {
-  return splits > 1 ? static_cast<int64_t>(total_rows) * hq * splits * (kD + 2) : 0;
+  return static_cast<int64_t>(total_rows) * hq * splits * (kD + 2);
 }
 
-int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream_t stream) {
+int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream_t stream,
+                           const ShrinkSide* shrink) {
   if (tab.seg.total_rows <= 0) return SWL_OK;
-  if (p.head_dim != kD || p.hq % p.hkv || p.hq / p.hkv > 8)
-    return set_error(SWL_ERR_ARG, "attention: head_dim 128 and at most 8 query heads per kv head");
+  if (p.head_dim != kD || p.page != kPageTok || p.hq % p.hkv || p.hq / p.hkv > 8)
+    return set_error(SWL_ERR_ARG, "attention: head_dim 128, page 16, at most 8 query heads per kv head");
   const int splits = attention_splits(tab.seg.total_rows, p.hkv, p.max_len);
-  if (splits > 1 && !p.part) return set_error(SWL_ERR_ARG, "attention: missing partial scratch");
+  if (!p.part) return set_error(SWL_ERR_ARG, "attention: missing partial scratch");
   const int G = p.hq / p.hkv;
   dim3 grid(tab.seg.total_rows, p.hkv, splits);
   paged_attention_kernel<<<grid, 32 * G, 0, stream>>>(tab, p, splits, p.part);
   SWL_CUDA_TRY(cudaGetLastError());
-  if (splits > 1) {
-    attention_combine_kernel<<<dim3(tab.seg.total_rows, p.hq), kD, 0, stream>>>(tab, p, splits, p.part);
-    SWL_CUDA_TRY(cudaGetLastError());
+  ShrinkSide none;
+  if (!shrink) {
+    for (int i = 0; i < kMaxSlots; ++i) none.A[i] = nullptr;
+    none.r = 0;
+    none.ws = nullptr;
+  } else if (shrink->r % 8 || shrink->r > 32) {
+    return set_error(SWL_ERR_ARG, "attention: shrink rank must be 8..32 in steps of 8");
   }
+  attention_combine_kernel<<<dim3(tab.seg.total_rows, p.hq), kD, 0, stream>>>(tab, p, splits, p.part,
+                                                                             shrink ? *shrink : none);
+  SWL_CUDA_TRY(cudaGetLastError());
   return SWL_OK;
 }
 

@@ -70,11 +70,11 @@ struct AttnParams {
   int max_pos;
   int max_len;                   // upper bound of any slot's context after this step
   __nv_bfloat16* q_rot;          // [total_rows, Hq * D] scratch for rotated q
-  float* part;                   // split partials, attention_scratch_floats() floats
+  float* part;                   // per-split records, attention_part_floats() floats
 };
 
 // Context splits the attention launch will use, and the fp32 partial-record
-// scratch it needs (0 when unsplit).
+// scratch it needs.
 int attention_splits(int total_rows, int hkv, int max_len);
 int64_t attention_part_floats(int total_rows, int hq, int splits);
 
@@ -99,8 +99,78 @@ int launch_lora_shrink(const LoraShrinkTable& tab, int64_t K, int R, int64_t x_s
 int launch_lora_expand(const LoraExpandTable& tab, const ExpandParams& p, const float* ws,
                        cudaStream_t stream);
 int launch_rope_append(const AttnTable& tab, const AttnParams& p, cudaStream_t stream);
-int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream_t stream);
+// Optional LoRA shrink fused into the attention combine (O projection):
+// ws[head][row][j] = sum_d out[row, head*D + d] * A[head*D + d, j].
+struct ShrinkSide {
+  const __nv_bfloat16* A[kMaxSlots];  // [hq*D, r] per slot, or nullptr
+  int r;
+  float* ws;
+};
+int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream_t stream,
+                           const ShrinkSide* shrink = nullptr);
 int launch_rms_norm(const NormTable& tab, const __nv_bfloat16* w, int64_t hidden, float eps,
                     int64_t x_stride, int64_t out_stride, cudaStream_t stream);
+
+// ---- fused round epilogues (fused_ops.cu) ------------------------------------------------
+struct QkvRopeTable {
+  RowSegments seg;
+  const __nv_bfloat16* base[kMaxSlots];  // QKV round output rows [rows, (hq + 2 hkv) * D]
+  const __nv_bfloat16* B[kMaxSlots];     // [(hq + 2 hkv) * D, r] lora_B rows, or nullptr
+  const int* block_table[kMaxSlots];
+  __nv_bfloat16* k_cache[kMaxSlots];
+  __nv_bfloat16* v_cache[kMaxSlots];
+  const int* seqlen[kMaxSlots];
+};
+struct QkvRopeParams {
+  int hq, hkv, head_dim, page;
+  int64_t base_stride;
+  const float* ws_in;  // QKV shrink partials [splits_in][total_rows][3 r]
+  int splits_in;
+  const __nv_bfloat16* cos_sin;
+  __nv_bfloat16* q_rot;  // [total_rows, hq * D]
+};
+
+struct ResidNormTable {
+  RowSegments seg;
+  const __nv_bfloat16* base[kMaxSlots];    // round output (or embedding) rows [rows, hidden]
+  const __nv_bfloat16* B[kMaxSlots];       // [hidden, r_in] lora_B of the finished round, or nullptr
+  __nv_bfloat16* h[kMaxSlots];             // hidden rows: residual in, new hidden out
+  __nv_bfloat16* x_out[kMaxSlots];         // normed rows (next round's slot input)
+  const __nv_bfloat16* A_next[kMaxSlots];  // [hidden, r_next] next round's shrink matrix, or nullptr
+};
+struct ResidNormParams {
+  int64_t hidden;
+  float post_scale;       // delta scale after the expand (0 = none)
+  const float* ws_in;     // finished round's shrink partials [splits_in][total_rows][r_in]
+  int splits_in;
+  int has_resid;          // 0: h = base (+ delta); 1: h = h + (base + delta)
+  const __nv_bfloat16* w; // RMSNorm weight [hidden]
+  float eps;
+  int64_t base_stride, h_stride, x_stride;
+  int r_next;
+  float* ws_next;         // [8][total_rows][r_next]
+};
+
+struct GuSiluTable {
+  RowSegments seg;
+  const __nv_bfloat16* base[kMaxSlots];    // Gate+Up round output rows [rows, 2 inter]
+  const __nv_bfloat16* B[kMaxSlots];       // [2 inter, r] lora_B rows, or nullptr
+  __nv_bfloat16* act[kMaxSlots];           // SiLU(gate) * up rows (Down round slot input)
+  const __nv_bfloat16* A_next[kMaxSlots];  // [inter, r_next] Down shrink matrix, or nullptr
+};
+struct GuSiluParams {
+  int64_t inter;
+  int64_t base_stride, act_stride;
+  const float* ws_in;  // Gate+Up shrink partials [splits_in][total_rows][2 r]
+  int splits_in;
+  int r_next;
+  float* ws_next;      // [ceil(inter / 256)][total_rows][r_next]
+};
+
+int launch_qkv_rope(const QkvRopeTable& tab, const QkvRopeParams& p, int r, cudaStream_t stream);
+int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p, int r_in,
+                             cudaStream_t stream);
+int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, cudaStream_t stream);
+int resid_norm_splits();
 
 }  // namespace swl

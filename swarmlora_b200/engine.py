@@ -142,8 +142,9 @@ class SlotGroup:
 
     def __init__(self, cfg: ModelConfig, base: BaseWeights, adapters: list, ctx_lens: list,
                  max_new: int, device: int = 0, seed: int = 0, kv_std: float = 1.0,
-                 round_algo: int = 1, worker_id0: int = 1000):
+                 round_algo: int = 1, worker_id0: int = 1000, fused: bool = True):
         self.cfg = cfg
+        self.fused = fused
         self.dev = torch.device("cuda", device)
         self.n = n = len(ctx_lens)
         self.base = base
@@ -187,6 +188,15 @@ class SlotGroup:
         self.part = torch.empty(max(1, nparts), dtype=torch.float32, device=self.dev)
         self.splits = max(1, min(8, -(-296 // n)))
         self.ws = torch.empty(self.splits * n * 3 * cfg.rank, dtype=torch.float32, device=self.dev)
+        # fused path: LoRA shrink partials of each round's input, produced by the
+        # epilogue kernel that writes that input
+        self.norm_splits = int(lib().swl_fused_norm_splits())
+        self.dn_splits = -(-I // 256)
+        f32 = dict(dtype=torch.float32, device=self.dev)
+        self.ws_qkv = torch.zeros(self.norm_splits * n * 3 * cfg.rank, **f32)
+        self.ws_o = torch.zeros(cfg.hq * n * cfg.rank, **f32)
+        self.ws_gu = torch.zeros(self.norm_splits * n * 2 * cfg.rank, **f32)
+        self.ws_dn = torch.zeros(self.dn_splits * n * cfg.rank, **f32)
         self.tokens = torch.zeros(n, dtype=torch.int64, device=self.dev)
         self._build_call_args()
         self.graph = None
@@ -230,6 +240,55 @@ class SlotGroup:
 
     def enqueue_step(self, stream: torch.cuda.Stream) -> None:
         """Queues one decode token for every slot on `stream` (no host sync)."""
+        if self.fused:
+            return self._enqueue_fused(stream)
+        return self._enqueue_unfused(stream)
+
+    def _enqueue_fused(self, stream: torch.cuda.Stream) -> None:
+        """Fused sequence: per layer 4 rounds + 6 worker kernels (each worker
+        kernel finishes one round's epilogue and starts the next round's LoRA)."""
+        L, cfg, n, st = lib(), self.cfg, self.n, stream.cuda_stream
+        H, I, D, r = cfg.hidden, cfg.inter, cfg.head_dim, cfg.rank
+        rows, s = self.a_rows, self.scaling
+        nl = cfg.layers
+        check(L.swl_copy_rows(n, self.a_tok, self.a_in, self.a_b8, st))
+        self._round(agg.OP_EMBED, 0, st)
+        # embedding -> h, RMSNorm -> QKV slot input, QKV shrink
+        check(L.swl_fused_resid_norm_shrink(n, rows, self.a_out, H, None, 0, 0.0, None, 0, 0, self.a_h, H,
+                                            self.base.in_norm[0].data_ptr(), H, cfg.eps, self.a_in, H,
+                                            self.A_qkv[0], 3 * r, self.ws_qkv.data_ptr(), st))
+        for l in range(nl):
+            self._round(agg.OP_QKV_FUSED, l, st)
+            check(L.swl_fused_qkv_rope(n, rows, self.a_out, cfg.qkv_n, self.B_qkv[l], r,
+                                       self.ws_qkv.data_ptr(), self.norm_splits, self.a_bt, self.a_kc[l],
+                                       self.a_vc[l], self.a_sl, cfg.hq, cfg.hkv, D, cfg.page,
+                                       self.cos_sin.data_ptr(), self.q_rot.data_ptr(), st))
+            check(L.swl_paged_attention_shrink(n, rows, self.a_bt, self.a_kc[l], self.a_vc[l], self.a_sl,
+                                               self.a_in, cfg.hq * D, cfg.hq, cfg.hkv, D, cfg.page,
+                                               1.0 / math.sqrt(D), self.max_len, self.q_rot.data_ptr(),
+                                               self.part.data_ptr(), self.A_o[l], r, self.ws_o.data_ptr(), st))
+            self._round(agg.OP_O_PROJ, l, st)
+            check(L.swl_fused_resid_norm_shrink(n, rows, self.a_out, H, self.B_o[l], r, s, self.ws_o.data_ptr(),
+                                                cfg.hq, 1, self.a_h, H, self.base.post_norm[l].data_ptr(), H,
+                                                cfg.eps, self.a_in, H, self.A_gu[l], 2 * r,
+                                                self.ws_gu.data_ptr(), st))
+            self._round(agg.OP_GATE_UP_FUSED, l, st)
+            check(L.swl_fused_gu_silu_shrink(n, rows, self.a_out, 2 * I, self.B_gu[l], r, self.ws_gu.data_ptr(),
+                                             self.norm_splits, I, self.a_in, I, self.A_dn[l], r,
+                                             self.ws_dn.data_ptr(), st))
+            self._round(agg.OP_DOWN_PROJ, l, st)
+            last = l == nl - 1
+            w_next = self.base.final_norm if last else self.base.in_norm[l + 1]
+            check(L.swl_fused_resid_norm_shrink(n, rows, self.a_out, H, self.B_dn[l], r, s, self.ws_dn.data_ptr(),
+                                                self.dn_splits, 1, self.a_h, H, w_next.data_ptr(), H, cfg.eps,
+                                                self.a_in, H, None if last else self.A_qkv[l + 1], 3 * r,
+                                                self.ws_qkv.data_ptr(), st))
+        self._round(agg.OP_LM_HEAD, 0, st)
+        check(L.swl_copy_rows(n, self.a_out, self.a_tok, self.a_b8, st))
+        check(L.swl_advance_i32(self.seqlens.data_ptr(), n, 1, st))
+
+    def _enqueue_unfused(self, stream: torch.cuda.Stream) -> None:
+        """Modular sequence (one kernel per operation), kept as a cross-check."""
         L, cfg, n, st = lib(), self.cfg, self.n, stream.cuda_stream
         H, I, D, r = cfg.hidden, cfg.inter, cfg.head_dim, cfg.rank
         sp, ws = self.splits, self.ws.data_ptr()
@@ -275,10 +334,13 @@ class SlotGroup:
         check(L.swl_advance_i32(self.seqlens.data_ptr(), n, 1, st))
 
     def launches_per_step(self) -> int:
-        """Kernel launches of one step (attention adds a combine launch when split)."""
-        attn = 2 if wo.attention_part_floats(self.n, self.cfg.hq, self.cfg.hkv, self.max_len) else 1
-        per_layer = 2 + 4 * 3 + 1 + attn  # norms, (shrink+round+expand)x4, rope, attention
-        return 3 + self.cfg.layers * per_layer + 1 + 2 + 1 + 1  # + LM head argmax
+        """Kernel launches of one step of this library's kernels."""
+        if self.fused:
+            # copy, embed, embed-norm; per layer 4 rounds + qkv_rope + attention (2) + 3 epilogues;
+            # LM head GEMM + argmax, copy, advance
+            return 3 + self.cfg.layers * 10 + 2 + 2
+        per_layer = 2 + 4 * 3 + 1 + 2  # norms, (shrink+round+expand)x4, rope, attention + combine
+        return 3 + self.cfg.layers * per_layer + 1 + 2 + 1 + 1
 
     def capture(self, stream: torch.cuda.Stream | None = None) -> None:
         """Captures one step into a CUDA graph (replayed by `replay`). Capture

@@ -43,14 +43,15 @@ def _check_tokens(got, want, logits, what):
             assert lg[g] >= lg.max() - BF_ULP * lg.max().abs(), f"{what}: slot {i} token {g} != {w}"
 
 
-def test_engine_matches_oracle_and_graph_replay(native, cuda):
+@pytest.mark.parametrize("fused", [True, False])
+def test_engine_matches_oracle_and_graph_replay(native, cuda, fused):
     from swarmlora_b200.engine import ModelConfig, SlotGroup, random_adapter, random_base
     cfg = ModelConfig(layers=2, vocab=4096)
     ctx = [20, 0, 31, 100, 7]
     n = len(ctx)
     base = random_base(cfg, seed=1, device=cuda, norm_noise=0.1)
     adapters = [random_adapter(cfg, seed=10 + i, device=cuda) if i != 2 else None for i in range(n)]
-    grp = SlotGroup(cfg, base, adapters, ctx, max_new=8, seed=3)
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=8, seed=3, fused=fused)
     try:
         base_c, ad_c = _cpu(base), _cpu(adapters)
         kc = [k.cpu() for k in grp.k_cache]
