@@ -56,6 +56,8 @@ def parse():
                          "(for ncu --profile-from-start off)")
     ap.add_argument("--profile-round", choices=["qkv", "o", "gate_up", "down"], default=None,
                     help="run only --steps launches of one round kind at M=--slots (small ncu case)")
+    ap.add_argument("--profile-attention", action="store_true",
+                    help="run only --steps paged-attention launches over one layer's KV (small ncu case)")
     return ap.parse_args()
 
 
@@ -473,8 +475,48 @@ def profile_round(args):
     return 0
 
 
+def profile_attention(args):
+    """Standalone decode attention case: --slots rows, contexts U[256,1024],
+    one layer of paged KV (> L2), --steps launches of attention + combine."""
+    import math
+    import torch
+    from swarmlora_b200 import worker_ops as wo
+    from swarmlora_b200.engine import LLAMA_3_1_8B as cfg
+    dev = torch.device("cuda:0")
+    n = args.slots
+    g = torch.Generator(device=dev).manual_seed(0)
+    ctx = [int(c) for c in torch.randint(CTX_LO, CTX_HI + 1, (n,), generator=torch.Generator().manual_seed(1))]
+    pps = (CTX_HI + 1 + 15) // 16
+    perm = torch.randperm(n * pps, generator=g, device=dev).to(torch.int32)
+    bts = [perm[i * pps:(i + 1) * pps].contiguous() for i in range(n)]
+    kc = torch.randn(n * pps, 16, cfg.hkv, cfg.head_dim, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(n * pps, 16, cfg.hkv, cfg.head_dim, generator=g, device=dev).to(torch.bfloat16)
+    sl = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    q = torch.randn(n, cfg.hq * cfg.head_dim, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    part = torch.empty(wo.attention_part_floats(n, cfg.hq, cfg.hkv, CTX_HI + 1), dtype=torch.float32, device=dev)
+    args_ = ([1] * n, bts, [kc] * n, [vc] * n, [sl[i:i + 1] for i in range(n)], [out[i:i + 1] for i in range(n)],
+             q, part, cfg.hq, cfg.hkv, CTX_HI + 1, 1.0 / math.sqrt(cfg.head_dim))
+    for _ in range(args.warmup):
+        wo.paged_attention(*args_)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        wo.paged_attention(*args_)
+    b.record()
+    b.synchronize()
+    kv_bytes = sum(ctx) * cfg.hkv * cfg.head_dim * 2 * 2
+    us = a.elapsed_time(b) * 1e3 / args.steps
+    print(json.dumps({"profile_attention": True, "rows": n, "kv_bytes": kv_bytes,
+                      "us_per_call_incl_host": us, "gbs": kv_bytes / us / 1e3}))
+    return 0
+
+
 def main():
     args = parse()
+    if args.profile_attention:
+        return profile_attention(args)
     if args.profile_round:
         return profile_round(args)
     if args.impl == "reference":

@@ -51,15 +51,23 @@ __device__ __forceinline__ void ld8(const __nv_bfloat16* p, float (&v)[8]) {
   }
 }
 
-// Rebuilds the bf16-rounded LoRA intermediate t[0..n) of global row gr from
-// `splits` fp32 partials ws[split][total_rows][n] into shared memory.
-__device__ __forceinline__ void rebuild_t(float* t, const float* ws, int splits, int total_rows,
+constexpr int kPartialsMax = 1024;  // floats of one row's shrink partials (splits * n)
+
+// Rebuilds the bf16-rounded LoRA intermediate t[0..n) of row gr from `splits`
+// fp32 partials laid out ws[row][split][n]: the CTA stages the row's
+// splits * n contiguous floats in shared memory, then n threads add them in
+// split order. Ends with a barrier.
+__device__ __forceinline__ void rebuild_t(float* t, float* buf, const float* ws, int splits,
                                           int gr, int n) {
+  const float* src = ws + static_cast<int64_t>(gr) * splits * n;
+  for (int e = threadIdx.x; e < splits * n; e += blockDim.x) buf[e] = src[e];
+  __syncthreads();
   for (int j = threadIdx.x; j < n; j += blockDim.x) {
     float s = 0.f;
-    for (int sp = 0; sp < splits; ++sp) s += ws[(static_cast<int64_t>(sp) * total_rows + gr) * n + j];
+    for (int sp = 0; sp < splits; ++sp) s += buf[sp * n + j];
     t[j] = bfr(s);
   }
+  __syncthreads();
 }
 
 template <int RANK>
@@ -80,12 +88,12 @@ template <int RANK>
 __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ QkvRopeTable tab,
                                                        const QkvRopeParams p) {
   __shared__ float t[3 * 32];
+  __shared__ float buf[kPartialsMax];
   const int gr = blockIdx.x;
   const int s = seg_row(tab.seg, gr);
   const int64_t local = gr - tab.seg.row_start[s];
   const __nv_bfloat16* B = tab.B[s];
-  if (B) rebuild_t(t, p.ws_in, p.splits_in, tab.seg.total_rows, gr, 3 * RANK);
-  __syncthreads();
+  if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 3 * RANK);
   const int pi = blockIdx.y * blockDim.x + threadIdx.x;
   const int heads = p.hq + 2 * p.hkv;
   const int half = p.head_dim / 2;
@@ -128,6 +136,7 @@ template <int RANK>
 __global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
                                                                 const ResidNormParams p) {
   extern __shared__ float sm[];  // xs[C] | t[32] | red[...]
+  __shared__ float buf[kPartialsMax];
   __shared__ float ss_part;
   __shared__ float warp_ss[4];
   const int q = static_cast<int>(ptx::cluster_rank());
@@ -140,8 +149,7 @@ __global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_con
   float* t = sm + C;
   float* red = t + 32;
   const __nv_bfloat16* B = tab.B[s];
-  if (RANK > 0 && B) rebuild_t(t, p.ws_in, p.splits_in, tab.seg.total_rows, gr, RANK);
-  __syncthreads();
+  if (RANK > 0 && B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, RANK);
   const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
   __nv_bfloat16* h = tab.h[s] + local * p.h_stride;
   float ss = 0.f;
@@ -210,7 +218,7 @@ __global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_con
     *reinterpret_cast<uint2*>(xo + n) = *reinterpret_cast<uint2*>(xv);
   }
   __syncthreads();
-  // next round's LoRA shrink over this CTA's columns: ws_next[q][gr][j]
+  // next round's LoRA shrink over this CTA's columns: ws_next[gr][q][j]
   const __nv_bfloat16* A = tab.A_next[s];
   if (A) {
     const int R = p.r_next, G = R / 8;
@@ -236,63 +244,81 @@ __global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_con
     for (int j = tid; j < R; j += blockDim.x) {
       float v = 0.f;
       for (int g = 0; g < kgroups; ++g) v += red[(g * G + j / 8) * 8 + (j & 7)];
-      p.ws_next[(static_cast<int64_t>(q) * tab.seg.total_rows + gr) * R + j] = v;
+      p.ws_next[(static_cast<int64_t>(gr) * kCluster + q) * R + j] = v;
     }
   }
   ptx::cluster_sync();  // peers may still read ss_part
 }
 
 // ---- after the Gate+Up round ----------------------------------------------------------
+// One thread per 4 consecutive columns of the SiLU product; CTA = (row, 1024
+// columns). The Down shrink partial of the CTA's columns goes to
+// ws_next[row][blockIdx.y][j].
 template <int RANK>
 __global__ void __launch_bounds__(256) gu_silu_shrink_kernel(const __grid_constant__ GuSiluTable tab,
                                                              const GuSiluParams p) {
   __shared__ float t[2 * 32];
+  __shared__ float buf[kPartialsMax];
   __shared__ float red[8][32];
   const int gr = blockIdx.x;
   const int s = seg_row(tab.seg, gr);
   const int64_t local = gr - tab.seg.row_start[s];
   const __nv_bfloat16* B = tab.B[s];
-  if (B) rebuild_t(t, p.ws_in, p.splits_in, tab.seg.total_rows, gr, 2 * RANK);
-  __syncthreads();
-  const int64_t n = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
-  float a = 0.f;
-  if (n < p.inter) {
+  if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 2 * RANK);
+  const int64_t n0 = (static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x) * 4;
+  const bool live = n0 < p.inter;
+  float a[4] = {0.f, 0.f, 0.f, 0.f};
+  if (live) {
     const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
-    float g = __bfloat162float(base[n]), u = __bfloat162float(base[n + p.inter]);
-    if (B) {
-      g = bfr(g + bfr(lora_dot<RANK>(t, B + n * RANK)));
-      u = bfr(u + bfr(lora_dot<RANK>(t + RANK, B + (n + p.inter) * RANK)));
+    const uint2 gu = *reinterpret_cast<const uint2*>(base + n0);
+    const uint2 uu = *reinterpret_cast<const uint2*>(base + n0 + p.inter);
+    const __nv_bfloat162* gv = reinterpret_cast<const __nv_bfloat162*>(&gu);
+    const __nv_bfloat162* uv = reinterpret_cast<const __nv_bfloat162*>(&uu);
+    float g[4], u[4];
+    const float2 g01 = __bfloat1622float2(gv[0]), g23 = __bfloat1622float2(gv[1]);
+    const float2 u01 = __bfloat1622float2(uv[0]), u23 = __bfloat1622float2(uv[1]);
+    g[0] = g01.x; g[1] = g01.y; g[2] = g23.x; g[3] = g23.y;
+    u[0] = u01.x; u[1] = u01.y; u[2] = u23.x; u[3] = u23.y;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (B) {
+        g[e] = bfr(g[e] + bfr(lora_dot<RANK>(t, B + (n0 + e) * RANK)));
+        u[e] = bfr(u[e] + bfr(lora_dot<RANK>(t + RANK, B + (n0 + e + p.inter) * RANK)));
+      }
+      const float sg = bfr(g[e] / (1.f + expf(-g[e])));
+      a[e] = bfr(sg * u[e]);
     }
-    const float sg = bfr(g / (1.f + expf(-g)));
-    a = bfr(sg * u);
-    tab.act[s][local * p.act_stride + n] = __float2bfloat16_rn(a);
+    __align__(8) __nv_bfloat162 av[2] = {__floats2bfloat162_rn(a[0], a[1]), __floats2bfloat162_rn(a[2], a[3])};
+    *reinterpret_cast<uint2*>(tab.act[s] + local * p.act_stride + n0) = *reinterpret_cast<uint2*>(av);
   }
   const __nv_bfloat16* A = tab.A_next[s];
   if (!A) return;
   const int R = p.r_next;
-  float part[32];
-  if (n < p.inter) {
-    for (int j = 0; j < R; j += 8) {
-      float v[8];
-      ld8(A + n * R + j, v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) part[j + e] = a * v[e];
-    }
-  } else {
-    for (int j = 0; j < R; ++j) part[j] = 0.f;
-  }
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int j = 0; j < R; ++j) {
-    float v = part[j];
+  for (int j0 = 0; j0 < R; j0 += 8) {
+    float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (live) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red[w][j] = v;
+      for (int e = 0; e < 4; ++e) {
+        float v[8];
+        ld8(A + (n0 + e) * R + j0, v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) part[q] = fmaf(a[e], v[q], part[q]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float v = part[q];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red[w][j0 + q] = v;
+    }
   }
   __syncthreads();
   if (threadIdx.x < R) {
     float v = 0.f;
     for (int ww = 0; ww < static_cast<int>(blockDim.x >> 5); ++ww) v += red[ww][threadIdx.x];
-    p.ws_next[(static_cast<int64_t>(blockIdx.y) * tab.seg.total_rows + gr) * R + threadIdx.x] = v;
+    p.ws_next[(static_cast<int64_t>(gr) * gridDim.y + blockIdx.y) * R + threadIdx.x] = v;
   }
 }
 
@@ -301,6 +327,7 @@ __global__ void __launch_bounds__(256) gu_silu_shrink_kernel(const __grid_consta
 int launch_qkv_rope(const QkvRopeTable& tab, const QkvRopeParams& p, int r, cudaStream_t stream) {
   if (tab.seg.total_rows <= 0) return SWL_OK;
   if (p.head_dim % 2 || p.head_dim > 256) return set_error(SWL_ERR_ARG, "qkv_rope: bad head_dim");
+  if (p.splits_in * 3 * r > kPartialsMax) return set_error(SWL_ERR_ARG, "qkv_rope: too many shrink partials");
   const int pairs = (p.hq + 2 * p.hkv) * (p.head_dim / 2);
   dim3 grid(tab.seg.total_rows, (pairs + 255) / 256);
   switch (r) {
@@ -318,6 +345,7 @@ int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p
   if (tab.seg.total_rows <= 0) return SWL_OK;
   if (p.hidden % (kCluster * 4)) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be a multiple of 32");
   if (p.r_next % 8 || p.r_next > 96) return set_error(SWL_ERR_ARG, "resid_norm: next rank layout must be 8..96 in steps of 8");
+  if (p.splits_in * r_in > kPartialsMax) return set_error(SWL_ERR_ARG, "resid_norm: too many shrink partials");
   const int64_t C = p.hidden / kCluster;
   const size_t smem = (C + 32 + 128 * 8) * sizeof(float);
   cudaLaunchConfig_t cfg = {};
@@ -345,7 +373,9 @@ int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p
 int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, cudaStream_t stream) {
   if (tab.seg.total_rows <= 0) return SWL_OK;
   if (p.r_next % 8 || p.r_next > 32) return set_error(SWL_ERR_ARG, "gu_silu: next rank must be 8..32 in steps of 8");
-  dim3 grid(tab.seg.total_rows, static_cast<unsigned>((p.inter + 255) / 256));
+  if (p.inter % 4) return set_error(SWL_ERR_ARG, "gu_silu: inter must be a multiple of 4");
+  if (p.splits_in * 2 * r > kPartialsMax) return set_error(SWL_ERR_ARG, "gu_silu: too many shrink partials");
+  dim3 grid(tab.seg.total_rows, static_cast<unsigned>((p.inter + 1023) / 1024));
   switch (r) {
     case 8: gu_silu_shrink_kernel<8><<<grid, 256, 0, stream>>>(tab, p); break;
     case 16: gu_silu_shrink_kernel<16><<<grid, 256, 0, stream>>>(tab, p); break;
@@ -357,5 +387,6 @@ int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, 
 }
 
 int resid_norm_splits() { return kCluster; }
+int gu_silu_splits(int64_t inter) { return static_cast<int>((inter + 1023) / 1024); }
 
 }  // namespace swl

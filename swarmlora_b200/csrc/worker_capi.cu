@@ -150,7 +150,7 @@ SWL_EXPORT int swl_paged_attention(int nseg, const int* rows, const void* const*
 }
 
 // swl_paged_attention plus the O projection's LoRA shrink on its output:
-// ws_o[head][row][j] = sum_d out[row, head*D + d] * A_o[i][head*D + d, j]
+// ws_o[row][head][j] = sum_d out[row, head*D + d] * A_o[i][head*D + d, j]
 // (A_o[i] = lora_A(o_proj)^T, [hq*D, r]; NULL for a slot without adapter).
 SWL_EXPORT int swl_paged_attention_shrink(int nseg, const int* rows, const void* const* block_tables,
                                           const void* const* k_cache, const void* const* v_cache,
@@ -177,7 +177,7 @@ SWL_EXPORT int swl_paged_attention_shrink(int nseg, const int* rows, const void*
 }
 
 // Fused epilogue of the QKV round: q|k|v = round output + LoRA delta (shrink
-// partials ws_in [splits_in][rows][3r], lora_B rows B[i] [(hq+2hkv)*D, r]),
+// partials ws_in [rows][splits_in][3r], lora_B rows B[i] [(hq+2hkv)*D, r]),
 // NeoX RoPE of q and k at position *seqlens[i] + t, k and v appended to the
 // paged cache, rotated q written to q_rot [total_rows, hq*D].
 SWL_EXPORT int swl_fused_qkv_rope(int nseg, const int* rows, const void* const* base,
@@ -210,7 +210,7 @@ SWL_EXPORT int swl_fused_qkv_rope(int nseg, const int* rows, const void* const* 
 // Fused epilogue of the O / Down round (and of the embedding): h = [h +]
 // (base + bf16(bf16(t @ B^T) * post_scale)), then x = RMSNorm(h) * w written to
 // x_out (the next round's slot input) and the next round's LoRA shrink
-// partials ws_next[8][rows][r_next] = x @ A_next (A_next[i] NULL: none).
+// partials ws_next[rows][8][r_next] = x @ A_next (A_next[i] NULL: none).
 SWL_EXPORT int swl_fused_resid_norm_shrink(int nseg, const int* rows, const void* const* base,
                                            int64_t base_stride, const void* const* B, int r_in,
                                            float post_scale, const float* ws_in, int splits_in,
@@ -245,9 +245,9 @@ SWL_EXPORT int swl_fused_resid_norm_shrink(int nseg, const int* rows, const void
 }
 
 // Fused epilogue of the Gate+Up round: gate/up = round output + LoRA delta
-// (partials ws_in [splits_in][rows][2r], lora_B rows B[i] [2*inter, r]),
+// (partials ws_in [rows][splits_in][2r], lora_B rows B[i] [2*inter, r]),
 // act = SiLU(gate) * up written to act[i] (the Down round's slot input), and
-// the Down LoRA shrink partials ws_next[ceil(inter/256)][rows][r_next].
+// the Down LoRA shrink partials ws_next[rows][ceil(inter/1024)][r_next].
 SWL_EXPORT int swl_fused_gu_silu_shrink(int nseg, const int* rows, const void* const* base,
                                         int64_t base_stride, const void* const* B, int r,
                                         const float* ws_in, int splits_in, int64_t inter,
@@ -275,6 +275,9 @@ SWL_EXPORT int swl_fused_gu_silu_shrink(int nseg, const int* rows, const void* c
 
 // Number of shrink partials swl_fused_resid_norm_shrink writes (its cluster size).
 SWL_EXPORT int swl_fused_norm_splits(void) { return resid_norm_splits(); }
+
+// Number of Down-shrink partials swl_fused_gu_silu_shrink writes per row.
+SWL_EXPORT int swl_fused_silu_splits(int64_t inter) { return gu_silu_splits(inter); }
 
 // LlamaRMSNorm over rows: out = w * bf16(x * rsqrt(mean(x^2) + eps)).
 SWL_EXPORT int swl_rms_norm(int nseg, const int* rows, const void* const* x, int64_t x_stride,

@@ -232,53 +232,85 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const __grid_constant_
 }
 
 // ---- paged attention -------------------------------------------------------------------
-// CTA = (token row, kv head, context split), one warp per query head of the
-// kv head's group. The split's pages stream through a 4-stage cp.async ring in
-// shared memory (one 16-token page of K and of V per stage; 16-byte pieces
-// XOR-swizzled by token so the warps' reads are conflict-free), shared by all
-// query heads of the group. Lanes: grp = lane / 4 takes one of 8 keys per step,
-// sub = lane % 4 holds 32 of the 128 dims. Online softmax in the log2 domain.
-// Every CTA writes a partial record [m, l, o[128]] per query head; the
-// combine kernel merges the splits.
+// CTA = one warp = (token row, kv head, context split). The warp computes all
+// G query heads of the kv head at once on tensor cores (mma.sync m16n8k16,
+// bf16 in, fp32 accumulate): per 16-token page,
+//   S[head, tok]  = Q[head, :] . K[tok, :]      (A = Q, heads padded to 16 rows;
+//                                                B = K^T via ldmatrix)
+//   P = exp2(S*scale*log2e - m)                 (online softmax in registers)
+//   O[head, dim] += P[head, tok] . V[tok, dim]  (A = P reused from the S
+//                                                accumulator, B = V via ldmatrix.trans)
+// Pages stream through a 3-stage cp.async ring in shared memory; each 16-byte
+// piece of a token row is stored XOR-swizzled by (token & 7) so the 8-row
+// ldmatrix reads hit 8 different bank groups. Tokens past the causal end are
+// zero-filled and masked. Each CTA writes one record [m, l, o[128]] per
+// query head; attention_combine_kernel merges the splits.
 constexpr int kD = 128;
 constexpr int kPageTok = 16;
-constexpr int kAttnStages = 4;
-constexpr int kTileBytes = kPageTok * kD * 2;  // one page of K (or V) of one head
+constexpr int kAttnStages = 3;
+constexpr int kTileBytes = kPageTok * kD * 2;  // one page of K (or V) of one head: 4 KB
+constexpr int kMaxSplitPages = 256;
 
-__global__ void __launch_bounds__(256) paged_attention_kernel(const __grid_constant__ AttnTable tab,
-                                                              const AttnParams p, int splits,
-                                                              float* __restrict__ part) {
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                              uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(32) paged_attention_kernel(const __grid_constant__ AttnTable tab,
+                                                             const AttnParams p, int splits,
+                                                             float* __restrict__ part) {
   __shared__ __align__(128) uint8_t kv_sm[kAttnStages][2][kTileBytes];
+  __shared__ int pages[kMaxSplitPages];
   const int gr = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x;
   const int G = p.hq / p.hkv;
-  const int nthreads = 32 * G;
-  const int h = kvh * G + w;
+  const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
   const int s = seg_of_row(tab.seg, gr);
   const int local = gr - tab.seg.row_start[s];
   const int L = *tab.seqlen[s] + local + 1;  // causal: keys 0 .. pos
   const int ntiles = (L + kPageTok - 1) / kPageTok;
   const int tb = static_cast<int>(static_cast<int64_t>(ntiles) * split / splits);
   const int te = static_cast<int>(static_cast<int64_t>(ntiles) * (split + 1) / splits);
-  const int nt = te - tb;
-  const int grp = lane >> 2, sub = lane & 3;
+  const int nt = min(te - tb, kMaxSplitPages);
   const int* bt = tab.block_table[s];
+  for (int i = lane; i < nt; i += 32) pages[i] = bt[tb + i];
+  __syncwarp();
   const __nv_bfloat16* kc = tab.k_cache[s];
   const __nv_bfloat16* vc = tab.v_cache[s];
+  const uint32_t sm0 = static_cast<uint32_t>(__cvta_generic_to_shared(&kv_sm[0][0][0]));
 
   auto load_tile = [&](int i, int st) {
-    const int tile = tb + i;
-    const int64_t page = bt[tile];
-    for (int c = threadIdx.x; c < 2 * kPageTok * 16; c += nthreads) {
-      const int kv = c >> 8, cc = c & 255;
+    const int64_t page = pages[i];
+    const int tok0 = (tb + i) * kPageTok;
+#pragma unroll 4
+    for (int cidx = lane; cidx < 2 * kPageTok * 16; cidx += 32) {
+      const int kv = cidx >> 8, cc = cidx & 255;
       const int tok = cc >> 4, ch = cc & 15;
-      const bool live = tile * kPageTok + tok < L;
-      const __nv_bfloat16* src =
-          (kv ? vc : kc) + ((page * p.page + tok) * p.hkv + kvh) * kD + ch * 8;
-      const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(&kv_sm[st][kv][0])) +
-                           tok * 256 + ((ch ^ (tok & 7)) << 4);
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
-                   "l"(live ? src : kc), "r"(live ? 16 : 0)
+      const bool live = tok0 + tok < L;
+      const __nv_bfloat16* src = (kv ? vc : kc) + ((page * p.page + tok) * p.hkv + kvh) * kD + ch * 8;
+      const uint32_t dst = sm0 + (st * 2 + kv) * kTileBytes + tok * 256 + ((ch ^ (tok & 7)) << 4);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(live ? src : kc),
+                   "r"(live ? 16 : 0)
                    : "memory");
     }
   };
@@ -288,94 +320,101 @@ __global__ void __launch_bounds__(256) paged_attention_kernel(const __grid_const
     asm volatile("cp.async.commit_group;" ::: "memory");
   }
 
-  const float qscale = p.scale * 1.4426950408889634f;
-  float q[32];
+  // Q as the A operand: rows = query heads of this kv head (g < G), k = dims.
+  uint32_t qa[8][2];
   {
-    const __nv_bfloat16* qp = p.q_rot + (static_cast<int64_t>(gr) * p.hq + h) * kD + sub * 32;
+    const bool real = g < G;
+    const __nv_bfloat16* qp = p.q_rot + (static_cast<int64_t>(gr) * p.hq + kvh * G + (real ? g : 0)) * kD;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float v[8];
-      load8(qp + c * 8, v);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) q[c * 8 + i] = v[i] * qscale;
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = real ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 2 * c) : 0u;
+      qa[ks][1] = real ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 8 + 2 * c) : 0u;
     }
   }
-  float m = -INFINITY, l = 0.f, o[32];
+  const float sl2 = p.scale * 1.4426950408889634f;
+  float m = -INFINITY, l = 0.f;
+  float o[16][4];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) o[i] = 0.f;
+  for (int nt8 = 0; nt8 < 16; ++nt8) o[nt8][0] = o[nt8][1] = o[nt8][2] = o[nt8][3] = 0.f;
+  // ldmatrix row address pieces of this lane
+  const int mi = lane >> 3, r8 = lane & 7;
 
   for (int i = 0; i < nt; ++i) {
     asm volatile("cp.async.wait_group %0;" ::"n"(kAttnStages - 2) : "memory");
-    __syncthreads();
+    __syncwarp();
     const int nx = i + kAttnStages - 1;
     if (nx < nt) load_tile(nx, nx % kAttnStages);
     asm volatile("cp.async.commit_group;" ::: "memory");
-    const uint8_t* ks = kv_sm[i % kAttnStages][0];
-    const uint8_t* vs = kv_sm[i % kAttnStages][1];
+    const int st = i % kAttnStages;
+    const uint32_t ks_base = sm0 + (st * 2 + 0) * kTileBytes;
+    const uint32_t vs_base = sm0 + (st * 2 + 1) * kTileBytes;
+    // S = Q K^T for tokens 0-7 (sa) and 8-15 (sb)
+    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int g8 = 0; g8 < kPageTok / 8; ++g8) {
-      const int tok = g8 * 8 + grp;
-      const bool valid = (tb + i) * kPageTok + tok < L;
-      float sc = 0.f;
+    for (int ks = 0; ks < 8; ++ks) {
+      // matrices: (tok 0-7, dims 16ks..+7), (tok 0-7, +8..15), (tok 8-15, ..), (tok 8-15, +8..)
+      const int tok = (mi >> 1) * 8 + r8;
+      const int ch = ks * 2 + (mi & 1);
+      uint32_t b0a, b1a, b0b, b1b;
+      ldsm_x4(ks_base + tok * 256 + ((ch ^ (tok & 7)) << 4), b0a, b1a, b0b, b1b);
+      mma_bf16_16816(sa, qa[ks][0], 0u, qa[ks][1], 0u, b0a, b1a);
+      mma_bf16_16816(sb, qa[ks][0], 0u, qa[ks][1], 0u, b0b, b1b);
+    }
+    const int tok0 = (tb + i) * kPageTok;
+    float sv[4] = {sa[0] * sl2, sa[1] * sl2, sb[0] * sl2, sb[1] * sl2};
+    const int tk[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 u = *reinterpret_cast<const uint4*>(ks + tok * 256 + (((4 * sub + c) ^ grp) << 4));
-        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&u);
+    for (int e = 0; e < 4; ++e)
+      if (tok0 + tk[e] >= L) sv[e] = -INFINITY;
+    float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(m, mx);
+    const float corr = (mn == -INFINITY) ? 1.f : exp2f(m - mn);
+    float pv[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(hv[e]);
-          sc = fmaf(q[c * 8 + 2 * e], f.x, sc);
-          sc = fmaf(q[c * 8 + 2 * e + 1], f.y, sc);
-        }
-      }
-      sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-      sc += __shfl_xor_sync(0xffffffffu, sc, 2);
-      if (!valid) sc = -INFINITY;
-      float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 4));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float mn = fmaxf(m, mx);
-      const float corr = mn == -INFINITY ? 1.f : exp2f(m - mn);
-      const float pr = valid ? exp2f(sc - mn) : 0.f;
-      float ps = pr + __shfl_xor_sync(0xffffffffu, pr, 4);
-      ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-      ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-      l = l * corr + ps;
+    for (int e = 0; e < 4; ++e) pv[e] = (mn == -INFINITY) ? 0.f : exp2f(sv[e] - mn);
+    l = l * corr + (pv[0] + pv[1] + pv[2] + pv[3]);
+    m = mn;
+    const uint32_t pa0 = pack_bf16(pv[0], pv[1]), pa2 = pack_bf16(pv[2], pv[3]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 u = *reinterpret_cast<const uint4*>(vs + tok * 256 + (((4 * sub + c) ^ grp) << 4));
-        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&u);
+    for (int nt8 = 0; nt8 < 16; ++nt8) {
+      o[nt8][0] *= corr;
+      o[nt8][1] *= corr;
+    }
+    // O += P V: per 16 dims one ldmatrix.trans x4 ->
+    // (tok 0-7, dims n0..n0+7), (tok 8-15, n0..), (tok 0-7, n0+8..), (tok 8-15, n0+8..)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(hv[e]);
-          o[c * 8 + 2 * e] = o[c * 8 + 2 * e] * corr + pr * f.x;
-          o[c * 8 + 2 * e + 1] = o[c * 8 + 2 * e + 1] * corr + pr * f.y;
-        }
-      }
-      m = mn;
+    for (int nd = 0; nd < 8; ++nd) {
+      const int tok = (mi & 1) * 8 + r8;
+      const int ch = nd * 2 + (mi >> 1);
+      uint32_t b0a, b1a, b0b, b1b;
+      ldsm_x4_trans(vs_base + tok * 256 + ((ch ^ (tok & 7)) << 4), b0a, b1a, b0b, b1b);
+      mma_bf16_16816(o[2 * nd], pa0, 0u, pa2, 0u, b0a, b1a);
+      mma_bf16_16816(o[2 * nd + 1], pa0, 0u, pa2, 0u, b0b, b1b);
     }
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 4);
-    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 8);
-    o[i] += __shfl_xor_sync(0xffffffffu, o[i], 16);
-  }
-  if (grp != 0) return;
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  if (g >= G) return;
+  const int h = kvh * G + g;
   float* rec = part + ((static_cast<int64_t>(gr) * p.hq + h) * splits + split) * (kD + 2);
-  if (sub == 0) {
+  if (c == 0) {
     rec[0] = m;
     rec[1] = l;
   }
 #pragma unroll
-  for (int i = 0; i < 32; ++i) rec[2 + sub * 32 + i] = o[i];
+  for (int nt8 = 0; nt8 < 16; ++nt8) {
+    rec[2 + nt8 * 8 + 2 * c] = o[nt8][0];
+    rec[2 + nt8 * 8 + 2 * c + 1] = o[nt8][1];
+  }
 }
 
 // Merges the context splits of one (row, head): O = sum_s 2^(m_s - M) o_s /
 // sum_s 2^(m_s - M) l_s, written as bf16 to the slot's attention output. With
 // a shrink side (A != nullptr) it also emits this head's share of the O
-// projection's LoRA shrink: ws[h][row][j] = sum_d out[d] * A[h*128 + d, j].
+// projection's LoRA shrink: ws[row][h][j] = sum_d out[d] * A[h*128 + d, j].
 __global__ void __launch_bounds__(128) attention_combine_kernel(const __grid_constant__ AttnTable tab,
                                                                 const AttnParams p, int splits,
                                                                 const float* __restrict__ part,
@@ -418,7 +457,7 @@ __global__ void __launch_bounds__(128) attention_combine_kernel(const __grid_con
   __syncthreads();
   if (d < sh.r) {
     const float v = red[0][d] + red[1][d] + red[2][d] + red[3][d];
-    sh.ws[(static_cast<int64_t>(h) * tab.seg.total_rows + gr) * sh.r + d] = v;
+    sh.ws[(static_cast<int64_t>(gr) * p.hq + h) * sh.r + d] = v;
   }
 }
 
@@ -549,10 +588,13 @@ int launch_rope_append(const AttnTable& tab, const AttnParams& p, cudaStream_t s
 }
 
 int attention_splits(int total_rows, int hkv, int max_len) {
-  // Enough context splits for ~4 CTAs per SM, at least 4 pages per split.
+  // One-warp CTAs: enough context splits for ~8 CTAs per SM with at least 2
+  // pages per split, and few enough pages per split for the page-id buffer.
   const int base = std::max(1, total_rows * hkv);
-  int splits = std::max(1, std::min((4 * 148 + base - 1) / base, max_len / (4 * kPageTok)));
-  return std::min(splits, 32);
+  const int pages = (max_len + kPageTok - 1) / kPageTok;
+  int splits = std::max(1, std::min(8 * 148 / base, pages / 2));
+  splits = std::max(splits, (pages + kMaxSplitPages - 1) / kMaxSplitPages);
+  return std::min(splits, 64);
 }
 
 int64_t attention_part_floats(int total_rows, int hq, int splits) {
@@ -564,11 +606,11 @@ int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream
   if (tab.seg.total_rows <= 0) return SWL_OK;
   if (p.head_dim != kD || p.page != kPageTok || p.hq % p.hkv || p.hq / p.hkv > 8)
     return set_error(SWL_ERR_ARG, "attention: head_dim 128, page 16, at most 8 query heads per kv head");
+  if (p.max_len > 64 * kMaxSplitPages * kPageTok) return set_error(SWL_ERR_ARG, "attention: context too long");
   const int splits = attention_splits(tab.seg.total_rows, p.hkv, p.max_len);
   if (!p.part) return set_error(SWL_ERR_ARG, "attention: missing partial scratch");
-  const int G = p.hq / p.hkv;
   dim3 grid(tab.seg.total_rows, p.hkv, splits);
-  paged_attention_kernel<<<grid, 32 * G, 0, stream>>>(tab, p, splits, p.part);
+  paged_attention_kernel<<<grid, 32, 0, stream>>>(tab, p, splits, p.part);
   SWL_CUDA_TRY(cudaGetLastError());
   ShrinkSide none;
   if (!shrink) {

@@ -100,7 +100,7 @@ int launch_lora_expand(const LoraExpandTable& tab, const ExpandParams& p, const 
                        cudaStream_t stream);
 int launch_rope_append(const AttnTable& tab, const AttnParams& p, cudaStream_t stream);
 // Optional LoRA shrink fused into the attention combine (O projection):
-// ws[head][row][j] = sum_d out[row, head*D + d] * A[head*D + d, j].
+// ws[row][head][j] = sum_d out[row, head*D + d] * A[head*D + d, j].
 struct ShrinkSide {
   const __nv_bfloat16* A[kMaxSlots];  // [hq*D, r] per slot, or nullptr
   int r;
@@ -124,7 +124,7 @@ struct QkvRopeTable {
 struct QkvRopeParams {
   int hq, hkv, head_dim, page;
   int64_t base_stride;
-  const float* ws_in;  // QKV shrink partials [splits_in][total_rows][3 r]
+  const float* ws_in;  // QKV shrink partials [total_rows][splits_in][3 r]
   int splits_in;
   const __nv_bfloat16* cos_sin;
   __nv_bfloat16* q_rot;  // [total_rows, hq * D]
@@ -141,14 +141,14 @@ struct ResidNormTable {
 struct ResidNormParams {
   int64_t hidden;
   float post_scale;       // delta scale after the expand (0 = none)
-  const float* ws_in;     // finished round's shrink partials [splits_in][total_rows][r_in]
+  const float* ws_in;     // finished round's shrink partials [total_rows][splits_in][r_in]
   int splits_in;
   int has_resid;          // 0: h = base (+ delta); 1: h = h + (base + delta)
   const __nv_bfloat16* w; // RMSNorm weight [hidden]
   float eps;
   int64_t base_stride, h_stride, x_stride;
   int r_next;
-  float* ws_next;         // [8][total_rows][r_next]
+  float* ws_next;         // [total_rows][8][r_next]
 };
 
 struct GuSiluTable {
@@ -161,10 +161,10 @@ struct GuSiluTable {
 struct GuSiluParams {
   int64_t inter;
   int64_t base_stride, act_stride;
-  const float* ws_in;  // Gate+Up shrink partials [splits_in][total_rows][2 r]
+  const float* ws_in;  // Gate+Up shrink partials [total_rows][splits_in][2 r]
   int splits_in;
   int r_next;
-  float* ws_next;      // [ceil(inter / 256)][total_rows][r_next]
+  float* ws_next;      // [total_rows][ceil(inter / 1024)][r_next]
 };
 
 int launch_qkv_rope(const QkvRopeTable& tab, const QkvRopeParams& p, int r, cudaStream_t stream);
@@ -172,5 +172,6 @@ int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p
                              cudaStream_t stream);
 int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, cudaStream_t stream);
 int resid_norm_splits();
+int gu_silu_splits(int64_t inter);
 
 }  // namespace swl

@@ -191,7 +191,7 @@ class SlotGroup:
         # fused path: LoRA shrink partials of each round's input, produced by the
         # epilogue kernel that writes that input
         self.norm_splits = int(lib().swl_fused_norm_splits())
-        self.dn_splits = -(-I // 256)
+        self.dn_splits = int(lib().swl_fused_silu_splits(I))
         f32 = dict(dtype=torch.float32, device=self.dev)
         self.ws_qkv = torch.zeros(self.norm_splits * n * 3 * cfg.rank, **f32)
         self.ws_o = torch.zeros(cfg.hq * n * cfg.rank, **f32)
