@@ -50,12 +50,18 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--slots", type=int, default=N_SLOTS)
+    ap.add_argument("--layers", type=int, default=32,
+                    help="decoder layers (32 = the benchmarked model; fewer only for small profiling cases)")
+    ap.add_argument("--vocab", type=int, default=128256,
+                    help="vocabulary (128256 = the benchmarked model; smaller only for profiling cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-step", action="store_true",
                     help="bracket the first timed step with cudaProfilerStart/Stop "
                          "(for ncu --profile-from-start off)")
     ap.add_argument("--profile-round", choices=["qkv", "o", "gate_up", "down"], default=None,
                     help="run only --steps launches of one round kind at M=--slots (small ncu case)")
+    ap.add_argument("--round-algo", type=int, default=0,
+                    help="round kernel for --profile-round: 0 auto, 1 cluster split-K, 3 stream-K")
     ap.add_argument("--profile-attention", action="store_true",
                     help="run only --steps paged-attention launches over one layer's KV (small ncu case)")
     return ap.parse_args()
@@ -326,9 +332,10 @@ def our_arm(args):
     world, rank, local = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    import dataclasses
     from swarmlora_b200.engine import LLAMA_3_1_8B, SlotGroup, random_adapter, random_base
 
-    cfg = LLAMA_3_1_8B
+    cfg = dataclasses.replace(LLAMA_3_1_8B, layers=args.layers, vocab=args.vocab)
     n = args.slots
     g = torch.Generator().manual_seed(1234 + rank)
     ctx = [int(c) for c in torch.randint(CTX_LO, CTX_HI + 1, (n,), generator=g)]
@@ -423,7 +430,7 @@ def our_arm(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init weights, adapters, KV contexts)",
-            "config": {"workload": "BASELINE config 2: Llama-3.1-8B shape (32 layers, vocab 128256), "
+            "config": {"workload": f"BASELINE config 2: Llama-3.1-8B shape ({cfg.layers} layers, vocab {cfg.vocab}), "
                                    f"{n} decode slots/GPU, distinct r=16 adapters on 7 projections, "
                                    f"ctx U[{CTX_LO},{CTX_HI}] paged 16, 1 token/slot/step, greedy",
                        "slots_per_gpu": n, "parallelism": f"{world} independent aggregator groups",
@@ -462,12 +469,12 @@ def profile_round(args):
     ins = [torch.randn(16, K, generator=g, device=dev).to(torch.bfloat16)[:1] for _ in range(args.slots)]
     outs = [torch.empty(16, N, dtype=torch.bfloat16, device=dev) for _ in range(args.slots)]
     for _ in range(args.warmup):
-        slot_gemm(W, ins, outs)
+        slot_gemm(W, ins, outs, algo=args.round_algo)
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
-        slot_gemm(W, ins, outs)
+        slot_gemm(W, ins, outs, algo=args.round_algo)
     b.record()
     b.synchronize()
     print(json.dumps({"profile_round": args.profile_round, "M": args.slots, "N": N, "K": K,

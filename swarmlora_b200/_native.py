@@ -81,6 +81,8 @@ SIGNATURES: dict[str, tuple] = {
     # ---- kernels callable directly
     "swl_slot_gemm": (_i32, [_p, _i64, _i64, _p, _i32, _pp, _pp, _pi32, _i64, _i64, _i32, _i32, _p]),
     "swl_round_device_error": (_i32, [_pu32]),
+    "swl_round_set_streamk_ctas_per_sm": (_i32, [_i32]),
+    "swl_round_set_streamk_ctas": (_i32, [_i32]),
     # ---- worker kernels
     "swl_lora_shrink": (_i32, [_i32, _pi32, _pp, _i64, _pp, _i64, _i32, _i32, _p, _p]),
     "swl_lora_expand": (_i32, [_i32, _pi32, _pp, _i64, _pp, _pp, _i64, _pp, _i64, _i64, _i32,
@@ -93,13 +95,14 @@ SIGNATURES: dict[str, tuple] = {
     "swl_rms_norm": (_i32, [_i32, _pi32, _pp, _i64, _pp, _i64, _p, _i64, _f32, _p]),
     "swl_copy_rows": (_i32, [_i32, _pp, _pp, _pi64, _p]),
     "swl_paged_attention_shrink": (_i32, [_i32, _pi32, _pp, _pp, _pp, _pp, _pp, _i64, _i32, _i32, _i32,
-                                          _i32, _f32, _i32, _p, _p, _pp, _i32, _p, _p]),
+                                          _i32, _f32, _i32, _p, _p, _pp, _i32, _p, _p, _i64, _p]),
     "swl_fused_qkv_rope": (_i32, [_i32, _pi32, _pp, _i64, _pp, _i32, _p, _i32, _pp, _pp, _pp, _pp,
-                                  _i32, _i32, _i32, _i32, _p, _p, _p]),
+                                  _i32, _i32, _i32, _i32, _p, _p, _p, _i64, _p]),
     "swl_fused_resid_norm_shrink": (_i32, [_i32, _pi32, _pp, _i64, _pp, _i32, _f32, _p, _i32, _i32,
-                                           _pp, _i64, _p, _i64, _f32, _pp, _i64, _pp, _i32, _p, _p]),
+                                           _pp, _i64, _p, _i64, _f32, _pp, _i64, _pp, _i32, _p, _p, _i64,
+                                           _p]),
     "swl_fused_gu_silu_shrink": (_i32, [_i32, _pi32, _pp, _i64, _pp, _i32, _p, _i32, _i64, _pp, _i64,
-                                        _pp, _i32, _p, _p]),
+                                        _pp, _i32, _p, _p, _i64, _p]),
     "swl_fused_norm_splits": (_i32, []),
     "swl_fused_silu_splits": (_i32, [_i64]),
     "swl_advance_i32": (_i32, [_p, _i32, _i32, _p]),

@@ -92,7 +92,7 @@ int g_capacity = 0;
 size_t g_map_bytes = 0;
 
 cudaStream_t g_stream = nullptr;
-int g_round_algo = kAlgoTensorCore;
+int g_round_algo = kAlgoAuto;
 int g_round_splits = 0;
 std::map<int, SamplingState> g_sampling;  // worker_id -> params (main-loop thread only)
 
@@ -285,6 +285,7 @@ SWL_EXPORT int swl_agg_init_slot_pool(int num_slots, int device_index, int hidde
     SWL_CUDA_TRY(cudaMemset(s.out, 0, p.out_bytes));
     SWL_CUDA_TRY(cudaIpcGetMemHandle(&s.out_handle, s.out));
   }
+  SWL_TRY(ensure_streamk_workspace());
   p.initialized = true;
   if (in_bytes) *in_bytes = p.in_bytes;
   if (out_bytes) *out_bytes = p.out_bytes;
@@ -507,11 +508,12 @@ SWL_EXPORT int swl_agg_init_queue(const char* shm_name, int capacity) {
   return SWL_OK;
 }
 
-// Round kernel selection: algo 0/1 = tensor cores, 2 = CUDA cores;
-// splits <= 0 = automatic K split.
+// Round kernel selection: 0 auto (cluster split-K), 1 cluster split-K,
+// 2 CUDA cores, 3 stream-K (<= 64 rows); splits <= 0 = automatic K split for
+// the cluster kernel.
 SWL_EXPORT int swl_agg_set_round_algo(int algo, int splits) {
-  if (algo < 0 || algo > 2) return set_error(SWL_ERR_ARG, "unknown round algo %d", algo);
-  g_round_algo = algo == kAlgoSimt ? kAlgoSimt : kAlgoTensorCore;
+  if (algo < 0 || algo > 3) return set_error(SWL_ERR_ARG, "unknown round algo %d", algo);
+  g_round_algo = algo;
   g_round_splits = splits;
   return SWL_OK;
 }

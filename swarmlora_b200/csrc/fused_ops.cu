@@ -83,6 +83,30 @@ __device__ __forceinline__ float lora_dot(const float* t, const __nv_bfloat16* b
   return d;
 }
 
+// Dot product of the rebuilt t (RANK floats) with a lora_B row held in
+// registers as RANK/8 16-byte vectors.
+template <int RANK>
+__device__ __forceinline__ float dot_regs(const float* t, const uint4 (&b)[RANK / 8]) {
+  float d = 0.f;
+#pragma unroll
+  for (int j = 0; j < RANK / 8; ++j) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&b[j]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      d = fmaf(t[8 * j + 2 * e], f.x, d);
+      d = fmaf(t[8 * j + 2 * e + 1], f.y, d);
+    }
+  }
+  return d;
+}
+
+template <int RANK>
+__device__ __forceinline__ void load_row(uint4 (&b)[RANK / 8], const __nv_bfloat16* row) {
+#pragma unroll
+  for (int j = 0; j < RANK / 8; ++j) b[j] = reinterpret_cast<const uint4*>(row)[j];
+}
+
 // ---- after the QKV round -------------------------------------------------------------
 template <int RANK>
 __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ QkvRopeTable tab,
@@ -90,24 +114,36 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
   __shared__ float t[3 * 32];
   __shared__ float buf[kPartialsMax];
   const int gr = blockIdx.x;
+  ptx::prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   const int s = seg_row(tab.seg, gr);
   const int64_t local = gr - tab.seg.row_start[s];
   const __nv_bfloat16* B = tab.B[s];
-  if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 3 * RANK);
   const int pi = blockIdx.y * blockDim.x + threadIdx.x;
   const int heads = p.hq + 2 * p.hkv;
   const int half = p.head_dim / 2;
-  if (pi >= heads * half) return;
-  const int head = pi / half, d = pi % half;
+  const bool live = pi < heads * half;
+  const int head = live ? pi / half : 0, d = pi % half;
   const int blk = head < p.hq ? 0 : (head < p.hq + p.hkv ? 1 : 2);
   const int64_t n1 = static_cast<int64_t>(head) * p.head_dim + d, n2 = n1 + half;
+  // loads that do not depend on the LoRA intermediate go first
   const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
-  float x1 = __bfloat162float(base[n1]), x2 = __bfloat162float(base[n2]);
-  if (B) {
-    x1 = bfr(x1 + bfr(lora_dot<RANK>(t + blk * RANK, B + n1 * RANK)));
-    x2 = bfr(x2 + bfr(lora_dot<RANK>(t + blk * RANK, B + n2 * RANK)));
+  float x1 = 0.f, x2 = 0.f;
+  uint4 b1[RANK / 8], b2[RANK / 8];
+  if (live) {
+    x1 = __bfloat162float(base[n1]);
+    x2 = __bfloat162float(base[n2]);
+    if (B) {
+      load_row<RANK>(b1, B + n1 * RANK);
+      load_row<RANK>(b2, B + n2 * RANK);
+    }
   }
   const int pos = *tab.seqlen[s] + static_cast<int>(local);
+  if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 3 * RANK);
+  if (!live) return;
+  if (B) {
+    x1 = bfr(x1 + bfr(dot_regs<RANK>(t + blk * RANK, b1)));
+    x2 = bfr(x2 + bfr(dot_regs<RANK>(t + blk * RANK, b2)));
+  }
   if (blk == 2) {
     const int page = tab.block_table[s][pos / p.page];
     const int64_t row = ((static_cast<int64_t>(page) * p.page + pos % p.page) * p.hkv + (head - p.hq - p.hkv)) * p.head_dim;
@@ -131,58 +167,80 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
 }
 
 // ---- after the O / Down round (and the embedding) ------------------------------------
-// Cluster of kCluster CTAs per token row; CTA q owns columns [q*C, (q+1)*C).
+// Cluster of kCluster CTAs per token row; CTA q owns columns [q*C, (q+1)*C),
+// one thread per 4 columns (blockDim = C / 4). The next shrink's A rows of the
+// CTA's columns (contiguous, C * R * 2 bytes) stream into shared memory with
+// cp.async from the start, overlapping the expand and the norm.
 template <int RANK>
-__global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
-                                                                const ResidNormParams p) {
-  extern __shared__ float sm[];  // xs[C] | t[32] | red[...]
+__global__ void __launch_bounds__(1024) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
+                                                                 const ResidNormParams p) {
+  extern __shared__ __align__(16) float sm[];  // a_tile | xs[C] | t[32] | red[blockDim * 8]
   __shared__ float buf[kPartialsMax];
   __shared__ float ss_part;
-  __shared__ float warp_ss[4];
+  __shared__ float warp_ss[32];
+  constexpr int RB = RANK > 0 ? RANK : 8;
   const int q = static_cast<int>(ptx::cluster_rank());
   const int gr = blockIdx.x / kCluster;
+  ptx::prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
   const int s = seg_row(tab.seg, gr);
   const int64_t local = gr - tab.seg.row_start[s];
   const int64_t C = p.hidden / kCluster;
   const int64_t c0 = q * C;
-  float* xs = sm;
-  float* t = sm + C;
+  const int R = p.r_next;
+  const __nv_bfloat16* A = tab.A_next[s];
+  __nv_bfloat16* a_tile = reinterpret_cast<__nv_bfloat16*>(sm);
+  float* xs = sm + (C * R) / 2;
+  float* t = xs + C;
   float* red = t + 32;
+  if (A) {
+    const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(a_tile));
+    const char* src0 = reinterpret_cast<const char*>(A + c0 * R);
+    for (int64_t k = threadIdx.x; k < C * R / 8; k += blockDim.x)
+      ptx::cp_async_16(dst0 + static_cast<uint32_t>(k * 16), src0 + k * 16, 16);
+    ptx::cp_async_commit();
+  }
   const __nv_bfloat16* B = tab.B[s];
-  if (RANK > 0 && B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, RANK);
+  const int64_t n = c0 + threadIdx.x * 4;
   const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
   __nv_bfloat16* h = tab.h[s] + local * p.h_stride;
-  float ss = 0.f;
-  for (int64_t c = threadIdx.x * 4; c < C; c += blockDim.x * 4) {
-    const int64_t n = c0 + c;
-    const uint2 bu = *reinterpret_cast<const uint2*>(base + n);
+  const uint2 bu = *reinterpret_cast<const uint2*>(base + n);
+  uint2 ru = make_uint2(0u, 0u);
+  if (p.has_resid) ru = *reinterpret_cast<const uint2*>(h + n);
+  const uint2 wu = *reinterpret_cast<const uint2*>(p.w + n);
+  uint4 bq[4][RB / 8];
+  if (RANK > 0 && B) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) load_row<RB>(bq[e], B + (n + e) * RANK);
+  }
+  if (RANK > 0 && B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, RANK);
+  float v[4];
+  {
     const __nv_bfloat162* bv = reinterpret_cast<const __nv_bfloat162*>(&bu);
-    float v[4];
     const float2 b01 = __bfloat1622float2(bv[0]), b23 = __bfloat1622float2(bv[1]);
     v[0] = b01.x; v[1] = b01.y; v[2] = b23.x; v[3] = b23.y;
-    if (RANK > 0 && B) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float d = bfr(lora_dot<(RANK > 0 ? RANK : 8)>(t, B + (n + e) * RANK));
-        if (p.post_scale != 0.f) d = bfr(d * p.post_scale);
-        v[e] = bfr(v[e] + d);
-      }
-    }
-    if (p.has_resid) {
-      const uint2 ru = *reinterpret_cast<const uint2*>(h + n);
-      const __nv_bfloat162* rv = reinterpret_cast<const __nv_bfloat162*>(&ru);
-      const float2 r01 = __bfloat1622float2(rv[0]), r23 = __bfloat1622float2(rv[1]);
-      v[0] = bfr(r01.x + v[0]); v[1] = bfr(r01.y + v[1]);
-      v[2] = bfr(r23.x + v[2]); v[3] = bfr(r23.y + v[3]);
-    }
-    __align__(8) __nv_bfloat162 hv[2] = {__floats2bfloat162_rn(v[0], v[1]), __floats2bfloat162_rn(v[2], v[3])};
-    *reinterpret_cast<uint2*>(h + n) = *reinterpret_cast<uint2*>(hv);
+  }
+  if (RANK > 0 && B) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      xs[c + e] = v[e];
-      ss = fmaf(v[e], v[e], ss);
+      float d = bfr(dot_regs<RB>(t, bq[e]));
+      if (p.post_scale != 0.f) d = bfr(d * p.post_scale);
+      v[e] = bfr(v[e] + d);
     }
   }
+  if (p.has_resid) {
+    const __nv_bfloat162* rv = reinterpret_cast<const __nv_bfloat162*>(&ru);
+    const float2 r01 = __bfloat1622float2(rv[0]), r23 = __bfloat1622float2(rv[1]);
+    v[0] = bfr(r01.x + v[0]); v[1] = bfr(r01.y + v[1]);
+    v[2] = bfr(r23.x + v[2]); v[3] = bfr(r23.y + v[3]);
+  }
+  {
+    __align__(8) __nv_bfloat162 hv[2] = {__floats2bfloat162_rn(v[0], v[1]), __floats2bfloat162_rn(v[2], v[3])};
+    *reinterpret_cast<uint2*>(h + n) = *reinterpret_cast<uint2*>(hv);
+  }
+  float ss = v[0] * v[0];
+  ss = fmaf(v[1], v[1], ss);
+  ss = fmaf(v[2], v[2], ss);
+  ss = fmaf(v[3], v[3], ss);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) warp_ss[threadIdx.x >> 5] = ss;
@@ -196,43 +254,39 @@ __global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_con
   float total = 0.f;
   const uint32_t my = static_cast<uint32_t>(__cvta_generic_to_shared(&ss_part));
   for (int r = 0; r < kCluster; ++r) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ptx::map_peer(my, r)) : "memory");
-    total += v;
+    float pv;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(ptx::map_peer(my, r)) : "memory");
+    total += pv;
   }
   const float inv = rsqrtf(total / static_cast<float>(p.hidden) + p.eps);
-  __nv_bfloat16* xo = tab.x_out[s] + local * p.x_stride;
-  for (int64_t c = threadIdx.x * 4; c < C; c += blockDim.x * 4) {
-    const int64_t n = c0 + c;
-    const uint2 wu = *reinterpret_cast<const uint2*>(p.w + n);
+  {
     const __nv_bfloat162* wv = reinterpret_cast<const __nv_bfloat162*>(&wu);
     const float2 w01 = __bfloat1622float2(wv[0]), w23 = __bfloat1622float2(wv[1]);
     const float wf[4] = {w01.x, w01.y, w23.x, w23.y};
     float x[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      x[e] = bfr(wf[e] * bfr(xs[c + e] * inv));
-      xs[c + e] = x[e];
+      x[e] = bfr(wf[e] * bfr(v[e] * inv));
+      xs[threadIdx.x * 4 + e] = x[e];
     }
     __align__(8) __nv_bfloat162 xv[2] = {__floats2bfloat162_rn(x[0], x[1]), __floats2bfloat162_rn(x[2], x[3])};
-    *reinterpret_cast<uint2*>(xo + n) = *reinterpret_cast<uint2*>(xv);
+    *reinterpret_cast<uint2*>(tab.x_out[s] + local * p.x_stride + n) = *reinterpret_cast<uint2*>(xv);
   }
-  __syncthreads();
-  // next round's LoRA shrink over this CTA's columns: ws_next[gr][q][j]
-  const __nv_bfloat16* A = tab.A_next[s];
   if (A) {
-    const int R = p.r_next, G = R / 8;
+    ptx::cp_async_wait_all();
+    __syncthreads();
+    // next round's LoRA shrink over this CTA's columns: ws_next[gr][q][j]
+    const int G = R / 8;
     const int kgroups = blockDim.x / G;
     const int tid = threadIdx.x;
     const bool active = tid < kgroups * G;
     const int cg = tid % G, kg = tid / G;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (active) {
-      int64_t k = kg;
 #pragma unroll 4
-      for (; k < C; k += kgroups) {
+      for (int64_t k = kg; k < C; k += kgroups) {
         float a[8];
-        ld8(A + (c0 + k) * R + cg * 8, a);
+        ld8(a_tile + k * R + cg * 8, a);
         const float xv = xs[k];
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] = fmaf(xv, a[e], acc[e]);
@@ -242,36 +296,58 @@ __global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_con
     for (int e = 0; e < 8; ++e) red[tid * 8 + e] = acc[e];
     __syncthreads();
     for (int j = tid; j < R; j += blockDim.x) {
-      float v = 0.f;
-      for (int g = 0; g < kgroups; ++g) v += red[(g * G + j / 8) * 8 + (j & 7)];
-      p.ws_next[(static_cast<int64_t>(gr) * kCluster + q) * R + j] = v;
+      float sum = 0.f;
+      for (int g = 0; g < kgroups; ++g) sum += red[(g * G + j / 8) * 8 + (j & 7)];
+      p.ws_next[(static_cast<int64_t>(gr) * kCluster + q) * R + j] = sum;
     }
   }
   ptx::cluster_sync();  // peers may still read ss_part
 }
 
 // ---- after the Gate+Up round ----------------------------------------------------------
-// One thread per 4 consecutive columns of the SiLU product; CTA = (row, 1024
+// One thread per 4 consecutive columns of the SiLU product; CTA = (row, 512
 // columns). The Down shrink partial of the CTA's columns goes to
 // ws_next[row][blockIdx.y][j].
 template <int RANK>
-__global__ void __launch_bounds__(256) gu_silu_shrink_kernel(const __grid_constant__ GuSiluTable tab,
+__global__ void __launch_bounds__(128) gu_silu_shrink_kernel(const __grid_constant__ GuSiluTable tab,
                                                              const GuSiluParams p) {
   __shared__ float t[2 * 32];
   __shared__ float buf[kPartialsMax];
-  __shared__ float red[8][32];
+  __shared__ float red[4][32];
   const int gr = blockIdx.x;
+  ptx::prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   const int s = seg_row(tab.seg, gr);
   const int64_t local = gr - tab.seg.row_start[s];
   const __nv_bfloat16* B = tab.B[s];
-  if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 2 * RANK);
+  const __nv_bfloat16* A = tab.A_next[s];
+  const int R = p.r_next;
   const int64_t n0 = (static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x) * 4;
   const bool live = n0 < p.inter;
-  float a[4] = {0.f, 0.f, 0.f, 0.f};
+  // loads that do not depend on the LoRA intermediate go first
+  uint2 gu = make_uint2(0u, 0u), uu = make_uint2(0u, 0u);
+  uint4 bg[4][RANK / 8], bu[4][RANK / 8], an[4][4];
   if (live) {
     const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
-    const uint2 gu = *reinterpret_cast<const uint2*>(base + n0);
-    const uint2 uu = *reinterpret_cast<const uint2*>(base + n0 + p.inter);
+    gu = *reinterpret_cast<const uint2*>(base + n0);
+    uu = *reinterpret_cast<const uint2*>(base + n0 + p.inter);
+    if (B) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        load_row<RANK>(bg[e], B + (n0 + e) * RANK);
+        load_row<RANK>(bu[e], B + (n0 + e + p.inter) * RANK);
+      }
+    }
+    if (A) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (j * 8 < R) an[e][j] = reinterpret_cast<const uint4*>(A + (n0 + e) * R)[j];
+    }
+  }
+  if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 2 * RANK);
+  float a[4] = {0.f, 0.f, 0.f, 0.f};
+  if (live) {
     const __nv_bfloat162* gv = reinterpret_cast<const __nv_bfloat162*>(&gu);
     const __nv_bfloat162* uv = reinterpret_cast<const __nv_bfloat162*>(&uu);
     float g[4], u[4];
@@ -282,8 +358,8 @@ __global__ void __launch_bounds__(256) gu_silu_shrink_kernel(const __grid_consta
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       if (B) {
-        g[e] = bfr(g[e] + bfr(lora_dot<RANK>(t, B + (n0 + e) * RANK)));
-        u[e] = bfr(u[e] + bfr(lora_dot<RANK>(t + RANK, B + (n0 + e + p.inter) * RANK)));
+        g[e] = bfr(g[e] + bfr(dot_regs<RANK>(t, bg[e])));
+        u[e] = bfr(u[e] + bfr(dot_regs<RANK>(t + RANK, bu[e])));
       }
       const float sg = bfr(g[e] / (1.f + expf(-g[e])));
       a[e] = bfr(sg * u[e]);
@@ -291,19 +367,22 @@ __global__ void __launch_bounds__(256) gu_silu_shrink_kernel(const __grid_consta
     __align__(8) __nv_bfloat162 av[2] = {__floats2bfloat162_rn(a[0], a[1]), __floats2bfloat162_rn(a[2], a[3])};
     *reinterpret_cast<uint2*>(tab.act[s] + local * p.act_stride + n0) = *reinterpret_cast<uint2*>(av);
   }
-  const __nv_bfloat16* A = tab.A_next[s];
   if (!A) return;
-  const int R = p.r_next;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int j0 = 0; j0 < R; j0 += 8) {
+#pragma unroll
+  for (int j0 = 0; j0 < 32; j0 += 8) {
+    if (j0 >= R) break;
     float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (live) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        float v[8];
-        ld8(A + (n0 + e) * R + j0, v);
+        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&an[e][j0 / 8]);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) part[q] = fmaf(a[e], v[q], part[q]);
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(hv[q]);
+          part[2 * q] = fmaf(a[e], f.x, part[2 * q]);
+          part[2 * q + 1] = fmaf(a[e], f.y, part[2 * q + 1]);
+        }
       }
     }
 #pragma unroll
@@ -347,10 +426,22 @@ int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p
   if (p.r_next % 8 || p.r_next > 96) return set_error(SWL_ERR_ARG, "resid_norm: next rank layout must be 8..96 in steps of 8");
   if (p.splits_in * r_in > kPartialsMax) return set_error(SWL_ERR_ARG, "resid_norm: too many shrink partials");
   const int64_t C = p.hidden / kCluster;
-  const size_t smem = (C + 32 + 128 * 8) * sizeof(float);
+  const int threads = static_cast<int>(C / 4);
+  if (threads > 1024 || threads % 32) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be a multiple of 1024 and <= 32768");
+  const size_t smem = C * p.r_next * 2 + (C + 32 + static_cast<size_t>(threads) * 8) * sizeof(float);
+  if (smem > 200 * 1024) return set_error(SWL_ERR_ARG, "resid_norm: shared memory too large");
+  cudaError_t ae = cudaSuccess;
+  switch (r_in) {
+    case 0: ae = cudaFuncSetAttribute(resid_norm_shrink_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); break;
+    case 8: ae = cudaFuncSetAttribute(resid_norm_shrink_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); break;
+    case 16: ae = cudaFuncSetAttribute(resid_norm_shrink_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); break;
+    case 32: ae = cudaFuncSetAttribute(resid_norm_shrink_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); break;
+    default: break;
+  }
+  if (ae != cudaSuccess) return set_error(SWL_ERR_CUDA, "resid_norm: %s", cudaGetErrorString(ae));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(tab.seg.total_rows * kCluster), 1, 1);
-  cfg.blockDim = dim3(128, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -375,11 +466,11 @@ int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, 
   if (p.r_next % 8 || p.r_next > 32) return set_error(SWL_ERR_ARG, "gu_silu: next rank must be 8..32 in steps of 8");
   if (p.inter % 4) return set_error(SWL_ERR_ARG, "gu_silu: inter must be a multiple of 4");
   if (p.splits_in * 2 * r > kPartialsMax) return set_error(SWL_ERR_ARG, "gu_silu: too many shrink partials");
-  dim3 grid(tab.seg.total_rows, static_cast<unsigned>((p.inter + 1023) / 1024));
+  dim3 grid(tab.seg.total_rows, static_cast<unsigned>((p.inter + 511) / 512));
   switch (r) {
-    case 8: gu_silu_shrink_kernel<8><<<grid, 256, 0, stream>>>(tab, p); break;
-    case 16: gu_silu_shrink_kernel<16><<<grid, 256, 0, stream>>>(tab, p); break;
-    case 32: gu_silu_shrink_kernel<32><<<grid, 256, 0, stream>>>(tab, p); break;
+    case 8: gu_silu_shrink_kernel<8><<<grid, 128, 0, stream>>>(tab, p); break;
+    case 16: gu_silu_shrink_kernel<16><<<grid, 128, 0, stream>>>(tab, p); break;
+    case 32: gu_silu_shrink_kernel<32><<<grid, 128, 0, stream>>>(tab, p); break;
     default: return set_error(SWL_ERR_ARG, "gu_silu: rank must be 8, 16 or 32");
   }
   SWL_CUDA_TRY(cudaGetLastError());
@@ -387,6 +478,6 @@ int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, 
 }
 
 int resid_norm_splits() { return kCluster; }
-int gu_silu_splits(int64_t inter) { return static_cast<int>((inter + 1023) / 1024); }
+int gu_silu_splits(int64_t inter) { return static_cast<int>((inter + 511) / 512); }
 
 }  // namespace swl

@@ -67,6 +67,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// As mbar_wait, but the thread sleeps `sleep_ns` between polls so a warp that
+// waits for a long time does not take issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                unsigned int* err_word, unsigned int code,
+                                                uint64_t timeout_ns, unsigned int sleep_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 15u) == 0 && globaltimer() - t0 > timeout_ns) {
+      if (err_word) atomicCAS(err_word, 0u, code);
+      return false;
+    }
+  }
+}
+
 // ---- TMA ----------------------------------------------------------------------
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -90,6 +107,28 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+
+// Hint: bring [ptr, ptr + bytes) into L2 (bytes a multiple of 16); no completion.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* ptr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(ptr)),
+               "r"(bytes)
+               : "memory");
+}
+
+// CTA `slice` of `nslices` issues L2 prefetches for its contiguous share of
+// [base, base + bytes) (thread 0 only, 1 MB per instruction).
+__device__ __forceinline__ void prefetch_l2_share(const void* base, int64_t bytes, int slice,
+                                                  int nslices) {
+  if (!base || bytes <= 0 || threadIdx.x != 0) return;
+  const int64_t per = ((bytes + nslices - 1) / nslices + 15) & ~int64_t(15);
+  int64_t b = static_cast<int64_t>(slice) * per;
+  const int64_t e = b + per < bytes ? b + per : bytes;
+  const char* p = static_cast<const char*>(base);
+  for (; b < e; b += (1 << 20)) {
+    const int64_t n = (e - b) < (1 << 20) ? (e - b) : (1 << 20);
+    prefetch_l2_bulk(p + b, static_cast<uint32_t>(n & ~int64_t(15)));
+  }
 }
 
 // ---- cp.async (LDGSTS) ----------------------------------------------------------

@@ -147,7 +147,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (i / STAGES) & 1;
         if (!ptx::mbar_wait(&full[s], ph, err, kErrWaitFull, kWaitTimeoutNs)) break;
         ptx::tc_fence_after();
-        ptx::fence_proxy_async_smem();  // gathered rows were written by cp.async
+        // (no proxy fence: cp.async completion is tracked by the mbarrier, as in
+        // CUTLASS's cp.async-fed UMMA mainloop)
         const uint32_t wa = ptx::smem_addr(w_st + s * kWStageBytes);
         const uint32_t xa = ptx::smem_addr(x_st + s * Cfg::kXStageBytes);
 #pragma unroll
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < nk; ++i) {
       const int s = i % STAGES;
       const uint32_t ph = (i / STAGES) & 1;
-      if (!ptx::mbar_wait(&empty[s], ph ^ 1, err, kErrWaitEmptyX, kWaitTimeoutNs)) break;
+      if (!ptx::mbar_wait_sleep(&empty[s], ph ^ 1, err, kErrWaitEmptyX, kWaitTimeoutNs, 64)) break;
       const int64_t k0 = static_cast<int64_t>(kb_begin + i) * kBlockK;
       const uint32_t xs = ptx::smem_addr(x_st + s * Cfg::kXStageBytes);
       for (int c = t; c < BN * 8; c += kGatherThreads) {
@@ -188,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
 
   // ---- epilogue ------------------------------------------------------------
-  const bool acc_ok = ptx::mbar_wait(accf, 0, err, kErrWaitAcc, kWaitTimeoutNs);
+  const bool acc_ok = ptx::mbar_wait_sleep(accf, 0, err, kErrWaitAcc, kWaitTimeoutNs, 128);
   __syncwarp();
   ptx::tc_fence_after();
   float* P = reinterpret_cast<float*>(smem);  // [BN tokens][128 weight rows] f32
@@ -384,6 +385,10 @@ int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void*
     tmap = &local;
   }
   const int m = tab.total_rows;
+  if (algo == kAlgoStreamK) {
+    if (m > 64) return set_error(SWL_ERR_ARG, "stream-K round: at most 64 token rows");
+    return launch_slot_round_streamk(tab, shape, *tmap, stream);
+  }
   if (m <= 32) return launch_tc<32>(tab, shape, *tmap, splits, stream);
   if (m <= 64) return launch_tc<64>(tab, shape, *tmap, splits, stream);
   if (m <= 128) return launch_tc<128>(tab, shape, *tmap, splits, stream);
@@ -391,10 +396,11 @@ int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void*
 }
 
 int read_and_clear_device_error(unsigned int* code) {
-  unsigned int v = 0, zero = 0;
+  unsigned int v = 0, zero = 0, v2 = 0;
   SWL_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_round_error_word, sizeof(v)));
   if (v) SWL_CUDA_TRY(cudaMemcpyToSymbol(g_round_error_word, &zero, sizeof(zero)));
-  *code = v;
+  SWL_TRY(read_and_clear_sk_error(&v2));
+  *code = v ? v : v2;
   return SWL_OK;
 }
 
@@ -406,7 +412,7 @@ using namespace swl;
 // rows[i] rows of K bf16 from in_ptrs[i] (row stride in_stride elements) and
 // writes rows[i] rows of N bf16 to out_ptrs[i] (row stride out_stride).
 // W is [N, K] row-major bf16 on the current device; bias is [N] or NULL.
-// algo: 0 auto (tensor cores), 1 tensor cores, 2 CUDA cores.
+// algo: 0 auto (= 1), 1 cluster split-K, 2 CUDA cores, 3 stream-K (<= 64 rows).
 // splits: K-split factor (cluster size) for the tensor-core path; <= 0 = auto.
 SWL_EXPORT int swl_slot_gemm(const void* W, int64_t N, int64_t K, const void* bias, int nslots,
                              const void* const* in_ptrs, void* const* out_ptrs, const int* rows,
@@ -436,8 +442,8 @@ SWL_EXPORT int swl_slot_gemm(const void* W, int64_t N, int64_t K, const void* bi
   }
   if ((shape.in_stride % 8) || (shape.out_stride % 4))
     return set_error(SWL_ERR_ARG, "swl_slot_gemm: row strides must keep rows aligned");
-  return launch_slot_round(tab, shape, W, nullptr, algo == kAlgoSimt ? kAlgoSimt : kAlgoTensorCore,
-                           splits, static_cast<cudaStream_t>(stream));
+  if (algo < 0 || algo > 3) return set_error(SWL_ERR_ARG, "swl_slot_gemm: unknown algo %d", algo);
+  return launch_slot_round(tab, shape, W, nullptr, algo, splits, static_cast<cudaStream_t>(stream));
 }
 
 // Reads (and clears) the device error word set by bounded waits in the round
@@ -446,3 +452,10 @@ SWL_EXPORT int swl_round_device_error(unsigned int* code) {
   if (!code) return set_error(SWL_ERR_ARG, "null code pointer");
   return read_and_clear_device_error(code);
 }
+
+// Tuning: persistent CTAs per SM of the stream-K round (1: 9-stage pipeline,
+// 2: two 5-stage pipelines per SM).
+SWL_EXPORT int swl_round_set_streamk_ctas_per_sm(int n) { return set_streamk_ctas_per_sm(n); }
+
+// Tuning: fixed number of stream-K CTAs (0 = SM count x CTAs per SM).
+SWL_EXPORT int swl_round_set_streamk_ctas(int n) { return set_streamk_ctas(n); }

@@ -37,9 +37,10 @@ struct RoundShape {
 };
 
 enum RoundAlgo : int {
-  kAlgoAuto = 0,
-  kAlgoTensorCore = 1,  // tcgen05 + TMA weight stream (the product path)
+  kAlgoAuto = 0,        // cluster split-K (measured faster than stream-K on B200)
+  kAlgoTensorCore = 1,  // tcgen05 + TMA, K split across a thread-block cluster (DSMEM reduce)
   kAlgoSimt = 2,        // plain CUDA-core kernel, used as an on-device cross-check
+  kAlgoStreamK = 3,     // tcgen05 + TMA, persistent stream-K (<= 64 rows)
 };
 
 // Encodes the TMA descriptor for a row-major [N, K] bf16 weight (box 64 x 128,
@@ -53,5 +54,16 @@ int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void*
 
 // Device error word written by bounded waits inside round kernels (0 = ok).
 int read_and_clear_device_error(unsigned int* code);
+
+// Stream-K rounds (slot_round_sk.cu). The workspace (fp32 partial tiles and
+// per-tile arrival counters) is allocated once per device; allocate it
+// before capturing a launch into a CUDA graph.
+int ensure_streamk_workspace();
+int reset_streamk_counters();
+int launch_slot_round_streamk(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& map,
+                              cudaStream_t stream);
+int read_and_clear_sk_error(unsigned int* code);
+int set_streamk_ctas_per_sm(int n);
+int set_streamk_ctas(int n);
 
 }  // namespace swl

@@ -157,7 +157,8 @@ SWL_EXPORT int swl_paged_attention_shrink(int nseg, const int* rows, const void*
                                           const void* const* seqlens, void* const* out,
                                           int64_t out_stride, int hq, int hkv, int head_dim, int page,
                                           float scale, int max_len, const void* q_rot, float* part,
-                                          const void* const* A_o, int r, float* ws_o, void* stream) {
+                                          const void* const* A_o, int r, float* ws_o,
+                                          const void* pf, int64_t pf_bytes, void* stream) {
   AttnTable t;
   SWL_TRY(fill_attn(&t, nseg, rows, nullptr, block_tables, const_cast<void* const*>(k_cache),
                     const_cast<void* const*>(v_cache), seqlens, out));
@@ -168,6 +169,8 @@ SWL_EXPORT int swl_paged_attention_shrink(int nseg, const int* rows, const void*
   p.max_len = max_len;
   p.q_rot = cast<__nv_bfloat16>(q_rot);
   p.part = part;
+  p.pf = pf;
+  p.pf_bytes = pf_bytes;
   ShrinkSide sh;
   for (int i = 0; i < kMaxSlots; ++i) sh.A[i] = (A_o && i < nseg) ? cast<const __nv_bfloat16>(A_o[i]) : nullptr;
   sh.r = r;
@@ -186,7 +189,7 @@ SWL_EXPORT int swl_fused_qkv_rope(int nseg, const int* rows, const void* const* 
                                   const void* const* block_tables, void* const* k_cache,
                                   void* const* v_cache, const void* const* seqlens, int hq,
                                   int hkv, int head_dim, int page, const void* cos_sin,
-                                  void* q_rot, void* stream) {
+                                  void* q_rot, const void* pf, int64_t pf_bytes, void* stream) {
   QkvRopeTable t;
   SWL_TRY(fill_segments(&t.seg, nseg, rows));
   for (int i = 0; i < nseg; ++i) {
@@ -204,6 +207,8 @@ SWL_EXPORT int swl_fused_qkv_rope(int nseg, const int* rows, const void* const* 
   p.splits_in = splits_in;
   p.cos_sin = cast<const __nv_bfloat16>(cos_sin);
   p.q_rot = cast<__nv_bfloat16>(q_rot);
+  p.pf = pf;
+  p.pf_bytes = pf_bytes;
   return launch_qkv_rope(t, p, r, static_cast<cudaStream_t>(stream));
 }
 
@@ -218,7 +223,7 @@ SWL_EXPORT int swl_fused_resid_norm_shrink(int nseg, const int* rows, const void
                                            const void* w, int64_t hidden, float eps,
                                            void* const* x_out, int64_t x_stride,
                                            const void* const* A_next, int r_next, float* ws_next,
-                                           void* stream) {
+                                           const void* pf, int64_t pf_bytes, void* stream) {
   ResidNormTable t;
   SWL_TRY(fill_segments(&t.seg, nseg, rows));
   for (int i = 0; i < nseg; ++i) {
@@ -241,19 +246,21 @@ SWL_EXPORT int swl_fused_resid_norm_shrink(int nseg, const int* rows, const void
   p.x_stride = x_stride;
   p.r_next = A_next ? r_next : 0;
   p.ws_next = ws_next;
+  p.pf = pf;
+  p.pf_bytes = pf_bytes;
   return launch_resid_norm_shrink(t, p, B ? r_in : 0, static_cast<cudaStream_t>(stream));
 }
 
 // Fused epilogue of the Gate+Up round: gate/up = round output + LoRA delta
 // (partials ws_in [rows][splits_in][2r], lora_B rows B[i] [2*inter, r]),
 // act = SiLU(gate) * up written to act[i] (the Down round's slot input), and
-// the Down LoRA shrink partials ws_next[rows][ceil(inter/1024)][r_next].
+// the Down LoRA shrink partials ws_next[rows][ceil(inter/512)][r_next].
 SWL_EXPORT int swl_fused_gu_silu_shrink(int nseg, const int* rows, const void* const* base,
                                         int64_t base_stride, const void* const* B, int r,
                                         const float* ws_in, int splits_in, int64_t inter,
                                         void* const* act, int64_t act_stride,
                                         const void* const* A_next, int r_next, float* ws_next,
-                                        void* stream) {
+                                        const void* pf, int64_t pf_bytes, void* stream) {
   GuSiluTable t;
   SWL_TRY(fill_segments(&t.seg, nseg, rows));
   for (int i = 0; i < nseg; ++i) {
@@ -270,6 +277,8 @@ SWL_EXPORT int swl_fused_gu_silu_shrink(int nseg, const int* rows, const void* c
   p.splits_in = splits_in;
   p.r_next = r_next;
   p.ws_next = ws_next;
+  p.pf = pf;
+  p.pf_bytes = pf_bytes;
   return launch_gu_silu_shrink(t, p, r, static_cast<cudaStream_t>(stream));
 }
 

@@ -21,6 +21,7 @@
 #include <algorithm>
 
 #include "common.h"
+#include "ptx.cuh"
 #include "worker_ops.h"
 
 namespace swl {
@@ -282,6 +283,8 @@ __global__ void __launch_bounds__(32) paged_attention_kernel(const __grid_consta
   __shared__ __align__(128) uint8_t kv_sm[kAttnStages][2][kTileBytes];
   __shared__ int pages[kMaxSplitPages];
   const int gr = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  ptx::prefetch_l2_share(p.pf, p.pf_bytes,
+                         (split * gridDim.y + kvh) * gridDim.x + gr, gridDim.x * gridDim.y * gridDim.z);
   const int lane = threadIdx.x;
   const int G = p.hq / p.hkv;
   const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates

@@ -71,6 +71,8 @@ struct AttnParams {
   int max_len;                   // upper bound of any slot's context after this step
   __nv_bfloat16* q_rot;          // [total_rows, Hq * D] scratch for rotated q
   float* part;                   // per-split records, attention_part_floats() floats
+  const void* pf;                // next round's weight to prefetch into L2 (or nullptr)
+  int64_t pf_bytes;
 };
 
 // Context splits the attention launch will use, and the fp32 partial-record
@@ -128,6 +130,8 @@ struct QkvRopeParams {
   int splits_in;
   const __nv_bfloat16* cos_sin;
   __nv_bfloat16* q_rot;  // [total_rows, hq * D]
+  const void* pf;        // next round's weight to prefetch into L2 (or nullptr)
+  int64_t pf_bytes;
 };
 
 struct ResidNormTable {
@@ -149,6 +153,8 @@ struct ResidNormParams {
   int64_t base_stride, h_stride, x_stride;
   int r_next;
   float* ws_next;         // [total_rows][8][r_next]
+  const void* pf;         // next round's weight to prefetch into L2 (or nullptr)
+  int64_t pf_bytes;
 };
 
 struct GuSiluTable {
@@ -164,7 +170,9 @@ struct GuSiluParams {
   const float* ws_in;  // Gate+Up shrink partials [total_rows][splits_in][2 r]
   int splits_in;
   int r_next;
-  float* ws_next;      // [total_rows][ceil(inter / 1024)][r_next]
+  float* ws_next;      // [total_rows][ceil(inter / 512)][r_next]
+  const void* pf;      // next round's weight to prefetch into L2 (or nullptr)
+  int64_t pf_bytes;
 };
 
 int launch_qkv_rope(const QkvRopeTable& tab, const QkvRopeParams& p, int r, cudaStream_t stream);

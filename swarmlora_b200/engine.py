@@ -142,9 +142,12 @@ class SlotGroup:
 
     def __init__(self, cfg: ModelConfig, base: BaseWeights, adapters: list, ctx_lens: list,
                  max_new: int, device: int = 0, seed: int = 0, kv_std: float = 1.0,
-                 round_algo: int = 1, worker_id0: int = 1000, fused: bool = True):
+                 round_algo: int = 0, worker_id0: int = 1000, fused: bool = True,
+                 prefetch=(), prefetch_cap: int = 80 << 20):
         self.cfg = cfg
         self.fused = fused
+        self.prefetch = tuple(prefetch or ())
+        self.pf_cap = int(prefetch_cap)
         self.dev = torch.device("cuda", device)
         self.n = n = len(ctx_lens)
         self.base = base
@@ -229,6 +232,20 @@ class SlotGroup:
         self.A_o, self.B_o = per_layer("A_o"), per_layer("B_o")
         self.A_gu, self.B_gu = per_layer("A_gu"), per_layer("B_gu")
         self.A_dn, self.B_dn = per_layer("A_down"), per_layer("B_down")
+        # next-round weights for the L2 prefetch issued by the worker kernels
+        self.wptr = {}
+        names = {agg.OP_QKV_FUSED: "qkv", agg.OP_O_PROJ: "o", agg.OP_GATE_UP_FUSED: "gate_up",
+                 agg.OP_DOWN_PROJ: "down"}
+        for l in range(cfg.layers):
+            for op, nm in names.items():
+                if nm not in self.prefetch:
+                    continue
+                W, N_, K_ = C.c_void_p(), C.c_int64(), C.c_int64()
+                check(lib().swl_agg_weight(l, op, C.byref(W), C.byref(N_), C.byref(K_)))
+                self.wptr[(l, op)] = (W.value, min(2 * N_.value * K_.value, self.pf_cap))
+        if "lm_head" in self.prefetch:
+            self.wptr["lm_head"] = (self.base.lm_head.data_ptr(),
+                                    min(self.base.lm_head.numel() * 2, self.pf_cap))
         self.ends_qkv = i64_array([cfg.hq * D, (cfg.hq + cfg.hkv) * D, cfg.qkv_n])
         self.ends_gu = i64_array([I, 2 * I, 2 * I])
         self.ends_h = i64_array([H, H, H])
@@ -254,35 +271,43 @@ class SlotGroup:
         check(L.swl_copy_rows(n, self.a_tok, self.a_in, self.a_b8, st))
         self._round(agg.OP_EMBED, 0, st)
         # embedding -> h, RMSNorm -> QKV slot input, QKV shrink
+        pf = self.wptr
+        none = (None, 0)
         check(L.swl_fused_resid_norm_shrink(n, rows, self.a_out, H, None, 0, 0.0, None, 0, 0, self.a_h, H,
                                             self.base.in_norm[0].data_ptr(), H, cfg.eps, self.a_in, H,
-                                            self.A_qkv[0], 3 * r, self.ws_qkv.data_ptr(), st))
+                                            self.A_qkv[0], 3 * r, self.ws_qkv.data_ptr(),
+                                            *pf.get((0, agg.OP_QKV_FUSED), none), st))
         for l in range(nl):
             self._round(agg.OP_QKV_FUSED, l, st)
             check(L.swl_fused_qkv_rope(n, rows, self.a_out, cfg.qkv_n, self.B_qkv[l], r,
                                        self.ws_qkv.data_ptr(), self.norm_splits, self.a_bt, self.a_kc[l],
                                        self.a_vc[l], self.a_sl, cfg.hq, cfg.hkv, D, cfg.page,
-                                       self.cos_sin.data_ptr(), self.q_rot.data_ptr(), st))
+                                       self.cos_sin.data_ptr(), self.q_rot.data_ptr(),
+                                       *pf.get((l, agg.OP_O_PROJ), none), st))
             check(L.swl_paged_attention_shrink(n, rows, self.a_bt, self.a_kc[l], self.a_vc[l], self.a_sl,
                                                self.a_in, cfg.hq * D, cfg.hq, cfg.hkv, D, cfg.page,
                                                1.0 / math.sqrt(D), self.max_len, self.q_rot.data_ptr(),
-                                               self.part.data_ptr(), self.A_o[l], r, self.ws_o.data_ptr(), st))
+                                               self.part.data_ptr(), self.A_o[l], r, self.ws_o.data_ptr(),
+                                               None, 0, st))
             self._round(agg.OP_O_PROJ, l, st)
             check(L.swl_fused_resid_norm_shrink(n, rows, self.a_out, H, self.B_o[l], r, s, self.ws_o.data_ptr(),
                                                 cfg.hq, 1, self.a_h, H, self.base.post_norm[l].data_ptr(), H,
                                                 cfg.eps, self.a_in, H, self.A_gu[l], 2 * r,
-                                                self.ws_gu.data_ptr(), st))
+                                                self.ws_gu.data_ptr(), *pf.get((l, agg.OP_GATE_UP_FUSED), none),
+                                                st))
             self._round(agg.OP_GATE_UP_FUSED, l, st)
             check(L.swl_fused_gu_silu_shrink(n, rows, self.a_out, 2 * I, self.B_gu[l], r, self.ws_gu.data_ptr(),
                                              self.norm_splits, I, self.a_in, I, self.A_dn[l], r,
-                                             self.ws_dn.data_ptr(), st))
+                                             self.ws_dn.data_ptr(), *pf.get((l, agg.OP_DOWN_PROJ), none), st))
             self._round(agg.OP_DOWN_PROJ, l, st)
             last = l == nl - 1
             w_next = self.base.final_norm if last else self.base.in_norm[l + 1]
             check(L.swl_fused_resid_norm_shrink(n, rows, self.a_out, H, self.B_dn[l], r, s, self.ws_dn.data_ptr(),
                                                 self.dn_splits, 1, self.a_h, H, w_next.data_ptr(), H, cfg.eps,
                                                 self.a_in, H, None if last else self.A_qkv[l + 1], 3 * r,
-                                                self.ws_qkv.data_ptr(), st))
+                                                self.ws_qkv.data_ptr(),
+                                                *pf.get("lm_head" if last else (l + 1, agg.OP_QKV_FUSED), none),
+                                                st))
         self._round(agg.OP_LM_HEAD, 0, st)
         check(L.swl_copy_rows(n, self.a_out, self.a_tok, self.a_b8, st))
         check(L.swl_advance_i32(self.seqlens.data_ptr(), n, 1, st))

@@ -12,7 +12,7 @@ import torch
 
 from ._native import check, i32_array, lib, ptr_array
 
-ALGO_AUTO, ALGO_TENSOR_CORE, ALGO_SIMT = 0, 1, 2
+ALGO_AUTO, ALGO_TENSOR_CORE, ALGO_SIMT, ALGO_STREAM_K = 0, 1, 2, 3
 
 
 def slot_gemm(W: torch.Tensor, inputs: list[torch.Tensor], outputs: list[torch.Tensor],

@@ -54,7 +54,7 @@ def _check(W, xs, b, outs, what):
 
 
 @pytest.mark.parametrize("name", list(SHAPES))
-@pytest.mark.parametrize("algo", [1, 2])
+@pytest.mark.parametrize("algo", [1, 2, 3])
 def test_decode_round_28_slots(native, cuda, name, algo):
     N, K = SHAPES[name]
     W, xs, b = _case(N, K, [1] * 28, seed=100 + len(name))
@@ -69,6 +69,19 @@ def test_ragged_rows(native, cuda, rows):
     W, xs, b = _case(N, K, rows, seed=sum(rows))
     outs = _run(W, xs, b, algo=1, pad_rows=max(16, max(rows)))
     _check(W, xs, b, outs, f"rows={rows}")
+
+
+@pytest.mark.parametrize("rows", [[1], [3, 0, 16, 1, 7], [1] * 64, [16, 16, 16, 15]])
+def test_stream_k_ragged_and_repeatable(native, cuda, rows):
+    """Stream-K rounds (<= 64 rows): ragged slots, and bit-identical results over
+    repeated launches (the per-tile arrival counters reset themselves)."""
+    for (N, K) in [(4096, 14336), (28672, 4096), (128256 // 4, 4096)]:
+        W, xs, b = _case(N, K, rows, seed=N + sum(rows))
+        outs = _run(W, xs, b, algo=3, pad_rows=max(16, max(rows)))
+        _check(W, xs, b, outs, f"stream-K N={N} K={K} rows={rows}")
+        again = _run(W, xs, b, algo=3, pad_rows=max(16, max(rows)))
+        for o, a in zip(outs, again):
+            assert torch.equal(o, a), "stream-K round is not deterministic"
 
 
 @pytest.mark.parametrize("splits", [1, 2, 3, 5, 8])
