@@ -107,42 +107,78 @@ __device__ __forceinline__ void load_row(uint4 (&b)[RANK / 8], const __nv_bfloat
   for (int j = 0; j < RANK / 8; ++j) b[j] = reinterpret_cast<const uint4*>(row)[j];
 }
 
+// Issues one bulk copy per non-null (dst, src, bytes) triple on a fresh
+// mbarrier (thread 0), so the CTA's big contiguous operand reads run on the
+// TMA engine instead of the load/store unit. Returns whether anything was issued.
+__device__ __forceinline__ bool stage_bulk(uint64_t* bar, void* d0, const void* s0, uint32_t b0,
+                                           void* d1, const void* s1, uint32_t b1, void* d2,
+                                           const void* s2, uint32_t b2) {
+  const uint32_t total = (s0 ? b0 : 0u) + (s1 ? b1 : 0u) + (s2 ? b2 : 0u);
+  if (total == 0) return false;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(bar, 1);
+    ptx::fence_mbar_init();
+    ptx::mbar_arrive_expect_tx(bar, total);
+    if (s0) ptx::bulk_load(d0, s0, b0, bar);
+    if (s1) ptx::bulk_load(d1, s1, b1, bar);
+    if (s2) ptx::bulk_load(d2, s2, b2, bar);
+  }
+  return true;
+}
+
+__device__ __forceinline__ float smem_dot(const float* t, const __nv_bfloat16* row, int rank) {
+  float d = 0.f;
+  for (int j = 0; j < rank; j += 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + j);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      d = fmaf(t[j + 2 * e], f.x, d);
+      d = fmaf(t[j + 2 * e + 1], f.y, d);
+    }
+  }
+  return d;
+}
+
 // ---- after the QKV round -------------------------------------------------------------
+// CTA = (row, 4 heads = 512 columns); thread = (head, d < 64) pair of columns.
 template <int RANK>
 __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ QkvRopeTable tab,
                                                        const QkvRopeParams p) {
+  __shared__ __align__(128) __nv_bfloat16 bs[512 * RANK];
   __shared__ float t[3 * 32];
   __shared__ float buf[kPartialsMax];
+  __shared__ __align__(8) uint64_t bar;
   const int gr = blockIdx.x;
   ptx::prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   const int s = seg_row(tab.seg, gr);
   const int64_t local = gr - tab.seg.row_start[s];
   const __nv_bfloat16* B = tab.B[s];
-  const int pi = blockIdx.y * blockDim.x + threadIdx.x;
-  const int heads = p.hq + 2 * p.hkv;
   const int half = p.head_dim / 2;
+  const int heads = p.hq + 2 * p.hkv;
+  const int64_t col0 = static_cast<int64_t>(blockIdx.y) * 4 * p.head_dim;
+  const int64_t ncols = min(static_cast<int64_t>(4 * p.head_dim), static_cast<int64_t>(heads) * p.head_dim - col0);
+  const bool staged = B && stage_bulk(&bar, bs, B + col0 * RANK, static_cast<uint32_t>(ncols * RANK * 2),
+                                      nullptr, nullptr, 0, nullptr, nullptr, 0);
+  const int pi = blockIdx.y * blockDim.x + threadIdx.x;
   const bool live = pi < heads * half;
   const int head = live ? pi / half : 0, d = pi % half;
   const int blk = head < p.hq ? 0 : (head < p.hq + p.hkv ? 1 : 2);
   const int64_t n1 = static_cast<int64_t>(head) * p.head_dim + d, n2 = n1 + half;
-  // loads that do not depend on the LoRA intermediate go first
   const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
   float x1 = 0.f, x2 = 0.f;
-  uint4 b1[RANK / 8], b2[RANK / 8];
   if (live) {
     x1 = __bfloat162float(base[n1]);
     x2 = __bfloat162float(base[n2]);
-    if (B) {
-      load_row<RANK>(b1, B + n1 * RANK);
-      load_row<RANK>(b2, B + n2 * RANK);
-    }
   }
   const int pos = *tab.seqlen[s] + static_cast<int>(local);
   if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 3 * RANK);
+  if (staged) ptx::mbar_wait(&bar, 0, nullptr, 0, 2000000000ull);
   if (!live) return;
   if (B) {
-    x1 = bfr(x1 + bfr(dot_regs<RANK>(t + blk * RANK, b1)));
-    x2 = bfr(x2 + bfr(dot_regs<RANK>(t + blk * RANK, b2)));
+    x1 = bfr(x1 + bfr(smem_dot(t + blk * RANK, bs + (n1 - col0) * RANK, RANK)));
+    x2 = bfr(x2 + bfr(smem_dot(t + blk * RANK, bs + (n2 - col0) * RANK, RANK)));
   }
   if (blk == 2) {
     const int page = tab.block_table[s][pos / p.page];
@@ -168,17 +204,20 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
 
 // ---- after the O / Down round (and the embedding) ------------------------------------
 // Cluster of kCluster CTAs per token row; CTA q owns columns [q*C, (q+1)*C),
-// one thread per 4 columns (blockDim = C / 4). The next shrink's A rows of the
-// CTA's columns (contiguous, C * R * 2 bytes) stream into shared memory with
-// cp.async from the start, overlapping the expand and the norm.
+// thread t the columns c0 + t + k*blockDim (k < C / blockDim). The finished
+// round's lora_B rows and the next shrink's A rows of those columns are
+// staged in shared memory by two bulk copies.
 template <int RANK>
-__global__ void __launch_bounds__(1024) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
-                                                                 const ResidNormParams p) {
-  extern __shared__ __align__(16) float sm[];  // a_tile | xs[C] | t[32] | red[blockDim * 8]
+__global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
+                                                                const ResidNormParams p) {
+  extern __shared__ __align__(128) uint8_t dsm[];  // a_tile [C][R] | b_tile [C][RANK] | xs[C] | red
+  __shared__ float t[32];
   __shared__ float buf[kPartialsMax];
   __shared__ float ss_part;
-  __shared__ float warp_ss[32];
+  __shared__ float warp_ss[4];
+  __shared__ __align__(8) uint64_t bar;
   constexpr int RB = RANK > 0 ? RANK : 8;
+  constexpr int kCols = 4;  // columns per thread (C = 4 * blockDim)
   const int q = static_cast<int>(ptx::cluster_rank());
   const int gr = blockIdx.x / kCluster;
   ptx::prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
@@ -188,59 +227,40 @@ __global__ void __launch_bounds__(1024) resid_norm_shrink_kernel(const __grid_co
   const int64_t c0 = q * C;
   const int R = p.r_next;
   const __nv_bfloat16* A = tab.A_next[s];
-  __nv_bfloat16* a_tile = reinterpret_cast<__nv_bfloat16*>(sm);
-  float* xs = sm + (C * R) / 2;
-  float* t = xs + C;
-  float* red = t + 32;
-  if (A) {
-    const uint32_t dst0 = static_cast<uint32_t>(__cvta_generic_to_shared(a_tile));
-    const char* src0 = reinterpret_cast<const char*>(A + c0 * R);
-    for (int64_t k = threadIdx.x; k < C * R / 8; k += blockDim.x)
-      ptx::cp_async_16(dst0 + static_cast<uint32_t>(k * 16), src0 + k * 16, 16);
-    ptx::cp_async_commit();
-  }
-  const __nv_bfloat16* B = tab.B[s];
-  const int64_t n = c0 + threadIdx.x * 4;
+  const __nv_bfloat16* B = RANK > 0 ? tab.B[s] : nullptr;
+  __nv_bfloat16* a_tile = reinterpret_cast<__nv_bfloat16*>(dsm);
+  __nv_bfloat16* b_tile = a_tile + C * R;
+  float* xs = reinterpret_cast<float*>(b_tile + C * RB);
+  float* red = xs + C;
+  const bool staged = stage_bulk(&bar, a_tile, A ? A + c0 * R : nullptr, static_cast<uint32_t>(C * R * 2),
+                                 b_tile, B ? B + c0 * RANK : nullptr, static_cast<uint32_t>(C * RB * 2),
+                                 nullptr, nullptr, 0);
   const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
   __nv_bfloat16* h = tab.h[s] + local * p.h_stride;
-  const uint2 bu = *reinterpret_cast<const uint2*>(base + n);
-  uint2 ru = make_uint2(0u, 0u);
-  if (p.has_resid) ru = *reinterpret_cast<const uint2*>(h + n);
-  const uint2 wu = *reinterpret_cast<const uint2*>(p.w + n);
-  uint4 bq[4][RB / 8];
-  if (RANK > 0 && B) {
+  float v[kCols], rv[kCols], wv[kCols];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) load_row<RB>(bq[e], B + (n + e) * RANK);
+  for (int k = 0; k < kCols; ++k) {
+    const int64_t n = c0 + threadIdx.x + k * blockDim.x;
+    v[k] = __bfloat162float(base[n]);
+    rv[k] = p.has_resid ? __bfloat162float(h[n]) : 0.f;
+    wv[k] = __bfloat162float(p.w[n]);
   }
-  if (RANK > 0 && B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, RANK);
-  float v[4];
-  {
-    const __nv_bfloat162* bv = reinterpret_cast<const __nv_bfloat162*>(&bu);
-    const float2 b01 = __bfloat1622float2(bv[0]), b23 = __bfloat1622float2(bv[1]);
-    v[0] = b01.x; v[1] = b01.y; v[2] = b23.x; v[3] = b23.y;
-  }
-  if (RANK > 0 && B) {
+  if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, RANK);
+  else __syncthreads();  // barrier init visible before anyone waits on it
+  if (staged) ptx::mbar_wait(&bar, 0, nullptr, 0, 2000000000ull);
+  float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float d = bfr(dot_regs<RB>(t, bq[e]));
+  for (int k = 0; k < kCols; ++k) {
+    const int64_t c = threadIdx.x + k * blockDim.x;
+    if (B) {
+      float d = bfr(smem_dot(t, b_tile + c * RANK, RANK));
       if (p.post_scale != 0.f) d = bfr(d * p.post_scale);
-      v[e] = bfr(v[e] + d);
+      v[k] = bfr(v[k] + d);
     }
+    if (p.has_resid) v[k] = bfr(rv[k] + v[k]);
+    h[c0 + c] = __float2bfloat16_rn(v[k]);
+    ss = fmaf(v[k], v[k], ss);
   }
-  if (p.has_resid) {
-    const __nv_bfloat162* rv = reinterpret_cast<const __nv_bfloat162*>(&ru);
-    const float2 r01 = __bfloat1622float2(rv[0]), r23 = __bfloat1622float2(rv[1]);
-    v[0] = bfr(r01.x + v[0]); v[1] = bfr(r01.y + v[1]);
-    v[2] = bfr(r23.x + v[2]); v[3] = bfr(r23.y + v[3]);
-  }
-  {
-    __align__(8) __nv_bfloat162 hv[2] = {__floats2bfloat162_rn(v[0], v[1]), __floats2bfloat162_rn(v[2], v[3])};
-    *reinterpret_cast<uint2*>(h + n) = *reinterpret_cast<uint2*>(hv);
-  }
-  float ss = v[0] * v[0];
-  ss = fmaf(v[1], v[1], ss);
-  ss = fmaf(v[2], v[2], ss);
-  ss = fmaf(v[3], v[3], ss);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) warp_ss[threadIdx.x >> 5] = ss;
@@ -259,21 +279,15 @@ __global__ void __launch_bounds__(1024) resid_norm_shrink_kernel(const __grid_co
     total += pv;
   }
   const float inv = rsqrtf(total / static_cast<float>(p.hidden) + p.eps);
-  {
-    const __nv_bfloat162* wv = reinterpret_cast<const __nv_bfloat162*>(&wu);
-    const float2 w01 = __bfloat1622float2(wv[0]), w23 = __bfloat1622float2(wv[1]);
-    const float wf[4] = {w01.x, w01.y, w23.x, w23.y};
-    float x[4];
+  __nv_bfloat16* xo = tab.x_out[s] + local * p.x_stride;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      x[e] = bfr(wf[e] * bfr(v[e] * inv));
-      xs[threadIdx.x * 4 + e] = x[e];
-    }
-    __align__(8) __nv_bfloat162 xv[2] = {__floats2bfloat162_rn(x[0], x[1]), __floats2bfloat162_rn(x[2], x[3])};
-    *reinterpret_cast<uint2*>(tab.x_out[s] + local * p.x_stride + n) = *reinterpret_cast<uint2*>(xv);
+  for (int k = 0; k < kCols; ++k) {
+    const int64_t c = threadIdx.x + k * blockDim.x;
+    const float x = bfr(wv[k] * bfr(v[k] * inv));
+    xs[c] = x;
+    xo[c0 + c] = __float2bfloat16_rn(x);
   }
   if (A) {
-    ptx::cp_async_wait_all();
     __syncthreads();
     // next round's LoRA shrink over this CTA's columns: ws_next[gr][q][j]
     const int G = R / 8;
@@ -305,15 +319,19 @@ __global__ void __launch_bounds__(1024) resid_norm_shrink_kernel(const __grid_co
 }
 
 // ---- after the Gate+Up round ----------------------------------------------------------
-// One thread per 4 consecutive columns of the SiLU product; CTA = (row, 512
-// columns). The Down shrink partial of the CTA's columns goes to
-// ws_next[row][blockIdx.y][j].
+// CTA = (row, 512 columns of the SiLU product), thread t the columns
+// t + 128k. The gate and up lora_B rows and the Down shrink's A rows of those
+// columns arrive by three bulk copies; the Down shrink partial of the CTA goes
+// to ws_next[row][blockIdx.y][j].
 template <int RANK>
 __global__ void __launch_bounds__(128) gu_silu_shrink_kernel(const __grid_constant__ GuSiluTable tab,
                                                              const GuSiluParams p) {
+  extern __shared__ __align__(128) uint8_t dsm[];  // bg [512][RANK] | bu [512][RANK] | an [512][R]
   __shared__ float t[2 * 32];
   __shared__ float buf[kPartialsMax];
   __shared__ float red[4][32];
+  __shared__ __align__(8) uint64_t bar;
+  constexpr int kColsCta = 512, kCols = 4;
   const int gr = blockIdx.x;
   ptx::prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   const int s = seg_row(tab.seg, gr);
@@ -321,51 +339,38 @@ __global__ void __launch_bounds__(128) gu_silu_shrink_kernel(const __grid_consta
   const __nv_bfloat16* B = tab.B[s];
   const __nv_bfloat16* A = tab.A_next[s];
   const int R = p.r_next;
-  const int64_t n0 = (static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x) * 4;
-  const bool live = n0 < p.inter;
-  // loads that do not depend on the LoRA intermediate go first
-  uint2 gu = make_uint2(0u, 0u), uu = make_uint2(0u, 0u);
-  uint4 bg[4][RANK / 8], bu[4][RANK / 8], an[4][4];
-  if (live) {
-    const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
-    gu = *reinterpret_cast<const uint2*>(base + n0);
-    uu = *reinterpret_cast<const uint2*>(base + n0 + p.inter);
-    if (B) {
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kColsCta;
+  const int64_t nc = min(static_cast<int64_t>(kColsCta), p.inter - n0);
+  __nv_bfloat16* bg = reinterpret_cast<__nv_bfloat16*>(dsm);
+  __nv_bfloat16* bu = bg + kColsCta * RANK;
+  __nv_bfloat16* an = bu + kColsCta * RANK;
+  const bool staged = stage_bulk(&bar, bg, B ? B + n0 * RANK : nullptr, static_cast<uint32_t>(nc * RANK * 2),
+                                 bu, B ? B + (n0 + p.inter) * RANK : nullptr, static_cast<uint32_t>(nc * RANK * 2),
+                                 an, A ? A + n0 * R : nullptr, static_cast<uint32_t>(nc * R * 2));
+  const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
+  float g[kCols], u[kCols];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        load_row<RANK>(bg[e], B + (n0 + e) * RANK);
-        load_row<RANK>(bu[e], B + (n0 + e + p.inter) * RANK);
-      }
-    }
-    if (A) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (j * 8 < R) an[e][j] = reinterpret_cast<const uint4*>(A + (n0 + e) * R)[j];
-    }
+  for (int k = 0; k < kCols; ++k) {
+    const int64_t c = threadIdx.x + k * blockDim.x;
+    g[k] = c < nc ? __bfloat162float(base[n0 + c]) : 0.f;
+    u[k] = c < nc ? __bfloat162float(base[n0 + c + p.inter]) : 0.f;
   }
   if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 2 * RANK);
-  float a[4] = {0.f, 0.f, 0.f, 0.f};
-  if (live) {
-    const __nv_bfloat162* gv = reinterpret_cast<const __nv_bfloat162*>(&gu);
-    const __nv_bfloat162* uv = reinterpret_cast<const __nv_bfloat162*>(&uu);
-    float g[4], u[4];
-    const float2 g01 = __bfloat1622float2(gv[0]), g23 = __bfloat1622float2(gv[1]);
-    const float2 u01 = __bfloat1622float2(uv[0]), u23 = __bfloat1622float2(uv[1]);
-    g[0] = g01.x; g[1] = g01.y; g[2] = g23.x; g[3] = g23.y;
-    u[0] = u01.x; u[1] = u01.y; u[2] = u23.x; u[3] = u23.y;
+  else __syncthreads();
+  if (staged) ptx::mbar_wait(&bar, 0, nullptr, 0, 2000000000ull);
+  float a[kCols];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (B) {
-        g[e] = bfr(g[e] + bfr(dot_regs<RANK>(t, bg[e])));
-        u[e] = bfr(u[e] + bfr(dot_regs<RANK>(t + RANK, bu[e])));
-      }
-      const float sg = bfr(g[e] / (1.f + expf(-g[e])));
-      a[e] = bfr(sg * u[e]);
+  for (int k = 0; k < kCols; ++k) {
+    const int64_t c = threadIdx.x + k * blockDim.x;
+    a[k] = 0.f;
+    if (c >= nc) continue;
+    if (B) {
+      g[k] = bfr(g[k] + bfr(smem_dot(t, bg + c * RANK, RANK)));
+      u[k] = bfr(u[k] + bfr(smem_dot(t + RANK, bu + c * RANK, RANK)));
     }
-    __align__(8) __nv_bfloat162 av[2] = {__floats2bfloat162_rn(a[0], a[1]), __floats2bfloat162_rn(a[2], a[3])};
-    *reinterpret_cast<uint2*>(tab.act[s] + local * p.act_stride + n0) = *reinterpret_cast<uint2*>(av);
+    const float sg = bfr(g[k] / (1.f + expf(-g[k])));
+    a[k] = bfr(sg * u[k]);
+    tab.act[s][local * p.act_stride + n0 + c] = __float2bfloat16_rn(a[k]);
   }
   if (!A) return;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -373,24 +378,21 @@ __global__ void __launch_bounds__(128) gu_silu_shrink_kernel(const __grid_consta
   for (int j0 = 0; j0 < 32; j0 += 8) {
     if (j0 >= R) break;
     float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (live) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&an[e][j0 / 8]);
+    for (int k = 0; k < kCols; ++k) {
+      const int64_t c = threadIdx.x + k * blockDim.x;
+      if (c >= nc) continue;
+      float v[8];
+      ld8(an + c * R + j0, v);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 f = __bfloat1622float2(hv[q]);
-          part[2 * q] = fmaf(a[e], f.x, part[2 * q]);
-          part[2 * q + 1] = fmaf(a[e], f.y, part[2 * q + 1]);
-        }
-      }
+      for (int e = 0; e < 8; ++e) part[e] = fmaf(a[k], v[e], part[e]);
     }
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      float v = part[q];
+    for (int e = 0; e < 8; ++e) {
+      float v = part[e];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) red[w][j0 + q] = v;
+      if (lane == 0) red[w][j0 + e] = v;
     }
   }
   __syncthreads();
@@ -426,9 +428,10 @@ int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p
   if (p.r_next % 8 || p.r_next > 96) return set_error(SWL_ERR_ARG, "resid_norm: next rank layout must be 8..96 in steps of 8");
   if (p.splits_in * r_in > kPartialsMax) return set_error(SWL_ERR_ARG, "resid_norm: too many shrink partials");
   const int64_t C = p.hidden / kCluster;
-  const int threads = static_cast<int>(C / 4);
-  if (threads > 1024 || threads % 32) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be a multiple of 1024 and <= 32768");
-  const size_t smem = C * p.r_next * 2 + (C + 32 + static_cast<size_t>(threads) * 8) * sizeof(float);
+  const int threads = 128;
+  if (C != 4 * threads) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be 4096 (8 CTAs x 128 threads x 4 columns)");
+  const int rb = r_in > 0 ? r_in : 8;
+  const size_t smem = C * p.r_next * 2 + C * rb * 2 + (C + static_cast<size_t>(threads) * 8) * sizeof(float);
   if (smem > 200 * 1024) return set_error(SWL_ERR_ARG, "resid_norm: shared memory too large");
   cudaError_t ae = cudaSuccess;
   switch (r_in) {
@@ -467,12 +470,24 @@ int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, 
   if (p.inter % 4) return set_error(SWL_ERR_ARG, "gu_silu: inter must be a multiple of 4");
   if (p.splits_in * 2 * r > kPartialsMax) return set_error(SWL_ERR_ARG, "gu_silu: too many shrink partials");
   dim3 grid(tab.seg.total_rows, static_cast<unsigned>((p.inter + 511) / 512));
+  const size_t smem = static_cast<size_t>(512) * (2 * r + p.r_next) * 2;
+  cudaError_t ae = cudaSuccess;
   switch (r) {
-    case 8: gu_silu_shrink_kernel<8><<<grid, 128, 0, stream>>>(tab, p); break;
-    case 16: gu_silu_shrink_kernel<16><<<grid, 128, 0, stream>>>(tab, p); break;
-    case 32: gu_silu_shrink_kernel<32><<<grid, 128, 0, stream>>>(tab, p); break;
+    case 8:
+      ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      gu_silu_shrink_kernel<8><<<grid, 128, smem, stream>>>(tab, p);
+      break;
+    case 16:
+      ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      gu_silu_shrink_kernel<16><<<grid, 128, smem, stream>>>(tab, p);
+      break;
+    case 32:
+      ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      gu_silu_shrink_kernel<32><<<grid, 128, smem, stream>>>(tab, p);
+      break;
     default: return set_error(SWL_ERR_ARG, "gu_silu: rank must be 8, 16 or 32");
   }
+  if (ae != cudaSuccess) return set_error(SWL_ERR_CUDA, "gu_silu: %s", cudaGetErrorString(ae));
   SWL_CUDA_TRY(cudaGetLastError());
   return SWL_OK;
 }
