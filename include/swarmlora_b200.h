@@ -231,6 +231,25 @@ int swl_paged_attention(int nseg, const int* rows, const void* const* block_tabl
                         const void* const* seqlens, void* const* out, int64_t out_stride, int hq,
                         int hkv, int head_dim, int page, float scale, int max_len,
                         const void* q_rot, float* part, void* stream);
+/* swl_paged_attention without the `part` argument, for callers that cannot
+ * allocate: a host whose memory is not managed by torch, or code on a path
+ * where allocating is not allowed. No counterpart in the reference (its
+ * attention, flash_attn_with_kvcache at worker_sync.py:196-203, allocates
+ * its own temporaries). The partial results live in an array compiled into
+ * the library, SWL_NOALLOC_ATTN_SCRATCH_FLOATS fp32 values per device
+ * (4 MiB); a launch needing more (swl_attention_part_floats) fails with
+ * SWL_ERR_ARG. Nothing is allocated. All calls on a device share that array
+ * and it keeps the last call's contents; calls on one stream are safe, calls
+ * that overlap on the GPU corrupt each other. Nothing in it needs to start at
+ * zero. The first call on a device looks up the array's address (this may
+ * load the library's code onto the device): make it before any stream
+ * capture begins. */
+#define SWL_NOALLOC_ATTN_SCRATCH_FLOATS 1048576
+int swl_paged_attention_noalloc(int nseg, const int* rows, const void* const* block_tables,
+                                const void* const* k_cache, const void* const* v_cache,
+                                const void* const* seqlens, void* const* out, int64_t out_stride,
+                                int hq, int hkv, int head_dim, int page, float scale, int max_len,
+                                const void* q_rot, void* stream);
 /* swl_paged_attention + the O projection's LoRA shrink on its output. */
 int swl_paged_attention_shrink(int nseg, const int* rows, const void* const* block_tables,
                                const void* const* k_cache, const void* const* v_cache,

@@ -4,6 +4,9 @@
 #include "common.h"
 #include "worker_ops.h"
 
+#include <atomic>
+#include <mutex>
+
 using namespace swl;
 
 namespace {
@@ -324,4 +327,91 @@ SWL_EXPORT int swl_copy_rows(int n, const void* const* src, void* const* dst, co
 SWL_EXPORT int swl_advance_i32(int* p, int n, int delta, void* stream) {
   if (n > 0 && !p) return set_error(SWL_ERR_ARG, "advance_i32: null pointer");
   return launch_advance_i32(p, n, delta, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------
+// Attention without caller scratch and without allocation.
+//
+// swl_paged_attention needs `part`, an fp32 buffer for the per-split partial
+// results that the combine step merges. Some callers cannot provide one: a
+// host whose allocator is not torch's (a foreign runtime bound over the C
+// ABI), or code running where any allocation is forbidden (inside a region
+// that must not touch the allocator, or on a path that must not fail on
+// memory). For them this entry point keeps the partials in a fixed array
+// compiled into the library, one copy per device, and allocates nothing.
+//
+// The array holds kNoAllocPartFloats fp32 values (4 MiB per device). A launch
+// shape that needs more (swl_attention_part_floats) is rejected with
+// SWL_ERR_ARG before anything is launched.
+//
+// The array is shared by every call on a device and keeps whatever the last
+// call wrote. Calls issued on one stream run one after another and are safe;
+// calls that can overlap on the GPU (two streams, two host threads) write the
+// same records and produce wrong results. Nothing in the array needs to start
+// at zero: each call writes every partial record before its combine step reads
+// it.
+//
+// The first call on a device looks up the array's device address
+// (cudaGetSymbolAddress, which may load this part of the library onto the
+// device) and caches it; later calls only launch. Make that first call before
+// any stream capture begins.
+namespace {
+constexpr int64_t kNoAllocPartFloats = int64_t{1} << 20;
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) float g_noalloc_attn_part[kNoAllocPartFloats];
+
+std::mutex g_noalloc_mu;
+std::atomic<float*> g_noalloc_part[kNoAllocMaxDevices];
+
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  SWL_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(SWL_ERR_ARG, "paged_attention_noalloc: device %d beyond %d", dev, kNoAllocMaxDevices);
+  float* p = g_noalloc_part[dev].load(std::memory_order_acquire);
+  if (!p) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    p = g_noalloc_part[dev].load(std::memory_order_relaxed);
+    if (!p) {
+      void* addr = nullptr;
+      SWL_CUDA_TRY(cudaGetSymbolAddress(&addr, g_noalloc_attn_part));
+      if (!addr) return set_error(SWL_ERR_CUDA, "paged_attention_noalloc: null scratch address");
+      p = static_cast<float*>(addr);
+      g_noalloc_part[dev].store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
+  return SWL_OK;
+}
+}  // namespace
+
+// swl_paged_attention with the same arguments minus `part`; the partials live
+// in the library's static per-device array described above.
+SWL_EXPORT int swl_paged_attention_noalloc(int nseg, const int* rows, const void* const* block_tables,
+                                           const void* const* k_cache, const void* const* v_cache,
+                                           const void* const* seqlens, void* const* out,
+                                           int64_t out_stride, int hq, int hkv, int head_dim, int page,
+                                           float scale, int max_len, const void* q_rot, void* stream) {
+  AttnTable t;
+  SWL_TRY(fill_attn(&t, nseg, rows, nullptr, block_tables, const_cast<void* const*>(k_cache),
+                    const_cast<void* const*>(v_cache), seqlens, out));
+  if (hkv <= 0) return set_error(SWL_ERR_ARG, "paged_attention_noalloc: hkv must be positive");
+  const int64_t need = attention_part_floats(t.seg.total_rows, hq,
+                                             attention_splits(t.seg.total_rows, hkv, max_len));
+  if (need > kNoAllocPartFloats)
+    return set_error(SWL_ERR_ARG,
+                     "paged_attention_noalloc: this launch needs %lld scratch floats, the static "
+                     "scratch holds %lld (use swl_paged_attention with caller scratch)",
+                     static_cast<long long>(need), static_cast<long long>(kNoAllocPartFloats));
+  float* part = nullptr;
+  SWL_TRY(noalloc_scratch(&part));
+  AttnParams p = {};
+  p.hq = hq; p.hkv = hkv; p.head_dim = head_dim; p.page = page;
+  p.out_stride = out_stride;
+  p.scale = scale;
+  p.max_len = max_len;
+  p.q_rot = cast<__nv_bfloat16>(q_rot);
+  p.part = part;
+  return launch_paged_attention(t, p, static_cast<cudaStream_t>(stream));
 }

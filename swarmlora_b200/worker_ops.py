@@ -112,6 +112,23 @@ def paged_attention(rows, block_tables, k_caches, v_caches, seqlens, outs, q_rot
                                     _stream(stream)))
 
 
+def paged_attention_noalloc(rows, block_tables, k_caches, v_caches, seqlens, outs, q_rot, hq: int,
+                            hkv: int, max_len: int, scale: float, head_dim: int = 128,
+                            page: int = 16, out_stride: int | None = None, stream=None) -> None:
+    """paged_attention with its partials in the library's static per-device
+    array (NOALLOC_ATTN_SCRATCH_FLOATS fp32): allocates nothing. Calls that
+    overlap on the GPU share that array and must not run concurrently."""
+    out_stride = out_stride if out_stride is not None else int(outs[0].stride(0))
+    check(lib().swl_paged_attention_noalloc(len(rows), i32_array(rows), _ptrs(block_tables),
+                                            _ptrs(k_caches), _ptrs(v_caches), _ptrs(seqlens),
+                                            _ptrs(outs), out_stride, hq, hkv, head_dim, page,
+                                            float(scale), max_len, q_rot.data_ptr(),
+                                            _stream(stream)))
+
+
+NOALLOC_ATTN_SCRATCH_FLOATS = 1 << 20
+
+
 def rms_norm(xs, outs, w: torch.Tensor, eps: float, rows=None, x_stride: int | None = None,
              out_stride: int | None = None, stream=None) -> None:
     rows = rows if rows is not None else [int(x.shape[0]) for x in xs]
