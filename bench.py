@@ -62,6 +62,8 @@ def parse():
                     help="run only --steps launches of one round kind at M=--slots (small ncu case)")
     ap.add_argument("--round-algo", type=int, default=0,
                     help="round kernel for --profile-round: 0 auto, 1 cluster split-K, 3 stream-K")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="launch every kernel fully serialized (no programmatic dependent launch)")
     ap.add_argument("--profile-attention", action="store_true",
                     help="run only --steps paged-attention launches over one layer's KV (small ncu case)")
     return ap.parse_args()
@@ -335,6 +337,8 @@ def our_arm(args):
     import dataclasses
     from swarmlora_b200.engine import LLAMA_3_1_8B, SlotGroup, random_adapter, random_base
 
+    import swarmlora_b200
+    swarmlora_b200.set_pdl(not args.no_pdl)
     cfg = dataclasses.replace(LLAMA_3_1_8B, layers=args.layers, vocab=args.vocab)
     n = args.slots
     g = torch.Generator().manual_seed(1234 + rank)
@@ -434,6 +438,7 @@ def our_arm(args):
                                    f"{n} decode slots/GPU, distinct r=16 adapters on 7 projections, "
                                    f"ctx U[{CTX_LO},{CTX_HI}] paged 16, 1 token/slot/step, greedy",
                        "slots_per_gpu": n, "parallelism": f"{world} independent aggregator groups",
+                       "launch": "serialized" if args.no_pdl else "programmatic dependent launch",
                        "l2": "weights (15 GB/step) far exceed L2; no flush needed",
                        "us_per_round": {k: v["us"] for k, v in rounds.items()},
                        "round_gbs": {k: v["gbs"] for k, v in rounds.items()}},

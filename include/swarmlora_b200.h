@@ -52,6 +52,11 @@ extern "C" {
 
 const char* swl_last_error(void);
 int swl_abi_version(void);
+/* Programmatic dependent launch for every later kernel launch of the library
+ * (on by default): each kernel may start while the previous kernel of its
+ * stream finishes, and waits for it before touching its outputs. Returns the
+ * previous setting. No counterpart in the reference (a launch option). */
+int swl_set_pdl(int on);
 
 /* ======================================================================
  * Shared-memory command ring and slot barrier — replaces the pybind module

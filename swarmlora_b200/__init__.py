@@ -19,3 +19,9 @@ OP_EMBED = 11
 OP_LM_HEAD = 12
 OP_SET_SAMPLING = 13
 MAX_SLOTS = 128
+
+
+def set_pdl(on: bool) -> bool:
+    """Programmatic dependent launch for the library's later kernel launches
+    (on by default); returns the previous setting."""
+    return bool(lib().swl_set_pdl(1 if on else 0))

@@ -25,6 +25,7 @@ _pu32 = C.POINTER(C.c_uint)
 SIGNATURES: dict[str, tuple] = {
     "swl_last_error": (_cp, []),
     "swl_abi_version": (_i32, []),
+    "swl_set_pdl": (_i32, [_i32]),
     # ---- ext_ipc_queue
     "swl_q_create": (_i32, [_i32, _i32, C.c_char_p, _i32]),
     "swl_q_open": (_i32, [_cp, _i32, _i32]),

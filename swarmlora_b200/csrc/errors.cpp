@@ -1,5 +1,8 @@
 // Thread-local last-error storage behind swl_last_error().
 #include "common.h"
+#include "launch.h"
+
+#include <atomic>
 
 namespace swl {
 
@@ -17,8 +20,15 @@ int set_error(int code, const char* fmt, ...) {
 
 const char* last_error() { return g_last_error.c_str(); }
 
+static std::atomic<int> g_pdl{1};
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+
 }  // namespace swl
 
 SWL_EXPORT const char* swl_last_error(void) { return swl::last_error(); }
 
 SWL_EXPORT int swl_abi_version(void) { return 1; }
+
+// Switches programmatic dependent launch for every later kernel launch of the
+// library (on by default); returns the previous setting.
+SWL_EXPORT int swl_set_pdl(int on) { return swl::g_pdl.exchange(on ? 1 : 0); }

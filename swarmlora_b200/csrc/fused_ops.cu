@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 
 #include "common.h"
+#include "launch.h"
 #include "ptx.cuh"
 #include "worker_ops.h"
 
@@ -161,6 +162,8 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
   const int64_t ncols = min(static_cast<int64_t>(4 * p.head_dim), static_cast<int64_t>(heads) * p.head_dim - col0);
   const bool staged = B && stage_bulk(&bar, bs, B + col0 * RANK, static_cast<uint32_t>(ncols * RANK * 2),
                                       nullptr, nullptr, 0, nullptr, nullptr, 0);
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const int pi = blockIdx.y * blockDim.x + threadIdx.x;
   const bool live = pi < heads * half;
   const int head = live ? pi / half : 0, d = pi % half;
@@ -235,6 +238,8 @@ __global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_con
   const bool staged = stage_bulk(&bar, a_tile, A ? A + c0 * R : nullptr, static_cast<uint32_t>(C * R * 2),
                                  b_tile, B ? B + c0 * RANK : nullptr, static_cast<uint32_t>(C * RB * 2),
                                  nullptr, nullptr, 0);
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
   __nv_bfloat16* h = tab.h[s] + local * p.h_stride;
   float v[kCols], rv[kCols], wv[kCols];
@@ -347,6 +352,8 @@ __global__ void __launch_bounds__(128) gu_silu_shrink_kernel(const __grid_consta
   const bool staged = stage_bulk(&bar, bg, B ? B + n0 * RANK : nullptr, static_cast<uint32_t>(nc * RANK * 2),
                                  bu, B ? B + (n0 + p.inter) * RANK : nullptr, static_cast<uint32_t>(nc * RANK * 2),
                                  an, A ? A + n0 * R : nullptr, static_cast<uint32_t>(nc * R * 2));
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
   float g[kCols], u[kCols];
 #pragma unroll
@@ -412,12 +419,11 @@ int launch_qkv_rope(const QkvRopeTable& tab, const QkvRopeParams& p, int r, cuda
   const int pairs = (p.hq + 2 * p.hkv) * (p.head_dim / 2);
   dim3 grid(tab.seg.total_rows, (pairs + 255) / 256);
   switch (r) {
-    case 8: qkv_rope_kernel<8><<<grid, 256, 0, stream>>>(tab, p); break;
-    case 16: qkv_rope_kernel<16><<<grid, 256, 0, stream>>>(tab, p); break;
-    case 32: qkv_rope_kernel<32><<<grid, 256, 0, stream>>>(tab, p); break;
+    case 8: SWL_CUDA_TRY(launch_kernel(qkv_rope_kernel<8>, grid, dim3(256), 0, stream, 1, tab, p)); break;
+    case 16: SWL_CUDA_TRY(launch_kernel(qkv_rope_kernel<16>, grid, dim3(256), 0, stream, 1, tab, p)); break;
+    case 32: SWL_CUDA_TRY(launch_kernel(qkv_rope_kernel<32>, grid, dim3(256), 0, stream, 1, tab, p)); break;
     default: return set_error(SWL_ERR_ARG, "qkv_rope: rank must be 8, 16 or 32");
   }
-  SWL_CUDA_TRY(cudaGetLastError());
   return SWL_OK;
 }
 
@@ -442,23 +448,12 @@ int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p
     default: break;
   }
   if (ae != cudaSuccess) return set_error(SWL_ERR_CUDA, "resid_norm: %s", cudaGetErrorString(ae));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(tab.seg.total_rows * kCluster), 1, 1);
-  cfg.blockDim = dim3(threads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kCluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  const dim3 grid(static_cast<unsigned>(tab.seg.total_rows * kCluster), 1, 1);
   switch (r_in) {
-    case 0: SWL_CUDA_TRY(cudaLaunchKernelEx(&cfg, resid_norm_shrink_kernel<0>, tab, p)); break;
-    case 8: SWL_CUDA_TRY(cudaLaunchKernelEx(&cfg, resid_norm_shrink_kernel<8>, tab, p)); break;
-    case 16: SWL_CUDA_TRY(cudaLaunchKernelEx(&cfg, resid_norm_shrink_kernel<16>, tab, p)); break;
-    case 32: SWL_CUDA_TRY(cudaLaunchKernelEx(&cfg, resid_norm_shrink_kernel<32>, tab, p)); break;
+    case 0: SWL_CUDA_TRY(launch_kernel(resid_norm_shrink_kernel<0>, grid, dim3(threads), smem, stream, kCluster, tab, p)); break;
+    case 8: SWL_CUDA_TRY(launch_kernel(resid_norm_shrink_kernel<8>, grid, dim3(threads), smem, stream, kCluster, tab, p)); break;
+    case 16: SWL_CUDA_TRY(launch_kernel(resid_norm_shrink_kernel<16>, grid, dim3(threads), smem, stream, kCluster, tab, p)); break;
+    case 32: SWL_CUDA_TRY(launch_kernel(resid_norm_shrink_kernel<32>, grid, dim3(threads), smem, stream, kCluster, tab, p)); break;
     default: return set_error(SWL_ERR_ARG, "resid_norm: input rank must be 0, 8, 16 or 32");
   }
   return SWL_OK;
@@ -475,15 +470,15 @@ int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, 
   switch (r) {
     case 8:
       ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      gu_silu_shrink_kernel<8><<<grid, 128, smem, stream>>>(tab, p);
+      if (ae == cudaSuccess) ae = launch_kernel(gu_silu_shrink_kernel<8>, grid, dim3(128), smem, stream, 1, tab, p);
       break;
     case 16:
       ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      gu_silu_shrink_kernel<16><<<grid, 128, smem, stream>>>(tab, p);
+      if (ae == cudaSuccess) ae = launch_kernel(gu_silu_shrink_kernel<16>, grid, dim3(128), smem, stream, 1, tab, p);
       break;
     case 32:
       ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      gu_silu_shrink_kernel<32><<<grid, 128, smem, stream>>>(tab, p);
+      if (ae == cudaSuccess) ae = launch_kernel(gu_silu_shrink_kernel<32>, grid, dim3(128), smem, stream, 1, tab, p);
       break;
     default: return set_error(SWL_ERR_ARG, "gu_silu: rank must be 8, 16 or 32");
   }

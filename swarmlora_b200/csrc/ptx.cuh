@@ -21,6 +21,18 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// ---- programmatic dependent launch ----------------------------------------------
+// A kernel launched with programmatic stream serialization may start while the
+// previous kernel in its stream is still running. grid_dep_wait() blocks until
+// that kernel has completed and its writes are visible; everything before it
+// may only touch data no earlier kernel of the stream writes (weights, adapter
+// tiles, launch tables). Without the launch attribute both are no-ops.
+// grid_dep_launch() lets the next kernel of the stream begin launching.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- mbarrier ---------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)

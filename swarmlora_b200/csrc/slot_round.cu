@@ -21,6 +21,7 @@
 #include <mutex>
 
 #include "common.h"
+#include "launch.h"
 #include "ptx.cuh"
 #include "slot_round.h"
 
@@ -127,10 +128,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
+  // The weight does not depend on earlier kernels: fill the whole ring before
+  // waiting for the kernel ahead in the stream (whose outputs are our inputs).
+  const int npre = min(nk, STAGES);
+  if (warp == 0 && lane == 0) {
+    const uint64_t pol = ptx::policy_evict_first();
+    for (int i = 0; i < npre; ++i) {
+      ptx::mbar_arrive_expect_tx(&full[i], kWStageBytes);
+      ptx::tma_load_2d(w_st + i * kWStageBytes, &wmap, &full[i], (kb_begin + i) * kBlockK, n0, pol);
+    }
+  }
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
+
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol = ptx::policy_evict_first();
-      for (int i = 0; i < nk; ++i) {
+      for (int i = npre; i < nk; ++i) {
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1;
         if (!ptx::mbar_wait(&empty[s], ph ^ 1, err, kErrWaitEmptyW, kWaitTimeoutNs)) break;
@@ -330,19 +344,10 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
   }
   splits = std::max(1, std::min(splits, std::min(8, nkb)));
 
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * splits), static_cast<unsigned>(m_chunks), 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  SWL_CUDA_TRY(cudaLaunchKernelEx(&cfg, slot_round_tc_kernel<BN>, map, tab, shape, splits));
+  SWL_CUDA_TRY(launch_kernel(slot_round_tc_kernel<BN>,
+                             dim3(static_cast<unsigned>(n_tiles * splits), static_cast<unsigned>(m_chunks), 1),
+                             dim3(kThreads, 1, 1), Cfg::kSmemBytes, stream, static_cast<unsigned>(splits),
+                             map, tab, shape, splits));
   return SWL_OK;
 }
 

@@ -8,6 +8,8 @@
 #include <cuda_bf16.h>
 
 #include "common.h"
+#include "launch.h"
+#include "ptx.cuh"
 #include "shm_abi.h"
 #include "vocab_ops.h"
 
@@ -19,6 +21,8 @@ namespace {
 __global__ void embed_gather_kernel(const __grid_constant__ TokenTable tab,
                                     const __nv_bfloat16* __restrict__ table, int64_t vocab,
                                     int64_t hidden) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const int gr = blockIdx.x;
   int lo = 0, hi = tab.nslots - 1;
   while (lo < hi) {
@@ -38,6 +42,8 @@ __global__ void embed_gather_kernel(const __grid_constant__ TokenTable tab,
 // (torch.argmax returns the first maximal index).
 __global__ void argmax_rows_kernel(const __nv_bfloat16* __restrict__ logits, int64_t vocab,
                                    int64_t ld, const __grid_constant__ TokenOuts outs) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const int row = blockIdx.x;
   const __nv_bfloat16* x = logits + row * ld;
   float best = -INFINITY;
@@ -89,9 +95,8 @@ int launch_embed_gather(const TokenTable& tab, const void* table, int64_t vocab,
                         cudaStream_t stream) {
   if (tab.total_rows <= 0) return SWL_OK;
   if (hidden % 8) return set_error(SWL_ERR_ARG, "embed: hidden must be a multiple of 8");
-  embed_gather_kernel<<<tab.total_rows, 256, 0, stream>>>(
-      tab, static_cast<const __nv_bfloat16*>(table), vocab, hidden);
-  SWL_CUDA_TRY(cudaGetLastError());
+  SWL_CUDA_TRY(launch_kernel(embed_gather_kernel, dim3(tab.total_rows), dim3(256), 0, stream, 1, tab,
+                             static_cast<const __nv_bfloat16*>(table), vocab, hidden));
   return SWL_OK;
 }
 
@@ -99,9 +104,8 @@ int launch_argmax_rows(const void* logits, int rows, int64_t vocab, int64_t ld,
                        const TokenOuts& outs, cudaStream_t stream) {
   if (rows <= 0) return SWL_OK;
   if (rows > kMaxSlots) return set_error(SWL_ERR_ARG, "argmax: too many rows");
-  argmax_rows_kernel<<<rows, 1024, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), vocab,
-                                                ld, outs);
-  SWL_CUDA_TRY(cudaGetLastError());
+  SWL_CUDA_TRY(launch_kernel(argmax_rows_kernel, dim3(rows), dim3(1024), 0, stream, 1,
+                             static_cast<const __nv_bfloat16*>(logits), vocab, ld, outs));
   return SWL_OK;
 }
 

@@ -21,6 +21,7 @@
 #include <algorithm>
 
 #include "common.h"
+#include "launch.h"
 #include "ptx.cuh"
 #include "worker_ops.h"
 
@@ -59,6 +60,8 @@ template <int ROWS>
 __global__ void __launch_bounds__(256) lora_shrink_kernel(const __grid_constant__ LoraShrinkTable tab,
                                                           int64_t K, int R, int64_t x_stride,
                                                           int splits, float* __restrict__ ws) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   extern __shared__ float red[];  // [256][ROWS * 8]
   const int seg = blockIdx.x / splits, split = blockIdx.x % splits;
   const __nv_bfloat16* A = tab.A[seg];
@@ -119,6 +122,8 @@ template <int RANK>
 __global__ void __launch_bounds__(256) lora_expand_kernel(const __grid_constant__ LoraExpandTable tab,
                                                           const ExpandParams p,
                                                           const float* __restrict__ ws) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   extern __shared__ float tsm[];  // [rows_chunk][R]
   constexpr int kRowsChunk = 16;
   const int seg = blockIdx.x;
@@ -202,6 +207,8 @@ __global__ void __launch_bounds__(256) lora_expand_kernel(const __grid_constant_
 // ---- RoPE + KV append ----------------------------------------------------------------
 __global__ void __launch_bounds__(256) rope_append_kernel(const __grid_constant__ AttnTable tab,
                                                           const AttnParams p) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const int gr = blockIdx.x;
   const int s = seg_of_row(tab.seg, gr);
   const int local = gr - tab.seg.row_start[s];
@@ -280,6 +287,8 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 __global__ void __launch_bounds__(32) paged_attention_kernel(const __grid_constant__ AttnTable tab,
                                                              const AttnParams p, int splits,
                                                              float* __restrict__ part) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   __shared__ __align__(128) uint8_t kv_sm[kAttnStages][2][kTileBytes];
   __shared__ int pages[kMaxSplitPages];
   const int gr = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
@@ -422,6 +431,8 @@ __global__ void __launch_bounds__(128) attention_combine_kernel(const __grid_con
                                                                 const AttnParams p, int splits,
                                                                 const float* __restrict__ part,
                                                                 const __grid_constant__ ShrinkSide sh) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const int gr = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int s = seg_of_row(tab.seg, gr);
   const int local = gr - tab.seg.row_start[s];
@@ -469,6 +480,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __grid_constant__ N
                                                        const __nv_bfloat16* __restrict__ w,
                                                        int64_t hidden, float eps, int64_t x_stride,
                                                        int64_t out_stride) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const int gr = blockIdx.x;
   const int s = seg_of_row(tab.seg, gr);
   const int64_t local = gr - tab.seg.row_start[s];
@@ -509,6 +522,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __grid_constant__ N
 // ---- batched copies / counters -------------------------------------------------------
 // One CTA per copy; 16-byte vectors when both ends and the size allow it.
 __global__ void copy_rows_kernel(const __grid_constant__ CopyTable tab) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const int i = blockIdx.x;
   const char* src = static_cast<const char*>(tab.src[i]);
   char* dst = static_cast<char*>(tab.dst[i]);
@@ -523,6 +538,8 @@ __global__ void copy_rows_kernel(const __grid_constant__ CopyTable tab) {
 }
 
 __global__ void advance_i32_kernel(int* p, int n, int delta) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] += delta;
 }
@@ -532,15 +549,13 @@ __global__ void advance_i32_kernel(int* p, int n, int delta) {
 int launch_copy_rows(const CopyTable& tab, int n, cudaStream_t stream) {
   if (n <= 0) return SWL_OK;
   if (n > kMaxSlots) return set_error(SWL_ERR_ARG, "copy_rows: at most %d copies per call", kMaxSlots);
-  copy_rows_kernel<<<n, 256, 0, stream>>>(tab);
-  SWL_CUDA_TRY(cudaGetLastError());
+  SWL_CUDA_TRY(launch_kernel(copy_rows_kernel, dim3(n), dim3(256), 0, stream, 1, tab));
   return SWL_OK;
 }
 
 int launch_advance_i32(int* p, int n, int delta, cudaStream_t stream) {
   if (n <= 0) return SWL_OK;
-  advance_i32_kernel<<<(n + 255) / 256, 256, 0, stream>>>(p, n, delta);
-  SWL_CUDA_TRY(cudaGetLastError());
+  SWL_CUDA_TRY(launch_kernel(advance_i32_kernel, dim3((n + 255) / 256), dim3(256), 0, stream, 1, p, n, delta));
   return SWL_OK;
 }
 
@@ -556,11 +571,12 @@ int launch_lora_shrink(const LoraShrinkTable& tab, int64_t K, int R, int64_t x_s
   }();
   dim3 grid(tab.seg.nseg * splits);
   if (rows_max <= 1) {
-    lora_shrink_kernel<1><<<grid, 256, 256 * 8 * sizeof(float), stream>>>(tab, K, R, x_stride, splits, ws);
+    SWL_CUDA_TRY(launch_kernel(lora_shrink_kernel<1>, grid, dim3(256), 256 * 8 * sizeof(float), stream, 1,
+                               tab, K, R, x_stride, splits, ws));
   } else {
-    lora_shrink_kernel<4><<<grid, 256, 256 * 32 * sizeof(float), stream>>>(tab, K, R, x_stride, splits, ws);
+    SWL_CUDA_TRY(launch_kernel(lora_shrink_kernel<4>, grid, dim3(256), 256 * 32 * sizeof(float), stream, 1,
+                               tab, K, R, x_stride, splits, ws));
   }
-  SWL_CUDA_TRY(cudaGetLastError());
   return SWL_OK;
 }
 
@@ -573,20 +589,18 @@ int launch_lora_expand(const LoraExpandTable& tab, const ExpandParams& p, const 
   dim3 grid(tab.seg.nseg, static_cast<unsigned>((n_out + 255) / 256));
   const size_t smem = 16 * p.r * p.nblocks * sizeof(float);
   switch (p.r) {
-    case 8: lora_expand_kernel<8><<<grid, 256, smem, stream>>>(tab, p, ws); break;
-    case 16: lora_expand_kernel<16><<<grid, 256, smem, stream>>>(tab, p, ws); break;
-    case 24: lora_expand_kernel<24><<<grid, 256, smem, stream>>>(tab, p, ws); break;
-    default: lora_expand_kernel<32><<<grid, 256, smem, stream>>>(tab, p, ws); break;
+    case 8: SWL_CUDA_TRY(launch_kernel(lora_expand_kernel<8>, grid, dim3(256), smem, stream, 1, tab, p, ws)); break;
+    case 16: SWL_CUDA_TRY(launch_kernel(lora_expand_kernel<16>, grid, dim3(256), smem, stream, 1, tab, p, ws)); break;
+    case 24: SWL_CUDA_TRY(launch_kernel(lora_expand_kernel<24>, grid, dim3(256), smem, stream, 1, tab, p, ws)); break;
+    default: SWL_CUDA_TRY(launch_kernel(lora_expand_kernel<32>, grid, dim3(256), smem, stream, 1, tab, p, ws)); break;
   }
-  SWL_CUDA_TRY(cudaGetLastError());
   return SWL_OK;
 }
 
 int launch_rope_append(const AttnTable& tab, const AttnParams& p, cudaStream_t stream) {
   if (tab.seg.total_rows <= 0) return SWL_OK;
   if (p.head_dim != kD) return set_error(SWL_ERR_ARG, "rope: head_dim must be 128");
-  rope_append_kernel<<<tab.seg.total_rows, 256, 0, stream>>>(tab, p);
-  SWL_CUDA_TRY(cudaGetLastError());
+  SWL_CUDA_TRY(launch_kernel(rope_append_kernel, dim3(tab.seg.total_rows), dim3(256), 0, stream, 1, tab, p));
   return SWL_OK;
 }
 
@@ -613,8 +627,7 @@ int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream
   const int splits = attention_splits(tab.seg.total_rows, p.hkv, p.max_len);
   if (!p.part) return set_error(SWL_ERR_ARG, "attention: missing partial scratch");
   dim3 grid(tab.seg.total_rows, p.hkv, splits);
-  paged_attention_kernel<<<grid, 32, 0, stream>>>(tab, p, splits, p.part);
-  SWL_CUDA_TRY(cudaGetLastError());
+  SWL_CUDA_TRY(launch_kernel(paged_attention_kernel, grid, dim3(32), 0, stream, 1, tab, p, splits, p.part));
   ShrinkSide none;
   if (!shrink) {
     for (int i = 0; i < kMaxSlots; ++i) none.A[i] = nullptr;
@@ -623,9 +636,8 @@ int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream
   } else if (shrink->r % 8 || shrink->r > 32) {
     return set_error(SWL_ERR_ARG, "attention: shrink rank must be 8..32 in steps of 8");
   }
-  attention_combine_kernel<<<dim3(tab.seg.total_rows, p.hq), kD, 0, stream>>>(tab, p, splits, p.part,
-                                                                             shrink ? *shrink : none);
-  SWL_CUDA_TRY(cudaGetLastError());
+  SWL_CUDA_TRY(launch_kernel(attention_combine_kernel, dim3(tab.seg.total_rows, p.hq), dim3(kD), 0, stream, 1,
+                             tab, p, splits, static_cast<const float*>(p.part), shrink ? *shrink : none));
   return SWL_OK;
 }
 
@@ -633,8 +645,8 @@ int launch_rms_norm(const NormTable& tab, const __nv_bfloat16* w, int64_t hidden
                     int64_t x_stride, int64_t out_stride, cudaStream_t stream) {
   if (tab.seg.total_rows <= 0) return SWL_OK;
   if (hidden % 8) return set_error(SWL_ERR_ARG, "rms_norm: hidden must be a multiple of 8");
-  rms_norm_kernel<<<tab.seg.total_rows, 256, 0, stream>>>(tab, w, hidden, eps, x_stride, out_stride);
-  SWL_CUDA_TRY(cudaGetLastError());
+  SWL_CUDA_TRY(launch_kernel(rms_norm_kernel, dim3(tab.seg.total_rows), dim3(256), 0, stream, 1, tab, w, hidden, eps,
+                             x_stride, out_stride));
   return SWL_OK;
 }
 

@@ -90,3 +90,38 @@ def test_engine_matches_oracle_and_graph_replay(native, cuda, fused):
             assert torch.equal(grp.tokens.cpu(), eager[step]), f"graph step {step} differs"
     finally:
         grp.close()
+
+
+def test_engine_pdl_matches_serialized_launches(native, cuda):
+    """Programmatic dependent launch (kernels start while the previous one
+    finishes) leaves every result bit-identical to fully serialized launches,
+    eager and replayed from a CUDA graph."""
+    import swarmlora_b200 as swl
+    from swarmlora_b200.engine import ModelConfig, SlotGroup, random_adapter, random_base
+    cfg = ModelConfig(layers=2, vocab=4096)
+    ctx = [20, 0, 31, 100, 7, 250]
+    base = random_base(cfg, seed=1, device=cuda, norm_noise=0.1)
+    adapters = [random_adapter(cfg, seed=10 + i, device=cuda) if i != 2 else None for i in range(len(ctx))]
+    results = {}
+    for pdl in (False, True):
+        prev = swl.set_pdl(pdl)
+        grp = SlotGroup(cfg, base, adapters, ctx, max_new=8, seed=3)
+        try:
+            grp.tokens.copy_(torch.tensor([5, 4095, 17, 0, 1234, 77]))
+            stream = torch.cuda.current_stream()
+            grp.enqueue_step(stream)
+            grp.capture()
+            for _ in range(3):
+                grp.replay()
+            torch.cuda.synchronize()
+            results[pdl] = (grp.tokens.cpu(), grp.h.cpu(), grp.read_slot_rows("in", cfg.hidden),
+                            [k.cpu() for k in grp.k_cache], [v.cpu() for v in grp.v_cache])
+        finally:
+            swl.set_pdl(prev)
+            grp.close()
+    a, b = results[False], results[True]
+    assert torch.equal(a[0], b[0])
+    assert torch.equal(a[1], b[1])
+    assert torch.equal(a[2], b[2])
+    for x, y in zip(a[3] + a[4], b[3] + b[4]):
+        assert torch.equal(x, y)
