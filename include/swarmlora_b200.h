@@ -227,6 +227,9 @@ int swl_rope_append(int nseg, const int* rows, const void* const* qkv, int64_t q
                     const void* const* block_tables, void* const* k_cache, void* const* v_cache,
                     const void* const* seqlens, int hq, int hkv, int head_dim, int page,
                     const void* cos_sin, int max_pos, void* q_rot, void* stream);
+/* Tuning of the attention launch: pages per context chunk and page-ring
+ * depth (2..4); 0 = automatic. A launch option, no counterpart in the reference. */
+int swl_attention_tune(int chunk_pages, int stages);
 /* fp32 scratch floats swl_paged_attention needs in `part`. */
 int64_t swl_attention_part_floats(int total_rows, int hq, int hkv, int max_len);
 /* Causal GQA attention over paged KV (flash_attn_with_kvcache semantics,

@@ -441,6 +441,9 @@ SWL_EXPORT int swl_agg_init_layer(int layer_idx, const void* q, int64_t q_rows, 
   SWL_CUDA_TRY(cudaSetDevice(g_device));
   SWL_CUDA_TRY(cudaMalloc(&L.qkv, (q_rows + k_rows + v_rows) * row_h));
   SWL_CUDA_TRY(cudaMalloc(&L.gu, (gate_rows + up_rows) * row_h));
+  // The caller's weights may still be in flight on any of its streams (the
+  // copy stream below does not wait for them).
+  SWL_CUDA_TRY(cudaDeviceSynchronize());
   char* dq = static_cast<char*>(L.qkv);
   SWL_CUDA_TRY(cudaMemcpyAsync(dq, q, q_rows * row_h, cudaMemcpyDeviceToDevice, g_stream));
   SWL_CUDA_TRY(cudaMemcpyAsync(dq + q_rows * row_h, k, k_rows * row_h, cudaMemcpyDeviceToDevice, g_stream));
@@ -558,14 +561,12 @@ SWL_EXPORT int swl_agg_execute_round(int op, int layer, int n, const int* slot_i
   std::string why;
   validate(cmds.data(), n, in_row, out_row, &good, &bad, &why);
   if (static_cast<int>(good.size()) != n) return set_error(SWL_ERR_OWNER, "execute_round: %s", why.c_str());
+  // A null stream is the legacy default stream (torch's default): the round
+  // runs there, ordered after whatever the caller queued on it, and the call
+  // returns once it is done.
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  bool own = st == nullptr;
-  if (own) {
-    SWL_TRY(ensure_stream());
-    st = g_stream;
-  }
   SWL_TRY(run_round(op, layer, good, st));
-  if (own) SWL_CUDA_TRY(cudaStreamSynchronize(st));
+  if (st == nullptr) SWL_CUDA_TRY(cudaStreamSynchronize(st));
   return SWL_OK;
 }
 

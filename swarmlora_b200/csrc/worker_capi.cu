@@ -129,6 +129,12 @@ SWL_EXPORT int64_t swl_attention_part_floats(int total_rows, int hq, int hkv, in
   return attention_part_floats(total_rows, hq, attention_splits(total_rows, hkv, max_len));
 }
 
+// Tuning knob of the attention launch: pages per context chunk and depth of
+// the page ring (2..4); 0 restores the automatic choice.
+SWL_EXPORT int swl_attention_tune(int chunk_pages, int stages) {
+  return set_attention_tuning(chunk_pages, stages);
+}
+
 // Causal GQA attention of each new token over its slot's paged cache
 // (flash_attn_with_kvcache semantics, worker_sync.py:196-203): token t of
 // slot i attends to cache positions 0 .. *seqlens[i] + t. max_len bounds

@@ -19,6 +19,8 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 
 #include "common.h"
 #include "launch.h"
@@ -240,24 +242,54 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const __grid_constant_
 }
 
 // ---- paged attention -------------------------------------------------------------------
-// CTA = one warp = (token row, kv head, context split). The warp computes all
-// G query heads of the kv head at once on tensor cores (mma.sync m16n8k16,
-// bf16 in, fp32 accumulate): per 16-token page,
-//   S[head, tok]  = Q[head, :] . K[tok, :]      (A = Q, heads padded to 16 rows;
-//                                                B = K^T via ldmatrix)
-//   P = exp2(S*scale*log2e - m)                 (online softmax in registers)
-//   O[head, dim] += P[head, tok] . V[tok, dim]  (A = P reused from the S
-//                                                accumulator, B = V via ldmatrix.trans)
-// Pages stream through a 3-stage cp.async ring in shared memory; each 16-byte
-// piece of a token row is stored XOR-swizzled by (token & 7) so the 8-row
-// ldmatrix reads hit 8 different bank groups. Tokens past the causal end are
-// zero-filled and masked. Each CTA writes one record [m, l, o[128]] per
-// query head; attention_combine_kernel merges the splits.
+// The work of one call is a stream of units, one unit = one 16-token page of
+// one token row (all kv heads): rows in order, then pages. Each CTA takes an
+// equal contiguous range of at least `min_units` units, so every CTA does the
+// same amount of work whatever the rows' context lengths; where its range
+// crosses a row boundary it finishes one partial result ("piece") and starts
+// the next.
+// A CTA has one warp per kv head. Warp w streams its head's slice of each page
+// (K and V token rows, 256 B each, plus the G query rows of its head group at
+// the first page of a piece) into its own slots of a ring of page stages with
+// cp.async, zero-filling tokens past the causal end; the warps never wait for
+// one another. Token rows sit hkv * 256 + 16 bytes apart, so the 8 rows one
+// ldmatrix reads fall in 8 different bank groups. Per page the warp computes,
+// on tensor cores (mma.sync m16n8k16, bf16 in, fp32 accumulate), with the
+// 16 tokens as the M dimension and the G query heads (padded to 8) as N:
+//   S^T[tok, head]  = K[tok, :] . Q[head, :]      (A = K via ldmatrix, B = Q^T)
+//   P = exp2(S*scale*log2e - m)                   (online softmax per head)
+//   O^T[dim, head] += V^T[dim, tok] . P^T[tok, head]  (A = V^T via ldmatrix.trans,
+//                                                      B = P^T from registers)
+// Each piece writes one record [m, l, o[128]] per query head at
+// [row][head][piece][...], the piece index counted from the first CTA whose
+// range touches the row; attention_combine_kernel merges them.
 constexpr int kD = 128;
 constexpr int kPageTok = 16;
-constexpr int kAttnStages = 3;
-constexpr int kTileBytes = kPageTok * kD * 2;  // one page of K (or V) of one head: 4 KB
-constexpr int kMaxSplitPages = 256;
+constexpr int kAttnStagesMax = 4;
+constexpr int kAttnMaxHkv = 8;
+constexpr int kAttnMaxRows = 256;
+constexpr int kMinUnits = 8;                             // pages per CTA at least
+constexpr int kAttnSmemMax = 227 * 1024 - 4096;          // dynamic ring budget
+constexpr uint64_t kAttnWaitNs = 2000000000ull;
+
+// Tuning overrides (0 = automatic): minimum pages per CTA and ring depth.
+std::atomic<int> g_attn_min_units{0};
+std::atomic<int> g_attn_stages{0};
+
+__host__ __device__ __forceinline__ int attn_row_bytes(int hkv) { return hkv * kD * 2 + 16; }
+__host__ __device__ __forceinline__ int attn_stage_bytes(int hq, int hkv) {
+  return 2 * kPageTok * attn_row_bytes(hkv) + hq * kD * 2;
+}
+
+// The partial scratch starts with a header the combine step reads: [0] units
+// per CTA, [1 + r] page prefix of row r (r = 0..rows), padded to 32 floats.
+__host__ __device__ __forceinline__ int64_t attn_hdr_floats(int rows) { return (rows + 2 + 31) / 32 * 32; }
+
+// Units per CTA: at least min_units, and enough that `grid` CTAs cover all.
+__device__ __forceinline__ int64_t attn_units_per_cta(int64_t total, int grid, int min_units) {
+  const int64_t w = (total + grid - 1) / grid;
+  return w > min_units ? w : min_units;
+}
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                                uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -284,163 +316,279 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-__global__ void __launch_bounds__(32) paged_attention_kernel(const __grid_constant__ AttnTable tab,
-                                                             const AttnParams p, int splits,
-                                                             float* __restrict__ part) {
+template <int kStages>
+__global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
+    paged_attention_kernel(const __grid_constant__ AttnTable tab, const AttnParams p, int max_pieces,
+                           int min_units, float* __restrict__ part) {
+  extern __shared__ __align__(128) uint8_t att_dyn[];
+  __shared__ int pre[kAttnMaxRows + 1];  // page prefix over rows
+  __shared__ int keys[kAttnMaxRows];     // keys (causal length) of each row
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hkv = p.hkv, G = p.hq / p.hkv;
+  const int row_bytes = attn_row_bytes(hkv);
+  const int kv_bytes = kPageTok * row_bytes;
+  const int stage_bytes = attn_stage_bytes(p.hq, hkv);
   ptx::grid_dep_wait();
   ptx::grid_dep_launch();
-  __shared__ __align__(128) uint8_t kv_sm[kAttnStages][2][kTileBytes];
-  __shared__ int pages[kMaxSplitPages];
-  const int gr = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-  ptx::prefetch_l2_share(p.pf, p.pf_bytes,
-                         (split * gridDim.y + kvh) * gridDim.x + gr, gridDim.x * gridDim.y * gridDim.z);
-  const int lane = threadIdx.x;
-  const int G = p.hq / p.hkv;
-  const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
-  const int s = seg_of_row(tab.seg, gr);
-  const int local = gr - tab.seg.row_start[s];
-  const int L = *tab.seqlen[s] + local + 1;  // causal: keys 0 .. pos
-  const int ntiles = (L + kPageTok - 1) / kPageTok;
-  const int tb = static_cast<int>(static_cast<int64_t>(ntiles) * split / splits);
-  const int te = static_cast<int>(static_cast<int64_t>(ntiles) * (split + 1) / splits);
-  const int nt = min(te - tb, kMaxSplitPages);
-  const int* bt = tab.block_table[s];
-  for (int i = lane; i < nt; i += 32) pages[i] = bt[tb + i];
-  __syncwarp();
-  const __nv_bfloat16* kc = tab.k_cache[s];
-  const __nv_bfloat16* vc = tab.v_cache[s];
-  const uint32_t sm0 = static_cast<uint32_t>(__cvta_generic_to_shared(&kv_sm[0][0][0]));
 
-  auto load_tile = [&](int i, int st) {
-    const int64_t page = pages[i];
-    const int tok0 = (tb + i) * kPageTok;
-#pragma unroll 4
-    for (int cidx = lane; cidx < 2 * kPageTok * 16; cidx += 32) {
-      const int kv = cidx >> 8, cc = cidx & 255;
-      const int tok = cc >> 4, ch = cc & 15;
-      const bool live = tok0 + tok < L;
-      const __nv_bfloat16* src = (kv ? vc : kc) + ((page * p.page + tok) * p.hkv + kvh) * kD + ch * 8;
-      const uint32_t dst = sm0 + (st * 2 + kv) * kTileBytes + tok * 256 + ((ch ^ (tok & 7)) << 4);
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(live ? src : kc),
-                   "r"(live ? 16 : 0)
-                   : "memory");
+  // Page prefix over the rows (every CTA derives the same unit stream).
+  const int rows = tab.seg.total_rows;
+  if (warp == 0) {
+    int carry = 0;
+    for (int r0 = 0; r0 < rows; r0 += 32) {
+      const int r = r0 + lane;
+      int v = 0;
+      if (r < rows) {
+        const int sg = seg_of_row(tab.seg, r);
+        const int L = *tab.seqlen[sg] + (r - tab.seg.row_start[sg]) + 1;
+        keys[r] = L;
+        v = (L + kPageTok - 1) / kPageTok;
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      if (r < rows) pre[r + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) pre[0] = 0;
+  }
+  __syncthreads();
+  const int64_t total = pre[rows];
+  const int64_t W = attn_units_per_cta(total, gridDim.x, min_units);
+  if (blockIdx.x == 0 && warp == 0) {
+    int* hdr = reinterpret_cast<int*>(part);
+    if (lane == 0) hdr[0] = static_cast<int>(W);
+    for (int r = lane; r <= rows; r += 32) hdr[1 + r] = pre[r];
+  }
+  float* const recs = part + attn_hdr_floats(rows);
+  const int64_t u0 = static_cast<int64_t>(blockIdx.x) * W;
+  const int64_t u1 = min(total, u0 + W);
+  if (u0 >= u1) return;
+  const int nunits = static_cast<int>(u1 - u0);
+  int r_start;
+  {
+    int lo = 0, hi = rows - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (pre[mid] <= u0) lo = mid;
+      else hi = mid - 1;
+    }
+    r_start = lo;
+  }
+  const int t_start = static_cast<int>(u0 - pre[r_start]);
+
+  const int kvh = warp;
+  const uint32_t sm0 = ptx::smem_addr(att_dyn);
+  const uint32_t head_off = kvh * kD * 2;
+  const uint32_t q_off = 2 * kv_bytes + kvh * G * kD * 2;  // this head group's query rows in a stage
+
+  // ---- loads: this warp's slice of unit (lr, lt) into stage `st` ----
+  const int ld_tok = lane >> 4, ld_ch = lane & 15;  // token parity and 16-byte chunk of this lane
+  int lr = r_start, lt = t_start;
+  auto issue = [&](int j) {
+    const int st = j % kStages;
+    const uint32_t ss = sm0 + st * stage_bytes;
+    const int sg = seg_of_row(tab.seg, lr);
+    const int live = min(kPageTok, keys[lr] - lt * kPageTok);
+    const int64_t page = tab.block_table[sg][lt];
+    const int64_t e0 = ((page * p.page + ld_tok) * hkv + kvh) * kD + ld_ch * 8;  // element offset, token ld_tok
+    const __nv_bfloat16* kp = tab.k_cache[sg] + e0;
+    const __nv_bfloat16* vp = tab.v_cache[sg] + e0;
+    const int64_t tstep = 2 * hkv * kD;  // two tokens
+#pragma unroll
+    for (int i = 0; i < kPageTok / 2; ++i) {
+      const int tok = ld_tok + 2 * i;
+      const bool ok = tok < live;
+      const uint32_t d = ss + tok * row_bytes + head_off + ld_ch * 16;
+      ptx::cp_async_16(d, ok ? static_cast<const void*>(kp + i * tstep) : static_cast<const void*>(kp), ok ? 16u : 0u);
+      ptx::cp_async_16(d + kv_bytes, ok ? static_cast<const void*>(vp + i * tstep) : static_cast<const void*>(vp),
+                       ok ? 16u : 0u);
+    }
+    if (j == 0 || lt == 0) {
+      const char* qp = reinterpret_cast<const char*>(p.q_rot + (static_cast<int64_t>(lr) * p.hq + kvh * G) * kD);
+      for (int e = lane; e < G * kD * 2 / 16; e += 32) ptx::cp_async_16(ss + q_off + e * 16, qp + e * 16, 16u);
+    }
+    if (++lt == pre[lr + 1] - pre[lr]) {
+      lt = 0;
+      ++lr;
     }
   };
 #pragma unroll
-  for (int i = 0; i < kAttnStages - 1; ++i) {
-    if (i < nt) load_tile(i, i);
-    asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int i = 0; i < kStages - 1; ++i) {
+    if (i < nunits) issue(i);
+    ptx::cp_async_commit();
   }
 
-  // Q as the A operand: rows = query heads of this kv head (g < G), k = dims.
-  uint32_t qa[8][2];
-  {
-    const bool real = g < G;
-    const __nv_bfloat16* qp = p.q_rot + (static_cast<int64_t>(gr) * p.hq + kvh * G + (real ? g : 0)) * kD;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      qa[ks][0] = real ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 2 * c) : 0u;
-      qa[ks][1] = real ? *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 8 + 2 * c) : 0u;
-    }
-  }
+  const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
+  const int mi = lane >> 3, r8 = lane & 7;  // ldmatrix matrix / row of this lane
   const float sl2 = p.scale * 1.4426950408889634f;
-  float m = -INFINITY, l = 0.f;
-  float o[16][4];
-#pragma unroll
-  for (int nt8 = 0; nt8 < 16; ++nt8) o[nt8][0] = o[nt8][1] = o[nt8][2] = o[nt8][3] = 0.f;
-  // ldmatrix row address pieces of this lane
-  const int mi = lane >> 3, r8 = lane & 7;
-
-  for (int i = 0; i < nt; ++i) {
-    asm volatile("cp.async.wait_group %0;" ::"n"(kAttnStages - 2) : "memory");
+  uint32_t qb[8][2];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads 2c, 2c+1
+  float o[8][4];                                            // O^T tiles: dims 16mt + (g, g+8) x heads (2c, 2c+1)
+  int r = r_start, t = t_start;
+  for (int j = 0; j < nunits; ++j) {
+    ptx::cp_async_wait_group<kStages - 2>();
     __syncwarp();
-    const int nx = i + kAttnStages - 1;
-    if (nx < nt) load_tile(nx, nx % kAttnStages);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    const int st = i % kAttnStages;
-    const uint32_t ks_base = sm0 + (st * 2 + 0) * kTileBytes;
-    const uint32_t vs_base = sm0 + (st * 2 + 1) * kTileBytes;
-    // S = Q K^T for tokens 0-7 (sa) and 8-15 (sb)
+    if (j + kStages - 1 < nunits) issue(j + kStages - 1);
+    ptx::cp_async_commit();
+    const int st = j % kStages;
+    const uint32_t ss = sm0 + st * stage_bytes;
+    const int tiles = pre[r + 1] - pre[r];
+    const int L = keys[r];
+    if (j == 0 || t == 0) {
+      // new piece: Q^T as the B operand (k = dims, n = query head g < G),
+      // fresh softmax state
+      const uint8_t* qs = att_dyn + st * stage_bytes + q_off;
+      const bool real = g < G;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        qb[ks][0] = real ? *reinterpret_cast<const uint32_t*>(qs + (g * kD + ks * 16 + 2 * c) * 2) : 0u;
+        qb[ks][1] = real ? *reinterpret_cast<const uint32_t*>(qs + (g * kD + ks * 16 + 8 + 2 * c) * 2) : 0u;
+      }
+      m0 = m1 = -INFINITY;
+      l0 = l1 = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    }
+    // S^T = K Q^T: A = K rows (tokens) x 16 dims per k-step, two chains
     float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      // matrices: (tok 0-7, dims 16ks..+7), (tok 0-7, +8..15), (tok 8-15, ..), (tok 8-15, +8..)
-      const int tok = (mi >> 1) * 8 + r8;
-      const int ch = ks * 2 + (mi & 1);
-      uint32_t b0a, b1a, b0b, b1b;
-      ldsm_x4(ks_base + tok * 256 + ((ch ^ (tok & 7)) << 4), b0a, b1a, b0b, b1b);
-      mma_bf16_16816(sa, qa[ks][0], 0u, qa[ks][1], 0u, b0a, b1a);
-      mma_bf16_16816(sb, qa[ks][0], 0u, qa[ks][1], 0u, b0b, b1b);
-    }
-    const int tok0 = (tb + i) * kPageTok;
-    float sv[4] = {sa[0] * sl2, sa[1] * sl2, sb[0] * sl2, sb[1] * sl2};
-    const int tk[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      if (tok0 + tk[e] >= L) sv[e] = -INFINITY;
-    float mx = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float mn = fmaxf(m, mx);
-    const float corr = (mn == -INFINITY) ? 1.f : exp2f(m - mn);
-    float pv[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) pv[e] = (mn == -INFINITY) ? 0.f : exp2f(sv[e] - mn);
-    l = l * corr + (pv[0] + pv[1] + pv[2] + pv[3]);
-    m = mn;
-    const uint32_t pa0 = pack_bf16(pv[0], pv[1]), pa2 = pack_bf16(pv[2], pv[3]);
-#pragma unroll
-    for (int nt8 = 0; nt8 < 16; ++nt8) {
-      o[nt8][0] *= corr;
-      o[nt8][1] *= corr;
-    }
-    // O += P V: per 16 dims one ldmatrix.trans x4 ->
-    // (tok 0-7, dims n0..n0+7), (tok 8-15, n0..), (tok 0-7, n0+8..), (tok 8-15, n0+8..)
-#pragma unroll
-    for (int nd = 0; nd < 8; ++nd) {
+    {
       const int tok = (mi & 1) * 8 + r8;
-      const int ch = nd * 2 + (mi >> 1);
-      uint32_t b0a, b1a, b0b, b1b;
-      ldsm_x4_trans(vs_base + tok * 256 + ((ch ^ (tok & 7)) << 4), b0a, b1a, b0b, b1b);
-      mma_bf16_16816(o[2 * nd], pa0, 0u, pa2, 0u, b0a, b1a);
-      mma_bf16_16816(o[2 * nd + 1], pa0, 0u, pa2, 0u, b0b, b1b);
+      const uint32_t a_row = ss + tok * row_bytes + head_off + (mi >> 1) * 16;
+#pragma unroll
+      for (int ks = 0; ks < 8; ks += 2) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        ldsm_x4(a_row + ks * 32, a0, a1, a2, a3);
+        ldsm_x4(a_row + ks * 32 + 32, b0, b1, b2, b3);
+        mma_bf16_16816(sa, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+        mma_bf16_16816(sb, b0, b1, b2, b3, qb[ks + 1][0], qb[ks + 1][1]);
+      }
+    }
+    // online softmax; this thread holds tokens g, g+8 of heads 2c, 2c+1
+    const int tok0 = t * kPageTok;
+    const bool live_lo = tok0 + g < L, live_hi = tok0 + g + 8 < L;
+    float v0 = live_lo ? (sa[0] + sb[0]) * sl2 : -INFINITY;  // tok g,   head 2c
+    float v1 = live_lo ? (sa[1] + sb[1]) * sl2 : -INFINITY;  // tok g,   head 2c+1
+    float v2 = live_hi ? (sa[2] + sb[2]) * sl2 : -INFINITY;  // tok g+8, head 2c
+    float v3 = live_hi ? (sa[3] + sb[3]) * sl2 : -INFINITY;  // tok g+8, head 2c+1
+    float mx0 = fmaxf(v0, v2), mx1 = fmaxf(v1, v3);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float corr0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
+    const float corr1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
+    const float p0 = mn0 == -INFINITY ? 0.f : exp2f(v0 - mn0);
+    const float p2 = mn0 == -INFINITY ? 0.f : exp2f(v2 - mn0);
+    const float p1 = mn1 == -INFINITY ? 0.f : exp2f(v1 - mn1);
+    const float p3 = mn1 == -INFINITY ? 0.f : exp2f(v3 - mn1);
+    l0 = l0 * corr0 + p0 + p2;
+    l1 = l1 * corr1 + p1 + p3;
+    m0 = mn0;
+    m1 = mn1;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      o[mt][0] *= corr0;
+      o[mt][2] *= corr0;
+      o[mt][1] *= corr1;
+      o[mt][3] *= corr1;
+    }
+    // P^T as the B operand: thread (g, c) needs P[head g][tok 2c, 2c+1, 2c+8, 2c+9],
+    // held by lanes (2c, g/2) and (2c+1, g/2) as (tok, tok+8) pairs of heads
+    // 2c', 2c'+1
+    uint32_t pb0, pb1;
+    {
+      const uint32_t xe = pack_bf16(p0, p2), xo = pack_bf16(p1, p3);
+      const int srcA = (2 * c) * 4 + (g >> 1), srcB = srcA + 4;
+      const uint32_t ae = __shfl_sync(0xffffffffu, xe, srcA), ao = __shfl_sync(0xffffffffu, xo, srcA);
+      const uint32_t be = __shfl_sync(0xffffffffu, xe, srcB), bo = __shfl_sync(0xffffffffu, xo, srcB);
+      const uint32_t A = (g & 1) ? ao : ae, B = (g & 1) ? bo : be;
+      pb0 = __byte_perm(A, B, 0x5410);
+      pb1 = __byte_perm(A, B, 0x7632);
+    }
+    // O^T += V^T P^T: A = V^T (16 dims x 16 tokens) via ldmatrix.trans
+    {
+      const int tok = (mi >> 1) * 8 + r8;
+      const uint32_t a_row = ss + kv_bytes + tok * row_bytes + head_off + (mi & 1) * 16;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_trans(a_row + mt * 32, a0, a1, a2, a3);
+        mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+      }
+    }
+    if (j == nunits - 1 || t == tiles - 1) {
+      // end of a piece: its record per query head
+      float lt0 = l0, lt1 = l1;
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        lt0 += __shfl_xor_sync(0xffffffffu, lt0, off);
+        lt1 += __shfl_xor_sync(0xffffffffu, lt1, off);
+      }
+      const int piece = static_cast<int>(blockIdx.x - pre[r] / W);
+      if (piece < max_pieces) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int hg = 2 * c + hh;
+          if (hg >= G) continue;
+          float* rec = recs + ((static_cast<int64_t>(r) * p.hq + kvh * G + hg) * max_pieces + piece) * (kD + 2);
+          if (g == 0) {
+            rec[0] = hh ? m1 : m0;
+            rec[1] = hh ? lt1 : lt0;
+          }
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            rec[2 + mt * 16 + g] = o[mt][hh];
+            rec[2 + mt * 16 + g + 8] = o[mt][2 + hh];
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (++t == tiles) {
+      t = 0;
+      ++r;
     }
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  l += __shfl_xor_sync(0xffffffffu, l, 1);
-  l += __shfl_xor_sync(0xffffffffu, l, 2);
-  if (g >= G) return;
-  const int h = kvh * G + g;
-  float* rec = part + ((static_cast<int64_t>(gr) * p.hq + h) * splits + split) * (kD + 2);
-  if (c == 0) {
-    rec[0] = m;
-    rec[1] = l;
-  }
-#pragma unroll
-  for (int nt8 = 0; nt8 < 16; ++nt8) {
-    rec[2 + nt8 * 8 + 2 * c] = o[nt8][0];
-    rec[2 + nt8 * 8 + 2 * c + 1] = o[nt8][1];
-  }
+  ptx::cp_async_wait_all();
 }
 
-// Merges the context splits of one (row, head): O = sum_s 2^(m_s - M) o_s /
-// sum_s 2^(m_s - M) l_s, written as bf16 to the slot's attention output. With
-// a shrink side (A != nullptr) it also emits this head's share of the O
-// projection's LoRA shrink: ws[row][h][j] = sum_d out[d] * A[h*128 + d, j].
+// Merges the pieces of one (row, head): O = sum_j 2^(m_j - M) o_j /
+// sum_j 2^(m_j - M) l_j, written as bf16 to the slot's attention output. The
+// pieces of a row are found from the header the attention kernel wrote (page
+// prefix over rows, units per CTA). With a shrink side (A != nullptr) it also
+// emits this head's share of the O projection's LoRA shrink:
+// ws[row][h][j] = sum_d out[d] * A[h*128 + d, j]; the adapter rows are read
+// before waiting for the attention kernel.
 __global__ void __launch_bounds__(128) attention_combine_kernel(const __grid_constant__ AttnTable tab,
-                                                                const AttnParams p, int splits,
+                                                                const AttnParams p, int max_pieces,
                                                                 const float* __restrict__ part,
                                                                 const __grid_constant__ ShrinkSide sh) {
-  ptx::grid_dep_wait();
-  ptx::grid_dep_launch();
   const int gr = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int s = seg_of_row(tab.seg, gr);
   const int local = gr - tab.seg.row_start[s];
-  const float* rec = part + (static_cast<int64_t>(gr) * p.hq + h) * splits * (kD + 2);
+  const __nv_bfloat16* A = sh.A[s];
+  const int nvec = sh.r / 8;
+  uint4 av[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    av[j] = (A && j < nvec) ? reinterpret_cast<const uint4*>(A + (static_cast<int64_t>(h) * kD + d) * sh.r)[j]
+                            : make_uint4(0u, 0u, 0u, 0u);
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
+  const int* hdr = reinterpret_cast<const int*>(part);
+  const int W = hdr[0], p0 = hdr[1 + gr], p1 = hdr[2 + gr];
+  const int nch = min((p1 - 1) / W - p0 / W + 1, max_pieces);
+  const float* rec = part + attn_hdr_floats(tab.seg.total_rows) +
+                     (static_cast<int64_t>(gr) * p.hq + h) * max_pieces * (kD + 2);
   float M = -INFINITY;
-  for (int i = 0; i < splits; ++i) M = fmaxf(M, rec[i * (kD + 2)]);
+  for (int i = 0; i < nch; ++i) M = fmaxf(M, rec[i * (kD + 2)]);
   float lsum = 0.f, acc = 0.f;
-  for (int i = 0; i < splits; ++i) {
+  for (int i = 0; i < nch; ++i) {
     const float mi = rec[i * (kD + 2)];
     const float wgt = mi == -INFINITY ? 0.f : exp2f(mi - M);
     lsum += wgt * rec[i * (kD + 2) + 1];
@@ -448,25 +596,29 @@ __global__ void __launch_bounds__(128) attention_combine_kernel(const __grid_con
   }
   const __nv_bfloat16 ob = __float2bfloat16_rn(lsum > 0.f ? acc / lsum : 0.f);
   tab.out[s][static_cast<int64_t>(local) * p.out_stride + h * kD + d] = ob;
-  const __nv_bfloat16* A = sh.A[s];
   if (!A) return;
   // shrink share of this head (r <= 32 columns)
   __shared__ float red[4][32];
   const float x = __bfloat162float(ob);
-  float t[32];
-  const __nv_bfloat16* ar = A + (static_cast<int64_t>(h) * kD + d) * sh.r;
-  for (int j = 0; j < sh.r; j += 8) {
-    float v[8];
-    load8(ar + j, v);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) t[j + e] = x * v[e];
-  }
   const int w = d >> 5, lane = d & 31;
-  for (int j = 0; j < sh.r; ++j) {
-    float v = t[j];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    if (lane == 0) red[w][j] = v;
+  for (int jv = 0; jv < 4; ++jv) {
+    if (jv >= nvec) break;
+    const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&av[jv]);
+#pragma unroll
+    for (int e2 = 0; e2 < 4; ++e2) {
+      const float2 f = __bfloat1622float2(hv[e2]);
+      float t0 = x * f.x, t1 = x * f.y;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        t0 += __shfl_xor_sync(0xffffffffu, t0, off);
+        t1 += __shfl_xor_sync(0xffffffffu, t1, off);
+      }
+      if (lane == 0) {
+        red[w][jv * 8 + 2 * e2] = t0;
+        red[w][jv * 8 + 2 * e2 + 1] = t1;
+      }
+    }
   }
   __syncthreads();
   if (d < sh.r) {
@@ -604,30 +756,86 @@ int launch_rope_append(const AttnTable& tab, const AttnParams& p, cudaStream_t s
   return SWL_OK;
 }
 
+AttnSplit attention_split(int total_rows, int hkv, int max_len) {
+  // Each CTA takes at least chunk_pages pages of the unit stream, so a row of
+  // P pages is cut into at most ceil(P / chunk_pages) + 1 pieces; `chunks`
+  // bounds the pieces of any row (the record stride).
+  (void)total_rows;
+  (void)hkv;
+  AttnSplit a;
+  const int o = g_attn_min_units.load(std::memory_order_relaxed);
+  a.chunk_pages = o > 0 ? o : kMinUnits;
+  const int pages = std::max(1, (max_len + kPageTok - 1) / kPageTok);
+  a.chunks = (pages + a.chunk_pages - 1) / a.chunk_pages + 1;
+  return a;
+}
+
 int attention_splits(int total_rows, int hkv, int max_len) {
-  // One-warp CTAs: enough context splits for ~8 CTAs per SM with at least 2
-  // pages per split, and few enough pages per split for the page-id buffer.
-  const int base = std::max(1, total_rows * hkv);
-  const int pages = (max_len + kPageTok - 1) / kPageTok;
-  int splits = std::max(1, std::min(8 * 148 / base, pages / 2));
-  splits = std::max(splits, (pages + kMaxSplitPages - 1) / kMaxSplitPages);
-  return std::min(splits, 64);
+  return attention_split(total_rows, hkv, max_len).chunks;
 }
 
 int64_t attention_part_floats(int total_rows, int hq, int splits) {
-  return static_cast<int64_t>(total_rows) * hq * splits * (kD + 2);
+  return attn_hdr_floats(total_rows) + static_cast<int64_t>(total_rows) * hq * splits * (kD + 2);
 }
+
+namespace {
+
+int sm_count_attn() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int S>
+int launch_attention_stages(const AttnTable& tab, const AttnParams& p, int grid, size_t smem,
+                            const AttnSplit& sp, cudaStream_t stream) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(paged_attention_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kAttnSmemMax);
+  });
+  if (attr_err != cudaSuccess)
+    return set_error(SWL_ERR_CUDA, "attention: smem attribute: %s", cudaGetErrorString(attr_err));
+  SWL_CUDA_TRY(launch_kernel(paged_attention_kernel<S>, dim3(grid), dim3(p.hkv * 32), smem, stream, 1,
+                             tab, p, sp.chunks, sp.chunk_pages, p.part));
+  return SWL_OK;
+}
+
+}  // namespace
 
 int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream_t stream,
                            const ShrinkSide* shrink) {
   if (tab.seg.total_rows <= 0) return SWL_OK;
-  if (p.head_dim != kD || p.page != kPageTok || p.hq % p.hkv || p.hq / p.hkv > 8)
-    return set_error(SWL_ERR_ARG, "attention: head_dim 128, page 16, at most 8 query heads per kv head");
-  if (p.max_len > 64 * kMaxSplitPages * kPageTok) return set_error(SWL_ERR_ARG, "attention: context too long");
-  const int splits = attention_splits(tab.seg.total_rows, p.hkv, p.max_len);
+  if (p.head_dim != kD || p.page != kPageTok || p.hkv <= 0 || p.hkv > kAttnMaxHkv || p.hq % p.hkv ||
+      p.hq / p.hkv > 8)
+    return set_error(SWL_ERR_ARG, "attention: head_dim 128, page 16, 1..%d kv heads, at most 8 query heads per kv head",
+                     kAttnMaxHkv);
+  if (tab.seg.total_rows > kAttnMaxRows)
+    return set_error(SWL_ERR_ARG, "attention: at most %d token rows per call", kAttnMaxRows);
+  if (p.max_len <= 0 || p.max_len > (1 << 20)) return set_error(SWL_ERR_ARG, "attention: max_len out of range");
+  if (reinterpret_cast<uintptr_t>(p.q_rot) & 15) return set_error(SWL_ERR_ARG, "attention: q must be 16-byte aligned");
+  for (int i = 0; i < tab.seg.nseg; ++i)
+    if ((reinterpret_cast<uintptr_t>(tab.k_cache[i]) | reinterpret_cast<uintptr_t>(tab.v_cache[i])) & 15)
+      return set_error(SWL_ERR_ARG, "attention: KV caches must be 16-byte aligned");
   if (!p.part) return set_error(SWL_ERR_ARG, "attention: missing partial scratch");
-  dim3 grid(tab.seg.total_rows, p.hkv, splits);
-  SWL_CUDA_TRY(launch_kernel(paged_attention_kernel, grid, dim3(32), 0, stream, 1, tab, p, splits, p.part));
+  const AttnSplit sp = attention_split(tab.seg.total_rows, p.hkv, p.max_len);
+  const int stage_bytes = attn_stage_bytes(p.hq, p.hkv);
+  int stages = std::min(kAttnStagesMax, kAttnSmemMax / stage_bytes);
+  if (const int o = g_attn_stages.load(std::memory_order_relaxed)) stages = std::min(stages, o);
+  if (stages < 2) return set_error(SWL_ERR_ARG, "attention: page stage of %d bytes too large", stage_bytes);
+  const size_t smem = static_cast<size_t>(stages) * stage_bytes;
+  // one CTA per SM, but no more CTAs than the units can keep busy
+  const int64_t units_max =
+      static_cast<int64_t>(tab.seg.total_rows) * ((p.max_len + kPageTok - 1) / kPageTok);
+  const int grid = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>((units_max + sp.chunk_pages - 1) / sp.chunk_pages, sm_count_attn())));
+  switch (stages) {
+    case 2: SWL_TRY(launch_attention_stages<2>(tab, p, grid, smem, sp, stream)); break;
+    case 3: SWL_TRY(launch_attention_stages<3>(tab, p, grid, smem, sp, stream)); break;
+    default: SWL_TRY(launch_attention_stages<4>(tab, p, grid, smem, sp, stream)); break;
+  }
   ShrinkSide none;
   if (!shrink) {
     for (int i = 0; i < kMaxSlots; ++i) none.A[i] = nullptr;
@@ -637,7 +845,7 @@ int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream
     return set_error(SWL_ERR_ARG, "attention: shrink rank must be 8..32 in steps of 8");
   }
   SWL_CUDA_TRY(launch_kernel(attention_combine_kernel, dim3(tab.seg.total_rows, p.hq), dim3(kD), 0, stream, 1,
-                             tab, p, splits, static_cast<const float*>(p.part), shrink ? *shrink : none));
+                             tab, p, sp.chunks, static_cast<const float*>(p.part), shrink ? *shrink : none));
   return SWL_OK;
 }
 
@@ -647,6 +855,14 @@ int launch_rms_norm(const NormTable& tab, const __nv_bfloat16* w, int64_t hidden
   if (hidden % 8) return set_error(SWL_ERR_ARG, "rms_norm: hidden must be a multiple of 8");
   SWL_CUDA_TRY(launch_kernel(rms_norm_kernel, dim3(tab.seg.total_rows), dim3(256), 0, stream, 1, tab, w, hidden, eps,
                              x_stride, out_stride));
+  return SWL_OK;
+}
+
+int set_attention_tuning(int chunk_pages, int stages) {
+  if (chunk_pages < 0 || chunk_pages > 4096 || (stages != 0 && (stages < 2 || stages > kAttnStagesMax)))
+    return set_error(SWL_ERR_ARG, "attention tuning: chunk_pages 0..4096, stages 0 or 2..%d", kAttnStagesMax);
+  g_attn_min_units.store(chunk_pages);
+  g_attn_stages.store(stages);
   return SWL_OK;
 }
 

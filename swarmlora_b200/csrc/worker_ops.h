@@ -70,14 +70,21 @@ struct AttnParams {
   int max_pos;
   int max_len;                   // upper bound of any slot's context after this step
   __nv_bfloat16* q_rot;          // [total_rows, Hq * D] scratch for rotated q
-  float* part;                   // per-split records, attention_part_floats() floats
+  float* part;                   // per-chunk records, attention_part_floats() floats
   const void* pf;                // next round's weight to prefetch into L2 (or nullptr)
   int64_t pf_bytes;
 };
 
-// Context splits the attention launch will use, and the fp32 partial-record
-// scratch it needs.
+// Context chunks the attention launch will use (each at most chunk_pages
+// pages of a row's context), and the fp32 partial-record scratch it needs.
+struct AttnSplit {
+  int chunk_pages;
+  int chunks;
+};
+AttnSplit attention_split(int total_rows, int hkv, int max_len);
 int attention_splits(int total_rows, int hkv, int max_len);
+// Overrides of the chunk size (pages) and page-ring depth; 0 = automatic.
+int set_attention_tuning(int chunk_pages, int stages);
 int64_t attention_part_floats(int total_rows, int hq, int splits);
 
 // RMSNorm over rows.

@@ -51,7 +51,7 @@ def test_noalloc_attention_matches_scratch_entry_point(native, cuda):
     lib = native.lib()
     stream = torch.cuda.current_stream().cuda_stream
     cases = [([1000, 3, 513, 77], [1, 1, 1, 1], 11),        # many context splits
-             ([0, 40, 7, 300, 2048, 16], [16, 1, 1, 4, 1, 2], 12)]  # ragged rows, other split count
+             ([0, 40, 7, 300, 1000, 16], [16, 1, 1, 4, 1, 2], 12)]  # ragged rows, other chunk count
     for ctx, rows, seed in cases:
         c = _case(ctx, rows, seed, cuda)
         total = sum(rows)
