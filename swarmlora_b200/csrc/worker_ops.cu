@@ -386,16 +386,19 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
 
   // ---- loads: this warp's slice of unit (lr, lt) into stage `st` ----
   const int ld_tok = lane >> 4, ld_ch = lane & 15;  // token parity and 16-byte chunk of this lane
+  // load position (row lr, page lt), its slot, and its page id fetched one
+  // unit ahead so the copies of a page never wait on the block-table read
   int lr = r_start, lt = t_start;
+  int lsg = seg_of_row(tab.seg, lr);
+  int next_page = tab.block_table[lsg][lt];
   auto issue = [&](int j) {
     const int st = j % kStages;
     const uint32_t ss = sm0 + st * stage_bytes;
-    const int sg = seg_of_row(tab.seg, lr);
     const int live = min(kPageTok, keys[lr] - lt * kPageTok);
-    const int64_t page = tab.block_table[sg][lt];
+    const int64_t page = next_page;
     const int64_t e0 = ((page * p.page + ld_tok) * hkv + kvh) * kD + ld_ch * 8;  // element offset, token ld_tok
-    const __nv_bfloat16* kp = tab.k_cache[sg] + e0;
-    const __nv_bfloat16* vp = tab.v_cache[sg] + e0;
+    const __nv_bfloat16* kp = tab.k_cache[lsg] + e0;
+    const __nv_bfloat16* vp = tab.v_cache[lsg] + e0;
     const int64_t tstep = 2 * hkv * kD;  // two tokens
 #pragma unroll
     for (int i = 0; i < kPageTok / 2; ++i) {
@@ -413,7 +416,9 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
     if (++lt == pre[lr + 1] - pre[lr]) {
       lt = 0;
       ++lr;
+      if (lr < rows) lsg = seg_of_row(tab.seg, lr);
     }
+    if (j + 1 < nunits) next_page = tab.block_table[lsg][lt];
   };
 #pragma unroll
   for (int i = 0; i < kStages - 1; ++i) {
