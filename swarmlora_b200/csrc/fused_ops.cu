@@ -52,7 +52,7 @@ __device__ __forceinline__ void ld8(const __nv_bfloat16* p, float (&v)[8]) {
   }
 }
 
-constexpr int kPartialsMax = 1024;  // floats of one row's shrink partials (splits * n)
+constexpr int kPartialsMax = 2048;  // floats of one row's shrink partials (splits * n)
 
 // Rebuilds the bf16-rounded LoRA intermediate t[0..n) of row gr from `splits`
 // fp32 partials laid out ws[row][split][n]: the CTA stages the row's
@@ -324,89 +324,174 @@ __global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_con
 }
 
 // ---- after the Gate+Up round ----------------------------------------------------------
-// CTA = (row, 512 columns of the SiLU product), thread t the columns
-// t + 128k. The gate and up lora_B rows and the Down shrink's A rows of those
-// columns arrive by three bulk copies; the Down shrink partial of the CTA goes
-// to ws_next[row][blockIdx.y][j].
+// Work units = (token row, block of kGuCols SiLU columns), rows in order. A
+// CTA of kGuCols threads (thread = column) walks an equal contiguous range of
+// units; each unit's operands (gate and up lora_B rows, the Down shrink's A
+// rows, the round's gate and up outputs) stream through a ring of kGuStages
+// shared-memory stages, five bulk copies per unit issued by one thread, so
+// loads of later units overlap the math of the current one. Per unit: LoRA expand + add on gate and up, SiLU(gate) *
+// up written into the Down round's slot input, and the unit's Down shrink
+// partial to ws_next[row][block][j].
+constexpr int kGuCols = 256;
+constexpr int kGuStages = 4;
+
 template <int RANK>
-__global__ void __launch_bounds__(128) gu_silu_shrink_kernel(const __grid_constant__ GuSiluTable tab,
-                                                             const GuSiluParams p) {
-  extern __shared__ __align__(128) uint8_t dsm[];  // bg [512][RANK] | bu [512][RANK] | an [512][R]
+__global__ void __launch_bounds__(kGuCols) gu_silu_shrink_kernel(const __grid_constant__ GuSiluTable tab,
+                                                                 const GuSiluParams p) {
+  extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ float t[2 * 32];
-  __shared__ float buf[kPartialsMax];
-  __shared__ float red[4][32];
-  __shared__ __align__(8) uint64_t bar;
-  constexpr int kColsCta = 512, kCols = 4;
-  const int gr = blockIdx.x;
-  ptx::prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
-  const int s = seg_row(tab.seg, gr);
-  const int64_t local = gr - tab.seg.row_start[s];
-  const __nv_bfloat16* B = tab.B[s];
-  const __nv_bfloat16* A = tab.A_next[s];
+  __shared__ float act_sm[kGuCols];
+  __shared__ float part_sm[kPartialsMax];
   const int R = p.r_next;
-  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kColsCta;
-  const int64_t nc = min(static_cast<int64_t>(kColsCta), p.inter - n0);
-  __nv_bfloat16* bg = reinterpret_cast<__nv_bfloat16*>(dsm);
-  __nv_bfloat16* bu = bg + kColsCta * RANK;
-  __nv_bfloat16* an = bu + kColsCta * RANK;
-  const bool staged = stage_bulk(&bar, bg, B ? B + n0 * RANK : nullptr, static_cast<uint32_t>(nc * RANK * 2),
-                                 bu, B ? B + (n0 + p.inter) * RANK : nullptr, static_cast<uint32_t>(nc * RANK * 2),
-                                 an, A ? A + n0 * R : nullptr, static_cast<uint32_t>(nc * R * 2));
+  // stage: bg [kGuCols][RANK] | bu [kGuCols][RANK] | an [kGuCols][R] | g [kGuCols] | u [kGuCols]
+  const int b_bytes = kGuCols * RANK * 2, a_bytes = kGuCols * R * 2, v_bytes = kGuCols * 2;
+  const int stage_bytes = 2 * b_bytes + a_bytes + 2 * v_bytes;
+  const int tid = threadIdx.x;
   ptx::grid_dep_wait();
   ptx::grid_dep_launch();
-  const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
-  float g[kCols], u[kCols];
-#pragma unroll
-  for (int k = 0; k < kCols; ++k) {
-    const int64_t c = threadIdx.x + k * blockDim.x;
-    g[k] = c < nc ? __bfloat162float(base[n0 + c]) : 0.f;
-    u[k] = c < nc ? __bfloat162float(base[n0 + c + p.inter]) : 0.f;
-  }
-  if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 2 * RANK);
-  else __syncthreads();
-  if (staged) ptx::mbar_wait(&bar, 0, nullptr, 0, 2000000000ull);
-  float a[kCols];
-#pragma unroll
-  for (int k = 0; k < kCols; ++k) {
-    const int64_t c = threadIdx.x + k * blockDim.x;
-    a[k] = 0.f;
-    if (c >= nc) continue;
-    if (B) {
-      g[k] = bfr(g[k] + bfr(smem_dot(t, bg + c * RANK, RANK)));
-      u[k] = bfr(u[k] + bfr(smem_dot(t + RANK, bu + c * RANK, RANK)));
-    }
-    const float sg = bfr(g[k] / (1.f + expf(-g[k])));
-    a[k] = bfr(sg * u[k]);
-    tab.act[s][local * p.act_stride + n0 + c] = __float2bfloat16_rn(a[k]);
-  }
-  if (!A) return;
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int j0 = 0; j0 < 32; j0 += 8) {
-    if (j0 >= R) break;
-    float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int k = 0; k < kCols; ++k) {
-      const int64_t c = threadIdx.x + k * blockDim.x;
-      if (c >= nc) continue;
-      float v[8];
-      ld8(an + c * R + j0, v);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) part[e] = fmaf(a[k], v[e], part[e]);
-    }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float v = part[e];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) red[w][j0 + e] = v;
-    }
+  const int nblk = static_cast<int>((p.inter + kGuCols - 1) / kGuCols);
+  const int total = tab.seg.total_rows * nblk;
+  const int W = (total + gridDim.x - 1) / gridDim.x;
+  const int u0 = blockIdx.x * W;
+  const int u1 = min(total, u0 + W);
+  if (u0 >= u1) return;
+  const int nunits = u1 - u0;
+  __shared__ __align__(8) uint64_t full[kGuStages];
+  if (tid == 0) {
+    for (int i = 0; i < kGuStages; ++i) ptx::mbar_init(&full[i], 1);
+    ptx::fence_mbar_init();
   }
   __syncthreads();
-  if (threadIdx.x < R) {
-    float v = 0.f;
-    for (int ww = 0; ww < static_cast<int>(blockDim.x >> 5); ++ww) v += red[ww][threadIdx.x];
-    p.ws_next[(static_cast<int64_t>(gr) * gridDim.y + blockIdx.y) * R + threadIdx.x] = v;
+
+  // Thread 0 stages unit j with five bulk copies (gate and up lora_B rows,
+  // Down shrink A rows, gate and up round outputs) on the stage's mbarrier.
+  int l_gr = u0 / nblk, l_blk = u0 - l_gr * nblk;
+  int l_s = seg_row(tab.seg, l_gr);
+  auto issue = [&](int j) {
+    const int64_t local = l_gr - tab.seg.row_start[l_s];
+    const int64_t n0 = static_cast<int64_t>(l_blk) * kGuCols;
+    const int nc = static_cast<int>(min(static_cast<int64_t>(kGuCols), p.inter - n0));
+    uint8_t* ss = dsm + (j % kGuStages) * stage_bytes;
+    uint64_t* bar = &full[j % kGuStages];
+    const __nv_bfloat16* B = tab.B[l_s];
+    const __nv_bfloat16* A = tab.A_next[l_s];
+    const uint32_t bb = static_cast<uint32_t>(nc) * RANK * 2, ab = static_cast<uint32_t>(nc) * R * 2,
+                   vb = static_cast<uint32_t>(nc) * 2;
+    ptx::mbar_arrive_expect_tx(bar, (B ? 2 * bb : 0u) + (A ? ab : 0u) + 2 * vb);
+    if (B) {
+      ptx::bulk_load(ss, B + n0 * RANK, bb, bar);
+      ptx::bulk_load(ss + b_bytes, B + (n0 + p.inter) * RANK, bb, bar);
+    }
+    if (A) ptx::bulk_load(ss + 2 * b_bytes, A + n0 * R, ab, bar);
+    const __nv_bfloat16* base = tab.base[l_s] + local * p.base_stride + n0;
+    ptx::bulk_load(ss + 2 * b_bytes + a_bytes, base, vb, bar);
+    ptx::bulk_load(ss + 2 * b_bytes + a_bytes + v_bytes, base + p.inter, vb, bar);
+    if (++l_blk == nblk) {
+      l_blk = 0;
+      if (++l_gr < tab.seg.total_rows) l_s = seg_row(tab.seg, l_gr);
+    }
+  };
+  if (tid == 0)
+    for (int i = 0; i < kGuStages - 1 && i < nunits; ++i) issue(i);
+
+  // shrink mapping: thread = (pair of partial columns jp, column group cg of 32)
+  const int sjp = tid >> 5, scg = tid & 31;
+  int gr = u0 / nblk, blk = u0 - gr * nblk;
+  int s = seg_row(tab.seg, gr);
+  int cur_row = -1;
+  float tg[RANK], tu[RANK];
+  for (int j = 0; j < nunits; ++j) {
+    __syncthreads();  // every thread is done with unit j-1: its stage may be refilled
+    if (tid == 0 && j + kGuStages - 1 < nunits) issue(j + kGuStages - 1);
+    ptx::mbar_wait(&full[j % kGuStages], (j / kGuStages) & 1, nullptr, 0, 2000000000ull);
+    const int64_t local = gr - tab.seg.row_start[s];
+    const int64_t n0 = static_cast<int64_t>(blk) * kGuCols;
+    const int nc = static_cast<int>(min(static_cast<int64_t>(kGuCols), p.inter - n0));
+    const __nv_bfloat16* B = tab.B[s];
+    const __nv_bfloat16* A = tab.A_next[s];
+    if (B && gr != cur_row) {
+      // this row's gate and up LoRA intermediates, bf16-rounded, from the
+      // shrink partials ws_in[row][split][2 RANK]: all threads fetch the
+      // partials at once, then 2 RANK threads add them in split order
+      const float* src = p.ws_in + static_cast<int64_t>(gr) * p.splits_in * 2 * RANK;
+      for (int e = tid; e < p.splits_in * 2 * RANK; e += kGuCols) part_sm[e] = src[e];
+      __syncthreads();
+      if (tid < 2 * RANK) {
+        float a = 0.f;
+        for (int sp = 0; sp < p.splits_in; ++sp) a += part_sm[sp * 2 * RANK + tid];
+        t[tid] = bfr(a);
+      }
+      __syncthreads();
+#pragma unroll
+      for (int e = 0; e < RANK; ++e) {
+        tg[e] = t[e];
+        tu[e] = t[RANK + e];
+      }
+    }
+    cur_row = gr;
+    const uint8_t* st = dsm + (j % kGuStages) * stage_bytes;
+    const __nv_bfloat16* sg = reinterpret_cast<const __nv_bfloat16*>(st + 2 * b_bytes + a_bytes);
+    const __nv_bfloat16* su = reinterpret_cast<const __nv_bfloat16*>(st + 2 * b_bytes + a_bytes + v_bytes);
+    float a = 0.f;
+    if (tid < nc) {
+      float g = __bfloat162float(sg[tid]), uu = __bfloat162float(su[tid]);
+      if (B) {
+        const uint4* bgr = reinterpret_cast<const uint4*>(st + tid * RANK * 2);
+        const uint4* bur = reinterpret_cast<const uint4*>(st + b_bytes + tid * RANK * 2);
+        float dg = 0.f, du = 0.f;
+#pragma unroll
+        for (int q = 0; q < RANK / 8; ++q) {
+          const uint4 x = bgr[q], y = bur[q];
+          const __nv_bfloat162* hx = reinterpret_cast<const __nv_bfloat162*>(&x);
+          const __nv_bfloat162* hy = reinterpret_cast<const __nv_bfloat162*>(&y);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 fx = __bfloat1622float2(hx[e]), fy = __bfloat1622float2(hy[e]);
+            dg = fmaf(tg[8 * q + 2 * e], fx.x, dg);
+            dg = fmaf(tg[8 * q + 2 * e + 1], fx.y, dg);
+            du = fmaf(tu[8 * q + 2 * e], fy.x, du);
+            du = fmaf(tu[8 * q + 2 * e + 1], fy.y, du);
+          }
+        }
+        g = bfr(g + bfr(dg));
+        uu = bfr(uu + bfr(du));
+      }
+      const float sgm = bfr(g / (1.f + expf(-g)));
+      a = bfr(sgm * uu);
+      tab.act[s][local * p.act_stride + n0 + tid] = __float2bfloat16_rn(a);
+    }
+    if (A) {
+      // Down shrink partial of this block: thread (jp, cg) sums columns
+      // cg, cg + 32, ... for partial columns 2jp, 2jp+1; the 32 groups of a
+      // warp reduce by shuffles
+      act_sm[tid] = a;
+      __syncthreads();
+      const __nv_bfloat16* an = reinterpret_cast<const __nv_bfloat16*>(st + 2 * b_bytes);
+      for (int jp = sjp; 2 * jp < R; jp += kGuCols / 32) {
+        float x0 = 0.f, x1 = 0.f;
+#pragma unroll 4
+        for (int cc = scg; cc < nc; cc += 32) {
+          const float av = act_sm[cc];
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(an + cc * R + 2 * jp));
+          x0 = fmaf(av, f.x, x0);
+          x1 = fmaf(av, f.y, x1);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          x0 += __shfl_xor_sync(0xffffffffu, x0, o);
+          x1 += __shfl_xor_sync(0xffffffffu, x1, o);
+        }
+        if (scg == 0) {
+          float* dst = p.ws_next + (static_cast<int64_t>(gr) * nblk + blk) * R + 2 * jp;
+          dst[0] = x0;
+          dst[1] = x1;
+        }
+      }
+    }
+    if (++blk == nblk) {
+      blk = 0;
+      if (++gr < tab.seg.total_rows) s = seg_row(tab.seg, gr);
+    }
   }
 }
 
@@ -462,32 +547,41 @@ int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p
 int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, cudaStream_t stream) {
   if (tab.seg.total_rows <= 0) return SWL_OK;
   if (p.r_next % 8 || p.r_next > 32) return set_error(SWL_ERR_ARG, "gu_silu: next rank must be 8..32 in steps of 8");
-  if (p.inter % 4) return set_error(SWL_ERR_ARG, "gu_silu: inter must be a multiple of 4");
+  if (p.inter % 8) return set_error(SWL_ERR_ARG, "gu_silu: inter must be a multiple of 8");
   if (p.splits_in * 2 * r > kPartialsMax) return set_error(SWL_ERR_ARG, "gu_silu: too many shrink partials");
-  dim3 grid(tab.seg.total_rows, static_cast<unsigned>((p.inter + 511) / 512));
-  const size_t smem = static_cast<size_t>(512) * (2 * r + p.r_next) * 2;
+  if (r != 8 && r != 16 && r != 32) return set_error(SWL_ERR_ARG, "gu_silu: rank must be 8, 16 or 32");
+  const size_t stage = static_cast<size_t>(kGuCols) * (2 * r + p.r_next) * 2 + 2 * kGuCols * 2;
+  const size_t smem = kGuStages * stage;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int64_t units = static_cast<int64_t>(tab.seg.total_rows) * ((p.inter + kGuCols - 1) / kGuCols);
+  const int per_sm = smem <= 110 * 1024 ? 2 : 1;
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(units, sms * per_sm)));
   cudaError_t ae = cudaSuccess;
   switch (r) {
     case 8:
-      ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      if (ae == cudaSuccess) ae = launch_kernel(gu_silu_shrink_kernel<8>, grid, dim3(128), smem, stream, 1, tab, p);
+      ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (ae == cudaSuccess) ae = launch_kernel(gu_silu_shrink_kernel<8>, dim3(grid), dim3(kGuCols), smem, stream, 1, tab, p);
       break;
     case 16:
-      ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      if (ae == cudaSuccess) ae = launch_kernel(gu_silu_shrink_kernel<16>, grid, dim3(128), smem, stream, 1, tab, p);
+      ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (ae == cudaSuccess) ae = launch_kernel(gu_silu_shrink_kernel<16>, dim3(grid), dim3(kGuCols), smem, stream, 1, tab, p);
       break;
-    case 32:
-      ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      if (ae == cudaSuccess) ae = launch_kernel(gu_silu_shrink_kernel<32>, grid, dim3(128), smem, stream, 1, tab, p);
+    default:
+      ae = cudaFuncSetAttribute(gu_silu_shrink_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (ae == cudaSuccess) ae = launch_kernel(gu_silu_shrink_kernel<32>, dim3(grid), dim3(kGuCols), smem, stream, 1, tab, p);
       break;
-    default: return set_error(SWL_ERR_ARG, "gu_silu: rank must be 8, 16 or 32");
   }
   if (ae != cudaSuccess) return set_error(SWL_ERR_CUDA, "gu_silu: %s", cudaGetErrorString(ae));
-  SWL_CUDA_TRY(cudaGetLastError());
   return SWL_OK;
 }
 
 int resid_norm_splits() { return kCluster; }
-int gu_silu_splits(int64_t inter) { return static_cast<int>((inter + 511) / 512); }
+int gu_silu_splits(int64_t inter) { return static_cast<int>((inter + kGuCols - 1) / kGuCols); }
 
 }  // namespace swl

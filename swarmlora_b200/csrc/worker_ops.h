@@ -177,7 +177,7 @@ struct GuSiluParams {
   const float* ws_in;  // Gate+Up shrink partials [total_rows][splits_in][2 r]
   int splits_in;
   int r_next;
-  float* ws_next;      // [total_rows][ceil(inter / 512)][r_next]
+  float* ws_next;      // [total_rows][gu_silu_splits(inter)][r_next]
   const void* pf;      // next round's weight to prefetch into L2 (or nullptr)
   int64_t pf_bytes;
 };
