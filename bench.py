@@ -418,6 +418,11 @@ def our_arm(args):
     e2e = n * world * args.steps / (e2e_ms / 1e3)
 
     # ---- per-round kernel times (roofline of the dominant kernel) --------------
+    # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one round
+    # launch at this workload, from the capture
+    #   ncu --set full --clock-control none -k regex:slot_round -s 1 -c 1 \
+    #       python bench.py --profile-round gate_up --steps 3 --warmup 1
+    ncu_traffic = {("gate_up", 28): 235_135_488 + 4_879_104}
     rounds = round_phase(grp, cfg)
     peak, peak_kind = measured_peaks()
     dom = max(rounds, key=lambda k: rounds[k]["us"])
@@ -450,7 +455,8 @@ def our_arm(args):
                     "d2h_bytes_per_step": 8 * n},
             "roofline": {"bound": "hbm", "kernel": f"slot_round_tc ({dom} round, M={n})",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "frac": round(achieved / peak, 4), "traffic": ncu_traffic.get((dom, n)),
+                         "traffic_unit": "bytes/launch", "algorithmic_bytes": rounds[dom]["bytes"],
                          "peak_source": peak_kind},
             "gpu_launches": launches,
             "clocks": clk,
