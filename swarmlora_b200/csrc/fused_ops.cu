@@ -28,6 +28,7 @@ namespace swl {
 namespace {
 
 constexpr int kCluster = 8;  // CTAs per row in resid_norm_shrink
+constexpr int kNormThreads = 256;  // threads per resid_norm_shrink CTA
 
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
@@ -211,16 +212,16 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
 // round's lora_B rows and the next shrink's A rows of those columns are
 // staged in shared memory by two bulk copies.
 template <int RANK>
-__global__ void __launch_bounds__(128) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
+__global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
                                                                 const ResidNormParams p) {
   extern __shared__ __align__(128) uint8_t dsm[];  // a_tile [C][R] | b_tile [C][RANK] | xs[C] | red
   __shared__ float t[32];
   __shared__ float buf[kPartialsMax];
   __shared__ float ss_part;
-  __shared__ float warp_ss[4];
+  __shared__ float warp_ss[kNormThreads / 32];
   __shared__ __align__(8) uint64_t bar;
   constexpr int RB = RANK > 0 ? RANK : 8;
-  constexpr int kCols = 4;  // columns per thread (C = 4 * blockDim)
+  constexpr int kCols = 512 / kNormThreads;  // columns per thread (C = 512 = kCols * blockDim)
   const int q = static_cast<int>(ptx::cluster_rank());
   const int gr = blockIdx.x / kCluster;
   ptx::prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
@@ -519,8 +520,8 @@ int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p
   if (p.r_next % 8 || p.r_next > 96) return set_error(SWL_ERR_ARG, "resid_norm: next rank layout must be 8..96 in steps of 8");
   if (p.splits_in * r_in > kPartialsMax) return set_error(SWL_ERR_ARG, "resid_norm: too many shrink partials");
   const int64_t C = p.hidden / kCluster;
-  const int threads = 128;
-  if (C != 4 * threads) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be 4096 (8 CTAs x 128 threads x 4 columns)");
+  const int threads = kNormThreads;
+  if (C != 512) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be 4096 (8 CTAs x 512 columns)");
   const int rb = r_in > 0 ? r_in : 8;
   const size_t smem = C * p.r_next * 2 + C * rb * 2 + (C + static_cast<size_t>(threads) * 8) * sizeof(float);
   if (smem > 200 * 1024) return set_error(SWL_ERR_ARG, "resid_norm: shared memory too large");
