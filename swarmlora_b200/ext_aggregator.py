@@ -146,7 +146,7 @@ def aggregator_main_loop_slots(num_slots: int, dtype_code: int) -> None:
 
 def execute_round(op: int, layer: int, slot_ids, worker_ids, bx, tx, stream=None) -> None:
     """One round over pool slots (what the main loop runs per op), queued on
-    `stream` (a torch.cuda.Stream; None = the library's stream, synchronised)."""
+    `stream` (a torch.cuda.Stream; None = the default stream, waited for)."""
     n = len(slot_ids)
     st = stream.cuda_stream if stream is not None else None
     check(lib().swl_agg_execute_round(int(op), int(layer), n, i32_array(slot_ids), i32_array(worker_ids),
