@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
 template <int RANK>
 __global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
                                                                 const ResidNormParams p) {
-  extern __shared__ __align__(128) uint8_t dsm[];  // a_tile [C][R] | b_tile [C][RANK] | xs[C] | red
+  extern __shared__ __align__(128) uint8_t dsm[];  // a_tile [C][R] | b_tile [C][RANK] | (C floats) | red
   __shared__ float t[32];
   __shared__ float buf[kPartialsMax];
   __shared__ float ss_part;
@@ -234,8 +234,7 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const _
   const __nv_bfloat16* B = RANK > 0 ? tab.B[s] : nullptr;
   __nv_bfloat16* a_tile = reinterpret_cast<__nv_bfloat16*>(dsm);
   __nv_bfloat16* b_tile = a_tile + C * R;
-  float* xs = reinterpret_cast<float*>(b_tile + C * RB);
-  float* red = xs + C;
+  float* red = reinterpret_cast<float*>(b_tile + C * RB) + C;  // [warp][R] shrink sums
   const bool staged = stage_bulk(&bar, a_tile, A ? A + c0 * R : nullptr, static_cast<uint32_t>(C * R * 2),
                                  b_tile, B ? B + c0 * RANK : nullptr, static_cast<uint32_t>(C * RB * 2),
                                  nullptr, nullptr, 0);
@@ -286,39 +285,61 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const _
   }
   const float inv = rsqrtf(total / static_cast<float>(p.hidden) + p.eps);
   __nv_bfloat16* xo = tab.x_out[s] + local * p.x_stride;
+  float xv[kCols];
 #pragma unroll
   for (int k = 0; k < kCols; ++k) {
     const int64_t c = threadIdx.x + k * blockDim.x;
-    const float x = bfr(wv[k] * bfr(v[k] * inv));
-    xs[c] = x;
-    xo[c0 + c] = __float2bfloat16_rn(x);
+    xv[k] = bfr(wv[k] * bfr(v[k] * inv));
+    xo[c0 + c] = __float2bfloat16_rn(xv[k]);
   }
   if (A) {
-    __syncthreads();
-    // next round's LoRA shrink over this CTA's columns: ws_next[gr][q][j]
-    const int G = R / 8;
-    const int kgroups = blockDim.x / G;
-    const int tid = threadIdx.x;
-    const bool active = tid < kgroups * G;
-    const int cg = tid % G, kg = tid / G;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (active) {
-#pragma unroll 4
-      for (int64_t k = kg; k < C; k += kgroups) {
-        float a[8];
-        ld8(a_tile + k * R + cg * 8, a);
-        const float xv = xs[k];
+    // next round's LoRA shrink over this CTA's columns, ws_next[gr][q][j]:
+    // each thread multiplies its columns into their A rows, eight partial
+    // columns at a time; a halving exchange over the warp leaves column
+    // 4*b4 + 2*b3 + b2 (bits of the lane) summed over 8 lanes, two more
+    // steps sum the rest; the warps' sums meet in red
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int jv = 0; jv < R / 8; ++jv) {
+      float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = fmaf(xv, a[e], acc[e]);
+      for (int k = 0; k < kCols; ++k) {
+        const int64_t c = threadIdx.x + k * blockDim.x;
+        const uint4 w4 = *reinterpret_cast<const uint4*>(a_tile + c * R + jv * 8);
+        const uint32_t wq[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          a8[2 * e] = fmaf(xv[k], __uint_as_float(wq[e] << 16), a8[2 * e]);
+          a8[2 * e + 1] = fmaf(xv[k], __uint_as_float(wq[e] & 0xffff0000u), a8[2 * e + 1]);
+        }
       }
-    }
 #pragma unroll
-    for (int e = 0; e < 8; ++e) red[tid * 8 + e] = acc[e];
+      for (int e = 0; e < 4; ++e) {
+        const bool up = lane & 16;
+        const float send = up ? a8[e] : a8[e + 4], kept = up ? a8[e + 4] : a8[e];
+        a8[e] = kept + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool up = lane & 8;
+        const float send = up ? a8[e] : a8[e + 2], kept = up ? a8[e + 2] : a8[e];
+        a8[e] = kept + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      {
+        const bool up = lane & 4;
+        const float send = up ? a8[0] : a8[1], kept = up ? a8[1] : a8[0];
+        a8[0] = kept + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+      a8[0] += __shfl_xor_sync(0xffffffffu, a8[0], 2);
+      a8[0] += __shfl_xor_sync(0xffffffffu, a8[0], 1);
+      if ((lane & 3) == 0)
+        red[warp * R + jv * 8 + ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1)] = a8[0];
+    }
     __syncthreads();
-    for (int j = tid; j < R; j += blockDim.x) {
+    if (threadIdx.x < R) {
       float sum = 0.f;
-      for (int g = 0; g < kgroups; ++g) sum += red[(g * G + j / 8) * 8 + (j & 7)];
-      p.ws_next[(static_cast<int64_t>(gr) * kCluster + q) * R + j] = sum;
+#pragma unroll
+      for (int w = 0; w < kNormThreads / 32; ++w) sum += red[w * R + threadIdx.x];
+      p.ws_next[(static_cast<int64_t>(gr) * kCluster + q) * R + threadIdx.x] = sum;
     }
   }
   ptx::cluster_sync();  // peers may still read ss_part
@@ -330,32 +351,39 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const _
 // units; each unit's operands (gate and up lora_B rows, the Down shrink's A
 // rows, the round's gate and up outputs) stream through a ring of kGuStages
 // shared-memory stages, five bulk copies per unit issued by one thread, so
-// loads of later units overlap the math of the current one. Per unit: LoRA expand + add on gate and up, SiLU(gate) *
-// up written into the Down round's slot input, and the unit's Down shrink
-// partial to ws_next[row][block][j].
+// loads of later units overlap the math of the current one. The adapter
+// copies of the first stages are issued before the wait for the Gate+Up
+// round. Per unit: LoRA expand + add on gate and up, SiLU(gate) * up written
+// into the Down round's slot input, and the unit's Down shrink partial to
+// ws_next[row][block][j] (each thread multiplies its column into its A row,
+// a warp sums its 32 columns by halving exchanges, the 8 warps through
+// shared memory).
 constexpr int kGuCols = 256;
-constexpr int kGuStages = 4;
+constexpr int kGuStages = 2;  // with 4 CTAs per SM (the register limit at 64 per thread)
+constexpr int kGuPartialsMax = 512;  // floats of one row's Gate/Up shrink partials
 
 template <int RANK>
 __global__ void __launch_bounds__(kGuCols) gu_silu_shrink_kernel(const __grid_constant__ GuSiluTable tab,
                                                                  const GuSiluParams p) {
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ float t[2 * 32];
-  __shared__ float act_sm[kGuCols];
-  __shared__ float part_sm[kPartialsMax];
+  __shared__ float red_sm[kGuCols / 32][32];
+  __shared__ float part_sm[kGuPartialsMax];
   const int R = p.r_next;
   // stage: bg [kGuCols][RANK] | bu [kGuCols][RANK] | an [kGuCols][R] | g [kGuCols] | u [kGuCols]
   const int b_bytes = kGuCols * RANK * 2, a_bytes = kGuCols * R * 2, v_bytes = kGuCols * 2;
   const int stage_bytes = 2 * b_bytes + a_bytes + 2 * v_bytes;
-  const int tid = threadIdx.x;
-  ptx::grid_dep_wait();
-  ptx::grid_dep_launch();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nblk = static_cast<int>((p.inter + kGuCols - 1) / kGuCols);
   const int total = tab.seg.total_rows * nblk;
   const int W = (total + gridDim.x - 1) / gridDim.x;
   const int u0 = blockIdx.x * W;
   const int u1 = min(total, u0 + W);
-  if (u0 >= u1) return;
+  if (u0 >= u1) {
+    ptx::grid_dep_wait();
+    ptx::grid_dep_launch();
+    return;
+  }
   const int nunits = u1 - u0;
   __shared__ __align__(8) uint64_t full[kGuStages];
   if (tid == 0) {
@@ -364,46 +392,62 @@ __global__ void __launch_bounds__(kGuCols) gu_silu_shrink_kernel(const __grid_co
   }
   __syncthreads();
 
-  // Thread 0 stages unit j with five bulk copies (gate and up lora_B rows,
-  // Down shrink A rows, gate and up round outputs) on the stage's mbarrier.
-  int l_gr = u0 / nblk, l_blk = u0 - l_gr * nblk;
-  int l_s = seg_row(tab.seg, l_gr);
-  auto issue = [&](int j) {
-    const int64_t local = l_gr - tab.seg.row_start[l_s];
-    const int64_t n0 = static_cast<int64_t>(l_blk) * kGuCols;
-    const int nc = static_cast<int>(min(static_cast<int64_t>(kGuCols), p.inter - n0));
+  // Thread 0 stages unit j on the stage's mbarrier: the adapter rows (gate
+  // and up lora_B, the Down shrink's A) with issue_w, the Gate+Up round's
+  // outputs with issue_v; the mbarrier expects both.
+  auto unit_at = [&](int j, int& gr_, int64_t& n0_, int& nc_, int& s_) {
+    const int u = u0 + j;
+    gr_ = u / nblk;
+    n0_ = static_cast<int64_t>(u - gr_ * nblk) * kGuCols;
+    nc_ = static_cast<int>(min(static_cast<int64_t>(kGuCols), p.inter - n0_));
+    s_ = seg_row(tab.seg, gr_);
+  };
+  auto issue_w = [&](int j) {
+    int gr_, nc_, s_;
+    int64_t n0_;
+    unit_at(j, gr_, n0_, nc_, s_);
     uint8_t* ss = dsm + (j % kGuStages) * stage_bytes;
     uint64_t* bar = &full[j % kGuStages];
-    const __nv_bfloat16* B = tab.B[l_s];
-    const __nv_bfloat16* A = tab.A_next[l_s];
-    const uint32_t bb = static_cast<uint32_t>(nc) * RANK * 2, ab = static_cast<uint32_t>(nc) * R * 2,
-                   vb = static_cast<uint32_t>(nc) * 2;
+    const __nv_bfloat16* B = tab.B[s_];
+    const __nv_bfloat16* A = tab.A_next[s_];
+    const uint32_t bb = static_cast<uint32_t>(nc_) * RANK * 2, ab = static_cast<uint32_t>(nc_) * R * 2,
+                   vb = static_cast<uint32_t>(nc_) * 2;
     ptx::mbar_arrive_expect_tx(bar, (B ? 2 * bb : 0u) + (A ? ab : 0u) + 2 * vb);
     if (B) {
-      ptx::bulk_load(ss, B + n0 * RANK, bb, bar);
-      ptx::bulk_load(ss + b_bytes, B + (n0 + p.inter) * RANK, bb, bar);
+      ptx::bulk_load(ss, B + n0_ * RANK, bb, bar);
+      ptx::bulk_load(ss + b_bytes, B + (n0_ + p.inter) * RANK, bb, bar);
     }
-    if (A) ptx::bulk_load(ss + 2 * b_bytes, A + n0 * R, ab, bar);
-    const __nv_bfloat16* base = tab.base[l_s] + local * p.base_stride + n0;
+    if (A) ptx::bulk_load(ss + 2 * b_bytes, A + n0_ * R, ab, bar);
+  };
+  auto issue_v = [&](int j) {
+    int gr_, nc_, s_;
+    int64_t n0_;
+    unit_at(j, gr_, n0_, nc_, s_);
+    uint8_t* ss = dsm + (j % kGuStages) * stage_bytes;
+    uint64_t* bar = &full[j % kGuStages];
+    const uint32_t vb = static_cast<uint32_t>(nc_) * 2;
+    const __nv_bfloat16* base = tab.base[s_] + (gr_ - tab.seg.row_start[s_]) * p.base_stride + n0_;
     ptx::bulk_load(ss + 2 * b_bytes + a_bytes, base, vb, bar);
     ptx::bulk_load(ss + 2 * b_bytes + a_bytes + v_bytes, base + p.inter, vb, bar);
-    if (++l_blk == nblk) {
-      l_blk = 0;
-      if (++l_gr < tab.seg.total_rows) l_s = seg_row(tab.seg, l_gr);
-    }
   };
+  const int npre = min(kGuStages - 1, nunits);
   if (tid == 0)
-    for (int i = 0; i < kGuStages - 1 && i < nunits; ++i) issue(i);
+    for (int i = 0; i < npre; ++i) issue_w(i);
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
+  if (tid == 0)
+    for (int i = 0; i < npre; ++i) issue_v(i);
 
-  // shrink mapping: thread = (pair of partial columns jp, column group cg of 32)
-  const int sjp = tid >> 5, scg = tid & 31;
   int gr = u0 / nblk, blk = u0 - gr * nblk;
   int s = seg_row(tab.seg, gr);
   int cur_row = -1;
   float tg[RANK], tu[RANK];
   for (int j = 0; j < nunits; ++j) {
     __syncthreads();  // every thread is done with unit j-1: its stage may be refilled
-    if (tid == 0 && j + kGuStages - 1 < nunits) issue(j + kGuStages - 1);
+    if (tid == 0 && j + kGuStages - 1 < nunits) {
+      issue_w(j + kGuStages - 1);
+      issue_v(j + kGuStages - 1);
+    }
     ptx::mbar_wait(&full[j % kGuStages], (j / kGuStages) & 1, nullptr, 0, 2000000000ull);
     const int64_t local = gr - tab.seg.row_start[s];
     const int64_t n0 = static_cast<int64_t>(blk) * kGuCols;
@@ -462,31 +506,50 @@ __global__ void __launch_bounds__(kGuCols) gu_silu_shrink_kernel(const __grid_co
       tab.act[s][local * p.act_stride + n0 + tid] = __float2bfloat16_rn(a);
     }
     if (A) {
-      // Down shrink partial of this block: thread (jp, cg) sums columns
-      // cg, cg + 32, ... for partial columns 2jp, 2jp+1; the 32 groups of a
-      // warp reduce by shuffles
-      act_sm[tid] = a;
-      __syncthreads();
+      // Down shrink partial of this block: column tid times its A row, eight
+      // partial columns at a time; a halving exchange over the warp leaves
+      // column 4*b4 + 2*b3 + b2 (bits of the lane) summed over 8 lanes, two
+      // more steps sum the rest; then the warps' sums meet in red_sm
       const __nv_bfloat16* an = reinterpret_cast<const __nv_bfloat16*>(st + 2 * b_bytes);
-      for (int jp = sjp; 2 * jp < R; jp += kGuCols / 32) {
-        float x0 = 0.f, x1 = 0.f;
-#pragma unroll 4
-        for (int cc = scg; cc < nc; cc += 32) {
-          const float av = act_sm[cc];
-          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(an + cc * R + 2 * jp));
-          x0 = fmaf(av, f.x, x0);
-          x1 = fmaf(av, f.y, x1);
+      for (int jv = 0; jv < R / 8; ++jv) {
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (tid < nc) {
+          const uint4 a4 = *reinterpret_cast<const uint4*>(an + tid * R + jv * 8);
+          const uint32_t w4[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            v[2 * q] = a * __uint_as_float(w4[q] << 16);
+            v[2 * q + 1] = a * __uint_as_float(w4[q] & 0xffff0000u);
+          }
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          x0 += __shfl_xor_sync(0xffffffffu, x0, o);
-          x1 += __shfl_xor_sync(0xffffffffu, x1, o);
+        for (int e = 0; e < 4; ++e) {
+          const bool up = lane & 16;
+          const float send = up ? v[e] : v[e + 4], kept = up ? v[e + 4] : v[e];
+          v[e] = kept + __shfl_xor_sync(0xffffffffu, send, 16);
         }
-        if (scg == 0) {
-          float* dst = p.ws_next + (static_cast<int64_t>(gr) * nblk + blk) * R + 2 * jp;
-          dst[0] = x0;
-          dst[1] = x1;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const bool up = lane & 8;
+          const float send = up ? v[e] : v[e + 2], kept = up ? v[e + 2] : v[e];
+          v[e] = kept + __shfl_xor_sync(0xffffffffu, send, 8);
         }
+        {
+          const bool up = lane & 4;
+          const float send = up ? v[0] : v[1], kept = up ? v[1] : v[0];
+          v[0] = kept + __shfl_xor_sync(0xffffffffu, send, 4);
+        }
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+        if ((lane & 3) == 0)
+          red_sm[warp][jv * 8 + ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1)] = v[0];
+      }
+      __syncthreads();
+      if (tid < R) {
+        float x = 0.f;
+#pragma unroll
+        for (int w = 0; w < kGuCols / 32; ++w) x += red_sm[w][tid];
+        p.ws_next[(static_cast<int64_t>(gr) * nblk + blk) * R + tid] = x;
       }
     }
     if (++blk == nblk) {
@@ -549,7 +612,7 @@ int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, 
   if (tab.seg.total_rows <= 0) return SWL_OK;
   if (p.r_next % 8 || p.r_next > 32) return set_error(SWL_ERR_ARG, "gu_silu: next rank must be 8..32 in steps of 8");
   if (p.inter % 8) return set_error(SWL_ERR_ARG, "gu_silu: inter must be a multiple of 8");
-  if (p.splits_in * 2 * r > kPartialsMax) return set_error(SWL_ERR_ARG, "gu_silu: too many shrink partials");
+  if (p.splits_in * 2 * r > kGuPartialsMax) return set_error(SWL_ERR_ARG, "gu_silu: too many shrink partials");
   if (r != 8 && r != 16 && r != 32) return set_error(SWL_ERR_ARG, "gu_silu: rank must be 8, 16 or 32");
   const size_t stage = static_cast<size_t>(kGuCols) * (2 * r + p.r_next) * 2 + 2 * kGuCols * 2;
   const size_t smem = kGuStages * stage;
@@ -561,7 +624,8 @@ int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, 
     if (sms <= 0) sms = 148;
   }
   const int64_t units = static_cast<int64_t>(tab.seg.total_rows) * ((p.inter + kGuCols - 1) / kGuCols);
-  const int per_sm = smem <= 110 * 1024 ? 2 : 1;
+  // CTAs one SM holds (227 KB of shared memory, ~4 KB static and reserved per CTA)
+  const int per_sm = static_cast<int>(std::max<size_t>(1, std::min<size_t>(4, (227 * 1024) / (smem + 4096))));
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(units, sms * per_sm)));
   cudaError_t ae = cudaSuccess;
   switch (r) {
