@@ -233,7 +233,11 @@ int swl_attention_tune(int chunk_pages, int stages);
 /* fp32 scratch floats swl_paged_attention needs in `part`. */
 int64_t swl_attention_part_floats(int total_rows, int hq, int hkv, int max_len);
 /* Causal GQA attention over paged KV (flash_attn_with_kvcache semantics,
- * worker_sync.py:196-203); `part` is caller scratch. */
+ * worker_sync.py:196-203); `part` is caller scratch. The context lengths and
+ * block tables are read before the launch waits for the kernel launched just
+ * ahead of it on the stream (programmatic dependent launch): that launch,
+ * when it is one of this library's kernels, must not write them (the
+ * RoPE/append launches that normally precede attention do not). */
 int swl_paged_attention(int nseg, const int* rows, const void* const* block_tables,
                         const void* const* k_cache, const void* const* v_cache,
                         const void* const* seqlens, void* const* out, int64_t out_stride, int hq,
@@ -269,7 +273,10 @@ int swl_paged_attention_shrink(int nseg, const int* rows, const void* const* blo
 int swl_rms_norm(int nseg, const int* rows, const void* const* x, int64_t x_stride,
                  void* const* out, int64_t out_stride, const void* w, int64_t hidden, float eps,
                  void* stream);
-/* Fused round epilogues (one launch between two rounds; worker_sync.py:1337-1409). */
+/* Fused round epilogues (one launch between two rounds; worker_sync.py:1337-1409).
+ * Each reads its adapters (and swl_fused_qkv_rope the context lengths, block
+ * tables and cos/sin cache) before waiting for the round launched just ahead
+ * of it, which must not write them. */
 int swl_fused_qkv_rope(int nseg, const int* rows, const void* const* base, int64_t base_stride,
                        const void* const* B, int r, const float* ws_in, int splits_in,
                        const void* const* block_tables, void* const* k_cache,

@@ -163,20 +163,32 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
   const int64_t ncols = min(static_cast<int64_t>(4 * p.head_dim), static_cast<int64_t>(heads) * p.head_dim - col0);
   const bool staged = B && stage_bulk(&bar, bs, B + col0 * RANK, static_cast<uint32_t>(ncols * RANK * 2),
                                       nullptr, nullptr, 0, nullptr, nullptr, 0);
-  ptx::grid_dep_wait();
-  ptx::grid_dep_launch();
   const int pi = blockIdx.y * blockDim.x + threadIdx.x;
   const bool live = pi < heads * half;
   const int head = live ? pi / half : 0, d = pi % half;
   const int blk = head < p.hq ? 0 : (head < p.hq + p.hkv ? 1 : 2);
   const int64_t n1 = static_cast<int64_t>(head) * p.head_dim + d, n2 = n1 + half;
+  // The token's position, its cos/sin and its cache page come from tables the
+  // QKV round ahead of this launch does not write: read before waiting for it.
+  const int pos = *tab.seqlen[s] + static_cast<int>(local);
+  float c = 0.f, sn = 0.f;
+  int page = 0;
+  if (live) {
+    if (blk != 2) {
+      const __nv_bfloat16* cs = p.cos_sin + static_cast<int64_t>(pos) * p.head_dim;
+      c = __bfloat162float(cs[d]);
+      sn = __bfloat162float(cs[half + d]);
+    }
+    if (blk != 0) page = tab.block_table[s][pos / p.page];
+  }
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
   const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
   float x1 = 0.f, x2 = 0.f;
   if (live) {
     x1 = __bfloat162float(base[n1]);
     x2 = __bfloat162float(base[n2]);
   }
-  const int pos = *tab.seqlen[s] + static_cast<int>(local);
   if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 3 * RANK);
   if (staged) ptx::mbar_wait(&bar, 0, nullptr, 0, 2000000000ull);
   if (!live) return;
@@ -185,21 +197,17 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
     x2 = bfr(x2 + bfr(smem_dot(t + blk * RANK, bs + (n2 - col0) * RANK, RANK)));
   }
   if (blk == 2) {
-    const int page = tab.block_table[s][pos / p.page];
     const int64_t row = ((static_cast<int64_t>(page) * p.page + pos % p.page) * p.hkv + (head - p.hq - p.hkv)) * p.head_dim;
     tab.v_cache[s][row + d] = __float2bfloat16_rn(x1);
     tab.v_cache[s][row + d + half] = __float2bfloat16_rn(x2);
     return;
   }
-  const __nv_bfloat16* cs = p.cos_sin + static_cast<int64_t>(pos) * p.head_dim;
-  const float c = __bfloat162float(cs[d]), sn = __bfloat162float(cs[half + d]);
   const float o1 = bfr(bfr(x1 * c) - bfr(x2 * sn));
   const float o2 = bfr(bfr(x2 * c) + bfr(x1 * sn));
   __nv_bfloat16* dst;
   if (blk == 0) {
     dst = p.q_rot + (static_cast<int64_t>(gr) * p.hq + head) * p.head_dim;
   } else {
-    const int page = tab.block_table[s][pos / p.page];
     dst = tab.k_cache[s] + ((static_cast<int64_t>(page) * p.page + pos % p.page) * p.hkv + (head - p.hq)) * p.head_dim;
   }
   dst[d] = __float2bfloat16_rn(o1);

@@ -3,8 +3,12 @@
 // swl_set_pdl(0), programmatic stream serialization, so a kernel's prologue
 // (barrier setup, TMEM allocation, weight and adapter tile loads) overlaps the
 // tail of the kernel before it. Every kernel launched this way calls
-// ptx::grid_dep_wait() before reading anything an earlier kernel writes and
-// before its first global write.
+// ptx::grid_dep_wait() before its first global write and before reading
+// anything the launch just ahead of it may write, and lets the next kernel
+// start only after that wait; so when a kernel starts, every launch two or
+// more places ahead of it on the stream has completed. The prologues use
+// this to read, before their wait, data only such earlier launches write
+// (weights, adapters, context lengths, block tables, the cos/sin cache).
 #pragma once
 
 #include <cuda_runtime.h>

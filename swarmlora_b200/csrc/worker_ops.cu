@@ -328,10 +328,12 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   const int row_bytes = attn_row_bytes(hkv);
   const int kv_bytes = kPageTok * row_bytes;
   const int stage_bytes = attn_stage_bytes(p.hq, hkv);
-  ptx::grid_dep_wait();
-  ptx::grid_dep_launch();
 
-  // Page prefix over the rows (every CTA derives the same unit stream).
+  // Page prefix over the rows (every CTA derives the same unit stream). The
+  // context lengths and block tables are not written by the launch just
+  // ahead of this one (that launch writes the new tokens' K/V and q): the
+  // prefix, this CTA's range and its first page id are set up before
+  // waiting for it.
   const int rows = tab.seg.total_rows;
   if (warp == 0) {
     int carry = 0;
@@ -357,16 +359,11 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   __syncthreads();
   const int64_t total = pre[rows];
   const int64_t W = attn_units_per_cta(total, gridDim.x, min_units);
-  if (blockIdx.x == 0 && warp == 0) {
-    int* hdr = reinterpret_cast<int*>(part);
-    if (lane == 0) hdr[0] = static_cast<int>(W);
-    for (int r = lane; r <= rows; r += 32) hdr[1 + r] = pre[r];
-  }
   float* const recs = part + attn_hdr_floats(rows);
   const int64_t u0 = static_cast<int64_t>(blockIdx.x) * W;
   const int64_t u1 = min(total, u0 + W);
-  if (u0 >= u1) return;
-  const int nunits = static_cast<int>(u1 - u0);
+  const bool idle = u0 >= u1;
+  const int nunits = idle ? 0 : static_cast<int>(u1 - u0);
   int r_start;
   {
     int lo = 0, hi = rows - 1;
@@ -390,7 +387,15 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   // unit ahead so the copies of a page never wait on the block-table read
   int lr = r_start, lt = t_start;
   int lsg = seg_of_row(tab.seg, lr);
-  int next_page = tab.block_table[lsg][lt];
+  int next_page = idle ? 0 : tab.block_table[lsg][lt];
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
+  if (blockIdx.x == 0 && warp == 0) {
+    int* hdr = reinterpret_cast<int*>(part);
+    if (lane == 0) hdr[0] = static_cast<int>(W);
+    for (int r = lane; r <= rows; r += 32) hdr[1 + r] = pre[r];
+  }
+  if (idle) return;
   auto issue = [&](int j) {
     const int st = j % kStages;
     const uint32_t ss = sm0 + st * stage_bytes;
@@ -585,19 +590,44 @@ __global__ void __launch_bounds__(128) attention_combine_kernel(const __grid_con
                             : make_uint4(0u, 0u, 0u, 0u);
   ptx::grid_dep_wait();
   ptx::grid_dep_launch();
+  // The header and the first kBatch records are loaded together (a record
+  // slot past the row's piece count holds stale data and is not used), so
+  // the common case costs one round trip to L2.
+  constexpr int kBatch = 12;
   const int* hdr = reinterpret_cast<const int*>(part);
-  const int W = hdr[0], p0 = hdr[1 + gr], p1 = hdr[2 + gr];
-  const int nch = min((p1 - 1) / W - p0 / W + 1, max_pieces);
   const float* rec = part + attn_hdr_floats(tab.seg.total_rows) +
                      (static_cast<int64_t>(gr) * p.hq + h) * max_pieces * (kD + 2);
-  float M = -INFINITY;
-  for (int i = 0; i < nch; ++i) M = fmaxf(M, rec[i * (kD + 2)]);
-  float lsum = 0.f, acc = 0.f;
-  for (int i = 0; i < nch; ++i) {
-    const float mi = rec[i * (kD + 2)];
-    const float wgt = mi == -INFINITY ? 0.f : exp2f(mi - M);
-    lsum += wgt * rec[i * (kD + 2) + 1];
-    acc += wgt * rec[i * (kD + 2) + 2 + d];
+  float mv[kBatch], lv[kBatch], ov[kBatch];
+#pragma unroll
+  for (int i = 0; i < kBatch; ++i) {
+    const bool in = i < max_pieces;
+    mv[i] = in ? rec[i * (kD + 2)] : 0.f;
+    lv[i] = in ? rec[i * (kD + 2) + 1] : 0.f;
+    ov[i] = in ? rec[i * (kD + 2) + 2 + d] : 0.f;
+  }
+  const int W = hdr[0], p0 = hdr[1 + gr], p1 = hdr[2 + gr];
+  const int nch = min((p1 - 1) / W - p0 / W + 1, max_pieces);
+  float M = -INFINITY, lsum = 0.f, acc = 0.f;
+  if (nch <= kBatch) {
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i)
+      if (i < nch) M = fmaxf(M, mv[i]);
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      if (i < nch) {
+        const float wgt = mv[i] == -INFINITY ? 0.f : exp2f(mv[i] - M);
+        lsum += wgt * lv[i];
+        acc += wgt * ov[i];
+      }
+    }
+  } else {
+    for (int i = 0; i < nch; ++i) M = fmaxf(M, rec[i * (kD + 2)]);
+    for (int i = 0; i < nch; ++i) {
+      const float mi = rec[i * (kD + 2)];
+      const float wgt = mi == -INFINITY ? 0.f : exp2f(mi - M);
+      lsum += wgt * rec[i * (kD + 2) + 1];
+      acc += wgt * rec[i * (kD + 2) + 2 + d];
+    }
   }
   const __nv_bfloat16 ob = __float2bfloat16_rn(lsum > 0.f ? acc / lsum : 0.f);
   tab.out[s][static_cast<int64_t>(local) * p.out_stride + h * kD + d] = ob;
