@@ -274,9 +274,11 @@ int swl_rms_norm(int nseg, const int* rows, const void* const* x, int64_t x_stri
                  void* const* out, int64_t out_stride, const void* w, int64_t hidden, float eps,
                  void* stream);
 /* Fused round epilogues (one launch between two rounds; worker_sync.py:1337-1409).
- * Each reads its adapters (and swl_fused_qkv_rope the context lengths, block
- * tables and cos/sin cache) before waiting for the round launched just ahead
- * of it, which must not write them. */
+ * Each reads its adapters and the shrink partials of its round's input
+ * (swl_fused_resid_norm_shrink also the residual and norm weight,
+ * swl_fused_qkv_rope the context lengths, block tables and cos/sin cache)
+ * before waiting for the round launched just ahead of it, which must not
+ * write them. */
 int swl_fused_qkv_rope(int nseg, const int* rows, const void* const* base, int64_t base_stride,
                        const void* const* B, int r, const float* ws_in, int splits_in,
                        const void* const* block_tables, void* const* k_cache,

@@ -181,6 +181,9 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
     }
     if (blk != 0) page = tab.block_table[s][pos / p.page];
   }
+  // the LoRA intermediate of the QKV input: shrink partials written two
+  // launches back, by the epilogue ahead of the QKV round
+  if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 3 * RANK);
   ptx::grid_dep_wait();
   ptx::grid_dep_launch();
   const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
@@ -189,7 +192,6 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
     x1 = __bfloat162float(base[n1]);
     x2 = __bfloat162float(base[n2]);
   }
-  if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, 3 * RANK);
   if (staged) ptx::mbar_wait(&bar, 0, nullptr, 0, 2000000000ull);
   if (!live) return;
   if (B) {
@@ -246,20 +248,24 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const _
   const bool staged = stage_bulk(&bar, a_tile, A ? A + c0 * R : nullptr, static_cast<uint32_t>(C * R * 2),
                                  b_tile, B ? B + c0 * RANK : nullptr, static_cast<uint32_t>(C * RB * 2),
                                  nullptr, nullptr, 0);
-  ptx::grid_dep_wait();
-  ptx::grid_dep_launch();
-  const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
+  // The residual, the norm weight and the finished round's shrink partials
+  // are written two or more launches back: read them before waiting for the
+  // round just ahead, whose output (base) is read after.
   __nv_bfloat16* h = tab.h[s] + local * p.h_stride;
   float v[kCols], rv[kCols], wv[kCols];
 #pragma unroll
   for (int k = 0; k < kCols; ++k) {
     const int64_t n = c0 + threadIdx.x + k * blockDim.x;
-    v[k] = __bfloat162float(base[n]);
     rv[k] = p.has_resid ? __bfloat162float(h[n]) : 0.f;
     wv[k] = __bfloat162float(p.w[n]);
   }
   if (B) rebuild_t(t, buf, p.ws_in, p.splits_in, gr, RANK);
   else __syncthreads();  // barrier init visible before anyone waits on it
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
+  const __nv_bfloat16* base = tab.base[s] + local * p.base_stride;
+#pragma unroll
+  for (int k = 0; k < kCols; ++k) v[k] = __bfloat162float(base[c0 + threadIdx.x + k * blockDim.x]);
   if (staged) ptx::mbar_wait(&bar, 0, nullptr, 0, 2000000000ull);
   float ss = 0.f;
 #pragma unroll
@@ -438,18 +444,39 @@ __global__ void __launch_bounds__(kGuCols) gu_silu_shrink_kernel(const __grid_co
     ptx::bulk_load(ss + 2 * b_bytes + a_bytes, base, vb, bar);
     ptx::bulk_load(ss + 2 * b_bytes + a_bytes + v_bytes, base + p.inter, vb, bar);
   };
+  // This row's gate and up LoRA intermediates, bf16-rounded, from the shrink
+  // partials ws_in[row][split][2 RANK] (written two launches back, by the
+  // epilogue ahead of the Gate+Up round): all threads fetch the partials at
+  // once, then 2 RANK threads add them in split order.
+  float tg[RANK], tu[RANK];
+  auto load_t = [&](int row) {
+    const float* src = p.ws_in + static_cast<int64_t>(row) * p.splits_in * 2 * RANK;
+    for (int e = tid; e < p.splits_in * 2 * RANK; e += kGuCols) part_sm[e] = src[e];
+    __syncthreads();
+    if (tid < 2 * RANK) {
+      float a = 0.f;
+      for (int sp = 0; sp < p.splits_in; ++sp) a += part_sm[sp * 2 * RANK + tid];
+      t[tid] = bfr(a);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < RANK; ++e) {
+      tg[e] = t[e];
+      tu[e] = t[RANK + e];
+    }
+  };
   const int npre = min(kGuStages - 1, nunits);
   if (tid == 0)
     for (int i = 0; i < npre; ++i) issue_w(i);
+  int gr = u0 / nblk, blk = u0 - gr * nblk;
+  int s = seg_row(tab.seg, gr);
+  if (tab.B[s]) load_t(gr);
+  int cur_row = gr;
   ptx::grid_dep_wait();
   ptx::grid_dep_launch();
   if (tid == 0)
     for (int i = 0; i < npre; ++i) issue_v(i);
 
-  int gr = u0 / nblk, blk = u0 - gr * nblk;
-  int s = seg_row(tab.seg, gr);
-  int cur_row = -1;
-  float tg[RANK], tu[RANK];
   for (int j = 0; j < nunits; ++j) {
     __syncthreads();  // every thread is done with unit j-1: its stage may be refilled
     if (tid == 0 && j + kGuStages - 1 < nunits) {
@@ -462,25 +489,7 @@ __global__ void __launch_bounds__(kGuCols) gu_silu_shrink_kernel(const __grid_co
     const int nc = static_cast<int>(min(static_cast<int64_t>(kGuCols), p.inter - n0));
     const __nv_bfloat16* B = tab.B[s];
     const __nv_bfloat16* A = tab.A_next[s];
-    if (B && gr != cur_row) {
-      // this row's gate and up LoRA intermediates, bf16-rounded, from the
-      // shrink partials ws_in[row][split][2 RANK]: all threads fetch the
-      // partials at once, then 2 RANK threads add them in split order
-      const float* src = p.ws_in + static_cast<int64_t>(gr) * p.splits_in * 2 * RANK;
-      for (int e = tid; e < p.splits_in * 2 * RANK; e += kGuCols) part_sm[e] = src[e];
-      __syncthreads();
-      if (tid < 2 * RANK) {
-        float a = 0.f;
-        for (int sp = 0; sp < p.splits_in; ++sp) a += part_sm[sp * 2 * RANK + tid];
-        t[tid] = bfr(a);
-      }
-      __syncthreads();
-#pragma unroll
-      for (int e = 0; e < RANK; ++e) {
-        tg[e] = t[e];
-        tu[e] = t[RANK + e];
-      }
-    }
+    if (B && gr != cur_row) load_t(gr);
     cur_row = gr;
     const uint8_t* st = dsm + (j % kGuStages) * stage_bytes;
     const __nv_bfloat16* sg = reinterpret_cast<const __nv_bfloat16*>(st + 2 * b_bytes + a_bytes);
