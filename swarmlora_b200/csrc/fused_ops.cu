@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
 template <int RANK>
 __global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
                                                                 const ResidNormParams p) {
-  extern __shared__ __align__(128) uint8_t dsm[];  // a_tile [C][R] | b_tile [C][RANK] | (C floats) | red
+  extern __shared__ __align__(128) uint8_t dsm[];  // a_tile [C][R] | b_tile [C][RANK] | red [warps][R]
   __shared__ float t[32];
   __shared__ float buf[kPartialsMax];
   __shared__ float ss_part;
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const _
   const __nv_bfloat16* B = RANK > 0 ? tab.B[s] : nullptr;
   __nv_bfloat16* a_tile = reinterpret_cast<__nv_bfloat16*>(dsm);
   __nv_bfloat16* b_tile = a_tile + C * R;
-  float* red = reinterpret_cast<float*>(b_tile + C * RB) + C;  // [warp][R] shrink sums
+  float* red = reinterpret_cast<float*>(b_tile + C * RB);  // [warp][R] shrink sums
   const bool staged = stage_bulk(&bar, a_tile, A ? A + c0 * R : nullptr, static_cast<uint32_t>(C * R * 2),
                                  b_tile, B ? B + c0 * RANK : nullptr, static_cast<uint32_t>(C * RB * 2),
                                  nullptr, nullptr, 0);
@@ -297,6 +297,7 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const _
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(ptx::map_peer(my, r)) : "memory");
     total += pv;
   }
+  ptx::cluster_arrive();  // done with the peers' ss_part; waited for before exit
   const float inv = rsqrtf(total / static_cast<float>(p.hidden) + p.eps);
   __nv_bfloat16* xo = tab.x_out[s] + local * p.x_stride;
   float xv[kCols];
@@ -356,7 +357,7 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const _
       p.ws_next[(static_cast<int64_t>(gr) * kCluster + q) * R + threadIdx.x] = sum;
     }
   }
-  ptx::cluster_sync();  // peers may still read ss_part
+  ptx::cluster_wait();  // peers may still read ss_part
 }
 
 // ---- after the Gate+Up round ----------------------------------------------------------
@@ -603,7 +604,7 @@ int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p
   const int threads = kNormThreads;
   if (C != 512) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be 4096 (8 CTAs x 512 columns)");
   const int rb = r_in > 0 ? r_in : 8;
-  const size_t smem = C * p.r_next * 2 + C * rb * 2 + (C + static_cast<size_t>(threads) * 8) * sizeof(float);
+  const size_t smem = C * p.r_next * 2 + C * rb * 2 + static_cast<size_t>(threads / 32) * p.r_next * sizeof(float);
   if (smem > 200 * 1024) return set_error(SWL_ERR_ARG, "resid_norm: shared memory too large");
   cudaError_t ae = cudaSuccess;
   switch (r_in) {

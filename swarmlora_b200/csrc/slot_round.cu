@@ -47,7 +47,7 @@ enum ErrCode : unsigned int {
 
 template <int BN>
 struct TcCfg {
-  static constexpr int kStages = BN == 32 ? 5 : (BN == 64 ? 4 : (BN == 128 ? 6 : 4));
+  static constexpr int kStages = BN == 32 ? 4 : (BN == 64 ? 4 : (BN == 128 ? 6 : 4));
   static constexpr int kXStageBytes = BN * 128;
   static constexpr int kPipeBytes = kStages * (kWStageBytes + kXStageBytes);
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kPipeBytes + 256 + BN * 16;
@@ -262,12 +262,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     *reinterpret_cast<uint2*>(row_out[r] + n) = packed;
   }
 
-  if (splits > 1) ptx::cluster_sync();  // peers may still read our P
+  // Done reading the peers' P; they may still read ours, so the CTA waits
+  // for the whole cluster before it exits (TMEM was last read before the
+  // barrier above, so it is released in between).
+  if (splits > 1) ptx::cluster_arrive();
   else __syncthreads();
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, Cfg::kTmemCols);
   }
+  if (splits > 1) ptx::cluster_wait();
 }
 
 // Plain CUDA-core round: one warp per (output feature, token row). Slow but
