@@ -204,6 +204,10 @@ int swl_ub_cleanup_worker_slots(void);
 int swl_slot_gemm(const void* W, int64_t N, int64_t K, const void* bias, int nslots,
                   const void* const* in_ptrs, void* const* out_ptrs, const int* rows,
                   int64_t in_stride, int64_t out_stride, int algo, int splits, void* stream);
+/* Greedy pick of the LM-head op (ext_aggregator.cpp:821-874, torch.argmax per
+ * row): out[r] (int64, device) = lowest index of the largest bf16 logit of
+ * row r (row stride ld elements); NaN never wins, no finite maximum gives 0. */
+int swl_argmax_rows(const void* logits, int rows, int64_t vocab, int64_t ld, int64_t* out, void* stream);
 /* Bounded-wait status of the round kernels (0 = none ran out); synchronous. */
 int swl_round_device_error(unsigned int* code);
 /* Tuning of the stream-K round (algo 3). */

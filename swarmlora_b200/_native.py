@@ -81,6 +81,7 @@ SIGNATURES: dict[str, tuple] = {
     "swl_ub_cleanup_worker_slots": (_i32, []),
     # ---- kernels callable directly
     "swl_slot_gemm": (_i32, [_p, _i64, _i64, _p, _i32, _pp, _pp, _pi32, _i64, _i64, _i32, _i32, _p]),
+    "swl_argmax_rows": (_i32, [_p, _i32, _i64, _i64, _p, _p]),
     "swl_round_device_error": (_i32, [_pu32]),
     "swl_round_set_streamk_ctas_per_sm": (_i32, [_i32]),
     "swl_round_set_streamk_ctas": (_i32, [_i32]),

@@ -381,7 +381,7 @@ template <int RANK>
 __global__ void __launch_bounds__(kGuCols) gu_silu_shrink_kernel(const __grid_constant__ GuSiluTable tab,
                                                                  const GuSiluParams p) {
   extern __shared__ __align__(128) uint8_t dsm[];
-  __shared__ float t[2 * 32];
+  __shared__ float t[2 * 32], t_next[2 * 32];
   __shared__ float red_sm[kGuCols / 32][32];
   __shared__ float part_sm[kGuPartialsMax];
   const int R = p.r_next;
@@ -445,25 +445,28 @@ __global__ void __launch_bounds__(kGuCols) gu_silu_shrink_kernel(const __grid_co
     ptx::bulk_load(ss + 2 * b_bytes + a_bytes, base, vb, bar);
     ptx::bulk_load(ss + 2 * b_bytes + a_bytes + v_bytes, base + p.inter, vb, bar);
   };
-  // This row's gate and up LoRA intermediates, bf16-rounded, from the shrink
+  // A row's gate and up LoRA intermediates, bf16-rounded, from the shrink
   // partials ws_in[row][split][2 RANK] (written two launches back, by the
   // epilogue ahead of the Gate+Up round): all threads fetch the partials at
-  // once, then 2 RANK threads add them in split order.
+  // once, then 2 RANK threads add them in split order into dst. Ends with a
+  // barrier. The range's first two rows are done before the wait.
   float tg[RANK], tu[RANK];
-  auto load_t = [&](int row) {
+  auto sum_t = [&](int row, float* dst) {
     const float* src = p.ws_in + static_cast<int64_t>(row) * p.splits_in * 2 * RANK;
     for (int e = tid; e < p.splits_in * 2 * RANK; e += kGuCols) part_sm[e] = src[e];
     __syncthreads();
     if (tid < 2 * RANK) {
       float a = 0.f;
       for (int sp = 0; sp < p.splits_in; ++sp) a += part_sm[sp * 2 * RANK + tid];
-      t[tid] = bfr(a);
+      dst[tid] = bfr(a);
     }
     __syncthreads();
+  };
+  auto use_t = [&](const float* src) {
 #pragma unroll
     for (int e = 0; e < RANK; ++e) {
-      tg[e] = t[e];
-      tu[e] = t[RANK + e];
+      tg[e] = src[e];
+      tu[e] = src[RANK + e];
     }
   };
   const int npre = min(kGuStages - 1, nunits);
@@ -471,7 +474,13 @@ __global__ void __launch_bounds__(kGuCols) gu_silu_shrink_kernel(const __grid_co
     for (int i = 0; i < npre; ++i) issue_w(i);
   int gr = u0 / nblk, blk = u0 - gr * nblk;
   int s = seg_row(tab.seg, gr);
-  if (tab.B[s]) load_t(gr);
+  const int r0 = gr;
+  const bool next_pre = (u1 - 1) / nblk > r0 && tab.B[seg_row(tab.seg, r0 + 1)] != nullptr;
+  if (tab.B[s]) {
+    sum_t(r0, t);
+    use_t(t);
+  }
+  if (next_pre) sum_t(r0 + 1, t_next);
   int cur_row = gr;
   ptx::grid_dep_wait();
   ptx::grid_dep_launch();
@@ -490,7 +499,14 @@ __global__ void __launch_bounds__(kGuCols) gu_silu_shrink_kernel(const __grid_co
     const int nc = static_cast<int>(min(static_cast<int64_t>(kGuCols), p.inter - n0));
     const __nv_bfloat16* B = tab.B[s];
     const __nv_bfloat16* A = tab.A_next[s];
-    if (B && gr != cur_row) load_t(gr);
+    if (B && gr != cur_row) {
+      if (gr == r0 + 1 && next_pre) {
+        use_t(t_next);
+      } else {
+        sum_t(gr, t);
+        use_t(t);
+      }
+    }
     cur_row = gr;
     const uint8_t* st = dsm + (j % kGuStages) * stage_bytes;
     const __nv_bfloat16* sg = reinterpret_cast<const __nv_bfloat16*>(st + 2 * b_bytes + a_bytes);
