@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--attn-stages", type=int, default=0, help="attention page-ring depth 2..4 (0 = auto)")
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch every kernel fully serialized (no programmatic dependent launch)")
+    ap.add_argument("--shard", action="store_true",
+                    help="column-sharded base weights over 2 GPUs (one slot group; torchrun, --gpus 2)")
     ap.add_argument("--profile-attention", action="store_true",
                     help="run only --steps paged-attention launches over one layer's KV (small ncu case)")
     return ap.parse_args()
@@ -549,8 +551,78 @@ def profile_attention(args):
     return 0
 
 
+def shard_arm(args):
+    """The multi-GPU configuration's column-sharded variant: ONE slot group
+    served by two GPUs, each holding half of every fused weight's output
+    columns and writing them into both GPUs' slot outputs from the round
+    epilogue (peer stores over NVLink). Prints one JSON line (rank 0)."""
+    import torch
+    world, rank, local = dist_setup(args.gpus)
+    if world != 2:
+        print(json.dumps({"shard": "unavailable", "why": "needs torchrun with 2 ranks (--gpus 2)"}))
+        return 0
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import dataclasses
+    from swarmlora_b200.engine import LLAMA_3_1_8B, SlotGroup, random_adapter, random_base
+    cfg = dataclasses.replace(LLAMA_3_1_8B, layers=args.layers, vocab=args.vocab)
+    n = args.slots
+    g = torch.Generator().manual_seed(1234)  # the same group on both GPUs
+    ctx = [int(c) for c in torch.randint(CTX_LO, CTX_HI + 1, (n,), generator=g)]
+    base = random_base(cfg, seed=1, device=dev)
+    adapters = [random_adapter(cfg, seed=100 + i, device=dev) for i in range(n)]
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=MAX_NEW + args.warmup + args.steps, device=local, seed=0)
+    grp.shard(rank)
+    start_tokens = torch.randint(0, cfg.vocab, (n,), generator=g)
+    grp.tokens.copy_(start_tokens)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        grp.enqueue_step(stream)
+    torch.cuda.synchronize()
+    grp.reset_positions()
+    grp.tokens.copy_(start_tokens)
+    grp.capture(stream)
+    for _ in range(args.warmup):
+        grp.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            grp.replay()
+    ev1.record(stream)
+    ev1.synchronize()
+    ms_max = max_over_ranks(ev0.elapsed_time(ev1), world, dev)
+    rounds = round_phase(grp, cfg)
+    from swarmlora_b200 import rounds as R
+    err = R.device_error()
+    toks = grp.tokens.cpu()
+    both = [None, None]
+    import torch.distributed as dist
+    dist.all_gather_object(both, toks.tolist())
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC + " (column-sharded base weights, one group on 2 GPUs)",
+            "value": round(n * args.steps / (ms_max / 1e3), 2), "unit": UNIT, "n_gpus": 2,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights, adapters, KV contexts)",
+            "config": {"workload": f"Llama-3.1-8B shape ({cfg.layers} layers, vocab {cfg.vocab}), {n} decode slots "
+                                   f"in one group, ctx U[{CTX_LO},{CTX_HI}]",
+                       "parallelism": "column-sharded base weights x2, outputs all-gathered by peer stores "
+                                      "from the round epilogue",
+                       "us_per_round": {k: v["us"] for k, v in rounds.items()}},
+            "ranks_agree": both[0] == both[1], "device_error": err}), flush=True)
+    grp.close()
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
+    if args.shard:
+        return shard_arm(args)
     if args.profile_attention:
         return profile_attention(args)
     if args.profile_round:

@@ -155,6 +155,22 @@ int swl_agg_execute_round(int op, int layer, int n, const int* slot_ids, const i
                           const int64_t* bx, const int64_t* tx, void* stream);
 /* aggregator_main_loop_slots (ext_aggregator.cpp:1024-1210); blocking. */
 int swl_agg_main_loop_slots(int num_slots, int dtype_code);
+/* Column-sharded base weights over a pair of GPUs, one process each (the
+ * multi-GPU configuration's variant with an NVLink all-gather of outputs; no
+ * reference counterpart). After the pool, layers and LM head are set up:
+ * swl_agg_shard_begin builds this GPU's row views (output columns
+ * [rank*N/2, ...)) of every fused weight; swl_agg_shard_handles exports the
+ * IPC handles (64 bytes each: sync words, logits, slot outputs 0..n-1) that
+ * the peer passes to swl_agg_shard_connect, which maps them and switches
+ * every round to the sharded kernel: each GPU computes its half of the
+ * columns and writes it into both GPUs' slot outputs by peer stores. Both
+ * GPUs must then run the same rounds in the same order; a round whose peer
+ * does not follow within 2 s records an error (swl_round_device_error).
+ * swl_agg_shard_end unmaps (call it on both GPUs before freeing a pool). */
+int swl_agg_shard_begin(int rank, int world);
+int swl_agg_shard_handles(unsigned char* out, int max_handles, int* count);
+int swl_agg_shard_connect(const unsigned char* peer, int count);
+int swl_agg_shard_end(void);
 
 /* ======================================================================
  * Worker slot I/O — replaces the pybind module ext_unified_barrier

@@ -64,6 +64,10 @@ SIGNATURES: dict[str, tuple] = {
     "swl_agg_set_round_algo": (_i32, [_i32, _i32]),
     "swl_agg_weight": (_i32, [_i32, _i32, _pp, _pi64, _pi64]),
     "swl_agg_execute_round": (_i32, [_i32, _i32, _i32, _pi32, _pi32, _pi64, _pi64, _p]),
+    "swl_agg_shard_begin": (_i32, [_i32, _i32]),
+    "swl_agg_shard_handles": (_i32, [_p, _i32, _pi32]),
+    "swl_agg_shard_connect": (_i32, [_p, _i32]),
+    "swl_agg_shard_end": (_i32, []),
     "swl_agg_main_loop_slots": (_i32, [_i32, _i32]),
     # ---- ext_unified_barrier
     "swl_ub_init_worker_slot_manager": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32]),

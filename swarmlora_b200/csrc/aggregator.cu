@@ -17,6 +17,7 @@
 #include <sys/mman.h>
 #include <unistd.h>
 
+#include <array>
 #include <chrono>
 #include <cstring>
 #include <map>
@@ -96,6 +97,38 @@ int g_round_algo = kAlgoAuto;
 int g_round_splits = 0;
 std::map<int, SamplingState> g_sampling;  // worker_id -> params (main-loop thread only)
 
+// Column-sharded base weights over two GPUs (one process per GPU; the
+// variant of the multi-GPU configuration with an NVLink all-gather of the
+// outputs): every round reads a row view of the fused weight holding this
+// GPU's half of the output columns and writes those columns into both GPUs'
+// slot outputs (the LM head into both GPUs' logits). The peer's buffers are
+// mapped from the IPC handles it exported; the worker-side kernels run on
+// both GPUs over the same inputs.
+struct ShardView {
+  int64_t col0 = 0, n = 0;
+  CUtensorMap tm;
+};
+struct Shard {
+  bool on = false;
+  int rank = 0;
+  unsigned int* sync = nullptr;       // this GPU's sync words (kSyncWords, zeroed)
+  unsigned int* peer_sync = nullptr;  // the peer's, mapped
+  void* peer_logits = nullptr;        // the peer's LM-head logits, mapped
+  std::vector<void*> peer_out;        // the peer's slot outputs by slot id, mapped
+  std::vector<std::array<ShardView, 4>> layer;  // QKV, O, Gate+Up, Down
+  ShardView lm;
+};
+Shard g_shard;
+
+// This GPU's half of an [N, K] weight: columns [col0, col0 + n), split at a
+// multiple of 8.
+int shard_view(ShardView* v, const void* W, int64_t N, int64_t K, int rank) {
+  const int64_t half = N / 2 / 8 * 8;
+  v->col0 = rank == 0 ? 0 : half;
+  v->n = rank == 0 ? half : N - half;
+  return encode_weight_tmap(&v->tm, static_cast<const char*>(W) + v->col0 * K * 2, v->n, K);
+}
+
 Mask128 load_mask(const std::atomic<uint64_t>* w) {
   return {w[0].load(std::memory_order_acquire), w[1].load(std::memory_order_acquire)};
 }
@@ -150,6 +183,34 @@ void validate(const RoundCmd* cmds, int n, int64_t in_row_bytes, int64_t out_row
   }
 }
 
+// Unmaps the peer's buffers and frees the sync words (back to unsharded rounds).
+int shard_end() {
+  if (!g_shard.sync && !g_shard.on) return SWL_OK;
+  SWL_CUDA_TRY(cudaSetDevice(g_device));
+  SWL_CUDA_TRY(cudaDeviceSynchronize());
+  if (g_shard.peer_sync) cudaIpcCloseMemHandle(g_shard.peer_sync);
+  if (g_shard.peer_logits) cudaIpcCloseMemHandle(g_shard.peer_logits);
+  for (void* q : g_shard.peer_out)
+    if (q) cudaIpcCloseMemHandle(q);
+  if (g_shard.sync) cudaFree(g_shard.sync);
+  g_shard = Shard();
+  return SWL_OK;
+}
+
+// Shard arguments of a round: slot i's peer rows are the peer's output
+// buffer of the same slot id, or row i of the peer's logits (LM head).
+ShardArgs shard_args(const std::vector<RoundCmd>& cmds, int64_t col0, bool logits, int64_t vocab) {
+  ShardArgs a;
+  for (int i = 0; i < kMaxSlots; ++i) a.peer_out[i] = nullptr;
+  for (size_t i = 0; i < cmds.size(); ++i)
+    a.peer_out[i] = logits ? static_cast<__nv_bfloat16*>(g_shard.peer_logits) + static_cast<int64_t>(i) * vocab
+                           : static_cast<__nv_bfloat16*>(g_shard.peer_out[cmds[i].slot_id]);
+  a.col0 = col0;
+  a.sync = g_shard.sync;
+  a.peer_sync = g_shard.peer_sync;
+  return a;
+}
+
 // Runs one round over validated commands on `stream` (no synchronisation).
 int run_round(int op, int layer, const std::vector<RoundCmd>& cmds, cudaStream_t stream) {
   if (cmds.empty()) return SWL_OK;
@@ -185,7 +246,15 @@ int run_round(int op, int layer, const std::vector<RoundCmd>& cmds, cudaStream_t
     tab.row_start[n] = n;
     tab.total_rows = n;
     RoundShape shape{g_vocab, g_embed_hidden, g_embed_hidden, g_vocab, nullptr};
-    SWL_TRY(launch_slot_round(tab, shape, g_lm_head, &g_tm_lm, g_round_algo, g_round_splits, stream));
+    if (g_shard.on) {
+      const ShardView& v = g_shard.lm;
+      shape.N = v.n;
+      const ShardArgs sh = shard_args(cmds, v.col0, true, g_vocab);
+      SWL_TRY(launch_slot_round_shard(tab, shape, static_cast<const char*>(g_lm_head) + v.col0 * g_embed_hidden * 2,
+                                      &v.tm, sh, g_round_splits, stream));
+    } else {
+      SWL_TRY(launch_slot_round(tab, shape, g_lm_head, &g_tm_lm, g_round_algo, g_round_splits, stream));
+    }
     return launch_argmax_rows(g_logits, n, g_vocab, g_vocab, outs, stream);
   }
   if (layer < 0 || layer >= g_num_layers)
@@ -194,21 +263,22 @@ int run_round(int op, int layer, const std::vector<RoundCmd>& cmds, cudaStream_t
   const void* W;
   const CUtensorMap* tm;
   RoundShape shape;
+  int view = 0;
   switch (op) {
     case kOpQkvFused:
-      W = L.qkv; tm = &L.tm_qkv;
+      W = L.qkv; tm = &L.tm_qkv; view = 0;
       shape = {L.q_dim + L.k_dim + L.v_dim, L.hidden, 0, 0, nullptr};
       break;
     case kOpOProj:
-      W = L.o; tm = &L.tm_o;
+      W = L.o; tm = &L.tm_o; view = 1;
       shape = {L.o_out, L.hidden, 0, 0, static_cast<const __nv_bfloat16*>(L.o_bias)};
       break;
     case kOpGateUpFused:
-      W = L.gu; tm = &L.tm_gu;
+      W = L.gu; tm = &L.tm_gu; view = 2;
       shape = {L.gate_dim + L.up_dim, L.hidden, 0, 0, nullptr};
       break;
     case kOpDownProj:
-      W = L.down; tm = &L.tm_down;
+      W = L.down; tm = &L.tm_down; view = 3;
       shape = {L.down_out, L.inter, 0, 0, static_cast<const __nv_bfloat16*>(L.down_bias)};
       break;
     default:
@@ -228,6 +298,14 @@ int run_round(int op, int layer, const std::vector<RoundCmd>& cmds, cudaStream_t
   }
   tab.row_start[n] = acc;
   tab.total_rows = acc;
+  if (g_shard.on) {
+    const ShardView& v = g_shard.layer[layer][view];
+    shape.N = v.n;  // the row stride of the outputs stays the full width
+    if (shape.bias) shape.bias += v.col0;
+    const ShardArgs sh = shard_args(cmds, v.col0, false, 0);
+    return launch_slot_round_shard(tab, shape, static_cast<const char*>(W) + v.col0 * shape.K * 2, &v.tm, sh,
+                                   g_round_splits, stream);
+  }
   return launch_slot_round(tab, shape, W, tm, g_round_algo, g_round_splits, stream);
 }
 
@@ -569,6 +647,90 @@ SWL_EXPORT int swl_agg_execute_round(int op, int layer, int n, const int* slot_i
   if (st == nullptr) SWL_CUDA_TRY(cudaStreamSynchronize(st));
   return SWL_OK;
 }
+
+// ===== column-sharded base weights (two GPUs) ==================================
+
+// After the slot pool, the layers and the LM head are initialised: builds this
+// GPU's row views of every fused weight and of the LM head (no copies) and
+// allocates its sync words. rank is 0 or 1 of a pair of GPUs (world 2). The
+// rounds stay unsharded until swl_agg_shard_connect has mapped the peer.
+SWL_EXPORT int swl_agg_shard_begin(int rank, int world) {
+  if (world != 2 || rank < 0 || rank > 1)
+    return set_error(SWL_ERR_ARG, "shard: a pair of GPUs (world 2, rank 0 or 1) is supported");
+  if (!g_pool.initialized || !g_weights_ready || !g_vocab_ready)
+    return set_error(SWL_ERR_STATE, "shard: initialise the slot pool, the layers and the LM head first");
+  SWL_TRY(shard_end());
+  SWL_CUDA_TRY(cudaSetDevice(g_device));
+  g_shard.rank = rank;
+  g_shard.layer.assign(g_num_layers, {});
+  for (int l = 0; l < g_num_layers; ++l) {
+    const Layer& L = g_layers[l];
+    SWL_TRY(shard_view(&g_shard.layer[l][0], L.qkv, L.q_dim + L.k_dim + L.v_dim, L.hidden, rank));
+    SWL_TRY(shard_view(&g_shard.layer[l][1], L.o, L.o_out, L.hidden, rank));
+    SWL_TRY(shard_view(&g_shard.layer[l][2], L.gu, L.gate_dim + L.up_dim, L.hidden, rank));
+    SWL_TRY(shard_view(&g_shard.layer[l][3], L.down, L.down_out, L.inter, rank));
+  }
+  SWL_TRY(shard_view(&g_shard.lm, g_lm_head, g_vocab, g_embed_hidden, rank));
+  void* p = nullptr;
+  SWL_CUDA_TRY(cudaMalloc(&p, kSyncWords * sizeof(unsigned int)));
+  SWL_CUDA_TRY(cudaMemset(p, 0, kSyncWords * sizeof(unsigned int)));
+  SWL_CUDA_TRY(cudaDeviceSynchronize());
+  g_shard.sync = static_cast<unsigned int*>(p);
+  return SWL_OK;
+}
+
+// IPC handles (64 bytes each) of this GPU's sync words, LM-head logits and
+// slot output buffers (slot ids 0 .. num_slots-1), in that order, for the
+// peer's swl_agg_shard_connect; *count = 2 + num_slots.
+SWL_EXPORT int swl_agg_shard_handles(unsigned char* out, int max_handles, int* count) {
+  if (!g_shard.sync) return set_error(SWL_ERR_STATE, "shard: call swl_agg_shard_begin first");
+  const int need = 2 + g_pool.num_slots;
+  if (count) *count = need;
+  if (!out || max_handles < need) return set_error(SWL_ERR_ARG, "shard: room for %d handles needed", need);
+  cudaIpcMemHandle_t h;
+  SWL_CUDA_TRY(cudaIpcGetMemHandle(&h, g_shard.sync));
+  memcpy(out, &h, sizeof(h));
+  SWL_CUDA_TRY(cudaIpcGetMemHandle(&h, g_logits));
+  memcpy(out + 64, &h, sizeof(h));
+  for (int i = 0; i < g_pool.num_slots; ++i) memcpy(out + 64 * (2 + i), &g_pool.slots[i].out_handle, 64);
+  return SWL_OK;
+}
+
+// Maps the peer's buffers from its handles (the layout of
+// swl_agg_shard_handles) and switches every round to the sharded kernel.
+// From then on both GPUs must run the same rounds in the same order: a
+// round waits for the peer's (with a time limit, after which the kernel
+// records an error that swl_round_device_error reports).
+SWL_EXPORT int swl_agg_shard_connect(const unsigned char* peer, int count) {
+  if (!g_shard.sync) return set_error(SWL_ERR_STATE, "shard: call swl_agg_shard_begin first");
+  if (!peer || count != 2 + g_pool.num_slots)
+    return set_error(SWL_ERR_ARG, "shard: expected %d peer handles", 2 + g_pool.num_slots);
+  if (g_shard.on) return set_error(SWL_ERR_STATE, "shard: already connected");
+  SWL_CUDA_TRY(cudaSetDevice(g_device));
+  auto open = [&](int i, void** ptr) -> int {
+    cudaIpcMemHandle_t h;
+    memcpy(&h, peer + 64 * i, sizeof(h));
+    SWL_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return SWL_OK;
+  };
+  void* p = nullptr;
+  int st = open(0, &p);
+  g_shard.peer_sync = static_cast<unsigned int*>(p);
+  if (st == SWL_OK) st = open(1, &g_shard.peer_logits);
+  g_shard.peer_out.assign(g_pool.num_slots, nullptr);
+  for (int i = 0; st == SWL_OK && i < g_pool.num_slots; ++i) st = open(2 + i, &g_shard.peer_out[i]);
+  if (st != SWL_OK) {
+    const std::string why = last_error();
+    shard_end();
+    return set_error(SWL_ERR_CUDA, "shard: mapping the peer's buffers failed: %s", why.c_str());
+  }
+  g_shard.on = true;
+  return SWL_OK;
+}
+
+// Unmaps the peer's buffers and returns to unsharded rounds. Call it on both
+// GPUs (and wait for both) before either frees its slot pool.
+SWL_EXPORT int swl_agg_shard_end(void) { return shard_end(); }
 
 // ===== main loop ===============================================================
 

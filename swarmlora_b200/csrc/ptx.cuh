@@ -96,6 +96,36 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity,
   }
 }
 
+// ---- flags shared with another GPU (peer memory over NVLink) ------------------
+// Stores `v` with release semantics at system scope: every write this thread
+// ordered before it (including other threads' writes it has synchronised
+// with) is visible to whoever reads the value with acquire semantics.
+__device__ __forceinline__ void st_release_sys(unsigned int* addr, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* addr) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+// Waits until the epoch counter at `addr` reaches `v` (wrap-safe), giving up
+// after `timeout_ns` of device time: then it records `code` in *err_word
+// (first error wins) and returns false; it never spins forever.
+__device__ __forceinline__ bool wait_epoch_sys(const unsigned int* addr, unsigned int v,
+                                               unsigned int* err_word, unsigned int code,
+                                               uint64_t timeout_ns) {
+  if (static_cast<int>(ld_acquire_sys(addr) - v) >= 0) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(64);
+    if (static_cast<int>(ld_acquire_sys(addr) - v) >= 0) return true;
+    if ((it & 63u) == 0 && globaltimer() - t0 > timeout_ns) {
+      if (err_word) atomicCAS(err_word, 0u, code);
+      return false;
+    }
+  }
+}
+
 // ---- TMA ----------------------------------------------------------------------
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");

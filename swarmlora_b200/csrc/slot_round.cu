@@ -43,6 +43,8 @@ enum ErrCode : unsigned int {
   kErrWaitFull = 2,
   kErrWaitEmptyX = 3,
   kErrWaitAcc = 4,
+  kErrWaitPeerStart = 5,  // the peer GPU did not start the same sharded round
+  kErrWaitPeerDone = 6,   // the peer GPU's half of a sharded round did not arrive
 };
 
 template <int BN>
@@ -50,7 +52,7 @@ struct TcCfg {
   static constexpr int kStages = BN == 32 ? 4 : (BN == 64 ? 4 : (BN == 128 ? 6 : 4));
   static constexpr int kXStageBytes = BN * 128;
   static constexpr int kPipeBytes = kStages * (kWStageBytes + kXStageBytes);
-  static constexpr int kSmemBytes = 1024 /*align slack*/ + kPipeBytes + 256 + BN * 16;
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kPipeBytes + 256 + BN * 24;
   static constexpr int kTmemCols = BN;
   static_assert(BN * kBlockW * 4 <= kPipeBytes, "epilogue tile must fit in pipeline smem");
 };
@@ -66,11 +68,11 @@ __device__ __forceinline__ int slot_of_row(const SlotTable& tab, int gr) {
   return lo;
 }
 
-template <int BN>
+template <int BN, bool kShard>
 __global__ void __launch_bounds__(kThreads, 1)
     slot_round_tc_kernel(const __grid_constant__ CUtensorMap wmap,
                          const __grid_constant__ SlotTable tab, const RoundShape shape,
-                         int splits) {
+                         int splits, const __grid_constant__ ShardArgs sh) {
   using Cfg = TcCfg<BN>;
   constexpr int STAGES = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -84,6 +86,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accf + 1);
   const __nv_bfloat16** row_in = reinterpret_cast<const __nv_bfloat16**>(tmem_holder + 2);
   __nv_bfloat16** row_out = reinterpret_cast<__nv_bfloat16**>(tmem_holder + 2 + 2 * BN);
+  __nv_bfloat16** row_peer = reinterpret_cast<__nv_bfloat16**>(tmem_holder + 2 + 4 * BN);
+  __shared__ int shard_ok;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rank = splits > 1 ? static_cast<int>(ptx::cluster_rank()) : 0;
@@ -100,15 +104,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int r = tid; r < BN; r += kThreads) {
     const __nv_bfloat16* pin = nullptr;
     __nv_bfloat16* pout = nullptr;
+    __nv_bfloat16* ppeer = nullptr;
     if (r < chunk_rows) {
       int gr = chunk_row0 + r;
       int s = slot_of_row(tab, gr);
       int64_t local = gr - tab.row_start[s];
       pin = tab.in[s] + local * shape.in_stride;
       pout = tab.out[s] + local * shape.out_stride;
+      if constexpr (kShard) {
+        pout += sh.col0;
+        ppeer = sh.peer_out[s] + local * shape.out_stride + sh.col0;
+      }
     }
     row_in[r] = pin;
     row_out[r] = pout;
+    row_peer[r] = ppeer;
   }
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -140,6 +150,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   ptx::grid_dep_wait();
   ptx::grid_dep_launch();
+  // Sharded round: this is round `epoch` on this GPU (the count of completed
+  // ones is only advanced by this launch's last CTA, after every CTA has read
+  // it). Having passed the dependency wait, this GPU has finished reading the
+  // previous round's outputs, which CTA 0 tells the peer.
+  unsigned int epoch = 0;
+  if constexpr (kShard) {
+    epoch = *reinterpret_cast<volatile unsigned int*>(sh.sync + kSyncEpoch) + 1;
+    if (blockIdx.x == 0 && blockIdx.y == 0 && tid == 0) ptx::st_release_sys(sh.peer_sync + kSyncStart, epoch);
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -224,6 +243,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (splits > 1) ptx::cluster_sync();
   else __syncthreads();
 
+  // Sharded round: the peer may still read its previous round's outputs
+  // until it has started this round; only then do our stores go there.
+  bool to_peer = false;
+  if constexpr (kShard) {
+    if (tid == 0) shard_ok = ptx::wait_epoch_sys(sh.sync + kSyncStart, epoch, err, kErrWaitPeerStart, kWaitTimeoutNs);
+    __syncthreads();
+    to_peer = shard_ok != 0;
+  }
+
   // Each CTA of the cluster reduces an equal share of the tile's 4-float groups.
   const int groups = chunk_rows * (kBlockW / 4);
   const int g_begin = static_cast<int>(static_cast<int64_t>(rank) * groups / splits);
@@ -260,6 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     packed.x = *reinterpret_cast<uint32_t*>(&lo);
     packed.y = *reinterpret_cast<uint32_t*>(&hi);
     *reinterpret_cast<uint2*>(row_out[r] + n) = packed;
+    if (kShard && to_peer) *reinterpret_cast<uint2*>(row_peer[r] + n) = packed;
   }
 
   // Done reading the peers' P; they may still read ours, so the CTA waits
@@ -272,6 +301,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tmem_dealloc(tmem, Cfg::kTmemCols);
   }
   if (splits > 1) ptx::cluster_wait();
+
+  if constexpr (kShard) {
+    // Every thread's peer stores are visible system-wide before its CTA
+    // arrives; the last CTA to arrive publishes the round to the peer and
+    // waits for the peer's half to have landed here.
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+      const unsigned int total = gridDim.x * gridDim.y;
+      if (atomicAdd(sh.sync + kSyncArrive, 1u) == total - 1) {
+        sh.sync[kSyncArrive] = 0;
+        sh.sync[kSyncEpoch] = epoch;
+        __threadfence_system();
+        ptx::st_release_sys(sh.peer_sync + kSyncDone, epoch);
+        ptx::wait_epoch_sys(sh.sync + kSyncDone, epoch, err, kErrWaitPeerDone, kWaitTimeoutNs);
+      }
+    }
+  }
 }
 
 // Plain CUDA-core round: one warp per (output feature, token row). Slow but
@@ -319,21 +366,22 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-template <int BN>
+template <int BN, bool kShard>
 int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& map, int splits,
-              cudaStream_t stream) {
+              const ShardArgs& sh, cudaStream_t stream) {
   using Cfg = TcCfg<BN>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(slot_round_tc_kernel<BN>,
+    attr_err = cudaFuncSetAttribute(slot_round_tc_kernel<BN, kShard>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   });
   if (attr_err != cudaSuccess)
     return set_error(SWL_ERR_CUDA, "slot round: smem attribute: %s", cudaGetErrorString(attr_err));
 
   const int n_tiles = static_cast<int>((shape.N + kBlockW - 1) / kBlockW);
-  const int m_chunks = (tab.total_rows + BN - 1) / BN;
+  // (a sharded round runs even with no rows: the peer waits for its flags)
+  const int m_chunks = std::max(kShard ? 1 : 0, (tab.total_rows + BN - 1) / BN);
   const int nkb = static_cast<int>((shape.K + kBlockK - 1) / kBlockK);
   if (splits <= 0) {
     // Largest power-of-two cluster (<= 8) that keeps the grid within the
@@ -348,11 +396,23 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
   }
   splits = std::max(1, std::min(splits, std::min(8, nkb)));
 
-  SWL_CUDA_TRY(launch_kernel(slot_round_tc_kernel<BN>,
+  SWL_CUDA_TRY(launch_kernel(slot_round_tc_kernel<BN, kShard>,
                              dim3(static_cast<unsigned>(n_tiles * splits), static_cast<unsigned>(m_chunks), 1),
                              dim3(kThreads, 1, 1), Cfg::kSmemBytes, stream, static_cast<unsigned>(splits),
-                             map, tab, shape, splits));
+                             map, tab, shape, splits, sh));
   return SWL_OK;
+}
+
+const ShardArgs& no_shard() {
+  static const ShardArgs none = [] {
+    ShardArgs a;
+    for (int i = 0; i < kMaxSlots; ++i) a.peer_out[i] = nullptr;
+    a.col0 = 0;
+    a.sync = nullptr;
+    a.peer_sync = nullptr;
+    return a;
+  }();
+  return none;
 }
 
 }  // namespace
@@ -398,10 +458,37 @@ int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void*
     if (m > 64) return set_error(SWL_ERR_ARG, "stream-K round: at most 64 token rows");
     return launch_slot_round_streamk(tab, shape, *tmap, stream);
   }
-  if (m <= 32) return launch_tc<32>(tab, shape, *tmap, splits, stream);
-  if (m <= 64) return launch_tc<64>(tab, shape, *tmap, splits, stream);
-  if (m <= 128) return launch_tc<128>(tab, shape, *tmap, splits, stream);
-  return launch_tc<256>(tab, shape, *tmap, splits, stream);
+  if (m <= 32) return launch_tc<32, false>(tab, shape, *tmap, splits, no_shard(), stream);
+  if (m <= 64) return launch_tc<64, false>(tab, shape, *tmap, splits, no_shard(), stream);
+  if (m <= 128) return launch_tc<128, false>(tab, shape, *tmap, splits, no_shard(), stream);
+  return launch_tc<256, false>(tab, shape, *tmap, splits, no_shard(), stream);
+}
+
+int launch_slot_round_shard(const SlotTable& tab, const RoundShape& shape, const void* W,
+                            const CUtensorMap* tmap, const ShardArgs& sh, int splits, cudaStream_t stream) {
+  if (tab.nslots > kMaxSlots) return set_error(SWL_ERR_ARG, "too many slots (%d)", tab.nslots);
+  if (shape.N <= 0 || shape.K <= 0 || (shape.N % 8) != 0 || (shape.K % 8) != 0 || sh.col0 < 0 || (sh.col0 % 4) != 0)
+    return set_error(SWL_ERR_ARG, "sharded round: N=%lld K=%lld col0=%lld must be multiples of 8 (col0 of 4)",
+                     (long long)shape.N, (long long)shape.K, (long long)sh.col0);
+  if (!sh.sync || !sh.peer_sync || (reinterpret_cast<uintptr_t>(sh.sync) & 63) ||
+      (reinterpret_cast<uintptr_t>(sh.peer_sync) & 63))
+    return set_error(SWL_ERR_ARG, "sharded round: sync words missing or not 64-byte aligned");
+  for (int i = 0; i < tab.nslots; ++i) {
+    const bool rows = tab.row_start[i + 1] > tab.row_start[i];
+    if (rows && (!sh.peer_out[i] || (reinterpret_cast<uintptr_t>(sh.peer_out[i]) & 7)))
+      return set_error(SWL_ERR_ARG, "sharded round: peer output of slot %d missing or not 8-byte aligned", i);
+  }
+  // An empty round still takes part in the exchange: the peer waits for it.
+  const int m = std::max(1, tab.total_rows);
+  CUtensorMap local;
+  if (!tmap) {
+    SWL_TRY(encode_weight_tmap(&local, W, shape.N, shape.K));
+    tmap = &local;
+  }
+  if (m <= 32) return launch_tc<32, true>(tab, shape, *tmap, splits, sh, stream);
+  if (m <= 64) return launch_tc<64, true>(tab, shape, *tmap, splits, sh, stream);
+  if (m <= 128) return launch_tc<128, true>(tab, shape, *tmap, splits, sh, stream);
+  return launch_tc<256, true>(tab, shape, *tmap, splits, sh, stream);
 }
 
 int read_and_clear_device_error(unsigned int* code) {

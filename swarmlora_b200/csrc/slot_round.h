@@ -36,6 +36,28 @@ struct RoundShape {
   const __nv_bfloat16* bias;  // [N] or nullptr
 };
 
+// Column shard of a round over two GPUs (the column-sharded base-weight
+// variant): this GPU holds rows [col0, col0 + N) of the fused weight, i.e.
+// output columns [col0, col0 + N), and its epilogue writes them both into its
+// own slot outputs and, by peer stores over NVLink, into the peer GPU's slot
+// outputs (the all-gather of the outputs, fused into the round). Two epoch
+// flags in each GPU's sync words order the exchange: a round stores into the
+// peer only after the peer has started the same round (so the peer's readers
+// of the previous round's outputs are done), and it completes only after the
+// peer's half has landed here.
+struct ShardArgs {
+  __nv_bfloat16* peer_out[kMaxSlots];  // the peer's slot output rows (slot i as tab.out[i])
+  int64_t col0;                        // first output column of this shard
+  unsigned int* sync;                  // this GPU's sync words (kSyncWords, zeroed once)
+  unsigned int* peer_sync;             // the peer's sync words, mapped into this process
+};
+// Sync word offsets (unsigned ints, each on its own 64-byte line).
+constexpr int kSyncArrive = 0;   // CTAs of this round that finished their stores
+constexpr int kSyncEpoch = 16;   // rounds completed on this GPU
+constexpr int kSyncDone = 32;    // written by the peer: rounds whose stores into us landed
+constexpr int kSyncStart = 48;   // written by the peer: rounds the peer has started
+constexpr int kSyncWords = 64;
+
 enum RoundAlgo : int {
   kAlgoAuto = 0,        // cluster split-K (measured faster than stream-K on B200)
   kAlgoTensorCore = 1,  // tcgen05 + TMA, K split across a thread-block cluster (DSMEM reduce)
@@ -51,6 +73,12 @@ int encode_weight_tmap(CUtensorMap* map, const void* W, int64_t N, int64_t K);
 // `splits` <= 0 picks the split-K factor automatically.
 int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void* W,
                       const CUtensorMap* tmap, int algo, int splits, cudaStream_t stream);
+
+// Launches one column-sharded round (tensor-core path only): W is this GPU's
+// [shape.N, K] row block of the fused weight, outputs go to columns
+// sh.col0 + [0, shape.N) of both GPUs' slot outputs.
+int launch_slot_round_shard(const SlotTable& tab, const RoundShape& shape, const void* W,
+                            const CUtensorMap* tmap, const ShardArgs& sh, int splits, cudaStream_t stream);
 
 // Device error word written by bounded waits inside round kernels (0 = ok).
 int read_and_clear_device_error(unsigned int* code);

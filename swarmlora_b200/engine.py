@@ -392,8 +392,28 @@ class SlotGroup:
     def reset_positions(self) -> None:
         self.seqlens.copy_(torch.tensor(self.ctx0, dtype=torch.int32))
 
+    def shard(self, rank: int, group=None) -> None:
+        """Column-sharded base weights with the other GPU of a two-process
+        torch.distributed `group` (both processes built with the same seeds
+        and inputs): from here on every round computes this GPU's half of the
+        output columns and writes it into both GPUs' slot outputs; the
+        worker-side kernels run on both GPUs. Call before `capture`."""
+        import torch.distributed as dist
+        agg.shard_begin(rank, 2)
+        both = [None, None]
+        dist.all_gather_object(both, agg.shard_handles(), group=group)
+        agg.shard_connect(both[1 - rank])
+        dist.barrier(group=group)
+        self._shard_group = (group,)
+
     def close(self) -> None:
         self.graph = None
+        if getattr(self, "_shard_group", None) is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize(self.dev)
+            agg.shard_end()
+            dist.barrier(group=self._shard_group[0])  # neither frees its pool while the peer maps it
+            self._shard_group = None
         for s, w in zip(self.slot_ids, self.worker_ids):
             agg.release_slot(s, w)
         agg.cleanup_slot_pool()

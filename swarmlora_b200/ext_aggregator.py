@@ -153,6 +153,36 @@ def execute_round(op: int, layer: int, slot_ids, worker_ids, bx, tx, stream=None
                                       i64_array(bx), i64_array(tx), st))
 
 
+def shard_begin(rank: int, world: int = 2) -> None:
+    """Column-sharded base weights over a pair of GPUs (one process each):
+    builds this GPU's half of every fused weight (a row view). Call after the
+    pool, the layers and the LM head are initialised."""
+    check(lib().swl_agg_shard_begin(int(rank), int(world)))
+
+
+def shard_handles() -> bytes:
+    """IPC handles (64 bytes each) of this GPU's sync words, logits and slot
+    outputs, for the peer's shard_connect."""
+    n = C.c_int(0)
+    lib().swl_agg_shard_handles(None, 0, C.byref(n))
+    buf = (C.c_ubyte * (64 * n.value))()
+    check(lib().swl_agg_shard_handles(buf, n.value, C.byref(n)))
+    return bytes(buf)
+
+
+def shard_connect(peer_handles: bytes) -> None:
+    """Maps the peer's buffers; from here on every round is column-sharded
+    and both GPUs must run the same rounds in the same order."""
+    n = len(peer_handles) // 64
+    buf = (C.c_ubyte * len(peer_handles)).from_buffer_copy(peer_handles)
+    check(lib().swl_agg_shard_connect(buf, n))
+
+
+def shard_end() -> None:
+    """Unmaps the peer's buffers (on both GPUs before either frees its pool)."""
+    check(lib().swl_agg_shard_end())
+
+
 def slot_buffers(slot_id: int) -> tuple[int, int]:
     """Aggregator-local device addresses (input, output) of a pool slot."""
     a, b = C.c_void_p(), C.c_void_p()
