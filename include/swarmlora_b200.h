@@ -155,6 +155,19 @@ int swl_agg_execute_round(int op, int layer, int n, const int* slot_ids, const i
                           const int64_t* bx, const int64_t* tx, void* stream);
 /* aggregator_main_loop_slots (ext_aggregator.cpp:1024-1210); blocking. */
 int swl_agg_main_loop_slots(int num_slots, int dtype_code);
+/* The QKV round of `layer` fused with the RoPE epilogue (swl_fused_qkv_rope's
+ * arguments; table entry i belongs to command i): each round tile is one head
+ * and adds its LoRA delta, applies NeoX RoPE and writes rotated q to q_rot
+ * and the new token's k / v into the paged caches; the QKV slot outputs are
+ * not written. Same results as swl_agg_execute_round(OP_QKV_FUSED) followed
+ * by swl_fused_qkv_rope, which it runs instead above 64 rows or with
+ * column-sharded weights. No reference counterpart (a fusion). */
+int swl_agg_execute_qkv_rope_round(int layer, int n, const int* slot_ids, const int* worker_ids,
+                                   const int64_t* bx, const int64_t* tx, const void* const* B, int r,
+                                   const float* ws_in, int splits_in, const void* const* block_tables,
+                                   void* const* k_cache, void* const* v_cache, const void* const* seqlens,
+                                   int hq, int hkv, int head_dim, int page, const void* cos_sin, void* q_rot,
+                                   void* stream);
 /* Column-sharded base weights over a pair of GPUs, one process each (the
  * multi-GPU configuration's variant with an NVLink all-gather of outputs; no
  * reference counterpart). After the pool, layers and LM head are set up:

@@ -64,6 +64,8 @@ SIGNATURES: dict[str, tuple] = {
     "swl_agg_set_round_algo": (_i32, [_i32, _i32]),
     "swl_agg_weight": (_i32, [_i32, _i32, _pp, _pi64, _pi64]),
     "swl_agg_execute_round": (_i32, [_i32, _i32, _i32, _pi32, _pi32, _pi64, _pi64, _p]),
+    "swl_agg_execute_qkv_rope_round": (_i32, [_i32, _i32, _pi32, _pi32, _pi64, _pi64, _pp, _i32, _p, _i32, _pp, _pp, _pp,
+                                               _pp, _i32, _i32, _i32, _i32, _p, _p, _p]),
     "swl_agg_shard_begin": (_i32, [_i32, _i32]),
     "swl_agg_shard_handles": (_i32, [_p, _i32, _pi32]),
     "swl_agg_shard_connect": (_i32, [_p, _i32]),

@@ -29,6 +29,7 @@
 #include "shm_abi.h"
 #include "slot_round.h"
 #include "vocab_ops.h"
+#include "worker_ops.h"
 
 using namespace swl;
 
@@ -644,6 +645,114 @@ SWL_EXPORT int swl_agg_execute_round(int op, int layer, int n, const int* slot_i
   // returns once it is done.
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   SWL_TRY(run_round(op, layer, good, st));
+  if (st == nullptr) SWL_CUDA_TRY(cudaStreamSynchronize(st));
+  return SWL_OK;
+}
+
+// The QKV round of `layer` over the given slots fused with the RoPE epilogue
+// (swl_fused_qkv_rope's arguments, table entry i = command i): each round
+// tile adds its head's LoRA delta, applies RoPE and writes rotated q to
+// q_rot and the new token's k / v into the caches; the QKV slot outputs are
+// not written. Above kQkvRopeMaxRows rows, or with column-sharded weights,
+// it runs as the round followed by the separate RoPE epilogue (which then
+// also leaves the round output in the slot outputs), with the same results.
+SWL_EXPORT int swl_agg_execute_qkv_rope_round(int layer, int n, const int* slot_ids, const int* worker_ids,
+                                              const int64_t* bx, const int64_t* tx, const void* const* B,
+                                              int r, const float* ws_in, int splits_in,
+                                              const void* const* block_tables, void* const* k_cache,
+                                              void* const* v_cache, const void* const* seqlens, int hq,
+                                              int hkv, int head_dim, int page, const void* cos_sin,
+                                              void* q_rot, void* stream) {
+  if (!g_pool.initialized || !g_weights_ready)
+    return set_error(SWL_ERR_STATE, "qkv/rope round: pool or weights not initialized");
+  if (n <= 0 || n > g_pool.num_slots || !slot_ids || !worker_ids || !bx || !tx || !block_tables || !k_cache ||
+      !v_cache || !seqlens)
+    return set_error(SWL_ERR_ARG, "qkv/rope round: invalid arguments");
+  if (layer < 0 || layer >= g_num_layers)
+    return set_error(SWL_ERR_ARG, "qkv/rope round: layer_idx %d out of range [0, %d)", layer, g_num_layers);
+  if (head_dim != 128) return set_error(SWL_ERR_ARG, "qkv/rope round: head_dim must be 128");
+  std::vector<RoundCmd> cmds(n);
+  for (int i = 0; i < n; ++i) {
+    if (bx[i] <= 0 || tx[i] <= 0 || bx[i] > 65536 || tx[i] > 65536)
+      return set_error(SWL_ERR_ARG, "qkv/rope round: invalid bx/tx dimensions");
+    cmds[i] = {slot_ids[i], worker_ids[i], bx[i] * tx[i]};
+  }
+  int64_t in_row, out_row;
+  row_bytes_for(kOpQkvFused, layer, &in_row, &out_row);
+  std::vector<RoundCmd> good;
+  std::vector<int> bad;
+  std::string why;
+  validate(cmds.data(), n, in_row, out_row, &good, &bad, &why);
+  if (static_cast<int>(good.size()) != n) return set_error(SWL_ERR_OWNER, "qkv/rope round: %s", why.c_str());
+  const Layer& L = g_layers[layer];
+  if (L.q_dim != static_cast<int64_t>(hq) * 128 || L.k_dim != static_cast<int64_t>(hkv) * 128 || L.v_dim != L.k_dim)
+    return set_error(SWL_ERR_ARG, "qkv/rope round: head counts do not match the layer's q/k/v rows");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int64_t rows = 0;
+  for (const RoundCmd& c : good) rows += c.rows;
+  if (rows > kQkvRopeMaxRows || g_shard.on || g_round_algo == kAlgoSimt || g_round_algo == kAlgoStreamK) {
+    SWL_TRY(run_round(kOpQkvFused, layer, good, st));
+    QkvRopeTable t;
+    t.seg.nseg = n;
+    int acc = 0;
+    for (int i = 0; i < n; ++i) {
+      const Slot& sl = g_pool.slots[good[i].slot_id];
+      t.seg.row_start[i] = acc;
+      acc += static_cast<int>(good[i].rows);
+      t.base[i] = static_cast<const __nv_bfloat16*>(sl.out);
+      t.B[i] = B ? static_cast<const __nv_bfloat16*>(B[i]) : nullptr;
+      t.block_table[i] = static_cast<const int*>(block_tables[i]);
+      t.k_cache[i] = static_cast<__nv_bfloat16*>(k_cache[i]);
+      t.v_cache[i] = static_cast<__nv_bfloat16*>(v_cache[i]);
+      t.seqlen[i] = static_cast<const int*>(seqlens[i]);
+    }
+    t.seg.row_start[n] = acc;
+    t.seg.total_rows = acc;
+    QkvRopeParams p{};
+    p.hq = hq; p.hkv = hkv; p.head_dim = head_dim; p.page = page;
+    p.base_stride = L.q_dim + L.k_dim + L.v_dim;
+    p.ws_in = ws_in;
+    p.splits_in = splits_in;
+    p.cos_sin = static_cast<const __nv_bfloat16*>(cos_sin);
+    p.q_rot = static_cast<__nv_bfloat16*>(q_rot);
+    SWL_TRY(launch_qkv_rope(t, p, r, st));
+  } else {
+    SlotTable tab;
+    QkvRopeEpi epi;
+    tab.nslots = n;
+    int acc = 0;
+    for (int i = 0; i < n; ++i) {
+      const Slot& sl = g_pool.slots[good[i].slot_id];
+      tab.row_start[i] = acc;
+      tab.in[i] = static_cast<const __nv_bfloat16*>(sl.in);
+      tab.out[i] = static_cast<__nv_bfloat16*>(sl.out);
+      acc += static_cast<int>(good[i].rows);
+      epi.B[i] = B ? static_cast<const __nv_bfloat16*>(B[i]) : nullptr;
+      epi.block_table[i] = static_cast<const int*>(block_tables[i]);
+      epi.k_cache[i] = static_cast<__nv_bfloat16*>(k_cache[i]);
+      epi.v_cache[i] = static_cast<__nv_bfloat16*>(v_cache[i]);
+      epi.seqlen[i] = static_cast<const int*>(seqlens[i]);
+    }
+    for (int i = n; i < kMaxSlots; ++i) {
+      epi.B[i] = nullptr;
+      epi.block_table[i] = nullptr;
+      epi.k_cache[i] = epi.v_cache[i] = nullptr;
+      epi.seqlen[i] = nullptr;
+    }
+    tab.row_start[n] = acc;
+    tab.total_rows = acc;
+    epi.ws_in = ws_in;
+    epi.splits_in = splits_in;
+    epi.rank = r;
+    epi.hq = hq;
+    epi.hkv = hkv;
+    epi.page = page;
+    epi.cos_sin = static_cast<const __nv_bfloat16*>(cos_sin);
+    epi.q_rot = static_cast<__nv_bfloat16*>(q_rot);
+    const int64_t N = L.q_dim + L.k_dim + L.v_dim;
+    RoundShape shape{N, L.hidden, L.hidden, N, nullptr};
+    SWL_TRY(launch_slot_round_qkv_rope(tab, shape, L.qkv, &L.tm_qkv, epi, g_round_splits, st));
+  }
   if (st == nullptr) SWL_CUDA_TRY(cudaStreamSynchronize(st));
   return SWL_OK;
 }

@@ -19,6 +19,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "common.h"
 #include "launch.h"
@@ -47,15 +48,49 @@ enum ErrCode : unsigned int {
   kErrWaitPeerDone = 6,   // the peer GPU's half of a sharded round did not arrive
 };
 
+// Extra argument of a plain round (nothing).
+struct NoEpi {
+  int unused;
+};
+
 template <int BN>
 struct TcCfg {
   static constexpr int kStages = BN == 32 ? 4 : (BN == 64 ? 4 : (BN == 128 ? 6 : 4));
   static constexpr int kXStageBytes = BN * 128;
   static constexpr int kPipeBytes = kStages * (kWStageBytes + kXStageBytes);
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kPipeBytes + 256 + BN * 24;
+  // per-row tables of the fused QKV/RoPE epilogue: slot, position, page, t[32]
+  static constexpr int kRopeBytes = BN * (3 * 4 + 32 * 4);
   static constexpr int kTmemCols = BN;
   static_assert(BN * kBlockW * 4 <= kPipeBytes, "epilogue tile must fit in pipeline smem");
 };
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// t . B_row over `rank` (a multiple of 8), in the order of the RoPE
+// epilogue's dot product (8 values per 16-byte load, pairs in order).
+__device__ __forceinline__ float lora_row_dot(const float* t, const __nv_bfloat16* row, int rank) {
+  float d = 0.f;
+  for (int j = 0; j < rank; j += 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + j);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      d = fmaf(t[j + 2 * e], f.x, d);
+      d = fmaf(t[j + 2 * e + 1], f.y, d);
+    }
+  }
+  return d;
+}
+
+__device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, const float (&v)[4]) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]), hi = __floats2bfloat162_rn(v[2], v[3]);
+  uint2 packed;
+  packed.x = *reinterpret_cast<const uint32_t*>(&lo);
+  packed.y = *reinterpret_cast<const uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(dst) = packed;
+}
 
 // Slot of global row `gr`: the largest s with row_start[s] <= gr.
 __device__ __forceinline__ int slot_of_row(const SlotTable& tab, int gr) {
@@ -68,11 +103,13 @@ __device__ __forceinline__ int slot_of_row(const SlotTable& tab, int gr) {
   return lo;
 }
 
-template <int BN, bool kShard>
+template <int BN, class Ex>
 __global__ void __launch_bounds__(kThreads, 1)
     slot_round_tc_kernel(const __grid_constant__ CUtensorMap wmap,
                          const __grid_constant__ SlotTable tab, const RoundShape shape,
-                         int splits, const __grid_constant__ ShardArgs sh) {
+                         int splits, const __grid_constant__ Ex ex) {
+  constexpr bool kShard = std::is_same<Ex, ShardArgs>::value;
+  constexpr bool kRope = std::is_same<Ex, QkvRopeEpi>::value;
   using Cfg = TcCfg<BN>;
   constexpr int STAGES = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -87,6 +124,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const __nv_bfloat16** row_in = reinterpret_cast<const __nv_bfloat16**>(tmem_holder + 2);
   __nv_bfloat16** row_out = reinterpret_cast<__nv_bfloat16**>(tmem_holder + 2 + 2 * BN);
   __nv_bfloat16** row_peer = reinterpret_cast<__nv_bfloat16**>(tmem_holder + 2 + 4 * BN);
+  int* rope_slot = reinterpret_cast<int*>(tmem_holder + 2 + 6 * BN);  // fused QKV/RoPE tables
+  int* rope_pos = rope_slot + BN;
+  int* rope_page = rope_pos + BN;
+  float* rope_t = reinterpret_cast<float*>(rope_page + BN);  // [BN][32]
   __shared__ int shard_ok;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -112,14 +153,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       pin = tab.in[s] + local * shape.in_stride;
       pout = tab.out[s] + local * shape.out_stride;
       if constexpr (kShard) {
-        pout += sh.col0;
-        ppeer = sh.peer_out[s] + local * shape.out_stride + sh.col0;
+        pout += ex.col0;
+        ppeer = ex.peer_out[s] + local * shape.out_stride + ex.col0;
+      }
+      if constexpr (kRope) {
+        // this row's position and cache page, which the launch ahead does
+        // not write (read before the dependency wait)
+        const int pos = *ex.seqlen[s] + static_cast<int>(local);
+        rope_slot[r] = s;
+        rope_pos[r] = pos;
+        rope_page[r] = (n0 >= ex.hq * 128) ? ex.block_table[s][pos / ex.page] : 0;
+        if (ex.B[s]) ptx::prefetch_l2_bulk(ex.B[s] + static_cast<int64_t>(n0) * ex.rank, 128u * ex.rank * 2u);
       }
     }
     row_in[r] = pin;
     row_out[r] = pout;
     row_peer[r] = ppeer;
   }
+
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(&full[s], 1 + kGatherThreads);
@@ -156,8 +207,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // previous round's outputs, which CTA 0 tells the peer.
   unsigned int epoch = 0;
   if constexpr (kShard) {
-    epoch = *reinterpret_cast<volatile unsigned int*>(sh.sync + kSyncEpoch) + 1;
-    if (blockIdx.x == 0 && blockIdx.y == 0 && tid == 0) ptx::st_release_sys(sh.peer_sync + kSyncStart, epoch);
+    epoch = *reinterpret_cast<volatile unsigned int*>(ex.sync + kSyncEpoch) + 1;
+    if (blockIdx.x == 0 && blockIdx.y == 0 && tid == 0) ptx::st_release_sys(ex.peer_sync + kSyncStart, epoch);
   }
 
   if (warp == 0) {
@@ -217,6 +268,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The arrival lands when this thread's copies have; no blocking here.
       ptx::cp_async_arrive_noinc(&full[s]);
     }
+    if constexpr (kRope) {
+      // While the MMA finishes: the LoRA intermediate of this tile's block
+      // (q, k or v) per row, t = bf16(sum of the shrink partials), which
+      // the epilogue ahead of this round writes (so read after the wait).
+      const int blk = n0 < ex.hq * 128 ? 0 : (n0 < (ex.hq + ex.hkv) * 128 ? 1 : 2);
+      const int count = chunk_rows * ex.rank;
+      if (ex.splits_in <= 8) {
+        // up to 8 splits: every load of 4 values is in flight at once
+#pragma unroll 4
+        for (int e = t; e < count; e += kGatherThreads) {
+          const int r = e / ex.rank, j = e - r * ex.rank;
+          const float* src = ex.ws_in + static_cast<int64_t>(chunk_row0 + r) * ex.splits_in * 3 * ex.rank +
+                             blk * ex.rank + j;
+          float v[8];
+#pragma unroll
+          for (int sp = 0; sp < 8; ++sp) v[sp] = sp < ex.splits_in ? src[sp * 3 * ex.rank] : 0.f;
+          float a = 0.f;
+#pragma unroll
+          for (int sp = 0; sp < 8; ++sp)
+            if (sp < ex.splits_in) a += v[sp];
+          rope_t[r * 32 + j] = __bfloat162float(__float2bfloat16_rn(a));
+        }
+      } else {
+        for (int e = t; e < count; e += kGatherThreads) {
+          const int r = e / ex.rank, j = e - r * ex.rank;
+          const float* src = ex.ws_in + static_cast<int64_t>(chunk_row0 + r) * ex.splits_in * 3 * ex.rank +
+                             blk * ex.rank + j;
+          float a = 0.f;
+          for (int sp = 0; sp < ex.splits_in; ++sp) a += src[static_cast<int64_t>(sp) * 3 * ex.rank];
+          rope_t[r * 32 + j] = __bfloat162float(__float2bfloat16_rn(a));
+        }
+      }
+    }
     ptx::cp_async_wait_all();  // never leave copies in flight into freed smem
   }
   __syncwarp();
@@ -247,16 +331,76 @@ __global__ void __launch_bounds__(kThreads, 1)
   // until it has started this round; only then do our stores go there.
   bool to_peer = false;
   if constexpr (kShard) {
-    if (tid == 0) shard_ok = ptx::wait_epoch_sys(sh.sync + kSyncStart, epoch, err, kErrWaitPeerStart, kWaitTimeoutNs);
+    if (tid == 0) shard_ok = ptx::wait_epoch_sys(ex.sync + kSyncStart, epoch, err, kErrWaitPeerStart, kWaitTimeoutNs);
     __syncthreads();
     to_peer = shard_ok != 0;
   }
 
+  const uint32_t pbase = ptx::smem_addr(P);
+  // the K-split sum of the 4 outputs at (row r, column c) of the tile
+  auto reduce4 = [&](int r, int c) -> float4 {
+    const uint32_t off = static_cast<uint32_t>((r * kBlockW + c) * 4);
+    if (splits == 1) return *reinterpret_cast<const float4*>(P + r * kBlockW + c);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < splits; ++p) {
+      const float4 v = ptx::ld_cluster_f4(ptx::map_peer(pbase + off, p));
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    return acc;
+  };
+  if constexpr (kRope) {
+    // Fused RoPE epilogue. Work item = (row, 4 columns c..c+3 and their NeoX
+    // partners c+64..c+67); the cluster's CTAs take equal shares.
+    const int items = chunk_rows * 16;
+    const int i_begin = static_cast<int>(static_cast<int64_t>(rank) * items / splits);
+    const int i_end = static_cast<int>(static_cast<int64_t>(rank + 1) * items / splits);
+    const int head = n0 / 128;
+    const int blk = head < ex.hq ? 0 : (head < ex.hq + ex.hkv ? 1 : 2);
+    for (int it = i_begin + tid; it < i_end; it += kThreads) {
+      const int r = it >> 4, c = (it & 15) * 4;
+      const float4 a = reduce4(r, c), b = reduce4(r, c + 64);
+      float x1[4] = {bf16_round(a.x), bf16_round(a.y), bf16_round(a.z), bf16_round(a.w)};
+      float x2[4] = {bf16_round(b.x), bf16_round(b.y), bf16_round(b.z), bf16_round(b.w)};
+      const int s = rope_slot[r];
+      const __nv_bfloat16* B = ex.B[s];
+      if (B) {
+        const float* t = rope_t + r * 32;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          x1[j] = bf16_round(x1[j] + bf16_round(lora_row_dot(t, B + static_cast<int64_t>(n0 + c + j) * ex.rank, ex.rank)));
+          x2[j] = bf16_round(x2[j] + bf16_round(lora_row_dot(t, B + static_cast<int64_t>(n0 + c + 64 + j) * ex.rank, ex.rank)));
+        }
+      }
+      const int gr = chunk_row0 + r;
+      const int pos = rope_pos[r];
+      const int64_t cache_row = (static_cast<int64_t>(rope_page[r]) * ex.page + pos % ex.page) * ex.hkv;
+      if (blk == 2) {
+        __nv_bfloat16* dst = ex.v_cache[s] + (cache_row + (head - ex.hq - ex.hkv)) * 128;
+        store_bf16x4(dst + c, x1);
+        store_bf16x4(dst + c + 64, x2);
+      } else {
+        const __nv_bfloat16* cs = ex.cos_sin + static_cast<int64_t>(pos) * 128;
+        float o1[4], o2[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float cv = __bfloat162float(cs[c + j]), sv = __bfloat162float(cs[64 + c + j]);
+          o1[j] = bf16_round(bf16_round(x1[j] * cv) - bf16_round(x2[j] * sv));
+          o2[j] = bf16_round(bf16_round(x2[j] * cv) + bf16_round(x1[j] * sv));
+        }
+        __nv_bfloat16* dst = blk == 0 ? ex.q_rot + (static_cast<int64_t>(gr) * ex.hq + head) * 128
+                                      : ex.k_cache[s] + (cache_row + (head - ex.hq)) * 128;
+        store_bf16x4(dst + c, o1);
+        store_bf16x4(dst + c + 64, o2);
+      }
+    }
+  }
   // Each CTA of the cluster reduces an equal share of the tile's 4-float groups.
-  const int groups = chunk_rows * (kBlockW / 4);
+  const int groups = kRope ? 0 : chunk_rows * (kBlockW / 4);
   const int g_begin = static_cast<int>(static_cast<int64_t>(rank) * groups / splits);
   const int g_end = static_cast<int>(static_cast<int64_t>(rank + 1) * groups / splits);
-  const uint32_t pbase = ptx::smem_addr(P);
   for (int g = g_begin + tid; g < g_end; g += kThreads) {
     const int r = g >> 5;
     const int c = (g & 31) * 4;
@@ -310,12 +454,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (tid == 0) {
       const unsigned int total = gridDim.x * gridDim.y;
-      if (atomicAdd(sh.sync + kSyncArrive, 1u) == total - 1) {
-        sh.sync[kSyncArrive] = 0;
-        sh.sync[kSyncEpoch] = epoch;
+      if (atomicAdd(ex.sync + kSyncArrive, 1u) == total - 1) {
+        ex.sync[kSyncArrive] = 0;
+        ex.sync[kSyncEpoch] = epoch;
         __threadfence_system();
-        ptx::st_release_sys(sh.peer_sync + kSyncDone, epoch);
-        ptx::wait_epoch_sys(sh.sync + kSyncDone, epoch, err, kErrWaitPeerDone, kWaitTimeoutNs);
+        ptx::st_release_sys(ex.peer_sync + kSyncDone, epoch);
+        ptx::wait_epoch_sys(ex.sync + kSyncDone, epoch, err, kErrWaitPeerDone, kWaitTimeoutNs);
       }
     }
   }
@@ -366,15 +510,17 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-template <int BN, bool kShard>
+template <int BN, class Ex>
 int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& map, int splits,
-              const ShardArgs& sh, cudaStream_t stream) {
+              const Ex& ex, cudaStream_t stream) {
   using Cfg = TcCfg<BN>;
+  constexpr bool kShard = std::is_same<Ex, ShardArgs>::value;
+  constexpr int smem_bytes = Cfg::kSmemBytes + (std::is_same<Ex, QkvRopeEpi>::value ? Cfg::kRopeBytes : 0);
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(slot_round_tc_kernel<BN, kShard>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    attr_err = cudaFuncSetAttribute(slot_round_tc_kernel<BN, Ex>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   });
   if (attr_err != cudaSuccess)
     return set_error(SWL_ERR_CUDA, "slot round: smem attribute: %s", cudaGetErrorString(attr_err));
@@ -396,23 +542,11 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
   }
   splits = std::max(1, std::min(splits, std::min(8, nkb)));
 
-  SWL_CUDA_TRY(launch_kernel(slot_round_tc_kernel<BN, kShard>,
+  SWL_CUDA_TRY(launch_kernel(slot_round_tc_kernel<BN, Ex>,
                              dim3(static_cast<unsigned>(n_tiles * splits), static_cast<unsigned>(m_chunks), 1),
-                             dim3(kThreads, 1, 1), Cfg::kSmemBytes, stream, static_cast<unsigned>(splits),
-                             map, tab, shape, splits, sh));
+                             dim3(kThreads, 1, 1), smem_bytes, stream, static_cast<unsigned>(splits),
+                             map, tab, shape, splits, ex));
   return SWL_OK;
-}
-
-const ShardArgs& no_shard() {
-  static const ShardArgs none = [] {
-    ShardArgs a;
-    for (int i = 0; i < kMaxSlots; ++i) a.peer_out[i] = nullptr;
-    a.col0 = 0;
-    a.sync = nullptr;
-    a.peer_sync = nullptr;
-    return a;
-  }();
-  return none;
 }
 
 }  // namespace
@@ -458,10 +592,40 @@ int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void*
     if (m > 64) return set_error(SWL_ERR_ARG, "stream-K round: at most 64 token rows");
     return launch_slot_round_streamk(tab, shape, *tmap, stream);
   }
-  if (m <= 32) return launch_tc<32, false>(tab, shape, *tmap, splits, no_shard(), stream);
-  if (m <= 64) return launch_tc<64, false>(tab, shape, *tmap, splits, no_shard(), stream);
-  if (m <= 128) return launch_tc<128, false>(tab, shape, *tmap, splits, no_shard(), stream);
-  return launch_tc<256, false>(tab, shape, *tmap, splits, no_shard(), stream);
+  const NoEpi none{0};
+  if (m <= 32) return launch_tc<32>(tab, shape, *tmap, splits, none, stream);
+  if (m <= 64) return launch_tc<64>(tab, shape, *tmap, splits, none, stream);
+  if (m <= 128) return launch_tc<128>(tab, shape, *tmap, splits, none, stream);
+  return launch_tc<256>(tab, shape, *tmap, splits, none, stream);
+}
+
+int launch_slot_round_qkv_rope(const SlotTable& tab, const RoundShape& shape, const void* W,
+                               const CUtensorMap* tmap, const QkvRopeEpi& epi, int splits,
+                               cudaStream_t stream) {
+  if (tab.nslots <= 0 || tab.total_rows <= 0) return SWL_OK;
+  if (tab.nslots > kMaxSlots) return set_error(SWL_ERR_ARG, "too many slots (%d)", tab.nslots);
+  if (tab.total_rows > kQkvRopeMaxRows)
+    return set_error(SWL_ERR_ARG, "fused QKV/RoPE round: at most %d rows", kQkvRopeMaxRows);
+  if (epi.hq <= 0 || epi.hkv <= 0 || shape.N != static_cast<int64_t>(epi.hq + 2 * epi.hkv) * 128 ||
+      shape.K <= 0 || (shape.K % 8) != 0 || shape.bias)
+    return set_error(SWL_ERR_ARG, "fused QKV/RoPE round: N must be (hq + 2 hkv) * 128, K a multiple of 8, no bias");
+  if (epi.rank < 0 || epi.rank > 32 || (epi.rank % 8) != 0 || epi.splits_in < 0 || epi.page <= 0 || !epi.cos_sin ||
+      !epi.q_rot || (reinterpret_cast<uintptr_t>(epi.q_rot) & 7))
+    return set_error(SWL_ERR_ARG, "fused QKV/RoPE round: invalid epilogue arguments");
+  for (int i = 0; i < tab.nslots; ++i) {
+    if (!epi.seqlen[i] || !epi.block_table[i] || !epi.k_cache[i] || !epi.v_cache[i] ||
+        (reinterpret_cast<uintptr_t>(epi.k_cache[i]) & 7) || (reinterpret_cast<uintptr_t>(epi.v_cache[i]) & 7))
+      return set_error(SWL_ERR_ARG, "fused QKV/RoPE round: slot %d tables missing or caches misaligned", i);
+    if (epi.B[i] && ((reinterpret_cast<uintptr_t>(epi.B[i]) & 15) || epi.rank == 0 || !epi.ws_in))
+      return set_error(SWL_ERR_ARG, "fused QKV/RoPE round: slot %d lora_B misaligned or without rank/partials", i);
+  }
+  CUtensorMap local;
+  if (!tmap) {
+    SWL_TRY(encode_weight_tmap(&local, W, shape.N, shape.K));
+    tmap = &local;
+  }
+  if (tab.total_rows <= 32) return launch_tc<32>(tab, shape, *tmap, splits, epi, stream);
+  return launch_tc<64>(tab, shape, *tmap, splits, epi, stream);
 }
 
 int launch_slot_round_shard(const SlotTable& tab, const RoundShape& shape, const void* W,
@@ -485,10 +649,10 @@ int launch_slot_round_shard(const SlotTable& tab, const RoundShape& shape, const
     SWL_TRY(encode_weight_tmap(&local, W, shape.N, shape.K));
     tmap = &local;
   }
-  if (m <= 32) return launch_tc<32, true>(tab, shape, *tmap, splits, sh, stream);
-  if (m <= 64) return launch_tc<64, true>(tab, shape, *tmap, splits, sh, stream);
-  if (m <= 128) return launch_tc<128, true>(tab, shape, *tmap, splits, sh, stream);
-  return launch_tc<256, true>(tab, shape, *tmap, splits, sh, stream);
+  if (m <= 32) return launch_tc<32>(tab, shape, *tmap, splits, sh, stream);
+  if (m <= 64) return launch_tc<64>(tab, shape, *tmap, splits, sh, stream);
+  if (m <= 128) return launch_tc<128>(tab, shape, *tmap, splits, sh, stream);
+  return launch_tc<256>(tab, shape, *tmap, splits, sh, stream);
 }
 
 int read_and_clear_device_error(unsigned int* code) {

@@ -58,6 +58,28 @@ constexpr int kSyncDone = 32;    // written by the peer: rounds whose stores int
 constexpr int kSyncStart = 48;   // written by the peer: rounds the peer has started
 constexpr int kSyncWords = 64;
 
+// The QKV round fused with its RoPE epilogue (decode launches, <= 64 rows):
+// a round tile is one head (128 output columns), so instead of the round's
+// bf16 output each tile adds the head's LoRA delta (bf16(t @ B^T) with t from
+// the shrink partials), applies NeoX RoPE to q and k heads at position
+// *seqlen + local row, and writes rotated q to q_rot and the new token's k / v
+// into its cache page; the same arithmetic, in the same order, as the round
+// followed by the separate RoPE epilogue.
+struct QkvRopeEpi {
+  const __nv_bfloat16* B[kMaxSlots];  // [(hq + 2 hkv) * 128, rank] lora_B rows per slot, or nullptr
+  const int* block_table[kMaxSlots];
+  __nv_bfloat16* k_cache[kMaxSlots];  // [pages, page, hkv, 128]
+  __nv_bfloat16* v_cache[kMaxSlots];
+  const int* seqlen[kMaxSlots];
+  const float* ws_in;                 // shrink partials [rows][splits_in][3 rank]
+  int splits_in, rank, hq, hkv, page;
+  const __nv_bfloat16* cos_sin;       // [positions, 128]: cos (64) | sin (64)
+  __nv_bfloat16* q_rot;               // [rows, hq * 128]
+};
+// Rows a fused QKV/RoPE launch takes at most (the tile's per-row tables live
+// in shared memory next to the pipeline).
+constexpr int kQkvRopeMaxRows = 64;
+
 enum RoundAlgo : int {
   kAlgoAuto = 0,        // cluster split-K (measured faster than stream-K on B200)
   kAlgoTensorCore = 1,  // tcgen05 + TMA, K split across a thread-block cluster (DSMEM reduce)
@@ -79,6 +101,12 @@ int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void*
 // sh.col0 + [0, shape.N) of both GPUs' slot outputs.
 int launch_slot_round_shard(const SlotTable& tab, const RoundShape& shape, const void* W,
                             const CUtensorMap* tmap, const ShardArgs& sh, int splits, cudaStream_t stream);
+
+// Launches the fused QKV/RoPE round (tab.total_rows <= kQkvRopeMaxRows, head
+// dim 128, no bias); tab's row-to-slot map is the one of the epilogue tables.
+int launch_slot_round_qkv_rope(const SlotTable& tab, const RoundShape& shape, const void* W,
+                               const CUtensorMap* tmap, const QkvRopeEpi& epi, int splits,
+                               cudaStream_t stream);
 
 // Device error word written by bounded waits inside round kernels (0 = ok).
 int read_and_clear_device_error(unsigned int* code);

@@ -143,9 +143,13 @@ class SlotGroup:
     def __init__(self, cfg: ModelConfig, base: BaseWeights, adapters: list, ctx_lens: list,
                  max_new: int, device: int = 0, seed: int = 0, kv_std: float = 1.0,
                  round_algo: int = 0, worker_id0: int = 1000, fused: bool = True,
-                 prefetch=(), prefetch_cap: int = 80 << 20):
+                 prefetch=(), prefetch_cap: int = 80 << 20, qkv_rope_fused: bool = False):
         self.cfg = cfg
         self.fused = fused
+        # qkv_rope_fused: the QKV round carries the RoPE epilogue (one launch
+        # instead of two; measured 3.5 us per layer slower than the separate
+        # epilogue kernel at 28 slots, so off by default)
+        self.qkv_rope_fused = bool(qkv_rope_fused) and "o" not in tuple(prefetch or ())
         self.prefetch = tuple(prefetch or ())
         self.pf_cap = int(prefetch_cap)
         self.dev = torch.device("cuda", device)
@@ -278,12 +282,20 @@ class SlotGroup:
                                             self.A_qkv[0], 3 * r, self.ws_qkv.data_ptr(),
                                             *pf.get((0, agg.OP_QKV_FUSED), none), st))
         for l in range(nl):
-            self._round(agg.OP_QKV_FUSED, l, st)
-            check(L.swl_fused_qkv_rope(n, rows, self.a_out, cfg.qkv_n, self.B_qkv[l], r,
-                                       self.ws_qkv.data_ptr(), self.norm_splits, self.a_bt, self.a_kc[l],
-                                       self.a_vc[l], self.a_sl, cfg.hq, cfg.hkv, D, cfg.page,
-                                       self.cos_sin.data_ptr(), self.q_rot.data_ptr(),
-                                       *pf.get((l, agg.OP_O_PROJ), none), st))
+            if self.qkv_rope_fused:
+                # the QKV round with the RoPE epilogue in its own epilogue
+                check(L.swl_agg_execute_qkv_rope_round(l, n, self.a_sids, self.a_wids, self.a_ones, self.a_ones,
+                                                       self.B_qkv[l], r, self.ws_qkv.data_ptr(), self.norm_splits,
+                                                       self.a_bt, self.a_kc[l], self.a_vc[l], self.a_sl, cfg.hq,
+                                                       cfg.hkv, D, cfg.page, self.cos_sin.data_ptr(),
+                                                       self.q_rot.data_ptr(), st))
+            else:
+                self._round(agg.OP_QKV_FUSED, l, st)
+                check(L.swl_fused_qkv_rope(n, rows, self.a_out, cfg.qkv_n, self.B_qkv[l], r,
+                                           self.ws_qkv.data_ptr(), self.norm_splits, self.a_bt, self.a_kc[l],
+                                           self.a_vc[l], self.a_sl, cfg.hq, cfg.hkv, D, cfg.page,
+                                           self.cos_sin.data_ptr(), self.q_rot.data_ptr(),
+                                           *pf.get((l, agg.OP_O_PROJ), none), st))
             check(L.swl_paged_attention_shrink(n, rows, self.a_bt, self.a_kc[l], self.a_vc[l], self.a_sl,
                                                self.a_in, cfg.hq * D, cfg.hq, cfg.hkv, D, cfg.page,
                                                1.0 / math.sqrt(D), self.max_len, self.q_rot.data_ptr(),
@@ -361,9 +373,10 @@ class SlotGroup:
     def launches_per_step(self) -> int:
         """Kernel launches of one step of this library's kernels."""
         if self.fused:
-            # copy, embed, embed-norm; per layer 4 rounds + qkv_rope + attention (2) + 3 epilogues;
-            # LM head GEMM + argmax, copy, advance
-            return 3 + self.cfg.layers * 10 + 2 + 2
+            # copy, embed, embed-norm; per layer 4 rounds + qkv_rope (unless the QKV round carries it)
+            # + attention (2) + 3 epilogues; LM head GEMM + argmax, copy, advance
+            per_layer = 9 if self.qkv_rope_fused else 10
+            return 3 + self.cfg.layers * per_layer + 2 + 2
         per_layer = 2 + 4 * 3 + 1 + 2  # norms, (shrink+round+expand)x4, rope, attention + combine
         return 3 + self.cfg.layers * per_layer + 1 + 2 + 1 + 1
 

@@ -125,3 +125,41 @@ def test_engine_pdl_matches_serialized_launches(native, cuda):
     assert torch.equal(a[2], b[2])
     for x, y in zip(a[3] + a[4], b[3] + b[4]):
         assert torch.equal(x, y)
+
+
+def test_qkv_round_with_rope_epilogue_matches_separate_launches(native, cuda):
+    """The QKV round carrying the RoPE epilogue (swl_agg_execute_qkv_rope_round)
+    against the round followed by swl_fused_qkv_rope: bit-identical q, K/V
+    cache appends, hidden states and tokens over two steps, with ragged
+    contexts (page boundaries, an empty context) and a slot without adapter."""
+    from swarmlora_b200.engine import ModelConfig, SlotGroup, random_adapter, random_base
+    cfg = ModelConfig(layers=2, vocab=4096)
+    ctx = [20, 0, 31, 100, 7, 15, 16]
+    base = random_base(cfg, seed=4, device=cuda, norm_noise=0.1)
+    adapters = [random_adapter(cfg, seed=40 + i, device=cuda) if i != 3 else None for i in range(len(ctx))]
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=8, seed=5)
+    try:
+        kc0 = [k.clone() for k in grp.k_cache]
+        vc0 = [v.clone() for v in grp.v_cache]
+        runs = {}
+        for fused_rope in (False, True):
+            for l in range(cfg.layers):
+                grp.k_cache[l].copy_(kc0[l])
+                grp.v_cache[l].copy_(vc0[l])
+            grp.reset_positions()
+            grp.tokens.copy_(torch.tensor([3, 99, 4000, 1, 2, 77, 1024]))
+            grp.qkv_rope_fused = fused_rope
+            out = []
+            for _ in range(2):
+                grp.enqueue_step(torch.cuda.current_stream())
+                torch.cuda.synchronize()
+                out.append((grp.tokens.cpu(), grp.h.cpu(), grp.q_rot.cpu()))
+            out.append(([k.cpu() for k in grp.k_cache], [v.cpu() for v in grp.v_cache]))
+            runs[fused_rope] = out
+        for step in range(2):
+            for a, b in zip(runs[False][step], runs[True][step]):
+                assert torch.equal(a, b), f"step {step}: fused QKV/RoPE round differs"
+        for a, b in zip(runs[False][2][0] + runs[False][2][1], runs[True][2][0] + runs[True][2][1]):
+            assert torch.equal(a, b), "K/V caches differ"
+    finally:
+        grp.close()
