@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     row_in[r] = pin;
     row_out[r] = pout;
-    row_peer[r] = ppeer;
+    if constexpr (kShard) row_peer[r] = ppeer;
   }
 
   if (tid == 0) {
