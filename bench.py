@@ -424,7 +424,7 @@ def our_arm(args):
     # launch at this workload, from the capture
     #   ncu --set full --clock-control none -k regex:slot_round -s 1 -c 1 \
     #       python bench.py --profile-round gate_up --steps 3 --warmup 1
-    ncu_traffic = {("gate_up", 28): 235_135_488 + 4_879_104}
+    ncu_traffic = {("gate_up", 28): 235_135_744 + 3_593_216}
     rounds = round_phase(grp, cfg)
     peak, peak_kind = measured_peaks()
     dom = max(rounds, key=lambda k: rounds[k]["us"])
