@@ -857,8 +857,11 @@ int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream
   if (!p.part) return set_error(SWL_ERR_ARG, "attention: missing partial scratch");
   const AttnSplit sp = attention_split(tab.seg.total_rows, p.hkv, p.max_len);
   const int stage_bytes = attn_stage_bytes(p.hq, p.hkv);
-  int stages = std::min(kAttnStagesMax, kAttnSmemMax / stage_bytes);
-  if (const int o = g_attn_stages.load(std::memory_order_relaxed)) stages = std::min(stages, o);
+  // two page stages per warp by default (one in flight while one is
+  // consumed): the 148 KB ring lets a CTA sit beside the RoPE epilogue's
+  // CTAs; deeper rings (tuning) measured no faster in the decode step
+  const int o = g_attn_stages.load(std::memory_order_relaxed);
+  const int stages = std::min(std::min(kAttnStagesMax, kAttnSmemMax / stage_bytes), o > 0 ? o : 2);
   if (stages < 2) return set_error(SWL_ERR_ARG, "attention: page stage of %d bytes too large", stage_bytes);
   const size_t smem = static_cast<size_t>(stages) * stage_bytes;
   // one CTA per SM, but no more CTAs than the units can keep busy
