@@ -137,6 +137,18 @@ def random_adapter(cfg: ModelConfig, seed: int, device, std: float = 0.02) -> li
     return out
 
 
+def exchange_with_peer(mine: bytes, rank: int, group=None) -> bytes:
+    """Gives `mine` to the other rank of a two-rank torch.distributed group
+    and returns what that rank gave (the IPC handles of the column-sharded
+    variant)."""
+    import torch.distributed as dist
+    if dist.get_world_size(group) != 2 or rank not in (0, 1):
+        raise ValueError("the peer exchange needs a group of exactly two ranks")
+    both = [None, None]
+    dist.all_gather_object(both, bytes(mine), group=group)
+    return both[1 - rank]
+
+
 class SlotGroup:
     """N decode slots on one aggregator (this process owns the pool)."""
 
@@ -413,9 +425,7 @@ class SlotGroup:
         worker-side kernels run on both GPUs. Call before `capture`."""
         import torch.distributed as dist
         agg.shard_begin(rank, 2)
-        both = [None, None]
-        dist.all_gather_object(both, agg.shard_handles(), group=group)
-        agg.shard_connect(both[1 - rank])
+        agg.shard_connect(exchange_with_peer(agg.shard_handles(), rank, group))
         dist.barrier(group=group)
         self._shard_group = (group,)
 
