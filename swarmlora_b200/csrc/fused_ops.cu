@@ -5,7 +5,7 @@
 //                    rotated q to the attention scratch.
 //  resid_norm_shrink after the O / Down round (and after the embedding):
 //                    LoRA expand (scaled after), + residual, RMSNorm of the
-//                    row (sum of squares reduced across a cluster of 8 CTAs
+//                    row (sum of squares reduced across a cluster of 4 CTAs
 //                    through distributed shared memory), normed row written
 //                    into the next round's slot input, and the next round's
 //                    LoRA shrink partials computed from it.
@@ -27,8 +27,9 @@ namespace swl {
 
 namespace {
 
-constexpr int kCluster = 8;  // CTAs per row in resid_norm_shrink
-constexpr int kNormThreads = 256;  // threads per resid_norm_shrink CTA
+constexpr int kCluster = 4;         // CTAs per row in resid_norm_shrink
+constexpr int kNormThreads = 512;   // threads per resid_norm_shrink CTA
+constexpr int kNormCols = 1024;     // columns per CTA (hidden 4096 / kCluster)
 
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
@@ -231,7 +232,7 @@ __global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const _
   __shared__ float warp_ss[kNormThreads / 32];
   __shared__ __align__(8) uint64_t bar;
   constexpr int RB = RANK > 0 ? RANK : 8;
-  constexpr int kCols = 512 / kNormThreads;  // columns per thread (C = 512 = kCols * blockDim)
+  constexpr int kCols = kNormCols / kNormThreads;  // columns per thread (C = kCols * blockDim)
   const int q = static_cast<int>(ptx::cluster_rank());
   const int gr = blockIdx.x / kCluster;
   ptx::prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
@@ -618,7 +619,9 @@ int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p
   if (p.splits_in * r_in > kPartialsMax) return set_error(SWL_ERR_ARG, "resid_norm: too many shrink partials");
   const int64_t C = p.hidden / kCluster;
   const int threads = kNormThreads;
-  if (C != 512) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be 4096 (8 CTAs x 512 columns)");
+  if (C != kNormCols)
+    return set_error(SWL_ERR_ARG, "resid_norm: hidden must be %d (%d CTAs x %d columns)", kCluster * kNormCols, kCluster,
+                     kNormCols);
   const int rb = r_in > 0 ? r_in : 8;
   const size_t smem = C * p.r_next * 2 + C * rb * 2 + static_cast<size_t>(threads / 32) * p.r_next * sizeof(float);
   if (smem > 200 * 1024) return set_error(SWL_ERR_ARG, "resid_norm: shared memory too large");
