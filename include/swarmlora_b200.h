@@ -330,7 +330,9 @@ int swl_fused_gu_silu_shrink(int nseg, const int* rows, const void* const* base,
                              int splits_in, int64_t inter, void* const* act, int64_t act_stride,
                              const void* const* A_next, int r_next, float* ws_next, const void* pf,
                              int64_t pf_bytes, void* stream);
-int swl_fused_norm_splits(void);
+/* Shrink partials per row that swl_fused_resid_norm_shrink writes for a
+ * group packed at LoRA rank `rank` (its cluster size: 4 up to rank 16, else 8). */
+int swl_fused_norm_splits(int rank);
 int swl_fused_silu_splits(int64_t inter);
 /* Batched device copies and an in-place counter advance. */
 int swl_copy_rows(int n, const void* const* src, void* const* dst, const int64_t* bytes,

@@ -19,14 +19,19 @@ def decode_step(cfg, base, adapters, k_cache, v_cache, block_tables, seqlens, to
 
     base: object with CPU bf16 lists q,k,v,o,gate,up,down,in_norm,post_norm and
     tensors final_norm, embed, lm_head (HF [out, in] layout).
-    adapters[i][layer][name] = (lora_A [r, in], lora_B [out, r]) or None.
+    adapters[i][layer][name] = (lora_A [r, in], lora_B [out, r]) or None; each
+    adapter's scaling is cfg.alpha / its own rank (load_lora_fast,
+    model_builder.py:147-149), so adapters of different ranks can share a step.
     k_cache/v_cache[layer]: [pages, page, hkv, D] (shared page pool).
     Returns (next_tokens [N] int64, final normed hidden [N, H], logits [N, vocab],
     last-layer hidden before the final norm [N, H]).
     """
     n = len(tokens)
-    s = cfg.alpha / cfg.rank
     D = cfg.head_dim
+
+    def scaling(ad):
+        return cfg.alpha / int(ad["q"][0].shape[0])
+
     scale = 1.0 / math.sqrt(D)
     ids = [torch.tensor([t]) for t in tokens]
     h = ref.embed_round(ids, base.embed)  # list of [1, H]
@@ -41,7 +46,7 @@ def decode_step(cfg, base, adapters, k_cache, v_cache, block_tables, seqlens, to
             ad = adapters[i][l] if adapters[i] is not None else None
             if ad is not None:
                 fA, fB = ref.pack_fused_lora([ad[p][0] for p in ("q", "k", "v")],
-                                             [ad[p][1] for p in ("q", "k", "v")], s, qkv_dims)
+                                             [ad[p][1] for p in ("q", "k", "v")], scaling(ad), qkv_dims)
                 parts = [ref.add_bf16(p, d) for p, d in
                          zip(parts, ref.fused_lora_delta(x[i], fA, fB, qkv_dims))]
             pos = torch.tensor([seqlens[i]])
@@ -58,7 +63,7 @@ def decode_step(cfg, base, adapters, k_cache, v_cache, block_tables, seqlens, to
             o = o_base[i]
             ad = adapters[i][l] if adapters[i] is not None else None
             if ad is not None:
-                o = ref.add_bf16(o, ref.lora_delta_scale_after(attn_out[i], ad["o"][0], ad["o"][1], s))
+                o = ref.add_bf16(o, ref.lora_delta_scale_after(attn_out[i], ad["o"][0], ad["o"][1], scaling(ad)))
             h.append(ref.add_bf16(residual[i], o))
         mlp_res = h
         x = [ref.rms_norm(hi, base.post_norm[l], cfg.eps) for hi in h]
@@ -69,7 +74,7 @@ def decode_step(cfg, base, adapters, k_cache, v_cache, block_tables, seqlens, to
             ad = adapters[i][l] if adapters[i] is not None else None
             if ad is not None:
                 fA, fB = ref.pack_fused_lora([ad["gate"][0], ad["up"][0]], [ad["gate"][1], ad["up"][1]],
-                                             s, [cfg.inter, cfg.inter])
+                                             scaling(ad), [cfg.inter, cfg.inter])
                 dg, du = ref.fused_lora_delta(x[i], fA, fB, [cfg.inter, cfg.inter])
                 gate, up = ref.add_bf16(gate, dg), ref.add_bf16(up, du)
             act.append(ref.silu_mul(gate, up))
@@ -79,7 +84,7 @@ def decode_step(cfg, base, adapters, k_cache, v_cache, block_tables, seqlens, to
             d = d_base[i]
             ad = adapters[i][l] if adapters[i] is not None else None
             if ad is not None:
-                d = ref.add_bf16(d, ref.lora_delta_scale_after(act[i], ad["down"][0], ad["down"][1], s))
+                d = ref.add_bf16(d, ref.lora_delta_scale_after(act[i], ad["down"][0], ad["down"][1], scaling(ad)))
             h.append(ref.add_bf16(mlp_res[i], d))
     final = torch.cat([ref.rms_norm(hi, base.final_norm, cfg.eps) for hi in h], 0)
     logits = ref.lm_head_logits(final, base.lm_head)

@@ -114,7 +114,7 @@ SIGNATURES: dict[str, tuple] = {
                                            _p]),
     "swl_fused_gu_silu_shrink": (_i32, [_i32, _pi32, _pp, _i64, _pp, _i32, _p, _i32, _i64, _pp, _i64,
                                         _pp, _i32, _p, _p, _i64, _p]),
-    "swl_fused_norm_splits": (_i32, []),
+    "swl_fused_norm_splits": (_i32, [_i32]),
     "swl_fused_silu_splits": (_i32, [_i64]),
     "swl_advance_i32": (_i32, [_p, _i32, _i32, _p]),
 }

@@ -16,6 +16,7 @@
 // The arithmetic (bf16 rounding points) is the same as the separate kernels
 // in worker_ops.cu and the reference's tensor ops (worker_sync.py:250-389,
 // model_builder.py:258-262, HF LlamaRMSNorm, vLLM rotary_embedding).
+#include <mutex>
 #include <cuda_bf16.h>
 
 #include "common.h"
@@ -27,9 +28,13 @@ namespace swl {
 
 namespace {
 
-constexpr int kCluster = 4;         // CTAs per row in resid_norm_shrink
-constexpr int kNormThreads = 512;   // threads per resid_norm_shrink CTA
-constexpr int kNormCols = 1024;     // columns per CTA (hidden 4096 / kCluster)
+// resid_norm_shrink: a cluster of CL CTAs per row (hidden 4096), CTA q owns
+// 4096 / CL columns, 2048 / CL threads with 2 columns each. CL = 4 when the
+// staged adapter tiles fit (input rank <= 16, next shrink width <= 48),
+// else 8; the next round's shrink gets one partial per CTA.
+constexpr int kNormHidden = 4096;
+__host__ __device__ constexpr int norm_threads(int cl) { return 2048 / cl; }
+int norm_cluster(int r_in, int r_next) { return (r_in <= 16 && r_next <= 48) ? 4 : 8; }
 
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
@@ -222,17 +227,19 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const __grid_constant__ Q
 // thread t the columns c0 + t + k*blockDim (k < C / blockDim). The finished
 // round's lora_B rows and the next shrink's A rows of those columns are
 // staged in shared memory by two bulk copies.
-template <int RANK>
-__global__ void __launch_bounds__(kNormThreads) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
+template <int RANK, int CL>
+__global__ void __launch_bounds__(norm_threads(CL)) resid_norm_shrink_kernel(const __grid_constant__ ResidNormTable tab,
                                                                 const ResidNormParams p) {
   extern __shared__ __align__(128) uint8_t dsm[];  // a_tile [C][R] | b_tile [C][RANK] | red [warps][R]
   __shared__ float t[32];
   __shared__ float buf[kPartialsMax];
   __shared__ float ss_part;
+  constexpr int kNormThreads = norm_threads(CL);
+  constexpr int kCluster = CL;
   __shared__ float warp_ss[kNormThreads / 32];
   __shared__ __align__(8) uint64_t bar;
   constexpr int RB = RANK > 0 ? RANK : 8;
-  constexpr int kCols = kNormCols / kNormThreads;  // columns per thread (C = kCols * blockDim)
+  constexpr int kCols = kNormHidden / CL / kNormThreads;  // columns per thread (C = kCols * blockDim)
   const int q = static_cast<int>(ptx::cluster_rank());
   const int gr = blockIdx.x / kCluster;
   ptx::prefetch_l2_share(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
@@ -611,38 +618,47 @@ int launch_qkv_rope(const QkvRopeTable& tab, const QkvRopeParams& p, int r, cuda
   return SWL_OK;
 }
 
+namespace {
+template <int RANK, int CL>
+int launch_resid_norm_cl(const ResidNormTable& tab, const ResidNormParams& p, size_t smem, cudaStream_t stream) {
+  static std::once_flag once;
+  static cudaError_t ae = cudaSuccess;
+  std::call_once(once, [] {
+    ae = cudaFuncSetAttribute(resid_norm_shrink_kernel<RANK, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              200 * 1024);
+  });
+  if (ae != cudaSuccess) return set_error(SWL_ERR_CUDA, "resid_norm: %s", cudaGetErrorString(ae));
+  const dim3 grid(static_cast<unsigned>(tab.seg.total_rows * CL), 1, 1);
+  SWL_CUDA_TRY(launch_kernel(resid_norm_shrink_kernel<RANK, CL>, grid, dim3(norm_threads(CL)), smem, stream, CL, tab,
+                             p));
+  return SWL_OK;
+}
+template <int CL>
+int launch_resid_norm_rank(const ResidNormTable& tab, const ResidNormParams& p, int r_in, size_t smem,
+                           cudaStream_t stream) {
+  switch (r_in) {
+    case 0: return launch_resid_norm_cl<0, CL>(tab, p, smem, stream);
+    case 8: return launch_resid_norm_cl<8, CL>(tab, p, smem, stream);
+    case 16: return launch_resid_norm_cl<16, CL>(tab, p, smem, stream);
+    case 32: return launch_resid_norm_cl<32, CL>(tab, p, smem, stream);
+    default: return set_error(SWL_ERR_ARG, "resid_norm: input rank must be 0, 8, 16 or 32");
+  }
+}
+}  // namespace
+
 int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p, int r_in,
                              cudaStream_t stream) {
   if (tab.seg.total_rows <= 0) return SWL_OK;
-  if (p.hidden % (kCluster * 4)) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be a multiple of 32");
+  if (p.hidden != kNormHidden) return set_error(SWL_ERR_ARG, "resid_norm: hidden must be %d", kNormHidden);
   if (p.r_next % 8 || p.r_next > 96) return set_error(SWL_ERR_ARG, "resid_norm: next rank layout must be 8..96 in steps of 8");
   if (p.splits_in * r_in > kPartialsMax) return set_error(SWL_ERR_ARG, "resid_norm: too many shrink partials");
-  const int64_t C = p.hidden / kCluster;
-  const int threads = kNormThreads;
-  if (C != kNormCols)
-    return set_error(SWL_ERR_ARG, "resid_norm: hidden must be %d (%d CTAs x %d columns)", kCluster * kNormCols, kCluster,
-                     kNormCols);
+  const int cl = norm_cluster(r_in, p.r_next);
+  const int64_t C = p.hidden / cl;
   const int rb = r_in > 0 ? r_in : 8;
-  const size_t smem = C * p.r_next * 2 + C * rb * 2 + static_cast<size_t>(threads / 32) * p.r_next * sizeof(float);
+  const size_t smem = C * p.r_next * 2 + C * rb * 2 + static_cast<size_t>(norm_threads(cl) / 32) * p.r_next * sizeof(float);
   if (smem > 200 * 1024) return set_error(SWL_ERR_ARG, "resid_norm: shared memory too large");
-  cudaError_t ae = cudaSuccess;
-  switch (r_in) {
-    case 0: ae = cudaFuncSetAttribute(resid_norm_shrink_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); break;
-    case 8: ae = cudaFuncSetAttribute(resid_norm_shrink_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); break;
-    case 16: ae = cudaFuncSetAttribute(resid_norm_shrink_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); break;
-    case 32: ae = cudaFuncSetAttribute(resid_norm_shrink_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); break;
-    default: break;
-  }
-  if (ae != cudaSuccess) return set_error(SWL_ERR_CUDA, "resid_norm: %s", cudaGetErrorString(ae));
-  const dim3 grid(static_cast<unsigned>(tab.seg.total_rows * kCluster), 1, 1);
-  switch (r_in) {
-    case 0: SWL_CUDA_TRY(launch_kernel(resid_norm_shrink_kernel<0>, grid, dim3(threads), smem, stream, kCluster, tab, p)); break;
-    case 8: SWL_CUDA_TRY(launch_kernel(resid_norm_shrink_kernel<8>, grid, dim3(threads), smem, stream, kCluster, tab, p)); break;
-    case 16: SWL_CUDA_TRY(launch_kernel(resid_norm_shrink_kernel<16>, grid, dim3(threads), smem, stream, kCluster, tab, p)); break;
-    case 32: SWL_CUDA_TRY(launch_kernel(resid_norm_shrink_kernel<32>, grid, dim3(threads), smem, stream, kCluster, tab, p)); break;
-    default: return set_error(SWL_ERR_ARG, "resid_norm: input rank must be 0, 8, 16 or 32");
-  }
-  return SWL_OK;
+  return cl == 4 ? launch_resid_norm_rank<4>(tab, p, r_in, smem, stream)
+                 : launch_resid_norm_rank<8>(tab, p, r_in, smem, stream);
 }
 
 int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, cudaStream_t stream) {
@@ -683,7 +699,7 @@ int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, 
   return SWL_OK;
 }
 
-int resid_norm_splits() { return kCluster; }
+int resid_norm_splits(int rank) { return norm_cluster(rank, 3 * rank); }
 int gu_silu_splits(int64_t inter) { return static_cast<int>((inter + kGuCols - 1) / kGuCols); }
 
 }  // namespace swl

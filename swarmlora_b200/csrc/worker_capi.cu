@@ -291,8 +291,9 @@ SWL_EXPORT int swl_fused_gu_silu_shrink(int nseg, const int* rows, const void* c
   return launch_gu_silu_shrink(t, p, r, static_cast<cudaStream_t>(stream));
 }
 
-// Number of shrink partials swl_fused_resid_norm_shrink writes (its cluster size).
-SWL_EXPORT int swl_fused_norm_splits(void) { return resid_norm_splits(); }
+// Number of shrink partials swl_fused_resid_norm_shrink writes per row (its
+// cluster size) for a group whose adapters are packed at LoRA rank `rank`.
+SWL_EXPORT int swl_fused_norm_splits(int rank) { return resid_norm_splits(rank); }
 
 // Number of Down-shrink partials swl_fused_gu_silu_shrink writes per row.
 SWL_EXPORT int swl_fused_silu_splits(int64_t inter) { return gu_silu_splits(inter); }

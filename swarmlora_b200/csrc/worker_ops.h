@@ -186,7 +186,7 @@ int launch_qkv_rope(const QkvRopeTable& tab, const QkvRopeParams& p, int r, cuda
 int launch_resid_norm_shrink(const ResidNormTable& tab, const ResidNormParams& p, int r_in,
                              cudaStream_t stream);
 int launch_gu_silu_shrink(const GuSiluTable& tab, const GuSiluParams& p, int r, cudaStream_t stream);
-int resid_norm_splits();
+int resid_norm_splits(int rank);  // shrink partials per row for a group of this LoRA rank
 int gu_silu_splits(int64_t inter);
 
 }  // namespace swl

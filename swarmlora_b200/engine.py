@@ -121,10 +121,12 @@ def random_base(cfg: ModelConfig, seed: int, device, std: float = 0.02,
         final_norm=norm(), embed=w(cfg.vocab, H), lm_head=w(cfg.vocab, H))
 
 
-def random_adapter(cfg: ModelConfig, seed: int, device, std: float = 0.02) -> list:
-    """Per layer: {'q': (A [r, in], B [out, r]), ...}, A, B ~ N(0, std)."""
+def random_adapter(cfg: ModelConfig, seed: int, device, std: float = 0.02, rank: int | None = None) -> list:
+    """Per layer: {'q': (A [r, in], B [out, r]), ...}, A, B ~ N(0, std); r is
+    `rank` (default cfg.rank)."""
     g = torch.Generator(device=device).manual_seed(seed)
-    H, I, D, r = cfg.hidden, cfg.inter, cfg.head_dim, cfg.rank
+    H, I, D = cfg.hidden, cfg.inter, cfg.head_dim
+    r = int(rank) if rank else cfg.rank
     dims = {"q": (H, cfg.hq * D), "k": (H, cfg.hkv * D), "v": (H, cfg.hkv * D),
             "o": (cfg.hq * D, H), "gate": (H, I), "up": (H, I), "down": (I, H)}
     out = []
@@ -186,9 +188,9 @@ class SlotGroup:
         self.slot_in = [b[0] for b in bufs]
         self.slot_out = [b[1] for b in bufs]
         # --- workers: adapters, KV, buffers ---------------------------------------
-        self.lora = [None if ad is None else
-                     [wo.pack_lora_layer(ad[l], cfg.alpha / cfg.rank) for l in range(cfg.layers)]
-                     for ad in adapters]
+        # every adapter is packed at the group's rank cfg.rank (zero-padded
+        # when smaller, its own alpha / r folded into the O / Down lora_B)
+        self.lora = [None if ad is None else self._pack(ad) for ad in adapters]
         pps = (self.max_len + cfg.page - 1) // cfg.page
         g = torch.Generator(device=self.dev).manual_seed(seed + 7)
         perm = torch.randperm(n * pps, generator=g, device=self.dev).to(torch.int32)
@@ -209,7 +211,7 @@ class SlotGroup:
         self.ws = torch.empty(self.splits * n * 3 * cfg.rank, dtype=torch.float32, device=self.dev)
         # fused path: LoRA shrink partials of each round's input, produced by the
         # epilogue kernel that writes that input
-        self.norm_splits = int(lib().swl_fused_norm_splits())
+        self.norm_splits = int(lib().swl_fused_norm_splits(cfg.rank))
         self.dn_splits = int(lib().swl_fused_silu_splits(I))
         f32 = dict(dtype=torch.float32, device=self.dev)
         self.ws_qkv = torch.zeros(self.norm_splits * n * 3 * cfg.rank, **f32)
@@ -266,6 +268,27 @@ class SlotGroup:
         self.ends_gu = i64_array([I, 2 * I, 2 * I])
         self.ends_h = i64_array([H, H, H])
         self.scaling = cfg.alpha / r
+
+    def _pack(self, adapter) -> list:
+        cfg = self.cfg
+        r = int(adapter[0]["q"][0].shape[0])
+        if r > cfg.rank or r % 8:
+            raise ValueError(f"adapter rank {r}: must be a multiple of 8 and at most the group's rank {cfg.rank}")
+        return [wo.pack_lora_layer(adapter[l], cfg.alpha / r, pad_rank=cfg.rank, post_scale=cfg.alpha / cfg.rank)
+                for l in range(cfg.layers)]
+
+    def set_adapter(self, i: int, adapter) -> None:
+        """Replaces slot i's adapter (per-layer dicts as random_adapter makes,
+        any rank up to the group's) in place: it is packed at the group's rank
+        and copied into the slot's existing buffers on the current stream, so
+        a captured step graph keeps working and its next replay uses it. Call
+        it between steps, ordered after the last step on that stream. A slot
+        built without an adapter has no buffers to swap into."""
+        if self.lora[i] is None:
+            raise ValueError(f"slot {i} was built without an adapter")
+        for old, new in zip(self.lora[i], self._pack(adapter)):
+            for name in ("A_qkv", "B_qkv", "A_o", "B_o", "A_gu", "B_gu", "A_down", "B_down"):
+                getattr(old, name).copy_(getattr(new, name))
 
     def _round(self, op, layer, st):
         check(lib().swl_agg_execute_round(op, layer, self.n, self.a_sids, self.a_wids, self.a_ones,

@@ -43,22 +43,44 @@ class LoraLayer:
     scaling: float
 
 
-def pack_lora_layer(w: dict, scaling: float) -> LoraLayer:
-    """w maps 'q','k','v','o','gate','up','down' -> (lora_A [r, in], lora_B [out, r])."""
-    def a_scaled(name):
-        return (w[name][0].t() * scaling).to(torch.bfloat16)  # A.t() * s in bf16 (model_builder.py:237)
+def pack_lora_layer(w: dict, scaling: float, pad_rank: int | None = None,
+                    post_scale: float | None = None) -> LoraLayer:
+    """w maps 'q','k','v','o','gate','up','down' -> (lora_A [r, in], lora_B [out, r]).
+
+    pad_rank packs the adapter at a larger rank (a group whose adapters have
+    different ranks runs its kernels at the largest): A and B get zero
+    columns, which add exact zeros, so the deltas are bit-identical.
+    post_scale is the scale the O / Down kernels apply after the expand (one
+    value per launch); the adapter's own `scaling` is reached by folding
+    scaling / post_scale into its O and Down lora_B, which is exact when that
+    ratio is a power of two (alpha / r for r in {8, 16, 32} and one alpha)."""
     r = int(w["q"][0].shape[0])
+    R = int(pad_rank) if pad_rank else r
+    if R < r:
+        raise ValueError(f"pad_rank {R} below the adapter's rank {r}")
+    fold = 1.0 if post_scale is None else float(scaling) / float(post_scale)
+
+    def pad(t):  # [rows, r] -> [rows, R]
+        return torch.nn.functional.pad(t, (0, R - t.shape[1])) if R > t.shape[1] else t
+
+    def a_scaled(name):
+        return pad((w[name][0].t() * scaling).to(torch.bfloat16))  # A.t() * s in bf16 (model_builder.py:237)
+
+    def b_folded(name):
+        b = w[name][1]
+        return pad((b.float() * fold).to(torch.bfloat16) if fold != 1.0 else b)
+
     return LoraLayer(
         A_qkv=torch.cat([a_scaled("q"), a_scaled("k"), a_scaled("v")], 1).contiguous(),
-        B_qkv=torch.cat([w["q"][1], w["k"][1], w["v"][1]], 0).contiguous(),
-        A_o=w["o"][0].t().contiguous(),
-        B_o=w["o"][1].contiguous(),
+        B_qkv=torch.cat([pad(w["q"][1]), pad(w["k"][1]), pad(w["v"][1])], 0).contiguous(),
+        A_o=pad(w["o"][0].t()).contiguous(),
+        B_o=b_folded("o").contiguous(),
         A_gu=torch.cat([a_scaled("gate"), a_scaled("up")], 1).contiguous(),
-        B_gu=torch.cat([w["gate"][1], w["up"][1]], 0).contiguous(),
-        A_down=w["down"][0].t().contiguous(),
-        B_down=w["down"][1].contiguous(),
-        rank=r,
-        scaling=float(scaling),
+        B_gu=torch.cat([pad(w["gate"][1]), pad(w["up"][1])], 0).contiguous(),
+        A_down=pad(w["down"][0].t()).contiguous(),
+        B_down=b_folded("down").contiguous(),
+        rank=R,
+        scaling=float(post_scale) if post_scale is not None else float(scaling),
     )
 
 

@@ -163,3 +163,73 @@ def test_qkv_round_with_rope_epilogue_matches_separate_launches(native, cuda):
             assert torch.equal(a, b), "K/V caches differ"
     finally:
         grp.close()
+
+
+def test_mixed_rank_adapters_and_hot_swap(native, cuda):
+    """Adapters of ranks 8, 16 and 32 in one group (the churn configuration's
+    rank mix), packed at the group's rank 32 with each adapter's own alpha/r
+    (load_lora_fast, model_builder.py:147-149), against the CPU oracle; then
+    two slots swap adapters in place (one to another rank) and both the eager
+    step and the CUDA graph captured before the swap follow the oracle."""
+    from oracle.decode import decode_step
+    from swarmlora_b200.engine import ModelConfig, SlotGroup, random_adapter, random_base
+    cfg = ModelConfig(layers=2, vocab=4096, rank=32, alpha=32)
+    ranks = [8, 16, 32, 8, 16]
+    ctx = [20, 5, 31, 100, 7]
+    base = random_base(cfg, seed=2, device=cuda, norm_noise=0.1)
+    adapters = [random_adapter(cfg, seed=70 + i, device=cuda, rank=r) for i, r in enumerate(ranks)]
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=8, seed=6)
+    try:
+        base_c = _cpu(base)
+        kc = [k.cpu() for k in grp.k_cache]
+        vc = [v.cpu() for v in grp.v_cache]
+        kc0 = [k.clone() for k in grp.k_cache]
+        vc0 = [v.clone() for v in grp.v_cache]
+        bts = [t.tolist() for t in grp.block_tables]
+        tokens, seq = [11, 22, 33, 44, 55], list(ctx)
+        grp.tokens.copy_(torch.tensor(tokens))
+        stream = torch.cuda.current_stream()
+
+        def check_step(what, ad_c):
+            nonlocal tokens, seq
+            grp.enqueue_step(stream)
+            torch.cuda.synchronize()
+            got = grp.tokens.cpu()
+            want, final, logits, h_last = decode_step(cfg, base_c, ad_c, kc, vc, bts, seq, tokens)
+            assert_close(grp.h, h_last, f"{what} last-layer hidden", atol_rms=ATOL_RMS_MULTILAYER)
+            _check_tokens(got, want, logits, what)
+            tokens, seq = got.tolist(), [s + 1 for s in seq]
+            return got
+
+        ad_c = _cpu(adapters)
+        check_step("mixed ranks step 0", ad_c)
+        grp.capture()  # before the swap: the graph must pick the swapped adapters up
+        check_step("mixed ranks step 1", ad_c)
+        # swap slot 1 (rank 16 -> 32) and slot 3 (rank 8 -> 16)
+        new1 = random_adapter(cfg, seed=91, device=cuda, rank=32)
+        new3 = random_adapter(cfg, seed=93, device=cuda, rank=16)
+        grp.set_adapter(1, new1)
+        grp.set_adapter(3, new3)
+        ad_c[1], ad_c[3] = _cpu(new1), _cpu(new3)
+        eager = check_step("after swap", ad_c)
+        # the graph captured before the swap, from the same state, gives the same token
+        k_now = [k.clone() for k in grp.k_cache]
+        v_now = [v.clone() for v in grp.v_cache]
+        for l in range(cfg.layers):
+            grp.k_cache[l].copy_(kc0[l])
+            grp.v_cache[l].copy_(vc0[l])
+        grp.reset_positions()
+        grp.tokens.copy_(torch.tensor([11, 22, 33, 44, 55]))
+        grp.set_adapter(1, adapters[1])  # replay the first two steps with the original adapters
+        grp.set_adapter(3, adapters[3])
+        for _ in range(2):
+            grp.replay()
+        grp.set_adapter(1, new1)
+        grp.set_adapter(3, new3)
+        grp.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(grp.tokens.cpu(), eager), "graph replay after the swap differs from the eager step"
+        for l in range(cfg.layers):
+            assert torch.equal(grp.k_cache[l], k_now[l]) and torch.equal(grp.v_cache[l], v_now[l])
+    finally:
+        grp.close()

@@ -133,3 +133,22 @@ def test_decode_step_matches_hf_llama():
     assert lerr < 2e-2, f"logits relative error {lerr:.3e}"
     top = hf_logits.float().max()
     assert hf_logits[0, int(nxt[0])].float() >= top - 2.0 ** -7 * top.abs() - 1e-3
+
+
+@pytest.mark.parametrize("r", [8, 16, 32])
+def test_rank_padding_and_scale_folding_are_exact(r):
+    """A group runs every adapter at its largest rank R: lora_A / lora_B get
+    zero rows / columns, and an O/Down adapter's own scale alpha/r is folded
+    into its lora_B as (alpha/r) / (alpha/R) so the kernels apply one scale
+    per launch. Through the oracle's scale-after LoRA (worker_sync.py:305,
+    :375) both are bit-identical to the adapter at its own rank."""
+    alpha, R, K, N = 32, 32, 512, 256
+    g = torch.Generator().manual_seed(r)
+    x = torch.randn(3, K, generator=g).to(BF)
+    A = (torch.randn(r, K, generator=g) * 0.02).to(BF)
+    B = (torch.randn(N, r, generator=g) * 0.02).to(BF)
+    want = ref.lora_delta_scale_after(x, A, B, alpha / r)
+    A_pad = torch.nn.functional.pad(A, (0, 0, 0, R - r))
+    B_pad = torch.nn.functional.pad((B.float() * ((alpha / r) / (alpha / R))).to(BF), (0, R - r))
+    got = ref.lora_delta_scale_after(x, A_pad, B_pad, alpha / R)
+    assert torch.equal(got, want)
