@@ -465,6 +465,7 @@ SWL_EXPORT int swl_agg_cleanup_slot_pool(void) {
   if (!g_pool.initialized) return SWL_OK;
   SWL_CUDA_TRY(cudaSetDevice(g_pool.device));
   SWL_CUDA_TRY(cudaDeviceSynchronize());
+  SWL_TRY(shard_end());  // a column-shard setup maps the peer's buffers by slot
   for (int i = 0; i < g_pool.num_slots; ++i) {
     Slot& s = g_pool.slots[i];
     if (s.in) cudaFree(s.in);
