@@ -15,7 +15,9 @@ from . import reference_math as ref
 
 
 def decode_step(cfg, base, adapters, k_cache, v_cache, block_tables, seqlens, tokens):
-    """One token for every slot.
+    """One step for every slot: tokens[i] is one token id, or a list of ids
+    (several new rows, e.g. a prefill chunk, at positions seqlens[i] ..
+    seqlens[i] + len - 1; the rows of a slot attend causally to each other).
 
     base: object with CPU bf16 lists q,k,v,o,gate,up,down,in_norm,post_norm and
     tensors final_norm, embed, lm_head (HF [out, in] layout).
@@ -24,7 +26,8 @@ def decode_step(cfg, base, adapters, k_cache, v_cache, block_tables, seqlens, to
     model_builder.py:147-149), so adapters of different ranks can share a step.
     k_cache/v_cache[layer]: [pages, page, hkv, D] (shared page pool).
     Returns (next_tokens [N] int64, final normed hidden [N, H], logits [N, vocab],
-    last-layer hidden before the final norm [N, H]).
+    last-layer hidden before the final norm [N, H]), all from each slot's
+    last row.
     """
     n = len(tokens)
     D = cfg.head_dim
@@ -33,7 +36,7 @@ def decode_step(cfg, base, adapters, k_cache, v_cache, block_tables, seqlens, to
         return cfg.alpha / int(ad["q"][0].shape[0])
 
     scale = 1.0 / math.sqrt(D)
-    ids = [torch.tensor([t]) for t in tokens]
+    ids = [torch.tensor(list(t) if isinstance(t, (list, tuple)) else [t]) for t in tokens]
     h = ref.embed_round(ids, base.embed)  # list of [1, H]
     qkv_dims = [cfg.hq * D, cfg.hkv * D, cfg.hkv * D]
     for l in range(cfg.layers):
@@ -49,14 +52,15 @@ def decode_step(cfg, base, adapters, k_cache, v_cache, block_tables, seqlens, to
                                              [ad[p][1] for p in ("q", "k", "v")], scaling(ad), qkv_dims)
                 parts = [ref.add_bf16(p, d) for p, d in
                          zip(parts, ref.fused_lora_delta(x[i], fA, fB, qkv_dims))]
-            pos = torch.tensor([seqlens[i]])
-            cs = ref.cos_sin_cache(ref.llama3_inv_freq(D), seqlens[i] + 1)
+            T = x[i].shape[0]
+            pos = torch.arange(seqlens[i], seqlens[i] + T)
+            cs = ref.cos_sin_cache(ref.llama3_inv_freq(D), seqlens[i] + T)
             q = ref.rope_neox(parts[0], pos, cs, D)
             k = ref.rope_neox(parts[1], pos, cs, D)
-            o = ref.attention_with_kvcache(q.reshape(1, cfg.hq, D), k.reshape(1, cfg.hkv, D),
-                                           parts[2].reshape(1, cfg.hkv, D), k_cache[l], v_cache[l],
+            o = ref.attention_with_kvcache(q.reshape(T, cfg.hq, D), k.reshape(T, cfg.hkv, D),
+                                           parts[2].reshape(T, cfg.hkv, D), k_cache[l], v_cache[l],
                                            block_tables[i], seqlens[i], scale)
-            attn_out.append(o.reshape(1, cfg.hq * D))
+            attn_out.append(o.reshape(T, cfg.hq * D))
         o_base = ref.slot_round(attn_out, base.o[l])
         h = []
         for i in range(n):
@@ -86,6 +90,6 @@ def decode_step(cfg, base, adapters, k_cache, v_cache, block_tables, seqlens, to
             if ad is not None:
                 d = ref.add_bf16(d, ref.lora_delta_scale_after(act[i], ad["down"][0], ad["down"][1], scaling(ad)))
             h.append(ref.add_bf16(mlp_res[i], d))
-    final = torch.cat([ref.rms_norm(hi, base.final_norm, cfg.eps) for hi in h], 0)
+    final = torch.cat([ref.rms_norm(hi[-1:], base.final_norm, cfg.eps) for hi in h], 0)
     logits = ref.lm_head_logits(final, base.lm_head)
-    return ref.greedy(logits), final, logits, torch.cat(h, 0)
+    return ref.greedy(logits), final, logits, torch.cat([hi[-1:] for hi in h], 0)

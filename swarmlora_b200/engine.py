@@ -202,10 +202,15 @@ class SlotGroup:
             self.v_cache.append((torch.randn(shape, generator=g, device=self.dev) * kv_std).to(BF16))
         self.seqlens = torch.tensor(ctx_lens, dtype=torch.int32, device=self.dev)
         self.cos_sin = cos_sin_cache(cfg, self.max_len + cfg.page, self.dev)
-        self.h = torch.empty(n, H, dtype=BF16, device=self.dev)
+        # a step carries up to max_rows new tokens per slot (prefill chunks):
+        # each slot's hidden rows are contiguous, h is every slot's first row
+        self.max_rows = mr = int(cfg.max_seq_per_step)
+        self.h_rows = torch.empty(n, mr, H, dtype=BF16, device=self.dev)
+        self.h = self.h_rows[:, 0]
         self.qkv = torch.empty(n, cfg.qkv_n, dtype=BF16, device=self.dev)
-        self.q_rot = torch.empty(n, cfg.hq * D, dtype=BF16, device=self.dev)
-        nparts = wo.attention_part_floats(n, cfg.hq, cfg.hkv, self.max_len)
+        self.q_rot = torch.empty(n * mr, cfg.hq * D, dtype=BF16, device=self.dev)
+        self.tok_in = torch.zeros(n, mr, dtype=torch.int64, device=self.dev)
+        nparts = wo.attention_part_floats(n * mr, cfg.hq, cfg.hkv, self.max_len)
         self.part = torch.empty(max(1, nparts), dtype=torch.float32, device=self.dev)
         self.splits = max(1, min(8, -(-296 // n)))
         self.ws = torch.empty(self.splits * n * 3 * cfg.rank, dtype=torch.float32, device=self.dev)
@@ -214,10 +219,10 @@ class SlotGroup:
         self.norm_splits = int(lib().swl_fused_norm_splits(cfg.rank))
         self.dn_splits = int(lib().swl_fused_silu_splits(I))
         f32 = dict(dtype=torch.float32, device=self.dev)
-        self.ws_qkv = torch.zeros(self.norm_splits * n * 3 * cfg.rank, **f32)
-        self.ws_o = torch.zeros(cfg.hq * n * cfg.rank, **f32)
-        self.ws_gu = torch.zeros(self.norm_splits * n * 2 * cfg.rank, **f32)
-        self.ws_dn = torch.zeros(self.dn_splits * n * cfg.rank, **f32)
+        self.ws_qkv = torch.zeros(self.norm_splits * n * mr * 3 * cfg.rank, **f32)
+        self.ws_o = torch.zeros(cfg.hq * n * mr * cfg.rank, **f32)
+        self.ws_gu = torch.zeros(self.norm_splits * n * mr * 2 * cfg.rank, **f32)
+        self.ws_dn = torch.zeros(self.dn_splits * n * mr * cfg.rank, **f32)
         self.tokens = torch.zeros(n, dtype=torch.int64, device=self.dev)
         self._build_call_args()
         self.graph = None
@@ -232,7 +237,7 @@ class SlotGroup:
         self.a_ones = i64_array([1] * n)
         self.a_in = ptr_array(self.slot_in)
         self.a_out = ptr_array(self.slot_out)
-        self.a_h = ptr_array([self.h[i].data_ptr() for i in range(n)])
+        self.a_h = ptr_array([self.h_rows[i].data_ptr() for i in range(n)])
         self.a_qkv = ptr_array([self.qkv[i].data_ptr() for i in range(n)])
         self.a_tok = ptr_array([self.tokens[i].data_ptr() for i in range(n)])
         self.a_b8 = i64_array([8] * n)
@@ -290,25 +295,49 @@ class SlotGroup:
             for name in ("A_qkv", "B_qkv", "A_o", "B_o", "A_gu", "B_gu", "A_down", "B_down"):
                 getattr(old, name).copy_(getattr(new, name))
 
-    def _round(self, op, layer, st):
+    def _round(self, op, layer, st, tx=None):
         check(lib().swl_agg_execute_round(op, layer, self.n, self.a_sids, self.a_wids, self.a_ones,
-                                          self.a_ones, st))
+                                          tx if tx is not None else self.a_ones, st))
 
-    def enqueue_step(self, stream: torch.cuda.Stream) -> None:
-        """Queues one decode token for every slot on `stream` (no host sync)."""
-        if self.fused:
-            return self._enqueue_fused(stream)
-        return self._enqueue_unfused(stream)
+    def enqueue_step(self, stream: torch.cuda.Stream, rows=None, tokens=None) -> None:
+        """Queues one step on `stream` (no host sync). By default every slot
+        decodes one token (its last output, `tokens`). With `rows` (new tokens
+        per slot, 1..max_rows) and `tokens` (their ids, one list per slot) the
+        step carries prefill chunks next to decode rows, the mixed
+        configuration: every new row goes through the layers, its K / V is
+        appended, and each slot's next token comes from its last row. The ids
+        are copied to the device first, so such a step is not for capture."""
+        if rows is None:
+            if self.fused:
+                return self._enqueue_fused(stream)
+            return self._enqueue_unfused(stream)
+        if not self.fused:
+            raise ValueError("steps with several rows per slot run the fused sequence")
+        rows = [int(x) for x in rows]
+        if len(rows) != self.n or any(x < 1 or x > self.max_rows for x in rows):
+            raise ValueError(f"rows: one count per slot in 1..{self.max_rows}")
+        if tokens is None or len(tokens) != self.n or any(len(t) != x for t, x in zip(tokens, rows)):
+            raise ValueError("tokens: one list of ids per slot, as long as its row count")
+        with torch.cuda.stream(stream):
+            for i, t in enumerate(tokens):
+                self.tok_in[i, :rows[i]].copy_(torch.tensor(t, dtype=torch.int64))
+        return self._enqueue_fused(stream, rows)
 
-    def _enqueue_fused(self, stream: torch.cuda.Stream) -> None:
+    def _enqueue_fused(self, stream: torch.cuda.Stream, row_counts=None) -> None:
         """Fused sequence: per layer 4 rounds + 6 worker kernels (each worker
         kernel finishes one round's epilogue and starts the next round's LoRA)."""
         L, cfg, n, st = lib(), self.cfg, self.n, stream.cuda_stream
         H, I, D, r = cfg.hidden, cfg.inter, cfg.head_dim, cfg.rank
-        rows, s = self.a_rows, self.scaling
+        s = self.scaling
         nl = cfg.layers
-        check(L.swl_copy_rows(n, self.a_tok, self.a_in, self.a_b8, st))
-        self._round(agg.OP_EMBED, 0, st)
+        if row_counts is None:
+            rows, tx = self.a_rows, None
+            check(L.swl_copy_rows(n, self.a_tok, self.a_in, self.a_b8, st))
+        else:
+            rows, tx = i32_array(row_counts), i64_array(row_counts)
+            check(L.swl_copy_rows(n, ptr_array([self.tok_in[i].data_ptr() for i in range(n)]), self.a_in,
+                                  i64_array([8 * x for x in row_counts]), st))
+        self._round(agg.OP_EMBED, 0, st, tx)
         # embedding -> h, RMSNorm -> QKV slot input, QKV shrink
         pf = self.wptr
         none = (None, 0)
@@ -319,13 +348,14 @@ class SlotGroup:
         for l in range(nl):
             if self.qkv_rope_fused:
                 # the QKV round with the RoPE epilogue in its own epilogue
-                check(L.swl_agg_execute_qkv_rope_round(l, n, self.a_sids, self.a_wids, self.a_ones, self.a_ones,
+                check(L.swl_agg_execute_qkv_rope_round(l, n, self.a_sids, self.a_wids, self.a_ones,
+                                                       tx if tx is not None else self.a_ones,
                                                        self.B_qkv[l], r, self.ws_qkv.data_ptr(), self.norm_splits,
                                                        self.a_bt, self.a_kc[l], self.a_vc[l], self.a_sl, cfg.hq,
                                                        cfg.hkv, D, cfg.page, self.cos_sin.data_ptr(),
                                                        self.q_rot.data_ptr(), st))
             else:
-                self._round(agg.OP_QKV_FUSED, l, st)
+                self._round(agg.OP_QKV_FUSED, l, st, tx)
                 check(L.swl_fused_qkv_rope(n, rows, self.a_out, cfg.qkv_n, self.B_qkv[l], r,
                                            self.ws_qkv.data_ptr(), self.norm_splits, self.a_bt, self.a_kc[l],
                                            self.a_vc[l], self.a_sl, cfg.hq, cfg.hkv, D, cfg.page,
@@ -336,17 +366,17 @@ class SlotGroup:
                                                1.0 / math.sqrt(D), self.max_len, self.q_rot.data_ptr(),
                                                self.part.data_ptr(), self.A_o[l], r, self.ws_o.data_ptr(),
                                                None, 0, st))
-            self._round(agg.OP_O_PROJ, l, st)
+            self._round(agg.OP_O_PROJ, l, st, tx)
             check(L.swl_fused_resid_norm_shrink(n, rows, self.a_out, H, self.B_o[l], r, s, self.ws_o.data_ptr(),
                                                 cfg.hq, 1, self.a_h, H, self.base.post_norm[l].data_ptr(), H,
                                                 cfg.eps, self.a_in, H, self.A_gu[l], 2 * r,
                                                 self.ws_gu.data_ptr(), *pf.get((l, agg.OP_GATE_UP_FUSED), none),
                                                 st))
-            self._round(agg.OP_GATE_UP_FUSED, l, st)
+            self._round(agg.OP_GATE_UP_FUSED, l, st, tx)
             check(L.swl_fused_gu_silu_shrink(n, rows, self.a_out, 2 * I, self.B_gu[l], r, self.ws_gu.data_ptr(),
                                              self.norm_splits, I, self.a_in, I, self.A_dn[l], r,
                                              self.ws_dn.data_ptr(), *pf.get((l, agg.OP_DOWN_PROJ), none), st))
-            self._round(agg.OP_DOWN_PROJ, l, st)
+            self._round(agg.OP_DOWN_PROJ, l, st, tx)
             last = l == nl - 1
             w_next = self.base.final_norm if last else self.base.in_norm[l + 1]
             check(L.swl_fused_resid_norm_shrink(n, rows, self.a_out, H, self.B_dn[l], r, s, self.ws_dn.data_ptr(),
@@ -355,9 +385,13 @@ class SlotGroup:
                                                 self.ws_qkv.data_ptr(),
                                                 *pf.get("lm_head" if last else (l + 1, agg.OP_QKV_FUSED), none),
                                                 st))
-        self._round(agg.OP_LM_HEAD, 0, st)
+        self._round(agg.OP_LM_HEAD, 0, st, tx)  # the greedy pick reads each slot's last row
         check(L.swl_copy_rows(n, self.a_out, self.a_tok, self.a_b8, st))
-        check(L.swl_advance_i32(self.seqlens.data_ptr(), n, 1, st))
+        if row_counts is None or len(set(row_counts)) == 1:
+            check(L.swl_advance_i32(self.seqlens.data_ptr(), n, 1 if row_counts is None else row_counts[0], st))
+        else:
+            with torch.cuda.stream(stream):
+                self.seqlens.add_(torch.tensor(row_counts, dtype=torch.int32).to(self.dev))
 
     def _enqueue_unfused(self, stream: torch.cuda.Stream) -> None:
         """Modular sequence (one kernel per operation), kept as a cross-check."""

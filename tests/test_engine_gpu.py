@@ -233,3 +233,50 @@ def test_mixed_rank_adapters_and_hot_swap(native, cuda):
             assert torch.equal(grp.k_cache[l], k_now[l]) and torch.equal(grp.v_cache[l], v_now[l])
     finally:
         grp.close()
+
+
+def test_mixed_prefill_and_decode_step(native, cuda):
+    """The mixed configuration's step through the engine: slots carrying
+    prefill chunks (16, 5 and 3 new tokens, one of them into an empty
+    context) next to decode rows, packed into each round's gathered rows,
+    against the CPU oracle (every new row's K / V appended, attention causal
+    among a slot's new rows, the next token from each slot's last row); then
+    a plain decode step from the resulting state."""
+    from oracle.decode import decode_step
+    from swarmlora_b200.engine import ModelConfig, SlotGroup, random_adapter, random_base
+    cfg = ModelConfig(layers=2, vocab=4096)
+    ctx = [0, 20, 31, 100, 7]
+    rows = [16, 1, 5, 1, 3]
+    base = random_base(cfg, seed=3, device=cuda, norm_noise=0.1)
+    adapters = [random_adapter(cfg, seed=80 + i, device=cuda) if i != 1 else None for i in range(len(ctx))]
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=32, seed=8)
+    try:
+        base_c, ad_c = _cpu(base), _cpu(adapters)
+        kc = [k.cpu() for k in grp.k_cache]
+        vc = [v.cpu() for v in grp.v_cache]
+        bts = [t.tolist() for t in grp.block_tables]
+        g = torch.Generator().manual_seed(9)
+        toks = [torch.randint(0, cfg.vocab, (r,), generator=g).tolist() for r in rows]
+        stream = torch.cuda.current_stream()
+        grp.enqueue_step(stream, rows=rows, tokens=toks)
+        torch.cuda.synchronize()
+        want, final, logits, h_last = decode_step(cfg, base_c, ad_c, kc, vc, bts, list(ctx), toks)
+        got_h = torch.stack([grp.h_rows[i, r - 1] for i, r in enumerate(rows)])
+        assert_close(got_h, h_last, "mixed step: last row's last-layer hidden", atol_rms=ATOL_RMS_MULTILAYER)
+        got = grp.tokens.cpu()
+        _check_tokens(got, want, logits, "mixed step")
+        seq = [c + r for c, r in zip(ctx, rows)]
+        assert grp.seqlens.cpu().tolist() == seq
+        for l in range(cfg.layers):  # layer l > 0's K / V come from hidden states after l layers
+            tol = {} if l == 0 else {"atol_rms": ATOL_RMS_MULTILAYER}
+            assert_close(grp.k_cache[l], kc[l], f"layer {l} K cache after the mixed step", **tol)
+            assert_close(grp.v_cache[l], vc[l], f"layer {l} V cache after the mixed step", **tol)
+        # a plain decode step continues from there
+        tokens = got.tolist()
+        grp.enqueue_step(stream)
+        torch.cuda.synchronize()
+        want, final, logits, h_last = decode_step(cfg, base_c, ad_c, kc, vc, bts, seq, tokens)
+        assert_close(grp.h, h_last, "decode after the mixed step: last-layer hidden", atol_rms=ATOL_RMS_MULTILAYER)
+        _check_tokens(grp.tokens.cpu(), want, logits, "decode after the mixed step")
+    finally:
+        grp.close()
