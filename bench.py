@@ -66,6 +66,9 @@ def parse():
     ap.add_argument("--attn-stages", type=int, default=0, help="attention page-ring depth 2..4 (0 = auto)")
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch every kernel fully serialized (no programmatic dependent launch)")
+    ap.add_argument("--churn", type=float, default=0.0, metavar="SECONDS",
+                    help="adapter-pool churn on one GPU for SECONDS of arrivals (ranks 8/16/32, swap on miss)")
+    ap.add_argument("--churn-slots", type=int, default=64)
     ap.add_argument("--shard", action="store_true",
                     help="column-sharded base weights over 2 GPUs (one slot group; torchrun, --gpus 2)")
     ap.add_argument("--profile-attention", action="store_true",
@@ -619,8 +622,62 @@ def shard_arm(args):
     return 0
 
 
+def churn_arm(args):
+    """The churn configuration on one GPU: a seeded trace of Poisson arrivals
+    (8/s), lognormal prompts and outputs, Zipf adapter ids over a pool of 500
+    adapters of ranks 8/16/32 (random-init, made on the device when missed),
+    an LRU cache of 32 of them, prefill in 16-row chunks next to decode rows
+    (at most 256 rows a step), all-decode steps replayed from a CUDA graph.
+    The clock is the device time of steps and swaps. Prints one JSON line."""
+    import dataclasses
+    import torch
+    from swarmlora_b200.churn import ChurnConfig, ChurnRunner, adapter_ranks, make_trace
+    from swarmlora_b200.engine import LLAMA_3_1_8B, SlotGroup, random_adapter, random_base
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ccfg = ChurnConfig()
+    cfg = dataclasses.replace(LLAMA_3_1_8B, layers=args.layers, vocab=args.vocab, rank=max(ccfg.ranks))
+    ranks = adapter_ranks(ccfg)
+
+    def load(aid):
+        return random_adapter(cfg, seed=10_000 + aid, device=dev, rank=int(ranks[aid]))
+    n = args.churn_slots
+    base = random_base(cfg, seed=1, device=dev)
+    a0 = load(0)
+    grp = SlotGroup(cfg, base, [a0] * n, [0] * n, max_new=ccfg.prompt_clip[1] + ccfg.output_clip[1] + 16,
+                    device=0, seed=0)
+    stream = torch.cuda.Stream(dev)
+
+    def timer(fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / 1e3
+    with torch.cuda.stream(stream):
+        grp.enqueue_step(stream)  # kernel attributes before capture
+    torch.cuda.synchronize()
+    for i in range(n):
+        grp.set_context(i, 0)
+    grp.capture(stream)
+    trace = make_trace(ccfg, args.churn, seed=0)
+    st = ChurnRunner(grp, trace, ccfg, load, timer, cfg.vocab, stream=stream).run()
+    print(json.dumps({"metric": "churn: decode tokens per device second (Llama-3.1-8B shape)",
+                      "requests": len(trace), **st.summary(), "dtype": "bf16",
+                      "config": {"workload": f"{args.churn:g} s of arrivals at {ccfg.rate}/s, pool {ccfg.pool_size} "
+                                             f"adapters r in {list(ccfg.ranks)}, cache {ccfg.cache_adapters}, "
+                                             f"{n} slots, {cfg.layers} layers, vocab {cfg.vocab}",
+                                 "data": "synthetic (seeded trace, random-init weights and adapters)"}}), flush=True)
+    grp.close()
+    return 0
+
+
 def main():
     args = parse()
+    if args.churn:
+        return churn_arm(args)
     if args.shard:
         return shard_arm(args)
     if args.profile_attention:

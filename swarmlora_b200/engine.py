@@ -471,6 +471,13 @@ class SlotGroup:
         torch.cuda.synchronize()
         return out
 
+    def set_context(self, i: int, length: int = 0) -> None:
+        """Sets slot i's cached length (a new request starts at 0; its pages
+        are reused), ordered on the current stream."""
+        if not 0 <= length <= self.max_len:
+            raise ValueError(f"context {length} outside 0..{self.max_len}")
+        self.seqlens[i].fill_(int(length))
+
     def reset_positions(self) -> None:
         self.seqlens.copy_(torch.tensor(self.ctx0, dtype=torch.int32))
 

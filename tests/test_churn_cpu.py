@@ -1,0 +1,87 @@
+"""The adapter-churn driver (swarmlora_b200.churn) on the CPU: the synthetic
+trace's distributions, the LRU adapter cache, and a full run of the step
+loop against a fake slot group that records what each step asked for."""
+import numpy as np
+import torch
+
+from swarmlora_b200.churn import AdapterCache, ChurnConfig, ChurnRunner, adapter_ranks, make_trace
+
+
+def test_trace_follows_its_distributions():
+    cfg = ChurnConfig()
+    tr = make_trace(cfg, 300.0, seed=1)
+    assert tr == make_trace(cfg, 300.0, seed=1)  # seeded
+    arr = np.array([r.arrival for r in tr])
+    assert np.all(np.diff(arr) >= 0) and arr[-1] < 300.0
+    assert abs(len(tr) / 300.0 - cfg.rate) < 0.5  # Poisson rate
+    prompts = np.array([r.prompt for r in tr])
+    outputs = np.array([r.output for r in tr])
+    assert prompts.min() >= 32 and prompts.max() <= 2048
+    assert outputs.min() >= 16 and outputs.max() <= 512
+    assert 200 <= np.median(prompts) <= 320 and 100 <= np.median(outputs) <= 160
+    counts = np.bincount([r.adapter for r in tr], minlength=cfg.pool_size)
+    assert counts.argmax() == 0 and counts[0] > counts[10] > 0  # Zipf: id 0 most popular
+    ranks = adapter_ranks(cfg)
+    assert set(np.unique(ranks)) == {8, 16, 32} and len(ranks) == cfg.pool_size
+
+
+def test_adapter_cache_is_lru():
+    c = AdapterCache(2)
+    loads = []
+
+    def load(aid):
+        loads.append(aid)
+        return f"A{aid}"
+    assert c.get(1, load) == ("A1", False, None)
+    assert c.get(2, load) == ("A2", False, None)
+    assert c.get(1, load) == ("A1", True, None)
+    assert c.get(3, load) == ("A3", False, 2)  # 2 was least recently used
+    assert c.get(2, load) == ("A2", False, 1)
+    assert loads == [1, 2, 3, 2] and (c.hits, c.misses) == (1, 4) and len(c) == 2
+
+
+class FakeGroup:
+    """Records the steps; each step's next token is a function of its inputs."""
+
+    def __init__(self, n, vocab=1000):
+        self.n, self.max_rows, self.max_len, self.vocab = n, 16, 4096, vocab
+        self.tokens = torch.zeros(n, dtype=torch.int64)
+        self.ctx = [0] * n
+        self.adapter = [None] * n
+        self.steps = []
+
+    def set_adapter(self, i, a):
+        self.adapter[i] = a
+
+    def set_context(self, i, length):
+        self.ctx[i] = length
+
+    def enqueue_step(self, stream, rows=None, tokens=None):
+        rows = rows or [1] * self.n
+        tokens = tokens or [[int(t)] for t in self.tokens]
+        self.steps.append((list(rows), [list(t) for t in tokens], list(self.ctx), list(self.adapter)))
+        for i in range(self.n):
+            self.ctx[i] += rows[i]
+            self.tokens[i] = (sum(tokens[i]) + 7 * i) % self.vocab
+
+
+def test_runner_serves_every_request():
+    cfg = ChurnConfig(rate=20.0, cache_adapters=3, pool_size=20, prompt_median=40, prompt_clip=(1, 80),
+                      output_median=12, output_clip=(1, 30), max_step_rows=24)
+    trace = make_trace(cfg, 2.0, seed=3)
+    g = FakeGroup(4)
+    runner = ChurnRunner(g, trace, cfg, load_adapter=lambda aid: f"adapter{aid}", timer=lambda fn: (fn(), 0.005)[1],
+                         vocab=g.vocab)
+    st = runner.run()
+    assert st.completed == len(trace)
+    assert st.prefill_tokens == sum(r.prompt for r in trace)
+    assert st.decode_tokens == sum(r.output - 1 for r in trace)
+    assert st.cache_hits + st.cache_misses == len(trace) and st.swaps <= len(trace)
+    for r in trace:  # first token after the whole prompt, done after the whole output
+        assert r.start >= r.arrival and r.first_token > r.start and r.done >= r.first_token
+    for rows, toks, ctx, adapters in g.steps:
+        assert all(1 <= x <= 16 for x in rows) and [len(t) for t in toks] == rows
+        assert sum(rows) <= cfg.max_step_rows
+        assert all(c + x <= g.max_len for c, x in zip(ctx, rows))
+    s = st.summary()
+    assert s["decode_tok_per_s"] > 0 and s["ttft_p50_s"] is not None
