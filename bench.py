@@ -626,7 +626,8 @@ def churn_arm(args):
     """The churn configuration on one GPU: a seeded trace of Poisson arrivals
     (8/s), lognormal prompts and outputs, Zipf adapter ids over a pool of 500
     adapters of ranks 8/16/32 (random-init, made on the device when missed),
-    an LRU cache of 32 of them, prefill in 16-row chunks next to decode rows
+    an LRU cache of 32 of them packed into slabs (a swap is one device
+    copy), prefill in 16-row chunks next to decode rows
     (at most 256 rows a step), all-decode steps replayed from a CUDA graph.
     The clock is the device time of steps and swaps. Prints one JSON line."""
     import dataclasses
@@ -639,13 +640,14 @@ def churn_arm(args):
     cfg = dataclasses.replace(LLAMA_3_1_8B, layers=args.layers, vocab=args.vocab, rank=max(ccfg.ranks))
     ranks = adapter_ranks(ccfg)
 
-    def load(aid):
-        return random_adapter(cfg, seed=10_000 + aid, device=dev, rank=int(ranks[aid]))
     n = args.churn_slots
     base = random_base(cfg, seed=1, device=dev)
-    a0 = load(0)
+    a0 = random_adapter(cfg, seed=10_000, device=dev, rank=int(ranks[0]))
     grp = SlotGroup(cfg, base, [a0] * n, [0] * n, max_new=ccfg.prompt_clip[1] + ccfg.output_clip[1] + 16,
                     device=0, seed=0)
+
+    def load(aid):  # a miss makes the adapter on the device and packs it into a slab
+        return grp.pack_adapter(random_adapter(cfg, seed=10_000 + aid, device=dev, rank=int(ranks[aid])))
     stream = torch.cuda.Stream(dev)
 
     def timer(fn):

@@ -117,7 +117,8 @@ class AdapterCache:
 class ChurnStats:
     steps: int = 0
     device_s: float = 0.0                  # sum of the measured step times
-    swap_s: float = 0.0                    # device time of the admissions (adapter swaps)
+    swap_s: float = 0.0                    # device time of the admissions (loads, swaps, resets)
+    load_s: float = 0.0                    # part of swap_s spent loading missed adapters
     completed: int = 0
     decode_tokens: int = 0
     prefill_tokens: int = 0
@@ -131,6 +132,7 @@ class ChurnStats:
         def pct(xs, q):
             return float(np.percentile(xs, q)) if xs else None
         return {"steps": self.steps, "device_s": round(self.device_s, 4), "swap_s": round(self.swap_s, 4),
+                "load_s": round(self.load_s, 4),
                 "completed": self.completed,
                 "decode_tokens": self.decode_tokens, "prefill_tokens": self.prefill_tokens,
                 "decode_tok_per_s": round(self.decode_tokens / self.device_s, 2) if self.device_s else None,
@@ -148,9 +150,11 @@ class ChurnRunner:
     set_context(i, length), enqueue_step(stream, rows=..., tokens=...) and
     tokens (the device next-token ids). timer(fn) runs fn on `stream` and
     returns its device time in seconds. load_adapter(aid) returns the
-    adapter (per-layer dicts) of a pool id; the cache keeps what it returned.
-    Admissions (adapter swaps, context resets) run on the same stream and
-    their time counts on the clock as well (stats.swap_s)."""
+    adapter of a pool id in a form set_adapter takes (SlotGroup: a
+    PackedAdapter, so a swap is one device copy); the cache keeps what it
+    returned. Admissions (loads on a miss, adapter swaps, context resets) run
+    on the same stream and their time counts on the clock as well
+    (stats.swap_s, of which stats.load_s loads)."""
 
     def __init__(self, group, trace: list[Request], cfg: ChurnConfig, load_adapter, timer, vocab: int,
                  stream=None, seed: int = 0):
@@ -177,7 +181,7 @@ class ChurnRunner:
             if req.prompt + req.output > self.g.max_len:
                 raise ValueError(f"request {req.rid}: {req.prompt + req.output} tokens exceed the "
                                  f"group's context {self.g.max_len}")
-            adapter, hit, _ = self.cache.get(req.adapter, self.load_adapter)
+            adapter, hit, _ = self.cache.get(req.adapter, self._load)
             if self.slot_adapter[i] != req.adapter:
                 self.g.set_adapter(i, adapter)
                 self.slot_adapter[i] = req.adapter
@@ -186,6 +190,11 @@ class ChurnRunner:
             self.g.set_context(i, 0)
             req.start = now
             self.slot_req[i] = req
+
+    def _load(self, aid: int):
+        out = []
+        self.stats.load_s += self.timer(lambda: out.append(self.load_adapter(aid)))
+        return out[0]
 
     def run(self, max_steps: int | None = None) -> ChurnStats:
         queue, pending = deque(), deque(self.trace)

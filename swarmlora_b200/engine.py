@@ -189,8 +189,12 @@ class SlotGroup:
         self.slot_out = [b[1] for b in bufs]
         # --- workers: adapters, KV, buffers ---------------------------------------
         # every adapter is packed at the group's rank cfg.rank (zero-padded
-        # when smaller, its own alpha / r folded into the O / Down lora_B)
-        self.lora = [None if ad is None else self._pack(ad) for ad in adapters]
+        # when smaller, its own alpha / r folded into the O / Down lora_B),
+        # each slot's in one slab (a swap is one device copy)
+        self.packed = [None if ad is None else
+                       wo.pack_lora_slab(ad.layers, rank=ad.rank) if isinstance(ad, wo.PackedAdapter) else
+                       self.pack_adapter(ad) for ad in adapters]
+        self.lora = [None if p is None else p.layers for p in self.packed]
         pps = (self.max_len + cfg.page - 1) // cfg.page
         g = torch.Generator(device=self.dev).manual_seed(seed + 7)
         perm = torch.randperm(n * pps, generator=g, device=self.dev).to(torch.int32)
@@ -274,26 +278,36 @@ class SlotGroup:
         self.ends_h = i64_array([H, H, H])
         self.scaling = cfg.alpha / r
 
-    def _pack(self, adapter) -> list:
+    def pack_adapter(self, adapter) -> wo.PackedAdapter:
+        """An adapter (per-layer dicts as random_adapter makes, any rank that
+        is a multiple of 8 up to the group's) packed at the group's rank into
+        one slab: the form a cache of resident adapters keeps, ready for
+        set_adapter."""
         cfg = self.cfg
         r = int(adapter[0]["q"][0].shape[0])
         if r > cfg.rank or r % 8:
             raise ValueError(f"adapter rank {r}: must be a multiple of 8 and at most the group's rank {cfg.rank}")
-        return [wo.pack_lora_layer(adapter[l], cfg.alpha / r, pad_rank=cfg.rank, post_scale=cfg.alpha / cfg.rank)
-                for l in range(cfg.layers)]
+        return wo.pack_lora_slab([wo.pack_lora_layer(adapter[l], cfg.alpha / r, pad_rank=cfg.rank,
+                                                     post_scale=cfg.alpha / cfg.rank)
+                                  for l in range(cfg.layers)], rank=r)
 
     def set_adapter(self, i: int, adapter) -> None:
-        """Replaces slot i's adapter (per-layer dicts as random_adapter makes,
-        any rank up to the group's) in place: it is packed at the group's rank
-        and copied into the slot's existing buffers on the current stream, so
-        a captured step graph keeps working and its next replay uses it. Call
-        it between steps, ordered after the last step on that stream. A slot
-        built without an adapter has no buffers to swap into."""
-        if self.lora[i] is None:
+        """Replaces slot i's adapter in place, from a PackedAdapter
+        (pack_adapter: one device copy of its slab) or from per-layer dicts
+        (packed first). The copy runs on the current stream into the slot's
+        existing buffers, so a captured step graph keeps working and its next
+        replay uses the new adapter. Call it between steps, ordered after the
+        last step on that stream. A slot built without an adapter has no
+        buffers to swap into."""
+        if self.packed[i] is None:
             raise ValueError(f"slot {i} was built without an adapter")
-        for old, new in zip(self.lora[i], self._pack(adapter)):
-            for name in ("A_qkv", "B_qkv", "A_o", "B_o", "A_gu", "B_gu", "A_down", "B_down"):
-                getattr(old, name).copy_(getattr(new, name))
+        if not isinstance(adapter, wo.PackedAdapter):
+            adapter = self.pack_adapter(adapter)
+        dst = self.packed[i]
+        if adapter.slab.numel() != dst.slab.numel() or adapter.slab.device != dst.slab.device:
+            raise ValueError("packed adapter does not match the group's layout (model, rank or device)")
+        dst.slab.copy_(adapter.slab)
+        dst.rank = adapter.rank
 
     def _round(self, op, layer, st, tx=None):
         check(lib().swl_agg_execute_round(op, layer, self.n, self.a_sids, self.a_wids, self.a_ones,

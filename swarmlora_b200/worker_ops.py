@@ -84,6 +84,45 @@ def pack_lora_layer(w: dict, scaling: float, pad_rank: int | None = None,
     )
 
 
+LORA_FIELDS = ("A_qkv", "B_qkv", "A_o", "B_o", "A_gu", "B_gu", "A_down", "B_down")
+_SLAB_ALIGN = 128  # elements: every tensor of a slab starts on a 256-byte boundary
+
+
+@dataclass
+class PackedAdapter:
+    """All layers of one adapter in one contiguous bf16 buffer (`slab`);
+    `layers` are LoraLayers whose tensors are views into it. Adapters packed
+    at the same rank for the same model share the layout, so a slot's adapter
+    is replaced by one device copy of the slab."""
+    slab: torch.Tensor
+    layers: list
+    rank: int            # the adapter's own rank (the slab holds it padded)
+
+
+def pack_lora_slab(layers: list, rank: int | None = None) -> PackedAdapter:
+    """Copies packed layers (pack_lora_layer) into one slab, fields in
+    LORA_FIELDS order layer after layer."""
+    offs, total = [], 0
+    for L in layers:
+        row = []
+        for f in LORA_FIELDS:
+            t = getattr(L, f)
+            row.append((total, tuple(t.shape)))
+            total += -(-t.numel() // _SLAB_ALIGN) * _SLAB_ALIGN
+        offs.append(row)
+    slab = torch.empty(total, dtype=torch.bfloat16, device=layers[0].A_qkv.device)
+    views = []
+    for L, row in zip(layers, offs):
+        kw = {}
+        for f, (o, shape) in zip(LORA_FIELDS, row):
+            n = shape[0] * shape[1]
+            v = slab[o:o + n].view(shape)
+            v.copy_(getattr(L, f))
+            kw[f] = v
+        views.append(LoraLayer(**kw, rank=L.rank, scaling=L.scaling))
+    return PackedAdapter(slab, views, int(rank) if rank is not None else layers[0].rank)
+
+
 def lora_shrink(xs, As, K: int, R: int, splits: int, ws: torch.Tensor, x_stride: int | None = None,
                 rows=None, stream=None) -> None:
     rows = rows if rows is not None else [int(x.shape[0]) for x in xs]

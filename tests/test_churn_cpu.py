@@ -1,9 +1,11 @@
 """The adapter-churn driver (swarmlora_b200.churn) on the CPU: the synthetic
-trace's distributions, the LRU adapter cache, and a full run of the step
-loop against a fake slot group that records what each step asked for."""
+trace's distributions, the LRU adapter cache, a full run of the step loop
+against a fake slot group that records what each step asked for, and the
+packed-adapter slab a swap copies."""
 import numpy as np
 import torch
 
+from swarmlora_b200 import worker_ops as wo
 from swarmlora_b200.churn import AdapterCache, ChurnConfig, ChurnRunner, adapter_ranks, make_trace
 
 
@@ -77,6 +79,7 @@ def test_runner_serves_every_request():
     assert st.prefill_tokens == sum(r.prompt for r in trace)
     assert st.decode_tokens == sum(r.output - 1 for r in trace)
     assert st.cache_hits + st.cache_misses == len(trace) and st.swaps <= len(trace)
+    assert abs(st.load_s - 0.005 * st.cache_misses) < 1e-9 and st.swap_s >= st.load_s
     for r in trace:  # first token after the whole prompt, done after the whole output
         assert r.start >= r.arrival and r.first_token > r.start and r.done >= r.first_token
     for rows, toks, ctx, adapters in g.steps:
@@ -85,3 +88,40 @@ def test_runner_serves_every_request():
         assert all(c + x <= g.max_len for c, x in zip(ctx, rows))
     s = st.summary()
     assert s["decode_tok_per_s"] > 0 and s["ttft_p50_s"] is not None
+
+
+def _tiny_adapter(g, r, H=64, I=96, q=64, kv=32):
+    dims = {"q": (H, q), "k": (H, kv), "v": (H, kv), "o": (q, H), "gate": (H, I), "up": (H, I), "down": (I, H)}
+    return [{nm: ((torch.randn(r, i, generator=g) * 0.02).to(torch.bfloat16),
+                  (torch.randn(o, r, generator=g) * 0.02).to(torch.bfloat16)) for nm, (i, o) in dims.items()}
+            for _ in range(3)]
+
+
+def test_packed_adapter_slab_layout_and_swap():
+    """Adapters of ranks 8 and 16 packed at rank 16 share one slab layout;
+    the slab's views hold the packed tensors, start on 256-byte boundaries,
+    and copying one slab into another swaps every layer's tensors."""
+    g = torch.Generator().manual_seed(4)
+    R, alpha = 16, 32
+
+    def pack(ad):
+        r = int(ad[0]["q"][0].shape[0])
+        layers = [wo.pack_lora_layer(w, alpha / r, pad_rank=R, post_scale=alpha / R) for w in ad]
+        return layers, wo.pack_lora_slab(layers, rank=r)
+    la, pa = pack(_tiny_adapter(g, 8))
+    lb, pb = pack(_tiny_adapter(g, 16))
+    assert pa.slab.numel() == pb.slab.numel() and (pa.rank, pb.rank) == (8, 16)
+    base = pa.slab.data_ptr()
+    for packed, layers in ((pa, la), (pb, lb)):
+        for v, L in zip(packed.layers, layers):
+            assert v.rank == R
+            for f in wo.LORA_FIELDS:
+                t = getattr(v, f)
+                assert torch.equal(t, getattr(L, f)) and t.is_contiguous()
+                assert t.untyped_storage().data_ptr() == packed.slab.untyped_storage().data_ptr()
+                assert (t.data_ptr() - packed.slab.data_ptr()) % 256 == 0
+    assert all((getattr(v, f).data_ptr() - base) % 256 == 0 for v in pa.layers for f in wo.LORA_FIELDS)
+    pa.slab.copy_(pb.slab)  # the swap: one copy replaces every tensor
+    for v, L in zip(pa.layers, lb):
+        for f in wo.LORA_FIELDS:
+            assert torch.equal(getattr(v, f), getattr(L, f))

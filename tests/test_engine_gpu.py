@@ -224,8 +224,8 @@ def test_mixed_rank_adapters_and_hot_swap(native, cuda):
         grp.set_adapter(3, adapters[3])
         for _ in range(2):
             grp.replay()
-        grp.set_adapter(1, new1)
-        grp.set_adapter(3, new3)
+        grp.set_adapter(1, grp.pack_adapter(new1))  # packed slabs: one device copy per swap
+        grp.set_adapter(3, grp.pack_adapter(new3))
         grp.replay()
         torch.cuda.synchronize()
         assert torch.equal(grp.tokens.cpu(), eager), "graph replay after the swap differs from the eager step"
