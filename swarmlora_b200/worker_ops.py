@@ -85,7 +85,7 @@ def pack_lora_layer(w: dict, scaling: float, pad_rank: int | None = None,
 
 
 LORA_FIELDS = ("A_qkv", "B_qkv", "A_o", "B_o", "A_gu", "B_gu", "A_down", "B_down")
-_SLAB_ALIGN = 128  # elements: every tensor of a slab starts on a 256-byte boundary
+_SLAB_ALIGN = 256  # elements: every tensor of a slab starts on a 512-byte boundary, as torch allocates
 
 
 @dataclass

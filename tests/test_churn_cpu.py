@@ -99,7 +99,7 @@ def _tiny_adapter(g, r, H=64, I=96, q=64, kv=32):
 
 def test_packed_adapter_slab_layout_and_swap():
     """Adapters of ranks 8 and 16 packed at rank 16 share one slab layout;
-    the slab's views hold the packed tensors, start on 256-byte boundaries,
+    the slab's views hold the packed tensors, start on 512-byte boundaries,
     and copying one slab into another swaps every layer's tensors."""
     g = torch.Generator().manual_seed(4)
     R, alpha = 16, 32
@@ -119,8 +119,8 @@ def test_packed_adapter_slab_layout_and_swap():
                 t = getattr(v, f)
                 assert torch.equal(t, getattr(L, f)) and t.is_contiguous()
                 assert t.untyped_storage().data_ptr() == packed.slab.untyped_storage().data_ptr()
-                assert (t.data_ptr() - packed.slab.data_ptr()) % 256 == 0
-    assert all((getattr(v, f).data_ptr() - base) % 256 == 0 for v in pa.layers for f in wo.LORA_FIELDS)
+                assert (t.data_ptr() - packed.slab.data_ptr()) % 512 == 0
+    assert all((getattr(v, f).data_ptr() - base) % 512 == 0 for v in pa.layers for f in wo.LORA_FIELDS)
     pa.slab.copy_(pb.slab)  # the swap: one copy replaces every tensor
     for v, L in zip(pa.layers, lb):
         for f in wo.LORA_FIELDS:
