@@ -278,16 +278,20 @@ class SlotGroup:
         self.ends_h = i64_array([H, H, H])
         self.scaling = cfg.alpha / r
 
-    def pack_adapter(self, adapter) -> wo.PackedAdapter:
-        """An adapter (per-layer dicts as random_adapter makes, any rank that
-        is a multiple of 8 up to the group's) packed at the group's rank into
-        one slab: the form a cache of resident adapters keeps, ready for
-        set_adapter."""
+    def pack_adapter(self, adapter, scaling: float | None = None) -> wo.PackedAdapter:
+        """An adapter (per-layer dicts as random_adapter or
+        adapters.AdapterLoader.load make, any rank up to the group's) packed
+        at the group's rank into one slab: the form a cache of resident
+        adapters keeps, ready for set_adapter. `scaling` is the adapter's
+        lora_alpha / r (default the group's alpha / r); its ratio to the
+        group's alpha / rank is folded into the O / Down lora_B, exact when
+        that ratio is a power of two."""
         cfg = self.cfg
         r = int(adapter[0]["q"][0].shape[0])
-        if r > cfg.rank or r % 8:
-            raise ValueError(f"adapter rank {r}: must be a multiple of 8 and at most the group's rank {cfg.rank}")
-        return wo.pack_lora_slab([wo.pack_lora_layer(adapter[l], cfg.alpha / r, pad_rank=cfg.rank,
+        if not 1 <= r <= cfg.rank:
+            raise ValueError(f"adapter rank {r}: must be at most the group's rank {cfg.rank}")
+        s = float(scaling) if scaling is not None else cfg.alpha / r
+        return wo.pack_lora_slab([wo.pack_lora_layer(adapter[l], s, pad_rank=cfg.rank,
                                                      post_scale=cfg.alpha / cfg.rank)
                                   for l in range(cfg.layers)], rank=r)
 

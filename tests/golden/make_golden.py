@@ -11,7 +11,12 @@ own Python code for the hot path's worker-side arithmetic (on CPU):
     Llama-3.1 LlamaRotaryEmbedding (the worker's rotary module,
     model_builder.py:293-303);
   * PagedKVCache block bookkeeping (paged_attention.py:7-128) on a scripted
-    sequence of allocations, frees and advances.
+    sequence of allocations, frees and advances;
+  * two tiny adapter directories written by the reference's adapter
+    generator (generate_adapters.py:65-129: fp32 safetensors in the PEFT
+    layout), one with every projection at alpha = r, one at rank 8 with
+    lora_alpha 16 and without v_proj / down_proj, and what the reference's
+    loader (model_builder.py:137-183, load_lora_fast) reads from them.
 
 Run from the repository root where the reference checkout is available:
     python tests/golden/make_golden.py /path/to/reference
@@ -121,8 +126,46 @@ def paged_case(pa):
     return {"num_blocks": c.num_blocks, "block_size": 16, "script": PAGED_SCRIPT, "snaps": snaps}
 
 
+# (in_features, out_features) of a 2-layer model with hidden 64, 2 / 1
+# heads of 32, intermediate 96 (engine.ModelConfig(hidden=64, inter=96,
+# layers=2, hq=2, hkv=1, head_dim=32))
+TINY_MODULES = {"self_attn.q_proj": (64, 64), "self_attn.k_proj": (64, 32), "self_attn.v_proj": (64, 32),
+                "self_attn.o_proj": (64, 64), "mlp.gate_proj": (64, 96), "mlp.up_proj": (64, 96),
+                "mlp.down_proj": (96, 64)}
+
+
+def adapter_cases(mb, ref_root: Path):
+    import importlib.util
+    import json
+    from safetensors.torch import save_file
+    spec = importlib.util.spec_from_file_location("ref_generate_adapters", ref_root / "generate_adapters.py")
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    partial = {k: v for k, v in TINY_MODULES.items() if k not in ("self_attn.v_proj", "mlp.down_proj")}
+    out = {}
+    for name, rank, alpha, mods, seed in (("adapter_r4", 4, None, TINY_MODULES, 11),
+                                          ("adapter_r8_partial", 8, 16, partial, 12)):
+        d = OUT / name
+        d.mkdir(exist_ok=True)
+        save_file(gen.generate_adapter(rank, seed=seed, num_layers=2, modules=mods),
+                  str(d / "adapter_model.safetensors"))
+        cfg = gen.make_config(rank)
+        if alpha is not None:
+            cfg["lora_alpha"] = alpha
+        cfg["target_modules"] = sorted({k.split(".")[1] for k in mods})
+        (d / "adapter_config.json").write_text(json.dumps(cfg, indent=2))
+        loaded, config = mb.load_lora_fast(str(d), "cpu", BF)
+        out[name] = {"r": config["r"], "lora_alpha": config.get("lora_alpha", config["r"]),
+                     "modules": {(layer, mod): (m.lora_A["default"].weight.detach().clone(),
+                                                m.lora_B["default"].weight.detach().clone(),
+                                                float(m.scaling["default"]))
+                                 for layer, ms in loaded.items() for mod, m in ms.items()}}
+    return out
+
+
 def main(ref_root: str) -> None:
     mb, pa = _import_reference(Path(ref_root))
+    torch.save(adapter_cases(mb, Path(ref_root)), OUT / "adapter_load.pt")
     g = torch.Generator().manual_seed(20261201)
     torch.save({"qkv": fused_lora_case(mb, g, 256, (256, 64, 64), 8, 2.0, 3),
                 "qkv_missing_k": fused_lora_case(mb, g, 256, (256, 64, 64), 8, 2.0, 2, missing=(1,)),
