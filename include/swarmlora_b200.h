@@ -145,7 +145,8 @@ int swl_agg_init_queue(const char* shm_name, int capacity);
 /* Round kernel: 0 auto (= 1), 1 tcgen05 cluster split-K, 2 CUDA cores,
  * 3 tcgen05 stream-K (<= 64 rows); splits <= 0 = automatic K split. */
 int swl_agg_set_round_algo(int algo, int splits);
-/* Fused weight of (layer, op) and its [N, K] shape. */
+/* Fused weight of (layer, op) and its [N, K] shape; OP_EMBED / OP_LM_HEAD
+ * give the [vocab, hidden] tables (layer ignored). */
 int swl_agg_weight(int layer, int op, const void** W, int64_t* N, int64_t* K);
 /* One round over pool slots — execute_batched_gemm_slots (ext_aggregator.cpp:
  * 470-626), execute_batched_embed_slots (:630-706) or the greedy LM head
@@ -168,6 +169,36 @@ int swl_agg_execute_qkv_rope_round(int layer, int n, const int* slot_ids, const 
                                    void* const* k_cache, void* const* v_cache, const void* const* seqlens,
                                    int hq, int hkv, int head_dim, int page, const void* cos_sin, void* q_rot,
                                    void* stream);
+/* Donor weight transfer for multi-GPU bring-up — export_weight_ipc_handles /
+ * import_weights_from_ipc (ext_aggregator.cpp:1216-1406). One record per
+ * weight, in this order: per layer l, records 6l..6l+5 = fused qkv
+ * [q+k+v, hidden], o [o_out, hidden], fused gate_up [gate+up, hidden], down
+ * [down_out, inter], o_bias [o_out, 1], down_bias [down_out, 1] (rows 0 =
+ * absent); then embed and lm_head [vocab, hidden]. All bf16 row-major.
+ * dims holds 5 int64 per layer: q, k, v, gate, up output sizes. Unlike the
+ * reference's handles, a record names the allocation holding the weight
+ * and the weight's byte offset in it, so weights inside a larger allocation
+ * (a caching allocator's block) are exported correctly. */
+typedef struct swl_weight_ipc {
+  unsigned char handle[64]; /* cudaIpcMemHandle_t of the allocation */
+  uint64_t offset;          /* bytes from the allocation's base */
+  int64_t rows, cols;
+} swl_weight_ipc;
+/* Fills `recs` (room for cap = 6 * num_layers + 2 records) and `dims`
+ * (5 * num_layers) from this aggregator's weights; with recs == NULL only
+ * *num_layers and *device_index are returned. Needs the layers and the LM
+ * head initialised. The donor process must keep its weights alive until
+ * every receiver's import has returned. */
+int swl_agg_export_weights(swl_weight_ipc* recs, int cap, int64_t* dims, int* num_layers,
+                           int* device_index);
+/* Replaces this aggregator's weights with copies of a donor's (another
+ * process, any GPU of the node): maps each distinct allocation once, checks
+ * every record against the mapped range, copies all weights into one
+ * library-owned arena on device_index (peer copies over NVLink when the
+ * donor is another GPU), unmaps, and leaves the aggregator as after
+ * init_aggregator_finalize + init_embed_lm_head_weights. */
+int swl_agg_import_weights(const swl_weight_ipc* recs, int count, const int64_t* dims, int num_layers,
+                           int device_index);
 /* Column-sharded base weights over a pair of GPUs, one process each (the
  * multi-GPU configuration's variant with an NVLink all-gather of outputs; no
  * reference counterpart). After the pool, layers and LM head are set up:

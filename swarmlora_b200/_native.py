@@ -21,6 +21,15 @@ _psz = C.POINTER(C.c_size_t)
 _pp = C.POINTER(C.c_void_p)
 _pu32 = C.POINTER(C.c_uint)
 
+
+class WeightIpc(C.Structure):
+    """swl_weight_ipc: one weight of a donor export (allocation handle, byte
+    offset in it, bf16 [rows, cols]; rows 0 = absent)."""
+    _fields_ = [("handle", C.c_ubyte * 64), ("offset", C.c_uint64), ("rows", C.c_int64), ("cols", C.c_int64)]
+
+
+_pwipc = C.POINTER(WeightIpc)
+
 # name -> (restype, argtypes). Kept in the same order as include/swarmlora_b200.h.
 SIGNATURES: dict[str, tuple] = {
     "swl_last_error": (_cp, []),
@@ -66,6 +75,8 @@ SIGNATURES: dict[str, tuple] = {
     "swl_agg_execute_round": (_i32, [_i32, _i32, _i32, _pi32, _pi32, _pi64, _pi64, _p]),
     "swl_agg_execute_qkv_rope_round": (_i32, [_i32, _i32, _pi32, _pi32, _pi64, _pi64, _pp, _i32, _p, _i32, _pp, _pp, _pp,
                                                _pp, _i32, _i32, _i32, _i32, _p, _p, _p]),
+    "swl_agg_export_weights": (_i32, [_pwipc, _i32, _pi64, _pi32, _pi32]),
+    "swl_agg_import_weights": (_i32, [_pwipc, _i32, _pi64, _i32, _i32]),
     "swl_agg_shard_begin": (_i32, [_i32, _i32]),
     "swl_agg_shard_handles": (_i32, [_p, _i32, _pi32]),
     "swl_agg_shard_connect": (_i32, [_p, _i32]),

@@ -20,13 +20,14 @@ from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
+INCLUDE = PKG.parent / "include"  # the public C header, checked against the definitions
 BUILD = PKG / "_build"
 LIBDIR = PKG / "_lib"
 LIB = LIBDIR / "libswarmlora_b200.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
-          "--expt-relaxed-constexpr", "-I", str(CSRC)]
+          "--expt-relaxed-constexpr", "-I", str(CSRC), "-I", str(INCLUDE)]
 
 
 def nvcc() -> str:
@@ -41,7 +42,7 @@ def _sources():
 
 
 def _headers_mtime() -> float:
-    hs = list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh"))
+    hs = list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
     return max((h.stat().st_mtime for h in hs), default=0.0)
 
 

@@ -12,6 +12,8 @@
 //  * o_proj / down_proj / embed / lm_head weights are borrowed (the caller
 //    keeps them alive), q|k|v and gate|up are fused into library-owned copies,
 //    the same memory behaviour as the reference's detach()/cat().
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <fcntl.h>
 #include <sys/mman.h>
@@ -27,6 +29,7 @@
 
 #include "common.h"
 #include "shm_abi.h"
+#include "swarmlora_b200.h"
 #include "slot_round.h"
 #include "vocab_ops.h"
 #include "worker_ops.h"
@@ -65,6 +68,7 @@ struct Layer {
   const void* down_bias = nullptr;
   int64_t q_dim = 0, k_dim = 0, v_dim = 0, gate_dim = 0, up_dim = 0;
   int64_t hidden = 0, inter = 0, o_out = 0, down_out = 0;
+  bool owns_fused = true;  // qkv / gu are separate allocations (not in g_arena)
   CUtensorMap tm_qkv, tm_o, tm_gu, tm_down;
 };
 
@@ -81,8 +85,9 @@ int g_num_layers = 0;
 bool g_weights_ready = false;
 int g_device = 0;
 
-const void* g_embed = nullptr;    // borrowed [vocab, hidden]
-const void* g_lm_head = nullptr;  // borrowed [vocab, hidden]
+const void* g_embed = nullptr;    // borrowed [vocab, hidden] (or in g_arena)
+const void* g_lm_head = nullptr;  // borrowed [vocab, hidden] (or in g_arena)
+void* g_arena = nullptr;          // every weight, after swl_agg_import_weights
 CUtensorMap g_tm_lm;
 int64_t g_vocab = 0, g_embed_hidden = 0;
 bool g_vocab_ready = false;
@@ -480,14 +485,33 @@ SWL_EXPORT int swl_agg_cleanup_slot_pool(void) {
 
 // ===== weights ===============================================================
 
+// Frees the library-owned weights: the fused copies, or the arena of an
+// import (which also held embed / lm_head, so those are forgotten with it).
+int free_weights() {
+  SWL_TRY(shard_end());  // its row views point into these weights
+  for (Layer& L : g_layers) {
+    if (L.owns_fused) {
+      if (L.qkv) cudaFree(L.qkv);
+      if (L.gu) cudaFree(L.gu);
+    }
+    L.qkv = L.gu = nullptr;
+  }
+  if (g_arena) {
+    SWL_CUDA_TRY(cudaDeviceSynchronize());
+    cudaFree(g_arena);
+    g_arena = nullptr;
+    g_embed = g_lm_head = nullptr;
+    g_vocab_ready = false;
+  }
+  g_weights_ready = false;
+  return SWL_OK;
+}
+
 // ext_aggregator.cpp:338-345 init_aggregator_begin.
 SWL_EXPORT int swl_agg_init_begin(int num_layers, int device_index) {
   if (num_layers <= 0) return set_error(SWL_ERR_ARG, "init_aggregator_begin: num_layers must be > 0");
   SWL_CUDA_TRY(cudaSetDevice(device_index));
-  for (Layer& L : g_layers) {
-    if (L.qkv) cudaFree(L.qkv);
-    if (L.gu) cudaFree(L.gu);
-  }
+  SWL_TRY(free_weights());
   g_layers.assign(num_layers, Layer());
   g_num_layers = num_layers;
   g_device = device_index;
@@ -511,8 +535,10 @@ SWL_EXPORT int swl_agg_init_layer(int layer_idx, const void* q, int64_t q_rows, 
   if (!q || !k || !v || !o || !gate || !up || !down)
     return set_error(SWL_ERR_ARG, "init_aggregator_layer: null weight");
   Layer& L = g_layers[layer_idx];
-  if (L.qkv) cudaFree(L.qkv);
-  if (L.gu) cudaFree(L.gu);
+  if (L.owns_fused) {
+    if (L.qkv) cudaFree(L.qkv);
+    if (L.gu) cudaFree(L.gu);
+  }
   L = Layer();
   L.q_dim = q_rows; L.k_dim = k_rows; L.v_dim = v_rows;
   L.gate_dim = gate_rows; L.up_dim = up_rows;
@@ -572,6 +598,220 @@ SWL_EXPORT int swl_agg_init_embed_lm_head(const void* embed, const void* lm_head
   return SWL_OK;
 }
 
+// ===== donor weight transfer ==================================================
+
+constexpr int kRecsPerLayer = 6;  // qkv, o, gate_up, down, o_bias, down_bias
+constexpr size_t kArenaAlign = 512;
+
+PFN_cuMemGetAddressRange_v3020 address_range_fn() {
+  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+  });
+  return fn;
+}
+
+// The allocation holding `p`: its base and size.
+int allocation_of(const void* p, char** base, size_t* size) {
+  auto fn = address_range_fn();
+  if (!fn) return set_error(SWL_ERR_CUDA, "cuMemGetAddressRange is unavailable");
+  CUdeviceptr b = 0;
+  size_t n = 0;
+  CUresult r = fn(&b, &n, reinterpret_cast<CUdeviceptr>(p));
+  if (r != CUDA_SUCCESS) return set_error(SWL_ERR_CUDA, "cuMemGetAddressRange failed (%d)", static_cast<int>(r));
+  *base = reinterpret_cast<char*>(b);
+  *size = n;
+  return SWL_OK;
+}
+
+// One handle per allocation, so a receiver maps each allocation once.
+using HandleCache = std::vector<std::pair<char*, cudaIpcMemHandle_t>>;
+
+int export_one(HandleCache& cache, swl_weight_ipc* rec, const void* p, int64_t rows, int64_t cols) {
+  memset(rec, 0, sizeof(*rec));
+  if (!p || rows <= 0) return SWL_OK;  // absent (bias)
+  char* base = nullptr;
+  size_t size = 0;
+  SWL_TRY(allocation_of(p, &base, &size));
+  const cudaIpcMemHandle_t* hp = nullptr;
+  for (const auto& c : cache)
+    if (c.first == base) hp = &c.second;
+  if (!hp) {
+    cudaIpcMemHandle_t h;
+    SWL_CUDA_TRY(cudaIpcGetMemHandle(&h, base));
+    cache.emplace_back(base, h);
+    hp = &cache.back().second;
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(rec->handle), "IPC handle size");
+  memcpy(rec->handle, hp, sizeof(rec->handle));
+  rec->offset = static_cast<uint64_t>(static_cast<const char*>(p) - base);
+  rec->rows = rows;
+  rec->cols = cols;
+  return SWL_OK;
+}
+
+// export_weight_ipc_handles (ext_aggregator.cpp:1216-1291), as records with
+// offsets (layout in the public header).
+SWL_EXPORT int swl_agg_export_weights(swl_weight_ipc* recs, int cap, int64_t* dims, int* num_layers,
+                                      int* device_index) {
+  if (!g_weights_ready) return set_error(SWL_ERR_STATE, "export_weight_ipc_handles: weights not initialized");
+  if (!g_vocab_ready)
+    return set_error(SWL_ERR_STATE, "export_weight_ipc_handles: embed/lm_head not initialized");
+  if (num_layers) *num_layers = g_num_layers;
+  if (device_index) *device_index = g_device;
+  if (!recs) return SWL_OK;
+  const int need = kRecsPerLayer * g_num_layers + 2;
+  if (cap < need || !dims) return set_error(SWL_ERR_ARG, "export_weight_ipc_handles: room for %d records needed", need);
+  SWL_CUDA_TRY(cudaSetDevice(g_device));
+  HandleCache cache;
+  for (int l = 0; l < g_num_layers; ++l) {
+    const Layer& L = g_layers[l];
+    swl_weight_ipc* r = recs + kRecsPerLayer * l;
+    SWL_TRY(export_one(cache, r + 0, L.qkv, L.q_dim + L.k_dim + L.v_dim, L.hidden));
+    SWL_TRY(export_one(cache, r + 1, L.o, L.o_out, L.hidden));
+    SWL_TRY(export_one(cache, r + 2, L.gu, L.gate_dim + L.up_dim, L.hidden));
+    SWL_TRY(export_one(cache, r + 3, L.down, L.down_out, L.inter));
+    SWL_TRY(export_one(cache, r + 4, L.o_bias, L.o_bias ? L.o_out : 0, 1));
+    SWL_TRY(export_one(cache, r + 5, L.down_bias, L.down_bias ? L.down_out : 0, 1));
+    int64_t* d = dims + 5 * l;
+    d[0] = L.q_dim; d[1] = L.k_dim; d[2] = L.v_dim; d[3] = L.gate_dim; d[4] = L.up_dim;
+  }
+  SWL_TRY(export_one(cache, recs + kRecsPerLayer * g_num_layers, g_embed, g_vocab, g_embed_hidden));
+  SWL_TRY(export_one(cache, recs + kRecsPerLayer * g_num_layers + 1, g_lm_head, g_vocab, g_embed_hidden));
+  return SWL_OK;
+}
+
+// Checks the records' shapes against each other before anything is mapped.
+int check_import_records(const swl_weight_ipc* recs, const int64_t* dims, int L) {
+  const swl_weight_ipc& emb = recs[kRecsPerLayer * L];
+  const swl_weight_ipc& lm = recs[kRecsPerLayer * L + 1];
+  const int64_t hidden = emb.cols;
+  if (emb.rows <= 0 || hidden <= 0 || lm.rows != emb.rows || lm.cols != hidden)
+    return set_error(SWL_ERR_ARG, "import_weights_from_ipc: embed / lm_head shapes disagree");
+  for (int l = 0; l < L; ++l) {
+    const swl_weight_ipc* r = recs + kRecsPerLayer * l;
+    const int64_t* d = dims + 5 * l;
+    for (int j = 0; j < 5; ++j)
+      if (d[j] <= 0) return set_error(SWL_ERR_ARG, "import_weights_from_ipc: layer %d has a dimension <= 0", l);
+    const int64_t inter = r[3].cols;
+    const bool ok = r[0].rows == d[0] + d[1] + d[2] && r[0].cols == hidden && r[1].rows > 0 &&
+                    r[1].cols == hidden && r[2].rows == d[3] + d[4] && r[2].cols == hidden &&
+                    r[3].rows > 0 && inter > 0 && (r[4].rows == 0 || (r[4].rows == r[1].rows && r[4].cols == 1)) &&
+                    (r[5].rows == 0 || (r[5].rows == r[3].rows && r[5].cols == 1));
+    if (!ok) return set_error(SWL_ERR_ARG, "import_weights_from_ipc: layer %d shapes disagree", l);
+  }
+  return SWL_OK;
+}
+
+// import_weights_from_ipc (ext_aggregator.cpp:1294-1406).
+SWL_EXPORT int swl_agg_import_weights(const swl_weight_ipc* recs, int count, const int64_t* dims,
+                                      int num_layers, int device_index) {
+  if (!recs || !dims || num_layers <= 0 || count != kRecsPerLayer * num_layers + 2)
+    return set_error(SWL_ERR_ARG, "import_weights_from_ipc: expected %d records for %d layers",
+                     kRecsPerLayer * num_layers + 2, num_layers);
+  SWL_TRY(check_import_records(recs, dims, num_layers));
+  SWL_CUDA_TRY(cudaSetDevice(device_index));
+  SWL_TRY(free_weights());
+  g_device = device_index;
+  SWL_TRY(ensure_stream());
+  std::vector<size_t> at(count, 0);
+  size_t total = 0;
+  for (int i = 0; i < count; ++i) {
+    if (recs[i].rows <= 0) continue;
+    at[i] = total;
+    total += (static_cast<size_t>(recs[i].rows) * recs[i].cols * 2 + kArenaAlign - 1) / kArenaAlign * kArenaAlign;
+  }
+  SWL_CUDA_TRY(cudaMalloc(&g_arena, total));
+  struct Mapped { cudaIpcMemHandle_t h; char* base; size_t size; };
+  std::vector<Mapped> maps;
+  int st = SWL_OK;
+  for (int i = 0; st == SWL_OK && i < count; ++i) {
+    const swl_weight_ipc& rec = recs[i];
+    if (rec.rows <= 0) continue;
+    const Mapped* m = nullptr;
+    for (const Mapped& x : maps)
+      if (!memcmp(&x.h, rec.handle, sizeof(x.h))) m = &x;
+    if (!m) {
+      Mapped x;
+      memcpy(&x.h, rec.handle, sizeof(x.h));
+      void* p = nullptr;
+      cudaError_t e = cudaIpcOpenMemHandle(&p, x.h, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) {
+        st = set_error(SWL_ERR_CUDA, "import_weights_from_ipc: mapping record %d failed: %s", i, cudaGetErrorString(e));
+        break;
+      }
+      x.base = static_cast<char*>(p);
+      char* b2 = nullptr;
+      st = allocation_of(p, &b2, &x.size);
+      maps.push_back(x);
+      if (st != SWL_OK) break;
+      m = &maps.back();
+    }
+    const size_t bytes = static_cast<size_t>(rec.rows) * rec.cols * 2;
+    if (rec.offset > m->size || bytes > m->size - rec.offset) {
+      st = set_error(SWL_ERR_ARG, "import_weights_from_ipc: record %d (%zu bytes at %llu) lies outside its %zu-byte allocation",
+                     i, bytes, static_cast<unsigned long long>(rec.offset), m->size);
+      break;
+    }
+    cudaError_t e = cudaMemcpyAsync(static_cast<char*>(g_arena) + at[i], m->base + rec.offset, bytes,
+                                    cudaMemcpyDefault, g_stream);
+    if (e != cudaSuccess) st = set_error(SWL_ERR_CUDA, "import_weights_from_ipc: copy of record %d failed: %s", i, cudaGetErrorString(e));
+  }
+  cudaError_t se = cudaStreamSynchronize(g_stream);
+  if (st == SWL_OK && se != cudaSuccess)
+    st = set_error(SWL_ERR_CUDA, "import_weights_from_ipc: copies failed: %s", cudaGetErrorString(se));
+  for (const Mapped& x : maps) cudaIpcCloseMemHandle(x.base);
+  if (st != SWL_OK) {
+    const std::string why = last_error();
+    cudaFree(g_arena);
+    g_arena = nullptr;
+    g_layers.clear();
+    g_num_layers = 0;
+    return set_error(SWL_ERR_CUDA, "%s", why.c_str());
+  }
+  char* arena = static_cast<char*>(g_arena);
+  g_layers.assign(num_layers, Layer());
+  g_num_layers = num_layers;
+  const int64_t hidden = recs[kRecsPerLayer * num_layers].cols;
+  for (int l = 0; l < num_layers && st == SWL_OK; ++l) {
+    Layer& L = g_layers[l];
+    const swl_weight_ipc* r = recs + kRecsPerLayer * l;
+    const size_t* a = at.data() + kRecsPerLayer * l;
+    const int64_t* d = dims + 5 * l;
+    L.owns_fused = false;
+    L.q_dim = d[0]; L.k_dim = d[1]; L.v_dim = d[2]; L.gate_dim = d[3]; L.up_dim = d[4];
+    L.hidden = hidden; L.inter = r[3].cols; L.o_out = r[1].rows; L.down_out = r[3].rows;
+    L.qkv = arena + a[0];
+    L.o = arena + a[1];
+    L.gu = arena + a[2];
+    L.down = arena + a[3];
+    L.o_bias = r[4].rows ? arena + a[4] : nullptr;
+    L.down_bias = r[5].rows ? arena + a[5] : nullptr;
+    st = encode_weight_tmap(&L.tm_qkv, L.qkv, r[0].rows, hidden);
+    if (st == SWL_OK) st = encode_weight_tmap(&L.tm_o, L.o, L.o_out, hidden);
+    if (st == SWL_OK) st = encode_weight_tmap(&L.tm_gu, L.gu, r[2].rows, hidden);
+    if (st == SWL_OK) st = encode_weight_tmap(&L.tm_down, L.down, L.down_out, L.inter);
+  }
+  if (st != SWL_OK) return st;
+  g_weights_ready = true;
+  const int64_t vocab = recs[kRecsPerLayer * num_layers].rows;
+  g_embed = arena + at[kRecsPerLayer * num_layers];
+  g_lm_head = arena + at[kRecsPerLayer * num_layers + 1];
+  g_vocab = vocab;
+  g_embed_hidden = hidden;
+  SWL_TRY(encode_weight_tmap(&g_tm_lm, g_lm_head, vocab, hidden));
+  if (g_logits) cudaFree(g_logits);
+  g_logits = nullptr;
+  SWL_CUDA_TRY(cudaMalloc(&g_logits, static_cast<size_t>(kMaxSlots) * vocab * 2));
+  g_vocab_ready = true;
+  return SWL_OK;
+}
+
 // ext_aggregator.cpp:427-459 init_aggregator_queue: map the queue segment
 // created by ext_ipc_queue.create_queue (this module's own view).
 SWL_EXPORT int swl_agg_init_queue(const char* shm_name, int capacity) {
@@ -602,8 +842,16 @@ SWL_EXPORT int swl_agg_set_round_algo(int algo, int splits) {
 }
 
 // The fused weight of (layer, op) and its [N, K] shape, for callers that
-// check a round against their own reference.
+// check a round against their own reference; OP_EMBED / OP_LM_HEAD give the
+// [vocab, hidden] tables (layer ignored).
 SWL_EXPORT int swl_agg_weight(int layer, int op, const void** W, int64_t* N, int64_t* K) {
+  if (op == kOpEmbed || op == kOpLmHead) {
+    if (!g_vocab_ready) return set_error(SWL_ERR_STATE, "weight: embed/lm_head not initialized");
+    *W = op == kOpEmbed ? g_embed : g_lm_head;
+    *N = g_vocab;
+    *K = g_embed_hidden;
+    return SWL_OK;
+  }
   if (layer < 0 || layer >= g_num_layers) return set_error(SWL_ERR_ARG, "weight: bad layer");
   const Layer& L = g_layers[layer];
   switch (op) {

@@ -11,7 +11,10 @@ they stay alive, as the reference's detach() does.
 
 Additions (not in the reference): `execute_round` runs one round over pool
 slots on a given stream, `slot_buffers` returns a slot's device addresses
-for in-process drivers, `set_round_algo` selects the round kernel.
+for in-process drivers, `set_round_algo` selects the round kernel. The
+donor weight transfer (`export_weight_ipc_handles` /
+`import_weights_from_ipc`) carries each weight's offset inside its
+allocation next to the reference's keys.
 """
 from __future__ import annotations
 
@@ -19,7 +22,7 @@ import ctypes as C
 
 import torch
 
-from ._native import check, i32_array, i64_array, lib
+from ._native import WeightIpc, check, i32_array, i64_array, lib
 
 OP_O_PROJ = 3
 OP_DOWN_PROJ = 6
@@ -143,6 +146,90 @@ def aggregator_main_loop_slots(num_slots: int, dtype_code: int) -> None:
 # ---------------------------------------------------------------------------
 # additions
 # ---------------------------------------------------------------------------
+
+_LAYER_WEIGHTS = ("qkv_weight", "o_weight", "gate_up_weight", "down_weight")
+_LAYER_DIMS = ("q_dim", "k_dim", "v_dim", "gate_dim", "up_dim")
+_DTYPE_BF16 = 15  # c10::ScalarType::BFloat16, the code the reference's export carries
+
+
+def export_weight_ipc_handles() -> dict:
+    """ext_aggregator.cpp:1216-1291: the reference's dict (handles as 64-byte
+    bytes, shapes as tuples, bias flags, per-layer dims, dtype_code) plus a
+    `*_offset` entry per handle: the weight's byte offset inside the
+    exported allocation. Keep this process's weights alive until every
+    importer has returned."""
+    L, dev = C.c_int(0), C.c_int(0)
+    check(lib().swl_agg_export_weights(None, 0, None, C.byref(L), C.byref(dev)))
+    n = 6 * L.value + 2
+    recs = (WeightIpc * n)()
+    dims = (C.c_int64 * (5 * L.value))()
+    check(lib().swl_agg_export_weights(recs, n, dims, C.byref(L), C.byref(dev)))
+
+    def put(d, name, r, one_d=False):
+        d[f"{name}_handle"] = bytes(r.handle)
+        d[f"{name}_offset"] = int(r.offset)
+        if one_d:
+            d[f"{name}_size"] = int(r.rows)
+        else:
+            d[f"{name}_shape"] = (int(r.rows), int(r.cols))
+    layers = []
+    for l in range(L.value):
+        r = recs[6 * l:6 * l + 6]
+        lh = {}
+        for name, rec in zip(_LAYER_WEIGHTS, r[:4]):
+            put(lh, name, rec)
+        for name, rec in (("o_bias", r[4]), ("down_bias", r[5])):
+            lh[f"has_{name}"] = rec.rows > 0
+            if rec.rows > 0:
+                put(lh, name, rec, one_d=True)
+        for j, k in enumerate(_LAYER_DIMS):
+            lh[k] = int(dims[5 * l + j])
+        layers.append(lh)
+    out = {"num_layers": L.value, "device_index": dev.value, "layers": layers, "dtype_code": _DTYPE_BF16}
+    put(out, "embed_weight", recs[6 * L.value])
+    put(out, "lm_head_weight", recs[6 * L.value + 1])
+    return out
+
+
+def import_weights_from_ipc(handles_dict: dict, target_device_index: int) -> None:
+    """ext_aggregator.cpp:1294-1406: copies a donor aggregator's weights
+    (export_weight_ipc_handles of another process) onto this process's
+    device; the aggregator is then as after init_aggregator_finalize and
+    init_embed_lm_head_weights. A dict without `*_offset` entries (the
+    reference's own export) reads each weight from its allocation's start."""
+    if int(handles_dict.get("dtype_code", _DTYPE_BF16)) != _DTYPE_BF16:
+        raise RuntimeError("import_weights_from_ipc: only bf16 weights are supported")
+    L = int(handles_dict["num_layers"])
+    layers = handles_dict["layers"]
+    if len(layers) != L:
+        raise RuntimeError(f"import_weights_from_ipc: {len(layers)} layer entries for num_layers={L}")
+    n = 6 * L + 2
+    recs = (WeightIpc * n)()
+    dims = (C.c_int64 * (5 * L))()
+
+    def get(r, d, name, one_d=False):
+        h = bytes(d[f"{name}_handle"])
+        if len(h) != 64:
+            raise RuntimeError(f"import_weights_from_ipc: {name}_handle must be 64 bytes")
+        C.memmove(r.handle, h, 64)
+        r.offset = int(d.get(f"{name}_offset", 0))
+        if one_d:
+            r.rows, r.cols = int(d[f"{name}_size"]), 1
+        else:
+            r.rows, r.cols = (int(x) for x in d[f"{name}_shape"])
+    for l, lh in enumerate(layers):
+        for j, name in enumerate(_LAYER_WEIGHTS):
+            get(recs[6 * l + j], lh, name)
+        for j, name in ((4, "o_bias"), (5, "down_bias")):
+            if lh.get(f"has_{name}"):
+                get(recs[6 * l + j], lh, name, one_d=True)
+        for j, k in enumerate(_LAYER_DIMS):
+            dims[5 * l + j] = int(lh[k])
+    get(recs[6 * L], handles_dict, "embed_weight")
+    get(recs[6 * L + 1], handles_dict, "lm_head_weight")
+    check(lib().swl_agg_import_weights(recs, n, dims, L, int(target_device_index)))
+    _borrowed.clear()  # the imported weights are library-owned
+
 
 def execute_round(op: int, layer: int, slot_ids, worker_ids, bx, tx, stream=None) -> None:
     """One round over pool slots (what the main loop runs per op), queued on
