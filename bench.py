@@ -69,6 +69,8 @@ def parse():
     ap.add_argument("--churn", type=float, default=0.0, metavar="SECONDS",
                     help="adapter-pool churn on one GPU for SECONDS of arrivals (ranks 8/16/32, swap on miss)")
     ap.add_argument("--churn-slots", type=int, default=64)
+    ap.add_argument("--churn-from-disk", action="store_true",
+                    help="churn: misses read PEFT adapter files (written to a temporary pool before the run)")
     ap.add_argument("--shard", action="store_true",
                     help="column-sharded base weights over 2 GPUs (one slot group; torchrun, --gpus 2)")
     ap.add_argument("--profile-attention", action="store_true",
@@ -625,8 +627,9 @@ def shard_arm(args):
 def churn_arm(args):
     """The churn configuration on one GPU: a seeded trace of Poisson arrivals
     (8/s), lognormal prompts and outputs, Zipf adapter ids over a pool of 500
-    adapters of ranks 8/16/32 (random-init, made on the device when missed),
-    an LRU cache of 32 of them packed into slabs (a swap is one device
+    adapters of ranks 8/16/32 (random-init, made on the device when missed,
+    or with --churn-from-disk read from PEFT adapter files written before the
+    run), an LRU cache of 32 of them packed into slabs (a swap is one device
     copy), prefill in 16-row chunks next to decode rows
     (at most 256 rows a step), all-decode steps replayed from a CUDA graph.
     The clock is the device time of steps and swaps. Prints one JSON line."""
@@ -646,7 +649,25 @@ def churn_arm(args):
     grp = SlotGroup(cfg, base, [a0] * n, [0] * n, max_new=ccfg.prompt_clip[1] + ccfg.output_clip[1] + 16,
                     device=0, seed=0)
 
-    def load(aid):  # a miss makes the adapter on the device and packs it into a slab
+    trace = make_trace(ccfg, args.churn, seed=0)
+    loader, pool_dir = None, None
+    if args.churn_from_disk:  # every adapter the trace uses, as a bf16 PEFT directory
+        import shutil
+        import tempfile
+        from swarmlora_b200.adapters import AdapterLoader, save_adapter
+        pool_dir = tempfile.mkdtemp(prefix="swl_adapter_pool_")
+        for aid in sorted({r.adapter for r in trace}):
+            save_adapter(os.path.join(pool_dir, f"lora-{aid}"),
+                         random_adapter(cfg, seed=10_000 + aid, device=dev, rank=int(ranks[aid])),
+                         alpha=cfg.alpha, dtype=torch.bfloat16)
+        loader = AdapterLoader(cfg, dev, allowed_bases=[pool_dir])
+
+    def load(aid):
+        """A miss: read the adapter's files (pinned staging, one copy to the
+        GPU) or make it on the device, then pack it into a slab."""
+        if loader is not None:
+            layers, conf = loader.load(os.path.join(pool_dir, f"lora-{aid}"))
+            return grp.pack_adapter(layers, scaling=conf["scaling"])
         return grp.pack_adapter(random_adapter(cfg, seed=10_000 + aid, device=dev, rank=int(ranks[aid])))
     stream = torch.cuda.Stream(dev)
 
@@ -664,13 +685,15 @@ def churn_arm(args):
     for i in range(n):
         grp.set_context(i, 0)
     grp.capture(stream)
-    trace = make_trace(ccfg, args.churn, seed=0)
     st = ChurnRunner(grp, trace, ccfg, load, timer, cfg.vocab, stream=stream).run()
+    if pool_dir:
+        shutil.rmtree(pool_dir, ignore_errors=True)
     print(json.dumps({"metric": "churn: decode tokens per device second (Llama-3.1-8B shape)",
                       "requests": len(trace), **st.summary(), "dtype": "bf16",
                       "config": {"workload": f"{args.churn:g} s of arrivals at {ccfg.rate}/s, pool {ccfg.pool_size} "
                                              f"adapters r in {list(ccfg.ranks)}, cache {ccfg.cache_adapters}, "
-                                             f"{n} slots, {cfg.layers} layers, vocab {cfg.vocab}",
+                                             f"{n} slots, {cfg.layers} layers, vocab {cfg.vocab}, "
+                                             f"misses {'read from PEFT files' if loader else 'made on the device'}",
                                  "data": "synthetic (seeded trace, random-init weights and adapters)"}}), flush=True)
     grp.close()
     return 0
