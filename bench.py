@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--slots", type=int, default=N_SLOTS)
+    ap.add_argument("--ctx-lo", type=int, default=CTX_LO,
+                    help="per-slot context ~U[lo, hi] (config 2: 256..1024; config 5: --slots 32 --ctx-lo 1024 --ctx-hi 4096)")
+    ap.add_argument("--ctx-hi", type=int, default=CTX_HI)
     ap.add_argument("--layers", type=int, default=32,
                     help="decoder layers (32 = the benchmarked model; fewer only for small profiling cases)")
     ap.add_argument("--vocab", type=int, default=128256,
@@ -71,6 +74,10 @@ def parse():
     ap.add_argument("--churn-slots", type=int, default=64)
     ap.add_argument("--churn-from-disk", action="store_true",
                     help="churn: misses read PEFT adapter files (written to a temporary pool before the run)")
+    ap.add_argument("--mixed", action="store_true",
+                    help="BASELINE config 3 on one GPU: prefill chunks of 4 slots packed beside 24 decode rows")
+    ap.add_argument("--mixed-chunk", type=int, default=16,
+                    help="prefill rows per prefill slot per step (16 = the reference's max_seq_per_step)")
     ap.add_argument("--shard", action="store_true",
                     help="column-sharded base weights over 2 GPUs (one slot group; torchrun, --gpus 2)")
     ap.add_argument("--profile-attention", action="store_true",
@@ -170,7 +177,7 @@ def measured_peaks():
 # CPU baseline (oracle port of the reference path)
 # ---------------------------------------------------------------------------
 
-def cpu_layer_sample(n_slots, seed=0):
+def cpu_layer_sample(n_slots, seed=0, ctx_lo=CTX_LO, ctx_hi=CTX_HI):
     """Builds one decoder layer + N slots on the host and returns a callable
     timing one layer step (all 4 rounds, LoRA, RoPE, attention, norms)."""
     import math
@@ -192,12 +199,12 @@ def cpu_layer_sample(n_slots, seed=0):
         fq = ref.pack_fused_lora([A["q"], A["k"], A["v"]], [B["q"], B["k"], B["v"]], s, [HQ * D, HKV * D, HKV * D])
         fg = ref.pack_fused_lora([A["g"], A["u"]], [B["g"], B["u"]], s, [I, I])
         ads.append((fq, fg, A, B))
-    ctx = [int(c) for c in torch.randint(CTX_LO, CTX_HI + 1, (n_slots,))]
-    pages_per = (CTX_HI + 16 + 15) // 16
+    ctx = [int(c) for c in torch.randint(ctx_lo, ctx_hi + 1, (n_slots,))]
+    pages_per = (ctx_hi + 16 + 15) // 16
     kc = torch.randn(n_slots * pages_per, 16, HKV, D).to(bf)
     vc = torch.randn(n_slots * pages_per, 16, HKV, D).to(bf)
     tables = [list(range(i * pages_per, (i + 1) * pages_per)) for i in range(n_slots)]
-    cs = ref.cos_sin_cache(ref.llama3_inv_freq(D), CTX_HI + 16)
+    cs = ref.cos_sin_cache(ref.llama3_inv_freq(D), ctx_hi + 16)
     xs = [torch.randn(1, H).to(bf) for _ in range(n_slots)]
 
     def mm(xl, W):  # the round: cat -> x @ W^T -> split (ext_aggregator.cpp:545-625)
@@ -246,11 +253,11 @@ def cpu_layer_sample(n_slots, seed=0):
     return step, lm_head_cost
 
 
-def cpu_baseline(n_slots, seconds_budget=20.0):
+def cpu_baseline(n_slots, seconds_budget=20.0, ctx_lo=CTX_LO, ctx_hi=CTX_HI):
     import torch
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    step, lm_cost = cpu_layer_sample(n_slots)
+    step, lm_cost = cpu_layer_sample(n_slots, ctx_lo=ctx_lo, ctx_hi=ctx_hi)
     step()  # warm-up
     t_lm = lm_cost()
     times = []
@@ -263,7 +270,8 @@ def cpu_baseline(n_slots, seconds_budget=20.0):
     t_layer = times[len(times) // 2]
     tok_s = n_slots / (32 * t_layer + t_lm)
     return {"value": round(tok_s, 4), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{len(times)} single-layer steps of {n_slots} decode slots (4 rounds + LoRA + RoPE + "
+            "sample": f"{len(times)} single-layer steps of {n_slots} decode slots at ctx U[{ctx_lo},{ctx_hi}] "
+                      f"(4 rounds + LoRA + RoPE + "
                       f"paged attention + norms, median {t_layer*1e3:.1f} ms) x 32 layers + one LM-head "
                       f"GEMV+argmax ({t_lm*1e3:.1f} ms); oracle/ on torch CPU, fp32 weights"}
 
@@ -275,7 +283,7 @@ def reference_arm(args):
         return 0
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    step, lm_cost = cpu_layer_sample(args.slots)
+    step, lm_cost = cpu_layer_sample(args.slots, ctx_lo=args.ctx_lo, ctx_hi=args.ctx_hi)
     t_lm = lm_cost()
     for _ in range(args.warmup):
         step()
@@ -291,8 +299,10 @@ def reference_arm(args):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_tok, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "BASELINE config 2: Llama-3.1-8B shape, 28 decode slots, r=16 adapters, "
-                                   "ctx U[256,1024]", "slots": args.slots, "layers": 32, "vocab": 128256,
+            "config": {"workload": f"BASELINE config {5 if (args.slots, args.ctx_lo, args.ctx_hi) == (32, 1024, 4096) else 2}: "
+                                   f"Llama-3.1-8B shape, {args.slots} decode slots, r=16 adapters, "
+                                   f"ctx U[{args.ctx_lo},{args.ctx_hi}]", "slots": args.slots, "layers": 32,
+                       "vocab": 128256,
                        "sample": "one decoder layer per step, extrapolated x32 + LM head"},
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": f"{args.steps} single-layer steps of {args.slots} slots on {threads} threads"},
@@ -305,14 +315,17 @@ def reference_arm(args):
 # our arm
 # ---------------------------------------------------------------------------
 
-def round_phase(grp, cfg, reps=3):
+def round_phase(grp, cfg, reps=3, rows=None):
     """Times each round kind over all layers' weights (> L2 in total) from a
-    CUDA graph; returns {op: us per launch} and the algorithmic bytes."""
+    CUDA graph; returns {op: us per launch} and the algorithmic bytes. `rows`
+    gives each slot's token rows (default one)."""
     import torch
     from swarmlora_b200 import ext_aggregator as agg
+    from swarmlora_b200._native import i64_array
     ops = {"qkv": agg.OP_QKV_FUSED, "o": agg.OP_O_PROJ, "gate_up": agg.OP_GATE_UP_FUSED,
            "down": agg.OP_DOWN_PROJ}
-    H, I, M = cfg.hidden, cfg.inter, grp.n
+    tx = i64_array(rows) if rows is not None else None
+    H, I, M = cfg.hidden, cfg.inter, (sum(rows) if rows is not None else grp.n)
     shapes = {"qkv": (cfg.qkv_n, H), "o": (H, cfg.hq * cfg.head_dim), "gate_up": (2 * I, H), "down": (H, I)}
     s = torch.cuda.Stream()
     out = {}
@@ -320,7 +333,7 @@ def round_phase(grp, cfg, reps=3):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             for l in range(cfg.layers):
-                grp._round(op, l, s.cuda_stream)
+                grp._round(op, l, s.cuda_stream, tx)
         g.replay()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -353,7 +366,7 @@ def our_arm(args):
     cfg = dataclasses.replace(LLAMA_3_1_8B, layers=args.layers, vocab=args.vocab)
     n = args.slots
     g = torch.Generator().manual_seed(1234 + rank)
-    ctx = [int(c) for c in torch.randint(CTX_LO, CTX_HI + 1, (n,), generator=g)]
+    ctx = [int(c) for c in torch.randint(args.ctx_lo, args.ctx_hi + 1, (n,), generator=g)]
     base = random_base(cfg, seed=1, device=dev)
     adapters = [random_adapter(cfg, seed=100 + rank * 1000 + i, device=dev) for i in range(n)]
     total_new = args.warmup + args.steps + args.warmup + args.steps + 4
@@ -439,7 +452,7 @@ def our_arm(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_baseline(n)
+            cpu = cpu_baseline(n, ctx_lo=args.ctx_lo, ctx_hi=args.ctx_hi)
         except Exception as e:  # report, do not fail the GPU number
             cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                    "sample": f"failed: {e}"}
@@ -450,9 +463,10 @@ def our_arm(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init weights, adapters, KV contexts)",
-            "config": {"workload": f"BASELINE config 2: Llama-3.1-8B shape ({cfg.layers} layers, vocab {cfg.vocab}), "
+            "config": {"workload": f"BASELINE config {5 if (n, args.ctx_lo, args.ctx_hi) == (32, 1024, 4096) else 2}: "
+                                   f"Llama-3.1-8B shape ({cfg.layers} layers, vocab {cfg.vocab}), "
                                    f"{n} decode slots/GPU, distinct r=16 adapters on 7 projections, "
-                                   f"ctx U[{CTX_LO},{CTX_HI}] paged 16, 1 token/slot/step, greedy",
+                                   f"ctx U[{args.ctx_lo},{args.ctx_hi}] paged 16, 1 token/slot/step, greedy",
                        "slots_per_gpu": n, "parallelism": f"{world} independent aggregator groups",
                        "launch": "serialized" if args.no_pdl else "programmatic dependent launch",
                        "l2": "weights (15 GB/step) far exceed L2; no flush needed",
@@ -624,6 +638,130 @@ def shard_arm(args):
     return 0
 
 
+def mixed_arm(args):
+    """BASELINE config 3 on one GPU: 28 slots of the 8B shape, 4 of them
+    prefilling prompts of U[512, 2048] tokens in chunks of --mixed-chunk rows
+    per step (a prompt that is done starts over as a new request) beside 24
+    decode slots at contexts U[256, 2048]; every step's rounds carry
+    4 * chunk + 24 rows. The step is a CUDA graph of the fixed row pattern;
+    each step first stages the prefill chunks' token ids into the group's
+    token buffer. value = new tokens (prefill + decode) per second; e2e adds
+    the chunks' ids from pinned host memory and reads the next tokens back
+    every step. Prints one JSON line."""
+    import dataclasses
+    import torch
+    import swarmlora_b200
+    from swarmlora_b200.engine import LLAMA_3_1_8B, SlotGroup, random_adapter, random_base
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    swarmlora_b200.set_pdl(not args.no_pdl)
+    chunk, n_pf, n_dec = int(args.mixed_chunk), 4, 24
+    n = n_pf + n_dec
+    if not 1 <= chunk or n_pf * chunk + n_dec > 256:
+        raise SystemExit("--mixed-chunk: 4 * chunk + 24 rows must stay within 256")
+    cfg = dataclasses.replace(LLAMA_3_1_8B, layers=args.layers, vocab=args.vocab, max_seq_per_step=chunk)
+    g = torch.Generator().manual_seed(4321)
+    prompts = [(int(x) + chunk - 1) // chunk * chunk for x in torch.randint(512, 2049, (n_pf,), generator=g)]
+    dec_ctx = [int(c) for c in torch.randint(256, 2049, (n_dec,), generator=g)]
+    steps_total = args.warmup + args.steps
+    base = random_base(cfg, seed=1, device=dev)
+    adapters = [random_adapter(cfg, seed=300 + i, device=dev) for i in range(n)]
+    grp = SlotGroup(cfg, base, adapters, [0] * n_pf + dec_ctx,
+                    max_new=max(max(prompts), 2 * steps_total + 8), device=0, seed=0)
+    rows = [chunk] * n_pf + [1] * n_dec
+    ids = torch.randint(0, cfg.vocab, (n_pf, max(prompts)), generator=g)
+    ids_dev = ids.to(dev)
+    grp.tokens.copy_(torch.randint(0, cfg.vocab, (n,), generator=g))
+    stream = torch.cuda.Stream(dev)
+    done = [0] * n_pf  # prefilled tokens of each prefill slot's current prompt
+
+    def stage(host_ids=None):
+        """Token ids of the next step into tok_in (decode rows: last outputs)."""
+        grp.tok_in[:, 0].copy_(grp.tokens)
+        for i in range(n_pf):
+            if done[i] + chunk > prompts[i]:  # prompt done: a new request on this slot
+                done[i] = 0
+                grp.set_context(i, 0)
+            src = host_ids[i] if host_ids is not None else ids_dev[i, done[i]:done[i] + chunk]
+            grp.tok_in[i, :chunk].copy_(src, non_blocking=True)
+            done[i] += chunk
+    with torch.cuda.stream(stream):
+        stage()
+        grp.enqueue_step(stream, rows=rows, tokens=[grp.tok_in[i, :x].tolist() for i, x in enumerate(rows)])
+    torch.cuda.synchronize()
+    grp.capture(stream, rows=rows)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            stage()
+            grp.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    time.sleep(0.25)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            stage()
+            grp.replay()
+    ev1.record(stream)
+    ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    time.sleep(0.1)
+    clk = clocks.stop()
+    new_rows = sum(rows)
+    value = new_rows * args.steps / (ms / 1e3)
+
+    # end to end: the chunks' ids from pinned host memory, next tokens back
+    h_ids = torch.empty(n_pf, chunk, dtype=torch.int64).pin_memory()
+    h_out = torch.empty(n, dtype=torch.int64).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            for i in range(n_pf):
+                d = done[i] if done[i] + chunk <= prompts[i] else 0
+                h_ids[i].copy_(ids[i, d:d + chunk])
+            stage(host_ids=h_ids)
+            grp.replay()
+            h_out.copy_(grp.tokens, non_blocking=True)
+            stream.synchronize()
+    e1.record(stream)
+    e1.synchronize()
+    e2e = new_rows * args.steps / (e0.elapsed_time(e1) / 1e3)
+
+    rounds = round_phase(grp, cfg, rows=rows)
+    peak, peak_kind = measured_peaks()
+    dom = max(rounds, key=lambda k: rounds[k]["us"])
+    achieved = rounds[dom]["bytes"] / rounds[dom]["us"] / 1e3
+    line = {
+        "metric": "mixed prefill+decode new tokens/s/GPU (Llama-3.1-8B shape, 4 prefill + 24 decode slots)",
+        "value": round(value, 2), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, adapters, prompts)",
+        "config": {"workload": f"BASELINE config 3: {cfg.layers} layers, vocab {cfg.vocab}; 4 slots prefilling "
+                               f"prompts U[512,2048] in {chunk}-row chunks + 24 decode slots at ctx U[256,2048], "
+                               f"{new_rows} rows per round, distinct r=16 adapters",
+                   "prefill_tok_s": round(n_pf * chunk * args.steps / (ms / 1e3), 2),
+                   "decode_tok_s": round(n_dec * args.steps / (ms / 1e3), 2),
+                   "l2": "weights (15 GB/step) far exceed L2; no flush needed",
+                   "us_per_round": {k: v["us"] for k, v in rounds.items()},
+                   "round_gbs": {k: v["gbs"] for k, v in rounds.items()}},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * n_pf * chunk,
+                "d2h_bytes_per_step": 8 * n},
+        "roofline": {"bound": "hbm", "kernel": f"slot_round_tc ({dom} round, M={new_rows})",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "algorithmic_bytes": rounds[dom]["bytes"], "peak_source": peak_kind},
+        "gpu_launches": grp.launches_per_step() * args.steps,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    grp.close()
+    return 0
+
+
 def churn_arm(args):
     """The churn configuration on one GPU: a seeded trace of Poisson arrivals
     (8/s), lognormal prompts and outputs, Zipf adapter ids over a pool of 500
@@ -703,6 +841,8 @@ def main():
     args = parse()
     if args.churn:
         return churn_arm(args)
+    if args.mixed:
+        return mixed_arm(args)
     if args.shard:
         return shard_arm(args)
     if args.profile_attention:

@@ -229,6 +229,7 @@ class SlotGroup:
         self.ws_dn = torch.zeros(self.dn_splits * n * mr * cfg.rank, **f32)
         self.tokens = torch.zeros(n, dtype=torch.int64, device=self.dev)
         self._build_call_args()
+        self._advance = {}
         self.graph = None
 
     # ------------------------------------------------------------------------------
@@ -409,7 +410,18 @@ class SlotGroup:
             check(L.swl_advance_i32(self.seqlens.data_ptr(), n, 1 if row_counts is None else row_counts[0], st))
         else:
             with torch.cuda.stream(stream):
-                self.seqlens.add_(torch.tensor(row_counts, dtype=torch.int32).to(self.dev))
+                self.seqlens.add_(self._advance_of(row_counts))
+
+    def _advance_of(self, row_counts) -> torch.Tensor:
+        """Device copy of a row pattern (the per-slot position advance), made
+        once per pattern outside any graph capture."""
+        key = tuple(int(x) for x in row_counts)
+        t = self._advance.get(key)
+        if t is None:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("a new row pattern inside a graph capture: pass it to capture(rows=...)")
+            t = self._advance[key] = torch.tensor(key, dtype=torch.int32, device=self.dev)
+        return t
 
     def _enqueue_unfused(self, stream: torch.cuda.Stream) -> None:
         """Modular sequence (one kernel per operation), kept as a cross-check."""
@@ -467,13 +479,25 @@ class SlotGroup:
         per_layer = 2 + 4 * 3 + 1 + 2  # norms, (shrink+round+expand)x4, rope, attention + combine
         return 3 + self.cfg.layers * per_layer + 1 + 2 + 1 + 1
 
-    def capture(self, stream: torch.cuda.Stream | None = None) -> None:
+    def capture(self, stream: torch.cuda.Stream | None = None, rows=None) -> None:
         """Captures one step into a CUDA graph (replayed by `replay`). Capture
-        does not execute the step, so the state is unchanged."""
+        does not execute the step, so the state is unchanged. With `rows`
+        (new tokens per slot, a fixed mixed pattern) the graph reads each
+        slot's token ids from `tok_in[i, :rows[i]]`, which the caller fills
+        before every replay."""
         s = stream or torch.cuda.Stream(self.dev)
+        if rows is not None:
+            rows = [int(x) for x in rows]
+            if len(rows) != self.n or any(x < 1 or x > self.max_rows for x in rows) or not self.fused:
+                raise ValueError(f"rows: one count per slot in 1..{self.max_rows} (fused sequence)")
+            if len(set(rows)) > 1:
+                self._advance_of(rows)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=s):
-            self.enqueue_step(s)
+            if rows is None:
+                self.enqueue_step(s)
+            else:
+                self._enqueue_fused(s, rows)
 
     def replay(self) -> None:
         self.graph.replay()

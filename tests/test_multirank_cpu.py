@@ -36,7 +36,7 @@ def _rank(rank, port, what, q):
             mine = bytes([rank]) * 64 * 3  # three 64-byte handles
             q.put((rank, exchange_with_peer(mine, rank)))
         elif what == "reference":
-            args = SimpleNamespace(gpus=2, steps=1, warmup=0, slots=4)
+            args = SimpleNamespace(gpus=2, steps=1, warmup=0, slots=4, ctx_lo=256, ctx_hi=1024)
             out = io.StringIO()
             with contextlib.redirect_stdout(out):
                 rc = bench.reference_arm(args)
