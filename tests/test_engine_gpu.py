@@ -258,8 +258,26 @@ def test_mixed_prefill_and_decode_step(native, cuda):
         g = torch.Generator().manual_seed(9)
         toks = [torch.randint(0, cfg.vocab, (r,), generator=g).tolist() for r in rows]
         stream = torch.cuda.current_stream()
+        kc0 = [k.clone() for k in grp.k_cache]
+        vc0 = [v.clone() for v in grp.v_cache]
         grp.enqueue_step(stream, rows=rows, tokens=toks)
         torch.cuda.synchronize()
+        # the same mixed step from a CUDA graph of the row pattern (token ids
+        # staged in tok_in) gives bit-identical tokens, hidden rows and caches
+        eager = (grp.tokens.clone(), grp.h_rows.clone(), [k.clone() for k in grp.k_cache],
+                 [v.clone() for v in grp.v_cache], grp.seqlens.clone())
+        grp.capture(rows=rows)
+        for l in range(cfg.layers):
+            grp.k_cache[l].copy_(kc0[l])
+            grp.v_cache[l].copy_(vc0[l])
+        grp.reset_positions()
+        for i, t in enumerate(toks):
+            grp.tok_in[i, :len(t)].copy_(torch.tensor(t))
+        grp.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(grp.tokens, eager[0]) and torch.equal(grp.seqlens, eager[4])
+        assert all(torch.equal(grp.h_rows[i, :r], eager[1][i, :r]) for i, r in enumerate(rows))
+        assert all(torch.equal(a, b) for a, b in zip(grp.k_cache + grp.v_cache, eager[2] + eager[3]))
         want, final, logits, h_last = decode_step(cfg, base_c, ad_c, kc, vc, bts, list(ctx), toks)
         got_h = torch.stack([grp.h_rows[i, r - 1] for i, r in enumerate(rows)])
         assert_close(got_h, h_last, "mixed step: last row's last-layer hidden", atol_rms=ATOL_RMS_MULTILAYER)
