@@ -147,8 +147,8 @@ class ChurnRunner:
     arrival time has passed are admitted to free slots in arrival order.
 
     group needs: n, max_rows, max_len, set_adapter(i, adapter),
-    set_context(i, length), enqueue_step(stream, rows=..., tokens=...) and
-    tokens (the device next-token ids). timer(fn) runs fn on `stream` and
+    set_context(i, length) and enqueue_step(stream, rows=..., tokens=...)
+    (a None entry of tokens: that slot's one row is its last output). timer(fn) runs fn on `stream` and
     returns its device time in seconds. load_adapter(aid) returns the
     adapter of a pool id in a form set_adapter takes (SlotGroup: a
     PackedAdapter, so a swap is one device copy); the cache keeps what it
@@ -261,7 +261,4 @@ class ChurnRunner:
             else:
                 self.g.enqueue_step(self.stream)
             return
-        if any(t is None for t in toks):
-            last = self.g.tokens.tolist()
-            toks = [[last[i]] if t is None else t for i, t in enumerate(toks)]
-        self.g.enqueue_step(self.stream, rows=rows, tokens=toks)
+        self.g.enqueue_step(self.stream, rows=rows, tokens=toks)  # None: the slot's last output, on the device

@@ -324,8 +324,11 @@ class SlotGroup:
         per slot, 1..max_rows) and `tokens` (their ids, one list per slot) the
         step carries prefill chunks next to decode rows, the mixed
         configuration: every new row goes through the layers, its K / V is
-        appended, and each slot's next token comes from its last row. The ids
-        are copied to the device first, so such a step is not for capture."""
+        appended, and each slot's next token comes from its last row. A
+        slot's entry of `tokens` may be None when it has one row: that row is
+        the slot's last output, taken on the device (no host round trip).
+        The ids are copied to the device first, so such a step is not for
+        capture (see `capture(rows=...)`)."""
         if rows is None:
             if self.fused:
                 return self._enqueue_fused(stream)
@@ -335,11 +338,16 @@ class SlotGroup:
         rows = [int(x) for x in rows]
         if len(rows) != self.n or any(x < 1 or x > self.max_rows for x in rows):
             raise ValueError(f"rows: one count per slot in 1..{self.max_rows}")
-        if tokens is None or len(tokens) != self.n or any(len(t) != x for t, x in zip(tokens, rows)):
-            raise ValueError("tokens: one list of ids per slot, as long as its row count")
+        if tokens is None or len(tokens) != self.n or any(
+                (t is None and x != 1) or (t is not None and len(t) != x) for t, x in zip(tokens, rows)):
+            raise ValueError("tokens: one list of ids per slot, as long as its row count (None: one row, "
+                             "the slot's last output)")
         with torch.cuda.stream(stream):
+            if any(t is None for t in tokens):
+                self.tok_in[:, 0].copy_(self.tokens)
             for i, t in enumerate(tokens):
-                self.tok_in[i, :rows[i]].copy_(torch.tensor(t, dtype=torch.int64))
+                if t is not None:
+                    self.tok_in[i, :rows[i]].copy_(torch.tensor(t, dtype=torch.int64))
         return self._enqueue_fused(stream, rows)
 
     def _enqueue_fused(self, stream: torch.cuda.Stream, row_counts=None) -> None:

@@ -60,7 +60,9 @@ class FakeGroup:
 
     def enqueue_step(self, stream, rows=None, tokens=None):
         rows = rows or [1] * self.n
-        tokens = tokens or [[int(t)] for t in self.tokens]
+        tokens = tokens or [None] * self.n
+        assert all(t is not None or r == 1 for t, r in zip(tokens, rows))
+        tokens = [[int(self.tokens[i])] if t is None else t for i, t in enumerate(tokens)]
         self.steps.append((list(rows), [list(t) for t in tokens], list(self.ctx), list(self.adapter)))
         for i in range(self.n):
             self.ctx[i] += rows[i]

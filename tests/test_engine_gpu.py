@@ -260,7 +260,9 @@ def test_mixed_prefill_and_decode_step(native, cuda):
         stream = torch.cuda.current_stream()
         kc0 = [k.clone() for k in grp.k_cache]
         vc0 = [v.clone() for v in grp.v_cache]
-        grp.enqueue_step(stream, rows=rows, tokens=toks)
+        # one-row slots pass None: their row is the slot's last output, on the device
+        grp.tokens.copy_(torch.tensor([t[0] for t in toks]))
+        grp.enqueue_step(stream, rows=rows, tokens=[None if r == 1 else t for t, r in zip(toks, rows)])
         torch.cuda.synchronize()
         # the same mixed step from a CUDA graph of the row pattern (token ids
         # staged in tok_in) gives bit-identical tokens, hidden rows and caches
