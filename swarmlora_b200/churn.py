@@ -9,7 +9,9 @@ with lognormal prompt / output lengths and Zipf-distributed adapter ids over
 a pool of adapters of mixed ranks, an LRU cache of packed adapters on the
 GPU, and a step loop that packs prefill chunks and decode rows of all active
 requests into one engine step (SlotGroup.enqueue_step with per-slot rows).
-Slots without a request run one throw-away row from an empty context.
+A step runs only the slots that hold a request (SlotGroup.subset views);
+with a group that has no subset views, slots without a request run one
+throw-away row from an empty context.
 """
 from __future__ import annotations
 
@@ -157,8 +159,14 @@ class ChurnRunner:
     (stats.swap_s, of which stats.load_s loads)."""
 
     def __init__(self, group, trace: list[Request], cfg: ChurnConfig, load_adapter, timer, vocab: int,
-                 stream=None, seed: int = 0):
+                 stream=None, seed: int = 0, max_views: int = 8, capture_after: int = 8):
         self.g = group
+        self.views = OrderedDict()  # active slot tuple -> subset view (LRU)
+        self.max_views = int(max_views)
+        self.capture_after = int(capture_after)  # all-decode steps of one busy set before its graph
+        self._last_active = None
+        self._repeat = 0
+        self.use_views = hasattr(group, "subset")
         self.stream = stream
         self.trace = sorted(trace, key=lambda r: r.arrival)
         self.cfg = cfg
@@ -213,10 +221,12 @@ class ChurnRunner:
                 now = pending[0].arrival  # idle until the next arrival
                 continue
             rows, toks = [], []
-            budget = self.cfg.max_step_rows - self.g.n  # every slot has one row; prefill chunks share the rest
+            busy = sum(r is not None for r in self.slot_req) if self.use_views else self.g.n
+            budget = self.cfg.max_step_rows - busy  # every stepped slot has one row; prefill chunks share the rest
             for i, req in enumerate(self.slot_req):
                 if req is None:
-                    self.g.set_context(i, 0)  # a throw-away row from an empty context
+                    if not self.use_views:
+                        self.g.set_context(i, 0)  # a throw-away row from an empty context
                     rows.append(1)
                     toks.append([0])
                 elif req.prefilled < req.prompt:
@@ -251,10 +261,43 @@ class ChurnRunner:
                     self.slot_req[i] = None
         return self.stats
 
+    def _view(self, active: tuple):
+        v = self.views.get(active)
+        if v is None:
+            v = self.views[active] = self.g.subset(active)
+            while len(self.views) > self.max_views:
+                _, old = self.views.popitem(last=False)
+                old.close()
+        else:
+            self.views.move_to_end(active)
+        return v
+
     def _step(self, rows, toks):
         """One engine step; decode rows take each slot's last output token.
-        A step of one row per slot (decode and idle slots only) replays the
-        group's captured step graph when it has one."""
+        With subset views only the busy slots run: an all-decode step replays
+        the view's graph, captured once the same busy set has decoded
+        `capture_after` steps in a row (a capture costs about as much host
+        time as a few eager steps); other steps launch eagerly. Without views, a step of
+        one row per slot (decode and idle slots only) replays the group's
+        captured step graph when it has one."""
+        if self.use_views:
+            active = tuple(i for i, r in enumerate(self.slot_req) if r is not None)
+            v = self._view(active)
+            rows = [rows[i] for i in active]
+            toks = [toks[i] for i in active]
+            if all(x == 1 for x in rows) and all(t is None for t in toks):
+                self._repeat = self._repeat + 1 if active == self._last_active else 1
+                self._last_active = active
+                if v.graph is None and self._repeat >= self.capture_after:
+                    v.capture(self.stream)
+                if v.graph is not None:
+                    v.replay()
+                else:
+                    v.enqueue_step(self.stream)
+            else:
+                self._last_active, self._repeat = None, 0
+                v.enqueue_step(self.stream, rows=rows, tokens=toks)
+            return
         if all(x == 1 for x in rows) and all(t is None or t == [0] for t in toks):
             if getattr(self.g, "graph", None) is not None:
                 self.g.replay()

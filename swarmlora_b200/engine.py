@@ -27,6 +27,7 @@ replayed per token. Rounds go through the aggregator's C-ABI round entry
 """
 from __future__ import annotations
 
+import copy
 import ctypes as C
 import math
 from dataclasses import dataclass, field
@@ -230,6 +231,8 @@ class SlotGroup:
         self.tokens = torch.zeros(n, dtype=torch.int64, device=self.dev)
         self._build_call_args()
         self._advance = {}
+        self._subset = None          # slot indices of a subset view (SlotGroup.subset), else None
+        self._slot_index = list(range(n))
         self.graph = None
 
     # ------------------------------------------------------------------------------
@@ -345,9 +348,9 @@ class SlotGroup:
         with torch.cuda.stream(stream):
             if any(t is None for t in tokens):
                 self.tok_in[:, 0].copy_(self.tokens)
-            for i, t in enumerate(tokens):
+            for j, (i, t) in enumerate(zip(self._slot_index, tokens)):
                 if t is not None:
-                    self.tok_in[i, :rows[i]].copy_(torch.tensor(t, dtype=torch.int64))
+                    self.tok_in[i, :rows[j]].copy_(torch.tensor(t, dtype=torch.int64))
         return self._enqueue_fused(stream, rows)
 
     def _enqueue_fused(self, stream: torch.cuda.Stream, row_counts=None) -> None:
@@ -362,7 +365,7 @@ class SlotGroup:
             check(L.swl_copy_rows(n, self.a_tok, self.a_in, self.a_b8, st))
         else:
             rows, tx = i32_array(row_counts), i64_array(row_counts)
-            check(L.swl_copy_rows(n, ptr_array([self.tok_in[i].data_ptr() for i in range(n)]), self.a_in,
+            check(L.swl_copy_rows(n, ptr_array([self.tok_in[i].data_ptr() for i in self._slot_index]), self.a_in,
                                   i64_array([8 * x for x in row_counts]), st))
         self._round(agg.OP_EMBED, 0, st, tx)
         # embedding -> h, RMSNorm -> QKV slot input, QKV shrink
@@ -414,11 +417,21 @@ class SlotGroup:
                                                 st))
         self._round(agg.OP_LM_HEAD, 0, st, tx)  # the greedy pick reads each slot's last row
         check(L.swl_copy_rows(n, self.a_out, self.a_tok, self.a_b8, st))
-        if row_counts is None or len(set(row_counts)) == 1:
+        if self._subset is None and (row_counts is None or len(set(row_counts)) == 1):
             check(L.swl_advance_i32(self.seqlens.data_ptr(), n, 1 if row_counts is None else row_counts[0], st))
         else:
             with torch.cuda.stream(stream):
-                self.seqlens.add_(self._advance_of(row_counts))
+                self.seqlens.add_(self._advance_of(self._full_pattern(row_counts)))
+
+    def _full_pattern(self, row_counts) -> list:
+        """Per-slot position advance over the whole group (0 outside a subset)."""
+        rows = [1] * self.n if row_counts is None else [int(x) for x in row_counts]
+        if self._subset is None:
+            return rows
+        full = [0] * len(self.slot_ids)
+        for i, x in zip(self._subset, rows):
+            full[i] = x
+        return full
 
     def _advance_of(self, row_counts) -> torch.Tensor:
         """Device copy of a row pattern (the per-slot position advance), made
@@ -498,8 +511,8 @@ class SlotGroup:
             rows = [int(x) for x in rows]
             if len(rows) != self.n or any(x < 1 or x > self.max_rows for x in rows) or not self.fused:
                 raise ValueError(f"rows: one count per slot in 1..{self.max_rows} (fused sequence)")
-            if len(set(rows)) > 1:
-                self._advance_of(rows)
+        if self._subset is not None or (rows is not None and len(set(rows)) > 1):
+            self._advance_of(self._full_pattern(rows))
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=s):
             if rows is None:
@@ -543,8 +556,45 @@ class SlotGroup:
         dist.barrier(group=group)
         self._shard_group = (group,)
 
+    def subset(self, active) -> "SlotGroup":
+        """A view of this group whose steps run only the slots in `active`
+        (indices into this group): adapters, caches, positions and buffers
+        are shared, the kernels and rounds see only those slots (an idle
+        slot costs nothing, not even its adapter's bytes), positions advance
+        for those slots only, and the view keeps its own CUDA graph
+        (`capture` / `replay`). Its `rows` / `tokens` arguments have one
+        entry per active slot, in `active` order; `set_context` and
+        `set_adapter` still take group indices. Closing the view only drops
+        its graph."""
+        if self._subset is not None:
+            raise ValueError("a subset of a subset view")
+        if not self.fused:
+            raise ValueError("subset views run the fused sequence")
+        active = sorted(set(int(i) for i in active))
+        if not active or active[0] < 0 or active[-1] >= self.n:
+            raise ValueError(f"active slots must be indices in 0..{self.n - 1}")
+        v = copy.copy(self)
+        v._subset, v._slot_index, v.n, v.graph = tuple(active), list(active), len(active), None
+
+        def ptrs(arr):
+            return ptr_array([arr[i] for i in active])
+        k = len(active)
+        v.a_rows, v.a_ones = i32_array([1] * k), i64_array([1] * k)
+        v.a_sids = i32_array([self.slot_ids[i] for i in active])
+        v.a_wids = i32_array([self.worker_ids[i] for i in active])
+        v.a_in, v.a_out, v.a_h, v.a_qkv = ptrs(self.a_in), ptrs(self.a_out), ptrs(self.a_h), ptrs(self.a_qkv)
+        v.a_tok, v.a_bt, v.a_sl = ptrs(self.a_tok), ptrs(self.a_bt), ptrs(self.a_sl)
+        v.a_b8, v.a_bH = i64_array([8] * k), i64_array([2 * self.cfg.hidden] * k)
+        v.a_kc = [ptr_array([t.data_ptr()] * k) for t in self.k_cache]
+        v.a_vc = [ptr_array([t.data_ptr()] * k) for t in self.v_cache]
+        for name in ("A_qkv", "B_qkv", "A_o", "B_o", "A_gu", "B_gu", "A_dn", "B_dn"):
+            setattr(v, name, [ptrs(t) for t in getattr(self, name)])
+        return v
+
     def close(self) -> None:
         self.graph = None
+        if self._subset is not None:
+            return
         if getattr(self, "_shard_group", None) is not None:
             import torch.distributed as dist
             torch.cuda.synchronize(self.dev)

@@ -3,6 +3,7 @@ trace's distributions, the LRU adapter cache, a full run of the step loop
 against a fake slot group that records what each step asked for, and the
 packed-adapter slab a swap copies."""
 import numpy as np
+import pytest
 import torch
 
 from swarmlora_b200 import worker_ops as wo
@@ -43,14 +44,19 @@ def test_adapter_cache_is_lru():
 
 
 class FakeGroup:
-    """Records the steps; each step's next token is a function of its inputs."""
+    """Records the steps; each step's next token is a function of its inputs.
+    With views=True it offers subset views (SlotGroup.subset) whose steps run
+    only their slots."""
 
-    def __init__(self, n, vocab=1000):
+    def __init__(self, n, vocab=1000, views=False):
         self.n, self.max_rows, self.max_len, self.vocab = n, 16, 4096, vocab
         self.tokens = torch.zeros(n, dtype=torch.int64)
         self.ctx = [0] * n
         self.adapter = [None] * n
-        self.steps = []
+        self.steps = []   # (active slots, rows, token lists, contexts before, adapters)
+        self.captures = 0
+        if views:
+            self.subset = lambda active: FakeView(self, active)
 
     def set_adapter(self, i, a):
         self.adapter[i] = a
@@ -58,25 +64,53 @@ class FakeGroup:
     def set_context(self, i, length):
         self.ctx[i] = length
 
-    def enqueue_step(self, stream, rows=None, tokens=None):
-        rows = rows or [1] * self.n
-        tokens = tokens or [None] * self.n
+    def _do(self, active, rows, tokens):
+        rows = rows or [1] * len(active)
+        tokens = tokens or [None] * len(active)
+        assert len(rows) == len(tokens) == len(active)
         assert all(t is not None or r == 1 for t, r in zip(tokens, rows))
-        tokens = [[int(self.tokens[i])] if t is None else t for i, t in enumerate(tokens)]
-        self.steps.append((list(rows), [list(t) for t in tokens], list(self.ctx), list(self.adapter)))
-        for i in range(self.n):
-            self.ctx[i] += rows[i]
-            self.tokens[i] = (sum(tokens[i]) + 7 * i) % self.vocab
+        tokens = [[int(self.tokens[i])] if t is None else t for i, t in zip(active, tokens)]
+        self.steps.append((list(active), list(rows), [list(t) for t in tokens],
+                           [self.ctx[i] for i in active], [self.adapter[i] for i in active]))
+        for j, i in enumerate(active):
+            self.ctx[i] += rows[j]
+            self.tokens[i] = (sum(tokens[j]) + 7 * i) % self.vocab
+
+    def enqueue_step(self, stream, rows=None, tokens=None):
+        self._do(list(range(self.n)), rows, tokens)
 
 
-def test_runner_serves_every_request():
+class FakeView:
+    def __init__(self, g, active):
+        self.g, self.active, self.n, self.graph = g, list(active), len(active), None
+
+    def enqueue_step(self, stream, rows=None, tokens=None):
+        self.g._do(self.active, rows, tokens)
+
+    def capture(self, stream=None):
+        self.graph = "captured"
+        self.g.captures += 1
+
+    def replay(self):
+        self.g._do(self.active, None, None)
+
+    def close(self):
+        self.graph = None
+
+
+def _run(views):
     cfg = ChurnConfig(rate=20.0, cache_adapters=3, pool_size=20, prompt_median=40, prompt_clip=(1, 80),
                       output_median=12, output_clip=(1, 30), max_step_rows=24)
     trace = make_trace(cfg, 2.0, seed=3)
-    g = FakeGroup(4)
+    g = FakeGroup(4, views=views)
     runner = ChurnRunner(g, trace, cfg, load_adapter=lambda aid: f"adapter{aid}", timer=lambda fn: (fn(), 0.005)[1],
-                         vocab=g.vocab)
-    st = runner.run()
+                         vocab=g.vocab, capture_after=3)
+    return cfg, trace, g, runner.run()
+
+
+@pytest.mark.parametrize("views", [False, True])
+def test_runner_serves_every_request(views):
+    cfg, trace, g, st = _run(views)
     assert st.completed == len(trace)
     assert st.prefill_tokens == sum(r.prompt for r in trace)
     assert st.decode_tokens == sum(r.output - 1 for r in trace)
@@ -84,10 +118,19 @@ def test_runner_serves_every_request():
     assert abs(st.load_s - 0.005 * st.cache_misses) < 1e-9 and st.swap_s >= st.load_s
     for r in trace:  # first token after the whole prompt, done after the whole output
         assert r.start >= r.arrival and r.first_token > r.start and r.done >= r.first_token
-    for rows, toks, ctx, adapters in g.steps:
+    for active, rows, toks, ctx, adapters in g.steps:
         assert all(1 <= x <= 16 for x in rows) and [len(t) for t in toks] == rows
         assert sum(rows) <= cfg.max_step_rows
         assert all(c + x <= g.max_len for c, x in zip(ctx, rows))
+        if views:  # only busy slots step, each with its request's adapter
+            assert all(a is not None for a in adapters)
+        else:
+            assert active == list(range(g.n))
+    if views:
+        assert any(len(a) < g.n for a, *_ in g.steps) and g.captures > 0
+        # a slot's context grows only by the rows it ran: every request's
+        # prompt and output, never a throw-away row
+        assert sum(sum(rows) for _, rows, *_ in g.steps) == st.prefill_tokens + st.decode_tokens
     s = st.summary()
     assert s["decode_tok_per_s"] > 0 and s["ttft_p50_s"] is not None
 

@@ -300,3 +300,73 @@ def test_mixed_prefill_and_decode_step(native, cuda):
         _check_tokens(grp.tokens.cpu(), want, logits, "decode after the mixed step")
     finally:
         grp.close()
+
+
+def test_subset_view_steps_only_its_slots(native, cuda):
+    """SlotGroup.subset: a view over slots 0, 2 and 4 of a five-slot group
+    runs a decode step and then a mixed step (a 6-row prefill chunk on slot
+    2) for those slots only, against the CPU oracle on the same three slots;
+    the idle slots' positions and pages stay untouched, and the view's
+    captured graph replays its decode step bit-identically."""
+    from oracle.decode import decode_step
+    from swarmlora_b200.engine import ModelConfig, SlotGroup, random_adapter, random_base
+    cfg = ModelConfig(layers=2, vocab=4096)
+    ctx = [12, 40, 3, 77, 25]
+    active = [0, 2, 4]
+    base = random_base(cfg, seed=4, device=cuda, norm_noise=0.1)
+    adapters = [random_adapter(cfg, seed=60 + i, device=cuda) for i in range(len(ctx))]
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=16, seed=9)
+    try:
+        base_c = _cpu(base)
+        ad_c = [_cpu(adapters[i]) for i in active]
+        kc = [k.cpu() for k in grp.k_cache]
+        vc = [v.cpu() for v in grp.v_cache]
+        bts = [grp.block_tables[i].tolist() for i in active]
+        idle_pages = [p for i in (1, 3) for p in grp.block_tables[i].tolist()]
+        idle_k = [k.cpu()[idle_pages] for k in grp.k_cache]
+        tokens = [101, 202, 303, 404, 505]
+        grp.tokens.copy_(torch.tensor(tokens))
+        view = grp.subset(active)
+        stream = torch.cuda.current_stream()
+        view.enqueue_step(stream)
+        torch.cuda.synchronize()
+        seq = [ctx[i] for i in active]
+        want, final, logits, h_last = decode_step(cfg, base_c, ad_c, kc, vc, bts, seq, [tokens[i] for i in active])
+        got = grp.tokens.cpu()
+        assert_close(grp.h[active], h_last, "view decode: last-layer hidden", atol_rms=ATOL_RMS_MULTILAYER)
+        _check_tokens(got[active], want, logits, "view decode")
+        assert got[1] == 202 and got[3] == 404, "idle slots' tokens changed"
+        assert grp.seqlens.cpu().tolist() == [13, 40, 4, 77, 26]
+        assert all(torch.equal(k.cpu()[idle_pages], k0) for k, k0 in zip(grp.k_cache, idle_k))
+        # a mixed step on the view: slot 2 prefills 6 rows, slots 0 and 4 decode
+        seq = [s + 1 for s in seq]
+        g = torch.Generator().manual_seed(2)
+        chunk = torch.randint(0, cfg.vocab, (6,), generator=g).tolist()
+        dec = got.tolist()
+        view.enqueue_step(stream, rows=[1, 6, 1], tokens=[None, chunk, None])
+        torch.cuda.synchronize()
+        want, final, logits, h_last = decode_step(cfg, base_c, ad_c, kc, vc, bts, seq,
+                                                  [[dec[0]], chunk, [dec[4]]])
+        got_h = torch.stack([grp.h_rows[i, r - 1] for i, r in zip(active, [1, 6, 1])])
+        assert_close(got_h, h_last, "view mixed step: last row's hidden", atol_rms=ATOL_RMS_MULTILAYER)
+        _check_tokens(grp.tokens.cpu()[active], want, logits, "view mixed step")
+        assert grp.seqlens.cpu().tolist() == [14, 40, 10, 77, 27]
+        # the view's graph: replay from a saved state equals the eager step
+        state = ([k.clone() for k in grp.k_cache], [v.clone() for v in grp.v_cache], grp.seqlens.clone(),
+                 grp.tokens.clone())
+        view.enqueue_step(stream)
+        torch.cuda.synchronize()
+        eager = (grp.tokens.clone(), [k.clone() for k in grp.k_cache], grp.seqlens.clone())
+        view.capture(stream)
+        for l in range(cfg.layers):
+            grp.k_cache[l].copy_(state[0][l])
+            grp.v_cache[l].copy_(state[1][l])
+        grp.seqlens.copy_(state[2])
+        grp.tokens.copy_(state[3])
+        view.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(grp.tokens, eager[0]) and torch.equal(grp.seqlens, eager[2])
+        assert all(torch.equal(a, b) for a, b in zip(grp.k_cache, eager[1]))
+        view.close()
+    finally:
+        grp.close()
