@@ -747,7 +747,9 @@ SWL_EXPORT int swl_agg_import_weights(const swl_weight_ipc* recs, int count, con
       }
       x.base = static_cast<char*>(p);
       char* b2 = nullptr;
-      st = allocation_of(p, &b2, &x.size);
+      size_t n2 = 0;
+      st = allocation_of(p, &b2, &n2);
+      x.size = st == SWL_OK ? static_cast<size_t>(b2 + n2 - x.base) : 0;  // bytes mapped from x.base on
       maps.push_back(x);
       if (st != SWL_OK) break;
       m = &maps.back();
@@ -772,7 +774,7 @@ SWL_EXPORT int swl_agg_import_weights(const swl_weight_ipc* recs, int count, con
     g_arena = nullptr;
     g_layers.clear();
     g_num_layers = 0;
-    return set_error(SWL_ERR_CUDA, "%s", why.c_str());
+    return set_error(st, "%s", why.c_str());
   }
   char* arena = static_cast<char*>(g_arena);
   g_layers.assign(num_layers, Layer());
