@@ -13,6 +13,19 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA (B200, sm_100a) device")
 
 
+@pytest.fixture
+def scratch(request):
+    """A fresh directory for one test's files inside the repository
+    (tests/_scratch/<test>), removed afterwards."""
+    import re
+    import shutil
+    d = ROOT / "tests" / "_scratch" / re.sub(r"[^A-Za-z0-9_.-]", "_", request.node.name)
+    shutil.rmtree(d, ignore_errors=True)
+    d.mkdir(parents=True)
+    yield d
+    shutil.rmtree(d, ignore_errors=True)
+
+
 @pytest.fixture(scope="session")
 def native():
     """The C-ABI library (built if missing)."""

@@ -62,24 +62,24 @@ def test_packed_loaded_adapter_keeps_the_reference_prescale(golden):
     assert torch.equal(A_k[:, :8], golden["adapter_r8_partial"]["modules"][(1, MOD_NAME["k"])][0].t() * s)
 
 
-def test_save_then_load_round_trip(tmp_path):
+def test_save_then_load_round_trip(scratch):
     g = torch.Generator().manual_seed(3)
     dims = ad.module_dims(TINY)
     layers = [{p: ((torch.randn(8, i, generator=g) * 0.05).to(torch.bfloat16),
                    (torch.randn(o, 8, generator=g) * 0.05).to(torch.bfloat16)) for p, (i, o) in dims.items()}
               for _ in range(TINY.layers)]
-    ad.save_adapter(str(tmp_path / "a"), layers, alpha=16)
+    ad.save_adapter(str(scratch / "a"), layers, alpha=16)
     loader = ad.AdapterLoader(TINY, "cpu")
     for _ in range(2):  # the staging buffer is reused
-        got, config = loader.load(str(tmp_path / "a"))
+        got, config = loader.load(str(scratch / "a"))
         assert config["scaling"] == 2.0
         for l in range(TINY.layers):
             for p in dims:
                 assert torch.equal(got[l][p][0], layers[l][p][0]) and torch.equal(got[l][p][1], layers[l][p][1])
 
 
-def test_loader_refuses_what_the_reference_refuses(tmp_path):
-    base = tmp_path / "pool"
+def test_loader_refuses_what_the_reference_refuses(scratch):
+    base = scratch / "pool"
     (base / "bin_only").mkdir(parents=True)
     (base / "bin_only" / "adapter_config.json").write_text(json.dumps({"r": 4}))
     (base / "bin_only" / "adapter_model.bin").write_bytes(b"\x80")

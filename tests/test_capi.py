@@ -40,8 +40,8 @@ def test_python_binding_covers_exports(native):
     assert exported <= bound, f"unbound exports: {sorted(exported - bound)}"
 
 
-def test_header_compiles_as_c(tmp_path):
-    src = tmp_path / "use.c"
+def test_header_compiles_as_c(scratch):
+    src = scratch / "use.c"
     src.write_text('#include "swarmlora_b200.h"\nint main(void){return swl_abi_version() == 1 ? 0 : 1;}\n')
     res = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-fsyntax-only", f"-I{ROOT / 'include'}",
                           str(src)], capture_output=True, text=True)
