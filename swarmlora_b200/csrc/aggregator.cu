@@ -28,6 +28,7 @@
 #include <vector>
 
 #include "common.h"
+#include "agg_protocol.h"
 #include "shm_abi.h"
 #include "swarmlora_b200.h"
 #include "slot_round.h"
@@ -1096,67 +1097,6 @@ SWL_EXPORT int swl_agg_shard_end(void) { return shard_end(); }
 
 namespace {
 
-// ext_aggregator.cpp:879-978 aggregator_wait_for_slots: wait until every
-// active slot has set its ready bit; drop slots that signal leave mid-op
-// (checked every 10 ms) and evict slots not ready within 500 ms. Returns the
-// remaining slot count, or -1 when the quit flag is raised.
-int wait_for_slots(Mask128& active) {
-  using clk = std::chrono::steady_clock;
-  auto start = clk::now(), last_leave = start;
-  const auto kEvictAfter = std::chrono::milliseconds(500);
-  const auto kLeaveEvery = std::chrono::milliseconds(10);
-  long spins = 0;
-  for (;;) {
-    Mask128 ready = g_ctrl->per_slot_ready_mask.load();
-    Mask128 missing = active & ~ready;
-    if (missing.empty()) return active.count();
-    if (g_ctrl->quit_flag.load(std::memory_order_acquire)) return -1;
-    ++spins;
-    if (spins < kSpinTight) continue;
-    if (spins < kSpinYield) { cpu_relax(); continue; }
-    auto now = clk::now();
-    if (now - last_leave > kLeaveEvery) {
-      last_leave = now;
-      Mask128 leaving = g_ctrl->pending_slot_leaves.load() & active;
-      if (!leaving.empty()) {
-        active = active & ~leaving;
-        g_ctrl->pending_slot_leaves.and_with(~leaving);
-        g_ctrl->active_slot_mask.store(active);
-        g_ctrl->active_slot_count.store(active.count());
-        if (active.empty()) return 0;
-      }
-    }
-    if (now - start > kEvictAfter) {
-      Mask128 stuck = active & ~g_ctrl->per_slot_ready_mask.load();
-      if (!stuck.empty()) {
-        active = active & ~stuck;
-        g_ctrl->active_slot_mask.store(active);
-        g_ctrl->active_slot_count.store(active.count());
-        for (Mask128 r = stuck; !r.empty();) {
-          int sid = r.lowest();
-          r.clear(sid);
-          g_ctrl->evicted_slot_mask.set_bit(sid);
-        }
-        fprintf(stderr, "[swl aggregator] evicting stuck slot(s) mask=0x%llx:%llx; %d continue\n",
-                (unsigned long long)stuck.w[1], (unsigned long long)stuck.w[0], active.count());
-        if (active.empty()) return 0;
-        start = clk::now();
-        spins = 0;
-      }
-    }
-    cpu_relax();
-    cpu_relax();
-  }
-}
-
-// ext_aggregator.cpp:981-987 aggregator_signal_done_slots.
-void signal_done() {
-  g_ctrl->slot_ready_count.store(0, std::memory_order_release);
-  Mask128 active = g_ctrl->active_slot_mask.load();
-  g_ctrl->per_slot_ready_mask.and_with(~active);
-  g_ctrl->barrier_done_epoch.fetch_add(1, std::memory_order_release);
-}
-
 // ext_aggregator.cpp:991-1020 apply_pending_sampling_states.
 void apply_pending_sampling(const Mask128& joins) {
   Mask128 todo = g_ctrl->pending_sampling_mask.load() & joins;
@@ -1172,14 +1112,42 @@ void apply_pending_sampling(const Mask128& joins) {
   g_ctrl->pending_sampling_mask.and_with(~todo);
 }
 
-void evict(const std::vector<int>& slots, Mask128& active) {
-  for (int sid : slots) {
-    active.clear(sid);
-    g_ctrl->evicted_slot_mask.set_bit(sid);
+// The aggregator's side of run_main_loop: GPU rounds over validated
+// commands, sampling state, the pool's copy of the active set.
+struct AggHooks {
+  std::vector<RoundCmd> all, good;
+  void on_membership(const Mask128& active, const Mask128& joins) {
+    if (!joins.empty()) apply_pending_sampling(joins);
+    store_mask(g_pool.active_w, active);
+    g_pool.active_slot_count.store(active.count());
   }
-  g_ctrl->active_slot_mask.store(active);
-  g_ctrl->active_slot_count.store(active.count());
-}
+  void on_sampling(const DrainedCmd& c) {
+    SamplingState s;
+    s.do_sample = (c.x_key & 1) != 0;
+    s.temperature = static_cast<float>(c.x_key >> 1) / 10000.0f;
+    s.top_k = static_cast<int>(c.y0_key);
+    s.top_p = static_cast<float>(c.y1_key) / 10000.0f;
+    g_sampling[c.worker_id] = s;
+  }
+  void validate(int op, int layer, const std::vector<DrainedCmd>& cmds, std::vector<int>* bad) {
+    all.clear();
+    for (const DrainedCmd& c : cmds) all.push_back({c.slot_id, c.worker_id, c.rows});
+    int64_t in_row, out_row;
+    row_bytes_for(op, layer, &in_row, &out_row);
+    std::string why;
+    ::validate(all.data(), static_cast<int>(all.size()), in_row, out_row, &good, bad, &why);
+    if (!why.empty()) fprintf(stderr, "[swl aggregator] dropping commands: %s\n", why.c_str());
+  }
+  int round(int op, int layer, const std::vector<DrainedCmd>&, const std::vector<int>&) {
+    int st = run_round(op, layer, good, g_stream);
+    if (st == SWL_OK) {
+      cudaError_t e = cudaStreamSynchronize(g_stream);
+      if (e != cudaSuccess) st = set_error(SWL_ERR_CUDA, "round: %s", cudaGetErrorString(e));
+    }
+    if (st != SWL_OK) fprintf(stderr, "[swl aggregator] round op=%d layer=%d failed: %s\n", op, layer, last_error());
+    return st;
+  }
+};
 
 }  // namespace
 
@@ -1194,100 +1162,6 @@ SWL_EXPORT int swl_agg_main_loop_slots(int num_slots, int dtype_code) {
   if (dtype_code != 15) return set_error(SWL_ERR_ARG, "only bf16 (dtype_code 15) is supported");
   SWL_CUDA_TRY(cudaSetDevice(g_device));
   SWL_TRY(ensure_stream());
-  Mask128 active;
-  std::vector<RoundCmd> cmds, good;
-  std::vector<int> bad;
-  cmds.reserve(kMaxSlots);
-  while (g_ctrl->quit_flag.load(std::memory_order_acquire) == 0) {
-    Mask128 leaves, joins;
-    if (!g_ctrl->pending_slot_leaves.load().empty()) leaves = g_ctrl->pending_slot_leaves.take_all();
-    if (!leaves.empty()) active = active & ~leaves;
-    if (!g_ctrl->pending_slot_joins.load().empty()) joins = g_ctrl->pending_slot_joins.take_all();
-    if (!joins.empty()) {
-      apply_pending_sampling(joins);
-      active = active | joins;
-    }
-    int N = active.count();
-    g_ctrl->active_slot_mask.store(active);
-    g_ctrl->active_slot_count.store(N);
-    store_mask(g_pool.active_w, active);
-    g_pool.active_slot_count.store(N);
-    if (N == 0) {
-      std::this_thread::sleep_for(std::chrono::milliseconds(1));
-      continue;
-    }
-    const int ops_per_token = 1 + g_num_layers * 4 + 1;
-    for (int op_idx = 0; op_idx < ops_per_token; ++op_idx) {
-      int got = wait_for_slots(active);
-      if (got < 0) {
-        signal_done();
-        break;
-      }
-      if (got == 0) break;
-      N = got;
-      // Drain N commands, discarding entries of slots evicted meanwhile.
-      cmds.clear();
-      int tail = g_ctrl->tail.load(std::memory_order_acquire);
-      int drained = 0, op = -1, layer = -1;
-      bool quit = false;
-      while (static_cast<int>(cmds.size()) < N && drained < kMaxSlots + 8) {
-        Command* c = &g_ring[tail];
-        long spin = 0;
-        while (c->ready.load(std::memory_order_acquire) != 1) {
-          if (g_ctrl->quit_flag.load(std::memory_order_acquire)) { quit = true; break; }
-          if (++spin > 10000000) {
-            fprintf(stderr, "[swl aggregator] command not ready after drain wait; quitting\n");
-            g_ctrl->quit_flag.store(1, std::memory_order_release);
-            quit = true;
-            break;
-          }
-          if (spin > kSpinYield) cpu_relax();
-        }
-        if (quit) break;
-        c->ready.store(0, std::memory_order_release);
-        tail = (tail + 1) % g_capacity;
-        ++drained;
-        if (c->slot_id >= 0 && c->slot_id < kMaxSlots && active.test(c->slot_id)) {
-          if (op < 0) { op = c->op_type; layer = c->layer_idx; }
-          cmds.push_back({c->slot_id, c->worker_id, c->bx * c->tx});
-          if (c->op_type == kOpSetSampling) {
-            SamplingState s;
-            s.do_sample = (c->x_key & 1) != 0;
-            s.temperature = static_cast<float>(c->x_key >> 1) / 10000.0f;
-            s.top_k = static_cast<int>(c->y0_key);
-            s.top_p = static_cast<float>(c->y1_key) / 10000.0f;
-            g_sampling[c->worker_id] = s;
-          }
-        }
-      }
-      g_ctrl->tail.store(tail, std::memory_order_release);
-      if (quit || g_ctrl->quit_flag.load(std::memory_order_acquire)) {
-        signal_done();
-        break;
-      }
-      if (cmds.empty()) continue;
-      if (op == kOpSetSampling) {
-        signal_done();
-        continue;
-      }
-      int64_t in_row, out_row;
-      row_bytes_for(op, layer, &in_row, &out_row);
-      std::string why;
-      validate(cmds.data(), static_cast<int>(cmds.size()), in_row, out_row, &good, &bad, &why);
-      if (!why.empty()) fprintf(stderr, "[swl aggregator] dropping commands: %s\n", why.c_str());
-      if (!bad.empty()) evict(bad, active);
-      int st = run_round(op, layer, good, g_stream);
-      if (st == SWL_OK) {
-        cudaError_t e = cudaStreamSynchronize(g_stream);
-        if (e != cudaSuccess) st = set_error(SWL_ERR_CUDA, "round: %s", cudaGetErrorString(e));
-      }
-      if (st != SWL_OK) {
-        fprintf(stderr, "[swl aggregator] round op=%d layer=%d failed: %s\n", op, layer, last_error());
-        signal_done();
-        return st;  // device state is unknown; stop like the reference does
-      }
-      signal_done();
-    }
-  }
-  return SWL_OK;
+  AggHooks hooks;
+  return run_main_loop(g_ctrl, g_ring, g_capacity, 1 + g_num_layers * 4 + 1, hooks);
 }

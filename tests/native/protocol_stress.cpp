@@ -1,0 +1,170 @@
+// Stress run of the aggregator's host protocol in one process, for the
+// thread and address sanitizers: worker threads drive the worker-side queue
+// API (swarmlora_b200/csrc/ipc_queue.cpp: join, submit, ready, wait for the
+// epoch, leave) against an aggregator thread running run_main_loop
+// (swarmlora_b200/csrc/agg_protocol.h) with a host "round" in place of the
+// GPU round. Per-slot inputs and outputs are plain (non-atomic) arrays, so
+// the sanitizer sees whether the ring and the epoch publish them.
+//
+// Scenarios: workers joining at different times and leaving after different
+// token counts, one worker that stops mid-token (evicted by the barrier
+// timeout), one that submits a command under another worker's id (evicted
+// by validation). Exit status 0 and "protocol stress ok" on success.
+#include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "agg_protocol.h"
+#include "common.h"
+#include "swarmlora_b200.h"
+
+namespace swl {
+static thread_local std::string g_err;
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+const char* last_error() { return g_err.c_str(); }
+}  // namespace swl
+
+using namespace swl;
+
+namespace {
+
+constexpr int kWorkers = 10;
+constexpr int kLayers = 2;
+constexpr int kOpsPerToken = 1 + 4 * kLayers + 1;
+constexpr int kStall = 3;  // stops submitting mid-token
+constexpr int kRogue = 6;  // submits one command under another worker's id
+
+uint64_t g_in[kMaxSlots];   // a worker's input of the current op (plain data)
+uint64_t g_out[kMaxSlots];  // the round's output for the slot (plain data)
+std::atomic<int> g_failures{0};
+std::atomic<int> g_rounds{0};
+std::atomic<int> g_evicted_seen{0};
+
+void fail(const char* what, int slot) {
+  fprintf(stderr, "FAIL slot %d: %s\n", slot, what);
+  g_failures.fetch_add(1);
+}
+
+void op_of(int k, int* op, int* layer) {
+  static const int per_layer[4] = {kOpQkvFused, kOpOProj, kOpGateUpFused, kOpDownProj};
+  if (k == 0) { *op = kOpEmbed; *layer = 0; return; }
+  if (k == kOpsPerToken - 1) { *op = kOpLmHead; *layer = 0; return; }
+  *op = per_layer[(k - 1) % 4];
+  *layer = (k - 1) / 4;
+}
+
+bool wait_until(bool (*pred)(int), int slot, int ms) {
+  auto t0 = std::chrono::steady_clock::now();
+  while (!pred(slot)) {
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(ms)) return false;
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  return true;
+}
+bool is_active(int s) { return swl_q_slot_is_active(s) == 1; }
+bool is_inactive(int s) { return swl_q_slot_is_active(s) == 0; }
+bool is_evicted(int s) { return swl_q_is_slot_evicted(s) == 1; }
+
+struct HostHooks {
+  std::vector<int> owner;  // slot -> worker id
+  void on_membership(const Mask128&, const Mask128&) {}
+  void on_sampling(const DrainedCmd&) {}
+  void validate(int, int, const std::vector<DrainedCmd>& cmds, std::vector<int>* bad) {
+    for (const DrainedCmd& c : cmds)
+      if (c.worker_id != owner[c.slot_id] || c.rows != 1) bad->push_back(c.slot_id);
+  }
+  int round(int op, int layer, const std::vector<DrainedCmd>& cmds, const std::vector<int>& bad) {
+    for (const DrainedCmd& c : cmds) {
+      if (c.op_type != op || c.layer_idx != layer) fail("round mixes ops", c.slot_id);
+      bool refused = false;
+      for (int b : bad) refused |= b == c.slot_id;
+      if (refused) continue;
+      if (g_in[c.slot_id] != c.x_key) fail("slot input not visible to the round", c.slot_id);
+      g_out[c.slot_id] = c.x_key + 1;
+    }
+    g_rounds.fetch_add(1);
+    return 0;
+  }
+};
+
+void worker(int slot, int tokens, int join_delay_ms) {
+  const int wid = 1000 + slot;
+  std::this_thread::sleep_for(std::chrono::milliseconds(join_delay_ms));
+  swl_q_slot_signal_join(slot);
+  if (!wait_until(is_active, slot, 5000)) return fail("never activated", slot);
+  uint64_t counter = 0;
+  for (int t = 0; t < tokens; ++t) {
+    for (int k = 0; k < kOpsPerToken; ++k) {
+      if (slot == kStall && t == 2 && k == 3) {  // hang mid-token: the barrier evicts the slot
+        if (!wait_until(is_evicted, slot, 5000)) return fail("stalled slot was not evicted", slot);
+        g_evicted_seen.fetch_add(1);
+        return;
+      }
+      int op, layer;
+      op_of(k, &op, &layer);
+      const int64_t e0 = swl_q_get_barrier_done_epoch();
+      const uint64_t key = (static_cast<uint64_t>(slot) << 40) | ++counter;
+      g_in[slot] = key;
+      const int as = (slot == kRogue && t == 3 && k == 5) ? wid + 1 : wid;
+      int rc;
+      while ((rc = swl_q_submit_slot_command(op, layer, slot, as, 1, 1, 4096, key, 0, 0, 0, 0)) == SWL_ERR_FULL)
+        std::this_thread::yield();
+      if (rc != SWL_OK) return fail("submit failed", slot);
+      swl_q_slot_signal_ready(slot);
+      int64_t e = 0;
+      if (swl_q_wait_for_epoch(e0, 5000, &e) != SWL_OK) return fail("epoch did not move", slot);
+      if (is_evicted(slot)) {
+        if (as == wid) return fail("evicted without cause", slot);
+        g_evicted_seen.fetch_add(1);
+        return;
+      }
+      if (as != wid) return fail("foreign command was not refused", slot);
+      if (g_out[slot] != key + 1) return fail("round output missing", slot);
+    }
+  }
+  swl_q_slot_signal_leave(slot);
+  if (!wait_until(is_inactive, slot, 5000)) fail("leave not acknowledged", slot);
+}
+
+}  // namespace
+
+int main() {
+  char name[128];
+  if (swl_q_create(256, 256, name, sizeof(name)) != SWL_OK || swl_q_init_batch_control(kWorkers) != SWL_OK) {
+    fprintf(stderr, "queue setup failed: %s\n", last_error());
+    return 2;
+  }
+  auto* ctrl = static_cast<ControlBlock*>(swl_q_control_block());
+  auto* ring = reinterpret_cast<Command*>(reinterpret_cast<char*>(ctrl) + sizeof(ControlBlock));
+  HostHooks hooks;
+  hooks.owner.assign(kMaxSlots, -1);
+  for (int s = 0; s < kWorkers; ++s) hooks.owner[s] = 1000 + s;
+  ProtocolTimes times;
+  times.evict_after = std::chrono::milliseconds(100);
+  times.leave_every = std::chrono::milliseconds(2);
+  int loop_status = -99;
+  std::thread agg([&] { loop_status = run_main_loop(ctrl, ring, swl_q_capacity(), kOpsPerToken, hooks, times); });
+  std::vector<std::thread> ws;
+  for (int s = 0; s < kWorkers; ++s) ws.emplace_back(worker, s, 40 + 10 * (s % 4), (s % 3) * 15);
+  for (auto& w : ws) w.join();
+  swl_q_set_quit(1);
+  agg.join();
+  swl_q_close();
+  if (loop_status != 0) fail("main loop returned an error", -1);
+  if (g_evicted_seen.load() != 2) fail("expected exactly the stalled and the rogue slot evicted", -1);
+  if (g_failures.load()) return 1;
+  printf("protocol stress ok: %d rounds, %d workers, 2 evicted\n", g_rounds.load(), kWorkers);
+  return 0;
+}
