@@ -336,6 +336,11 @@ class SlotGroup:
             if self.fused:
                 return self._enqueue_fused(stream)
             return self._enqueue_unfused(stream)
+        return self._enqueue_fused(stream, self._stage_tokens(stream, rows, tokens))
+
+    def _stage_tokens(self, stream, rows, tokens) -> list:
+        """Checks a mixed step's rows / tokens and copies the ids into tok_in
+        (None: the slot's last output, on the device); returns the rows."""
         if not self.fused:
             raise ValueError("steps with several rows per slot run the fused sequence")
         rows = [int(x) for x in rows]
@@ -351,12 +356,14 @@ class SlotGroup:
             for j, (i, t) in enumerate(zip(self._slot_index, tokens)):
                 if t is not None:
                     self.tok_in[i, :rows[j]].copy_(torch.tensor(t, dtype=torch.int64))
-        return self._enqueue_fused(stream, rows)
+        return rows
 
-    def _enqueue_fused(self, stream: torch.cuda.Stream, row_counts=None) -> None:
+    def _enqueue_fused(self, stream: torch.cuda.Stream, row_counts=None, mark=None) -> None:
         """Fused sequence: per layer 4 rounds + 6 worker kernels (each worker
-        kernel finishes one round's epilogue and starts the next round's LoRA)."""
+        kernel finishes one round's epilogue and starts the next round's LoRA).
+        mark(kind), when given, is called after each launch (profile_step)."""
         L, cfg, n, st = lib(), self.cfg, self.n, stream.cuda_stream
+        mark = mark or (lambda kind: None)
         H, I, D, r = cfg.hidden, cfg.inter, cfg.head_dim, cfg.rank
         s = self.scaling
         nl = cfg.layers
@@ -368,6 +375,7 @@ class SlotGroup:
             check(L.swl_copy_rows(n, ptr_array([self.tok_in[i].data_ptr() for i in self._slot_index]), self.a_in,
                                   i64_array([8 * x for x in row_counts]), st))
         self._round(agg.OP_EMBED, 0, st, tx)
+        mark("embed")
         # embedding -> h, RMSNorm -> QKV slot input, QKV shrink
         pf = self.wptr
         none = (None, 0)
@@ -375,6 +383,7 @@ class SlotGroup:
                                             self.base.in_norm[0].data_ptr(), H, cfg.eps, self.a_in, H,
                                             self.A_qkv[0], 3 * r, self.ws_qkv.data_ptr(),
                                             *pf.get((0, agg.OP_QKV_FUSED), none), st))
+        mark("epilogue")
         for l in range(nl):
             if self.qkv_rope_fused:
                 # the QKV round with the RoPE epilogue in its own epilogue
@@ -384,29 +393,38 @@ class SlotGroup:
                                                        self.a_bt, self.a_kc[l], self.a_vc[l], self.a_sl, cfg.hq,
                                                        cfg.hkv, D, cfg.page, self.cos_sin.data_ptr(),
                                                        self.q_rot.data_ptr(), st))
+                mark("round")
             else:
                 self._round(agg.OP_QKV_FUSED, l, st, tx)
+                mark("round")
                 check(L.swl_fused_qkv_rope(n, rows, self.a_out, cfg.qkv_n, self.B_qkv[l], r,
                                            self.ws_qkv.data_ptr(), self.norm_splits, self.a_bt, self.a_kc[l],
                                            self.a_vc[l], self.a_sl, cfg.hq, cfg.hkv, D, cfg.page,
                                            self.cos_sin.data_ptr(), self.q_rot.data_ptr(),
                                            *pf.get((l, agg.OP_O_PROJ), none), st))
+                mark("epilogue")
             check(L.swl_paged_attention_shrink(n, rows, self.a_bt, self.a_kc[l], self.a_vc[l], self.a_sl,
                                                self.a_in, cfg.hq * D, cfg.hq, cfg.hkv, D, cfg.page,
                                                1.0 / math.sqrt(D), self.max_len, self.q_rot.data_ptr(),
                                                self.part.data_ptr(), self.A_o[l], r, self.ws_o.data_ptr(),
                                                None, 0, st))
+            mark("attention")
             self._round(agg.OP_O_PROJ, l, st, tx)
+            mark("round")
             check(L.swl_fused_resid_norm_shrink(n, rows, self.a_out, H, self.B_o[l], r, s, self.ws_o.data_ptr(),
                                                 cfg.hq, 1, self.a_h, H, self.base.post_norm[l].data_ptr(), H,
                                                 cfg.eps, self.a_in, H, self.A_gu[l], 2 * r,
                                                 self.ws_gu.data_ptr(), *pf.get((l, agg.OP_GATE_UP_FUSED), none),
                                                 st))
+            mark("epilogue")
             self._round(agg.OP_GATE_UP_FUSED, l, st, tx)
+            mark("round")
             check(L.swl_fused_gu_silu_shrink(n, rows, self.a_out, 2 * I, self.B_gu[l], r, self.ws_gu.data_ptr(),
                                              self.norm_splits, I, self.a_in, I, self.A_dn[l], r,
                                              self.ws_dn.data_ptr(), *pf.get((l, agg.OP_DOWN_PROJ), none), st))
+            mark("epilogue")
             self._round(agg.OP_DOWN_PROJ, l, st, tx)
+            mark("round")
             last = l == nl - 1
             w_next = self.base.final_norm if last else self.base.in_norm[l + 1]
             check(L.swl_fused_resid_norm_shrink(n, rows, self.a_out, H, self.B_dn[l], r, s, self.ws_dn.data_ptr(),
@@ -415,7 +433,9 @@ class SlotGroup:
                                                 self.ws_qkv.data_ptr(),
                                                 *pf.get("lm_head" if last else (l + 1, agg.OP_QKV_FUSED), none),
                                                 st))
+            mark("epilogue")
         self._round(agg.OP_LM_HEAD, 0, st, tx)  # the greedy pick reads each slot's last row
+        mark("lm_head")
         check(L.swl_copy_rows(n, self.a_out, self.a_tok, self.a_b8, st))
         if self._subset is None and (row_counts is None or len(set(row_counts)) == 1):
             check(L.swl_advance_i32(self.seqlens.data_ptr(), n, 1 if row_counts is None else row_counts[0], st))
@@ -489,6 +509,58 @@ class SlotGroup:
         self._round(agg.OP_LM_HEAD, 0, st)
         check(L.swl_copy_rows(n, self.a_out, self.a_tok, self.a_b8, st))
         check(L.swl_advance_i32(self.seqlens.data_ptr(), n, 1, st))
+
+    def profile_step(self, stream: torch.cuda.Stream | None = None, rows=None, tokens=None,
+                     print_line: bool | None = None) -> dict:
+        """Runs one step eagerly with a CUDA event after every launch and
+        returns the device time per launch kind in microseconds (embed,
+        round, attention, epilogue, lm_head) and the step's wall time, as the
+        reference worker's profiled token does (worker_sync.py:1427-1782,
+        PROFILE_LAYERS=1). Prints the reference's `[LAYER_PROFILE]` line
+        (gather_us / scatter_us are 0: rounds read and write the slot buffers
+        in place) when print_line is True, or None and PROFILE_LAYERS=1. The
+        events end programmatic overlap between launches, so the sum is an
+        upper bound of a replayed step."""
+        import os
+        import time
+        if not self.fused:
+            raise ValueError("profile_step runs the fused sequence")
+        s = stream or torch.cuda.current_stream(self.dev)
+        events = []
+
+        def mark(kind):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(s)
+            events.append((kind, e))
+        torch.cuda.synchronize(self.dev)
+        t0 = time.perf_counter()
+        start = torch.cuda.Event(enable_timing=True)
+        start.record(s)
+        if rows is None:
+            self._enqueue_fused(s, mark=mark)
+        else:
+            self._enqueue_fused(s, self._stage_tokens(s, rows, tokens), mark=mark)
+        end = torch.cuda.Event(enable_timing=True)
+        end.record(s)
+        end.synchronize()
+        wall_us = (time.perf_counter() - t0) * 1e6
+        out = {k: 0.0 for k in ("embed", "round", "attention", "epilogue", "lm_head")}
+        prev = start
+        for kind, e in events:
+            out[kind] += prev.elapsed_time(e) * 1e3
+            prev = e
+        out["device_us"] = start.elapsed_time(end) * 1e3
+        out["wall_us"] = wall_us
+        self._profile_token = getattr(self, "_profile_token", 0) + 1
+        if print_line or (print_line is None and os.environ.get("PROFILE_LAYERS") == "1"):
+            wid = self.worker_ids[self._slot_index[0]]
+            compute = wall_us  # no gather / scatter copies
+            print(f"[LAYER_PROFILE] worker={wid} token={self._profile_token} gather_us=0 scatter_us=0 "
+                  f"compute_us={compute:.0f} wall_us={wall_us:.0f} ipc_pct=0.0 slots={self.n} "
+                  f"round_us={out['round']:.0f} attn_us={out['attention']:.0f} epi_us={out['epilogue']:.0f} "
+                  f"embed_us={out['embed']:.0f} lm_head_us={out['lm_head']:.0f} device_us={out['device_us']:.0f}",
+                  flush=True)
+        return out
 
     def launches_per_step(self) -> int:
         """Kernel launches of one step of this library's kernels."""

@@ -370,3 +370,33 @@ def test_subset_view_steps_only_its_slots(native, cuda):
         view.close()
     finally:
         grp.close()
+
+
+def test_profile_step_reports_the_reference_line(native, cuda, capsys):
+    """SlotGroup.profile_step: one real step with per-launch device times,
+    and the `[LAYER_PROFILE]` line in the reference's key=value format
+    (worker_sync.py:1774-1777), parsed the way benchmarks/ipc_overhead.py
+    parses it."""
+    from swarmlora_b200.engine import ModelConfig, SlotGroup, random_adapter, random_base
+    cfg = ModelConfig(layers=2, vocab=4096)
+    ctx = [5, 17, 40]
+    base = random_base(cfg, seed=5, device=cuda)
+    grp = SlotGroup(cfg, base, [random_adapter(cfg, seed=90 + i, device=cuda) for i in range(3)], ctx,
+                    max_new=8, seed=2)
+    try:
+        grp.tokens.copy_(torch.tensor([1, 2, 3]))
+        prof = grp.profile_step(print_line=True)
+        assert grp.seqlens.cpu().tolist() == [6, 18, 41]
+        kinds = ("embed", "round", "attention", "epilogue", "lm_head")
+        assert all(prof[k] > 0 for k in kinds)
+        assert sum(prof[k] for k in kinds) <= prof["device_us"] + 1.0 <= prof["wall_us"] + 2.0
+        line = [ln for ln in capsys.readouterr().out.splitlines() if "[LAYER_PROFILE]" in ln][-1]
+        parts = {}
+        for tok in line.split():
+            if "=" in tok:
+                k, v = tok.split("=", 1)
+                parts[k] = float(v)
+        assert {"gather_us", "scatter_us", "compute_us", "wall_us", "ipc_pct"} <= set(parts)
+        assert parts["gather_us"] == parts["scatter_us"] == 0 and parts["slots"] == 3
+    finally:
+        grp.close()
