@@ -115,13 +115,21 @@ __device__ __forceinline__ bool wait_epoch_sys(const unsigned int* addr, unsigne
                                                unsigned int* err_word, unsigned int code,
                                                uint64_t timeout_ns) {
   if (static_cast<int>(ld_acquire_sys(addr) - v) >= 0) return true;
+  // The error word stays set until the host reads it: once one wait has
+  // given up (this launch or an earlier one), the others give up at once
+  // instead of each spending its own time limit.
+  auto failed = [&] { return err_word && *reinterpret_cast<volatile unsigned int*>(err_word) != 0u; };
+  if (failed()) return false;
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     __nanosleep(64);
     if (static_cast<int>(ld_acquire_sys(addr) - v) >= 0) return true;
-    if ((it & 63u) == 0 && globaltimer() - t0 > timeout_ns) {
-      if (err_word) atomicCAS(err_word, 0u, code);
-      return false;
+    if ((it & 63u) == 0) {
+      if (failed()) return false;
+      if (globaltimer() - t0 > timeout_ns) {
+        if (err_word) atomicCAS(err_word, 0u, code);
+        return false;
+      }
     }
   }
 }

@@ -8,8 +8,10 @@ Checks, on the engine test's model (Llama-3.1-8B layer shapes, 2 layers,
 4096-entry vocabulary, ragged contexts, one slot without adapter): both GPUs
 end every step with bit-identical tokens and hidden states, these match the
 CPU oracle like the one-GPU engine, a replayed CUDA graph reproduces the
-eager tokens, and no bounded wait of the exchange ran out. Needs two GPUs;
-host-side failures surface as exceptions in the child processes.
+eager tokens, and no bounded wait of the exchange ran out; and, with a peer
+that never runs the round, that the round gives up after the 2 s limit,
+reports it through swl_round_device_error and leaves the context usable.
+Needs two GPUs; host-side failures surface as exceptions in the children.
 """
 import copy
 import io
@@ -80,6 +82,46 @@ def _child(rank, port, q):
         q.put((rank, None, buf.getvalue(), (err_eager, err_replay)))
     except Exception as e:  # reported by the parent
         q.put((rank, f"{type(e).__name__}: {e}", None, None))
+
+
+def _child_missing_peer(rank, port, q):
+    """Rank 1 connects but never runs the round: rank 0's round gives up its
+    wait for the peer's start flag after the time limit, records the error
+    and returns (no peer stores), and the context stays usable."""
+    try:
+        import time
+        import torch.distributed as dist
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                                timeout=timedelta(seconds=120))
+        from swarmlora_b200 import ext_aggregator as agg
+        from swarmlora_b200 import rounds
+        from swarmlora_b200.engine import ModelConfig, SlotGroup, random_adapter, random_base
+        cfg = ModelConfig(layers=1, vocab=4096)
+        base = random_base(cfg, seed=1, device=dev)
+        grp = SlotGroup(cfg, base, [random_adapter(cfg, seed=10 + i, device=dev) for i in range(2)], [4, 9],
+                        max_new=4, device=rank, seed=3)
+        result = None
+        try:
+            rounds.device_error()  # start clean
+            grp.shard(rank)
+            if rank == 0:
+                s = torch.cuda.current_stream(dev)
+                t0 = time.perf_counter()
+                grp._round(agg.OP_QKV_FUSED, 0, s.cuda_stream)
+                torch.cuda.synchronize(dev)
+                elapsed = time.perf_counter() - t0
+                code = rounds.device_error()
+                ok = bool(torch.ones(4, device=dev).sum().item() == 4.0)  # the context still works
+                result = (code, elapsed, ok)
+            dist.barrier()  # rank 1 waits here, on the host, with nothing in flight
+        finally:
+            grp.close()
+            dist.destroy_process_group()
+        q.put((rank, None, result))
+    except Exception as e:  # reported by the parent
+        q.put((rank, f"{type(e).__name__}: {e}", None))
 
 
 def _cpu(x):
@@ -154,3 +196,31 @@ def test_column_sharded_rounds_on_two_gpus(native, cuda):
                 assert lg[g] >= lg.max() - BF_ULP * lg.max().abs(), f"step {step}: slot {i} token {g} != {w}"
         tokens = got_tok.tolist()
         seq = [s + 1 for s in seq]
+
+
+def test_missing_peer_round_gives_up_and_reports(native, cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_child_missing_peer, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            rank, err, result = q.get(timeout=600)
+            res[rank] = (err, result)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    for r in (0, 1):
+        assert res[r][0] is None, f"rank {r}: {res[r][0]}"
+    code, elapsed, ok = res[0][1]
+    assert code == 5, f"expected the peer-start wait to give up (5), got {code}"
+    # one 2 s limit for the whole round: the other CTAs give up at once
+    assert 1.5 < elapsed < 15.0, elapsed
+    assert ok
