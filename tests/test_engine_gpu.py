@@ -357,7 +357,7 @@ def test_subset_view_steps_only_its_slots(native, cuda):
         view.enqueue_step(stream)
         torch.cuda.synchronize()
         eager = (grp.tokens.clone(), [k.clone() for k in grp.k_cache], grp.seqlens.clone())
-        view.capture(stream)
+        view.capture()  # on a side stream (not the default one)
         for l in range(cfg.layers):
             grp.k_cache[l].copy_(state[0][l])
             grp.v_cache[l].copy_(state[1][l])
