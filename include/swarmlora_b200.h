@@ -145,6 +145,14 @@ int swl_agg_init_queue(const char* shm_name, int capacity);
 /* Round kernel: 0 auto (= 1), 1 tcgen05 cluster split-K, 2 CUDA cores,
  * 3 tcgen05 stream-K (<= 64 rows); splits <= 0 = automatic K split. */
 int swl_agg_set_round_algo(int algo, int splits);
+/* Sampling state of a worker for in-process drivers (the protocol sets it
+ * with OP_SET_SAMPLING / slot_set_pending_sampling, ext_aggregator.cpp:991-1020).
+ * The LM-head round samples each row with its own worker's state (the
+ * reference applies the first command's worker's state to the batch). */
+int swl_agg_set_worker_sampling(int worker_id, int do_sample, float temperature, int top_k, float top_p);
+/* Seed of the LM-head sampling; each sampling round draws with the next
+ * offset (restarted at 0 here). */
+int swl_agg_set_sampling_seed(uint64_t seed);
 /* Fused weight of (layer, op) and its [N, K] shape; OP_EMBED / OP_LM_HEAD
  * give the [vocab, hidden] tables (layer ignored). */
 int swl_agg_weight(int layer, int op, const void** W, int64_t* N, int64_t* K);
@@ -268,6 +276,23 @@ int swl_slot_gemm(const void* W, int64_t N, int64_t K, const void* bias, int nsl
  * row): out[r] (int64, device) = lowest index of the largest bf16 logit of
  * row r (row stride ld elements); NaN never wins, no finite maximum gives 0. */
 int swl_argmax_rows(const void* logits, int rows, int64_t vocab, int64_t ld, int64_t* out, void* stream);
+/* Sampling parameters of one row (OP_SET_SAMPLING state). */
+typedef struct swl_sampling {
+  int do_sample;
+  float temperature;
+  int top_k;
+  float top_p;
+} swl_sampling;
+/* Next token of each row (ext_aggregator.cpp:757-787, :821-874): rows with
+ * do_sample draw from softmax(bf16(logit / max(temperature, 0.01))) limited
+ * to the top_k largest (ties kept, 0 = no limit) and then to the top_p
+ * nucleus (kept while the running probability in descending order stays
+ * <= top_p; the first always), by the inverse CDF in index order at u[r]
+ * (device floats in [0, 1); NULL: derived from seed, offset and r); other
+ * rows take the argmax as swl_argmax_rows. params is a host array of rows
+ * entries; out is int64 device memory. */
+int swl_sample_rows(const void* logits, int rows, int64_t vocab, int64_t ld, const swl_sampling* params,
+                    const float* u, uint64_t seed, uint64_t offset, int64_t* out, void* stream);
 /* Bounded-wait status of the round kernels (0 = none ran out); synchronous. */
 int swl_round_device_error(unsigned int* code);
 /* Tuning of the stream-K round (algo 3). */

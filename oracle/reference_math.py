@@ -74,6 +74,71 @@ def greedy(logits: torch.Tensor) -> torch.Tensor:
     return logits.float().argmax(-1)
 
 
+def sample_distribution(logits: torch.Tensor, temperature: float, top_k: int,
+                        top_p: float) -> tuple[torch.Tensor, float]:
+    """The distribution the LM head samples one row of bf16 logits from
+    (ext_aggregator.cpp:757-787, :821-861): logits * (1 / max(T, 0.01))
+    rounded to bf16 (torch's bf16 division by a scalar multiplies by the
+    reciprocal), the top_k largest kept (ties at the k-th value kept:
+    `logits < threshold -> -inf`), then in descending order (ties in index
+    order) the tokens whose running probability is <= top_p, the first
+    always, then the softmax. The running sums are exact (float64) where the
+    reference rounds them to bf16. Returns (probabilities [V] float64, margin):
+    margin is the distance of top_p from the nearest running sum (inf without
+    top-p), i.e. how far the cut is from flipping."""
+    x = logits.reshape(-1)
+    V = x.numel()
+    inv = torch.tensor(1.0, dtype=torch.float32) / torch.tensor(max(float(temperature), 0.01), dtype=torch.float32)
+    xf = bf(x.float() * inv).double()
+    neg = torch.tensor(-math.inf, dtype=torch.float64)
+    keep = ~torch.isnan(xf)
+    if 0 < top_k < V:
+        thr = torch.topk(torch.where(keep, xf, neg), top_k).values[-1]
+        keep &= xf >= thr
+    xm = xf[keep].max()
+    w = torch.where(keep, torch.exp(xf - xm), torch.zeros((), dtype=torch.float64))
+    margin = math.inf
+    if top_p < 1.0:
+        order = torch.sort(torch.where(keep, xf, neg), descending=True, stable=True).indices
+        order = order[keep[order]]
+        cum = torch.cumsum(w[order], 0) / w.sum()
+        stay = cum <= top_p
+        stay[0] = True
+        margin = float((cum - top_p).abs().min())
+        cut = torch.zeros(V, dtype=torch.bool)
+        cut[order[stay]] = True
+        w = torch.where(cut, w, torch.zeros((), dtype=torch.float64))
+    return w / w.sum(), margin
+
+
+def sample_allowed(logits: torch.Tensor, temperature: float, top_k: int, top_p: float,
+                   slack: float) -> torch.Tensor:
+    """Tokens a correct sampler may draw from for one row when its running
+    sums carry rounding: the kept set of sample_distribution plus the tokens
+    whose exact running probability lies within `slack` above top_p."""
+    probs, _ = sample_distribution(logits, temperature, top_k, top_p + slack if top_p < 1.0 else top_p)
+    return probs > 0
+
+
+def sample_token(logits: torch.Tensor, do_sample: bool, temperature: float, top_k: int, top_p: float,
+                 u: float) -> tuple[int, float]:
+    """The LM head's next token for one row: the argmax (greedy), or the
+    draw from sample_distribution restated as the inverse CDF in index order
+    at the uniform u (the reference's torch.multinomial stream is not
+    reproducible; its distribution is). Returns (token, margin): the
+    distance of u and of top_p from the nearest decision boundary."""
+    x = logits.reshape(-1)
+    if not do_sample:
+        return int(x.float().argmax()), math.inf
+    probs, margin = sample_distribution(x, temperature, top_k, top_p)
+    cdf = torch.cumsum(probs, 0)
+    kept_idx = (probs > 0).nonzero().flatten()
+    token = int(torch.searchsorted(cdf, torch.tensor([float(u)], dtype=torch.float64), right=True)[0])
+    token = min(token, int(kept_idx[-1]))
+    margin = min(margin, float((cdf[kept_idx] - float(u)).abs().min()))
+    return token, margin
+
+
 # ---------------------------------------------------------------------------
 # Worker LoRA: model_builder.py:217-262, worker_sync.py:305/:375
 # ---------------------------------------------------------------------------

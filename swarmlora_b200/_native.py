@@ -30,6 +30,11 @@ class WeightIpc(C.Structure):
 
 _pwipc = C.POINTER(WeightIpc)
 
+
+class Sampling(C.Structure):
+    """swl_sampling: one row's sampling parameters."""
+    _fields_ = [("do_sample", C.c_int), ("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float)]
+
 # name -> (restype, argtypes). Kept in the same order as include/swarmlora_b200.h.
 SIGNATURES: dict[str, tuple] = {
     "swl_last_error": (_cp, []),
@@ -71,6 +76,8 @@ SIGNATURES: dict[str, tuple] = {
     "swl_agg_init_embed_lm_head": (_i32, [_p, _p, _i64, _i64]),
     "swl_agg_init_queue": (_i32, [_cp, _i32]),
     "swl_agg_set_round_algo": (_i32, [_i32, _i32]),
+    "swl_agg_set_worker_sampling": (_i32, [_i32, _i32, _f32, _i32, _f32]),
+    "swl_agg_set_sampling_seed": (_i32, [_u64]),
     "swl_agg_weight": (_i32, [_i32, _i32, _pp, _pi64, _pi64]),
     "swl_agg_execute_round": (_i32, [_i32, _i32, _i32, _pi32, _pi32, _pi64, _pi64, _p]),
     "swl_agg_execute_qkv_rope_round": (_i32, [_i32, _i32, _pi32, _pi32, _pi64, _pi64, _pp, _i32, _p, _i32, _pp, _pp, _pp,
@@ -99,6 +106,7 @@ SIGNATURES: dict[str, tuple] = {
     # ---- kernels callable directly
     "swl_slot_gemm": (_i32, [_p, _i64, _i64, _p, _i32, _pp, _pp, _pi32, _i64, _i64, _i32, _i32, _p]),
     "swl_argmax_rows": (_i32, [_p, _i32, _i64, _i64, _p, _p]),
+    "swl_sample_rows": (_i32, [_p, _i32, _i64, _i64, C.POINTER(Sampling), _p, _u64, _u64, _p, _p]),
     "swl_round_device_error": (_i32, [_pu32]),
     "swl_round_set_streamk_ctas_per_sm": (_i32, [_i32]),
     "swl_round_set_streamk_ctas": (_i32, [_i32]),

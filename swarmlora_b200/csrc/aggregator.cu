@@ -103,6 +103,8 @@ cudaStream_t g_stream = nullptr;
 int g_round_algo = kAlgoAuto;
 int g_round_splits = 0;
 std::map<int, SamplingState> g_sampling;  // worker_id -> params (main-loop thread only)
+uint64_t g_sample_seed = 0;                // LM-head sampling: uniforms from (seed, offset, row)
+uint64_t g_sample_offset = 0;              // advanced by every sampling LM-head round
 
 // Column-sharded base weights over two GPUs (one process per GPU; the
 // variant of the multi-GPU configuration with an NVLink all-gather of the
@@ -262,7 +264,22 @@ int run_round(int op, int layer, const std::vector<RoundCmd>& cmds, cudaStream_t
     } else {
       SWL_TRY(launch_slot_round(tab, shape, g_lm_head, &g_tm_lm, g_round_algo, g_round_splits, stream));
     }
-    return launch_argmax_rows(g_logits, n, g_vocab, g_vocab, outs, stream);
+    // each row with its own worker's sampling state (the reference applies
+    // the first command's worker's state to the whole batch,
+    // ext_aggregator.cpp:717-734); greedy when no row samples
+    SampleTable params;
+    bool any = false;
+    for (int i = 0; i < n; ++i) {
+      SampleParams q{0, 1.0f, 0, 1.0f};
+      auto it = g_sampling.find(cmds[i].worker_id);
+      if (it != g_sampling.end())
+        q = {it->second.do_sample ? 1 : 0, it->second.temperature, it->second.top_k, it->second.top_p};
+      params.p[i] = q;
+      any = any || q.do_sample != 0;
+    }
+    if (!any) return launch_argmax_rows(g_logits, n, g_vocab, g_vocab, outs, stream);
+    return launch_sample_rows(g_logits, n, g_vocab, g_vocab, params, nullptr, g_sample_seed, g_sample_offset++,
+                              outs, stream);
   }
   if (layer < 0 || layer >= g_num_layers)
     return set_error(SWL_ERR_ARG, "round: layer_idx %d out of range [0, %d)", layer, g_num_layers);
@@ -831,6 +848,22 @@ SWL_EXPORT int swl_agg_init_queue(const char* shm_name, int capacity) {
   g_ring = reinterpret_cast<Command*>(static_cast<char*>(p) + sizeof(ControlBlock));
   g_capacity = capacity;
   g_map_bytes = bytes;
+  return SWL_OK;
+}
+
+// Sampling state of a worker for in-process drivers (the protocol sets it
+// with OP_SET_SAMPLING or slot_set_pending_sampling).
+SWL_EXPORT int swl_agg_set_worker_sampling(int worker_id, int do_sample, float temperature, int top_k,
+                                           float top_p) {
+  if (worker_id < 0 || worker_id > 100000) return set_error(SWL_ERR_ARG, "set_worker_sampling: invalid worker_id");
+  g_sampling[worker_id] = {do_sample != 0, temperature, top_k, top_p};
+  return SWL_OK;
+}
+
+// Seed of the LM-head sampling; the draw offset restarts at 0.
+SWL_EXPORT int swl_agg_set_sampling_seed(uint64_t seed) {
+  g_sample_seed = seed;
+  g_sample_offset = 0;
   return SWL_OK;
 }
 

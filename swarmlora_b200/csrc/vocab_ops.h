@@ -31,4 +31,24 @@ struct TokenOuts {
 int launch_argmax_rows(const void* logits, int rows, int64_t vocab, int64_t ld,
                        const TokenOuts& outs, cudaStream_t stream);
 
+// Sampling parameters of one row (its worker's OP_SET_SAMPLING state);
+// the layout of the public swl_sampling.
+struct SampleParams {
+  int do_sample;
+  float temperature;
+  int top_k;
+  float top_p;
+};
+struct SampleTable {
+  SampleParams p[kMaxSlots];
+};
+
+// Row r's next token (int64) goes to *outs.p[r]: greedy rows take the
+// argmax, sampling rows draw from the temperature / top-k / top-p filtered
+// softmax with uniform u[r] (device floats in [0, 1)) or, when u is null,
+// one derived from (seed, offset, r).
+int launch_sample_rows(const void* logits, int rows, int64_t vocab, int64_t ld, const SampleTable& params,
+                       const float* u, uint64_t seed, uint64_t offset, const TokenOuts& outs,
+                       cudaStream_t stream);
+
 }  // namespace swl

@@ -277,6 +277,20 @@ def slot_buffers(slot_id: int) -> tuple[int, int]:
     return int(a.value), int(b.value)
 
 
+def set_worker_sampling(worker_id: int, do_sample: bool, temperature: float = 1.0, top_k: int = 0,
+                        top_p: float = 1.0) -> None:
+    """Sampling state of a worker for in-process drivers (the protocol sets it
+    through OP_SET_SAMPLING or slot_set_pending_sampling): the LM-head round
+    samples that worker's slot with it."""
+    check(lib().swl_agg_set_worker_sampling(int(worker_id), int(bool(do_sample)), float(temperature),
+                                            int(top_k), float(top_p)))
+
+
+def set_sampling_seed(seed: int) -> None:
+    """Seed of the LM-head sampling draws (their offset restarts at 0)."""
+    check(lib().swl_agg_set_sampling_seed(int(seed)))
+
+
 def set_round_algo(algo: int, splits: int = 0) -> None:
     """0/1: tensor-core round kernel (default); 2: CUDA-core cross-check kernel."""
     check(lib().swl_agg_set_round_algo(int(algo), int(splits)))

@@ -54,3 +54,30 @@ def device_error() -> int:
     code = ctypes.c_uint(0)
     check(lib().swl_round_device_error(ctypes.byref(code)))
     return int(code.value)
+
+
+def next_tokens(logits: torch.Tensor, params, u: torch.Tensor | None = None, seed: int = 0, offset: int = 0,
+                out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """The LM head's next token per row of bf16 logits [rows, >= vocab]
+    (vocab = logits.shape[1] unless the rows are padded: pass a view).
+    params: one (do_sample, temperature, top_k, top_p) per row; greedy rows
+    take the argmax, sampling rows draw with the reference's temperature /
+    top-k / top-p rule at u[row] (a float32 CUDA tensor) or at uniforms
+    derived from (seed, offset, row). Returns int64 tokens on the device."""
+    from ._native import Sampling
+    if logits.dtype != torch.bfloat16 or not logits.is_cuda or logits.stride(-1) != 1:
+        raise RuntimeError("next_tokens: logits must be bf16 CUDA with unit stride in the vocabulary")
+    rows, vocab = int(logits.shape[0]), int(logits.shape[1])
+    if len(params) != rows:
+        raise RuntimeError("next_tokens: one parameter set per row")
+    arr = (Sampling * max(1, rows))()
+    for i, (d, t, k, p) in enumerate(params):
+        arr[i].do_sample, arr[i].temperature, arr[i].top_k, arr[i].top_p = int(bool(d)), float(t), int(k), float(p)
+    if u is not None and (u.dtype != torch.float32 or not u.is_cuda or u.numel() < rows):
+        raise RuntimeError("next_tokens: u must be a float32 CUDA tensor with one value per row")
+    out = out if out is not None else torch.empty(rows, dtype=torch.int64, device=logits.device)
+    st = stream if stream is not None else torch.cuda.current_stream(logits.device)
+    check(lib().swl_sample_rows(logits.data_ptr(), rows, vocab, int(logits.stride(0)), arr,
+                                u.data_ptr() if u is not None else None, int(seed), int(offset), out.data_ptr(),
+                                st.cuda_stream))
+    return out
