@@ -103,6 +103,20 @@ inline void evict_slots(ControlBlock* ctrl, const std::vector<int>& slots, Mask1
   ctrl->active_slot_count.store(active.count());
 }
 
+// apply_pending_sampling_states (ext_aggregator.cpp:991-1020): hands the
+// sampling parameters that joining slots posted (slot_set_pending_sampling)
+// to fn(slot, params) and clears their pending bits.
+template <class Fn>
+inline void take_pending_sampling(ControlBlock* ctrl, const Mask128& joins, Fn&& fn) {
+  Mask128 todo = ctrl->pending_sampling_mask.load() & joins;
+  for (Mask128 r = todo; !r.empty();) {
+    int sid = r.lowest();
+    r.clear(sid);
+    fn(sid, ctrl->pending_sampling[sid]);
+  }
+  ctrl->pending_sampling_mask.and_with(~todo);
+}
+
 // Takes ring entries until n commands of active slots are collected,
 // discarding entries of slots evicted or gone meanwhile. Returns false when
 // the quit flag is raised (or raised here after an entry stayed unwritten

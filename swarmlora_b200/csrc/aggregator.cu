@@ -1132,17 +1132,10 @@ namespace {
 
 // ext_aggregator.cpp:991-1020 apply_pending_sampling_states.
 void apply_pending_sampling(const Mask128& joins) {
-  Mask128 todo = g_ctrl->pending_sampling_mask.load() & joins;
-  for (Mask128 r = todo; !r.empty();) {
-    int sid = r.lowest();
-    r.clear(sid);
+  take_pending_sampling(g_ctrl, joins, [](int sid, const PendingSampling& p) {
     int wid = g_pool.slots[sid].owner.load(std::memory_order_acquire);
-    if (wid >= 0) {
-      const PendingSampling& p = g_ctrl->pending_sampling[sid];
-      g_sampling[wid] = {p.do_sample, p.temperature, p.top_k, p.top_p};
-    }
-  }
-  g_ctrl->pending_sampling_mask.and_with(~todo);
+    if (wid >= 0) g_sampling[wid] = {p.do_sample, p.temperature, p.top_k, p.top_p};
+  });
 }
 
 // The aggregator's side of run_main_loop: GPU rounds over validated

@@ -6,8 +6,8 @@
 // GPU round. Per-slot inputs and outputs are plain (non-atomic) arrays, so
 // the sanitizer sees whether the ring and the epoch publish them.
 //
-// Scenarios: workers joining at different times and leaving after different
-// token counts, one worker that stops mid-token (evicted by the barrier
+// Scenarios: workers joining at different times (half of them posting
+// sampling parameters first) and leaving after different token counts, one worker that stops mid-token (evicted by the barrier
 // timeout), one that submits a command under another worker's id (evicted
 // by validation). Exit status 0 and "protocol stress ok" on success.
 #include <atomic>
@@ -77,9 +77,19 @@ bool is_active(int s) { return swl_q_slot_is_active(s) == 1; }
 bool is_inactive(int s) { return swl_q_slot_is_active(s) == 0; }
 bool is_evicted(int s) { return swl_q_is_slot_evicted(s) == 1; }
 
+std::atomic<int> g_sampling_taken{0};
+
 struct HostHooks {
   std::vector<int> owner;  // slot -> worker id
-  void on_membership(const Mask128&, const Mask128&) {}
+  ControlBlock* ctrl = nullptr;
+  void on_membership(const Mask128&, const Mask128& joins) {
+    take_pending_sampling(ctrl, joins, [](int sid, const PendingSampling& p) {
+      // the joining worker posted temperature 0.5 + slot and top_k = slot
+      if (!p.do_sample || p.top_k != sid || p.temperature != 0.5f + static_cast<float>(sid) || p.top_p != 0.9f)
+        fail("pending sampling parameters not visible at the join", sid);
+      g_sampling_taken.fetch_add(1);
+    });
+  }
   void on_sampling(const DrainedCmd&) {}
   void validate(int, int, const std::vector<DrainedCmd>& cmds, std::vector<int>* bad) {
     for (const DrainedCmd& c : cmds)
@@ -102,6 +112,8 @@ struct HostHooks {
 void worker(int slot, int tokens, int join_delay_ms) {
   const int wid = 1000 + slot;
   std::this_thread::sleep_for(std::chrono::milliseconds(join_delay_ms));
+  if (slot % 2 == 0)  // posted before the join, applied at the token boundary that admits the slot
+    swl_q_slot_set_pending_sampling(slot, 1, 0.5f + static_cast<float>(slot), slot, 0.9f);
   swl_q_slot_signal_join(slot);
   if (!wait_until(is_active, slot, 5000)) return fail("never activated", slot);
   uint64_t counter = 0;
@@ -149,6 +161,7 @@ int main() {
   auto* ctrl = static_cast<ControlBlock*>(swl_q_control_block());
   auto* ring = reinterpret_cast<Command*>(reinterpret_cast<char*>(ctrl) + sizeof(ControlBlock));
   HostHooks hooks;
+  hooks.ctrl = ctrl;
   hooks.owner.assign(kMaxSlots, -1);
   for (int s = 0; s < kWorkers; ++s) hooks.owner[s] = 1000 + s;
   ProtocolTimes times;
@@ -164,6 +177,7 @@ int main() {
   swl_q_close();
   if (loop_status != 0) fail("main loop returned an error", -1);
   if (g_evicted_seen.load() != 2) fail("expected exactly the stalled and the rogue slot evicted", -1);
+  if (g_sampling_taken.load() != (kWorkers + 1) / 2) fail("every posted sampling state taken once", -1);
   if (g_failures.load()) return 1;
   printf("protocol stress ok: %d rounds, %d workers, 2 evicted\n", g_rounds.load(), kWorkers);
   return 0;
