@@ -123,10 +123,11 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const __nv_
 constexpr int kSampleThreads = 1024;
 constexpr int kSampleWarps = kSampleThreads / 32;
 
-// Larger float -> larger key; NaN -> 0 (below -inf, never kept).
+// Larger float -> larger key; NaN -> 0 (below -inf, never kept); -0 and +0
+// share a key (they compare equal, so they tie as in torch's top-k / sort).
 __device__ __forceinline__ uint32_t order_key(float f) {
   if (f != f) return 0u;
-  const uint32_t b = __float_as_uint(f);
+  const uint32_t b = __float_as_uint(f == 0.0f ? 0.0f : f);
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 __device__ __forceinline__ float key_value(uint32_t k) {

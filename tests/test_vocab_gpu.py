@@ -74,7 +74,8 @@ def test_sampled_tokens_follow_the_reference_rule(native, cuda, vocab):
     argmax; a sampling row's token lies in the kept set (top-k with ties, the
     reference's top-p cut) and the uniform u lies in its interval of the
     kept softmax's CDF, up to the fp32 rounding of the kernel's sums. Rows
-    with planted ties at the top and a constant row are included."""
+    with planted ties at the top, a constant row and rows of coarse values
+    (ties everywhere, signed zeros) are included."""
     from oracle import reference_math as ref
     from swarmlora_b200.rounds import next_tokens
     rows = 2 * len(SAMPLE_CASES)
@@ -83,6 +84,9 @@ def test_sampled_tokens_follow_the_reference_rule(native, cuda, vocab):
     x[3, : min(4, vocab)] = 9.0          # four tied maxima
     x[7, :] = 0.5                        # all equal
     x[14, vocab // 2:] = -float("inf")   # half the vocabulary impossible
+    # coarse values: many ties, +0 and -0 among them (equal, as torch compares)
+    x[15:] = ((x[15:].float() * 4).round() / 4).to(BF)
+    x[16:, 1::2] = torch.where(x[16:, 1::2] == 0, torch.tensor(-0.0), x[16:, 1::2].float()).to(BF)
     params = [SAMPLE_CASES[r % len(SAMPLE_CASES)] for r in range(rows)]
     u = torch.rand(rows, generator=g)
     got = next_tokens(x.to(cuda), params, u=u.to(cuda)).cpu()
