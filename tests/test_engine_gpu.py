@@ -400,3 +400,54 @@ def test_profile_step_reports_the_reference_line(native, cuda, capsys):
         assert parts["gather_us"] == parts["scatter_us"] == 0 and parts["slots"] == 3
     finally:
         grp.close()
+
+
+def test_config2_full_size_step_properties(native, cuda):
+    """BASELINE config 2 at its full size (32 layers, vocabulary 128256, 28
+    slots with their own rank-16 adapters, contexts U[256, 1024]), checked
+    through properties that hold at any size: a step writes exactly one K
+    and one V row per slot and layer (at the slot's position; every other
+    byte of the page pools is unchanged) and advances every position by one;
+    the next tokens are valid ids; and a CUDA-graph replay from the same
+    state reproduces the eager step bit for bit (tokens, hidden rows, every
+    cache byte)."""
+    from swarmlora_b200.engine import LLAMA_3_1_8B, SlotGroup, random_adapter, random_base
+    cfg = LLAMA_3_1_8B
+    n = 28
+    g = torch.Generator().manual_seed(1234)
+    ctx = [int(c) for c in torch.randint(256, 1025, (n,), generator=g)]
+    base = random_base(cfg, seed=1, device=cuda)
+    adapters = [random_adapter(cfg, seed=100 + i, device=cuda) for i in range(n)]
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=4, seed=0)
+    try:
+        tokens0 = torch.randint(0, cfg.vocab, (n,), generator=g).to(cuda)
+        grp.tokens.copy_(tokens0)
+        k0 = [k.clone() for k in grp.k_cache]
+        v0 = [v.clone() for v in grp.v_cache]
+        stream = torch.cuda.current_stream()
+        grp.enqueue_step(stream)
+        torch.cuda.synchronize()
+        eager = (grp.tokens.clone(), grp.h.clone())
+        assert grp.seqlens.cpu().tolist() == [c + 1 for c in ctx]
+        assert int(eager[0].min()) >= 0 and int(eager[0].max()) < cfg.vocab
+        # exactly the (page, offset) rows at each slot's position changed
+        want = {(int(grp.block_tables[i][c // cfg.page]), c % cfg.page) for i, c in enumerate(ctx)}
+        for l in range(cfg.layers):
+            for now, before, what in ((grp.k_cache[l], k0[l], "K"), (grp.v_cache[l], v0[l], "V")):
+                rows = (now != before).flatten(2).any(-1).nonzero().tolist()
+                assert {tuple(r) for r in rows} == want, f"layer {l} {what}: rows written != the new rows"
+        kn = [k.clone() for k in grp.k_cache]
+        vn = [v.clone() for v in grp.v_cache]
+        # replay from the same starting state
+        for l in range(cfg.layers):
+            grp.k_cache[l].copy_(k0[l])
+            grp.v_cache[l].copy_(v0[l])
+        grp.reset_positions()
+        grp.tokens.copy_(tokens0)
+        grp.capture()
+        grp.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(grp.tokens, eager[0]) and torch.equal(grp.h, eager[1])
+        assert all(torch.equal(a, b) for a, b in zip(grp.k_cache + grp.v_cache, kn + vn))
+    finally:
+        grp.close()
