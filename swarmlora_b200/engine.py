@@ -75,7 +75,7 @@ def cos_sin_cache(cfg: ModelConfig, max_pos: int, device) -> torch.Tensor:
     from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
     hf = LlamaConfig(hidden_size=cfg.hidden, num_attention_heads=cfg.hq,
                      num_key_value_heads=cfg.hkv, head_dim=cfg.head_dim,
-                     rope_theta=cfg.rope_theta, rope_scaling=dict(cfg.rope_scaling),
+                     rope_theta=cfg.rope_theta, rope_scaling=dict(cfg.rope_scaling) if cfg.rope_scaling else None,
                      max_position_embeddings=max(max_pos, 131072))
     inv = LlamaRotaryEmbedding(config=hf).inv_freq.float().cpu()
     t = torch.arange(max_pos, dtype=torch.float32)
