@@ -57,6 +57,8 @@ def parse():
                     help="decoder layers (32 = the benchmarked model; fewer only for small profiling cases)")
     ap.add_argument("--vocab", type=int, default=128256,
                     help="vocabulary (128256 = the benchmarked model; smaller only for profiling cases)")
+    ap.add_argument("--checkpoint", default=None, metavar="DIR",
+                    help="decode with the base weights of an HF Llama checkpoint directory instead of random ones")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-step", action="store_true",
                     help="bracket the first timed step with cudaProfilerStart/Stop "
@@ -363,11 +365,15 @@ def our_arm(args):
     swarmlora_b200.set_pdl(not args.no_pdl)
     from swarmlora_b200 import worker_ops as _wo
     _wo.attention_tune(args.attn_chunk_pages, args.attn_stages)
-    cfg = dataclasses.replace(LLAMA_3_1_8B, layers=args.layers, vocab=args.vocab)
+    if args.checkpoint:
+        from swarmlora_b200.checkpoint import load_base
+        base, cfg = load_base(args.checkpoint, dev)
+    else:
+        cfg = dataclasses.replace(LLAMA_3_1_8B, layers=args.layers, vocab=args.vocab)
+        base = random_base(cfg, seed=1, device=dev)
     n = args.slots
     g = torch.Generator().manual_seed(1234 + rank)
     ctx = [int(c) for c in torch.randint(args.ctx_lo, args.ctx_hi + 1, (n,), generator=g)]
-    base = random_base(cfg, seed=1, device=dev)
     adapters = [random_adapter(cfg, seed=100 + rank * 1000 + i, device=dev) for i in range(n)]
     total_new = args.warmup + args.steps + args.warmup + args.steps + 4
     grp = SlotGroup(cfg, base, adapters, ctx, max_new=max(MAX_NEW, total_new), device=local, seed=rank)
@@ -462,7 +468,9 @@ def our_arm(args):
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded random-init weights, adapters, KV contexts)",
+            "data": ("base weights from " + os.path.basename(os.path.normpath(args.checkpoint))
+                     + "; synthetic adapters and KV contexts") if args.checkpoint
+                    else "synthetic (seeded random-init weights, adapters, KV contexts)",
             "config": {"workload": f"BASELINE config {5 if (n, args.ctx_lo, args.ctx_hi) == (32, 1024, 4096) else 2}: "
                                    f"Llama-3.1-8B shape ({cfg.layers} layers, vocab {cfg.vocab}), "
                                    f"{n} decode slots/GPU, distinct r=16 adapters on 7 projections, "
