@@ -102,7 +102,8 @@ size_t g_map_bytes = 0;
 cudaStream_t g_stream = nullptr;
 int g_round_algo = kAlgoAuto;
 int g_round_splits = 0;
-std::map<int, SamplingState> g_sampling;  // worker_id -> params (main-loop thread only)
+std::map<int, SamplingState> g_sampling;  // worker_id -> params
+std::mutex g_sampling_mu;                 // the loop thread and in-process setters both touch it
 uint64_t g_sample_seed = 0;                // LM-head sampling: uniforms from (seed, offset, row)
 uint64_t g_sample_offset = 0;              // advanced by every sampling LM-head round
 
@@ -271,6 +272,7 @@ int run_round(int op, int layer, const std::vector<RoundCmd>& cmds, cudaStream_t
     bool any = false;
     for (int i = 0; i < n; ++i) {
       SampleParams q{0, 1.0f, 0, 1.0f};
+      std::lock_guard<std::mutex> lock(g_sampling_mu);
       auto it = g_sampling.find(cmds[i].worker_id);
       if (it != g_sampling.end())
         q = {it->second.do_sample ? 1 : 0, it->second.temperature, it->second.top_k, it->second.top_p};
@@ -856,6 +858,7 @@ SWL_EXPORT int swl_agg_init_queue(const char* shm_name, int capacity) {
 SWL_EXPORT int swl_agg_set_worker_sampling(int worker_id, int do_sample, float temperature, int top_k,
                                            float top_p) {
   if (worker_id < 0 || worker_id > 100000) return set_error(SWL_ERR_ARG, "set_worker_sampling: invalid worker_id");
+  std::lock_guard<std::mutex> lock(g_sampling_mu);
   g_sampling[worker_id] = {do_sample != 0, temperature, top_k, top_p};
   return SWL_OK;
 }
@@ -1134,7 +1137,10 @@ namespace {
 void apply_pending_sampling(const Mask128& joins) {
   take_pending_sampling(g_ctrl, joins, [](int sid, const PendingSampling& p) {
     int wid = g_pool.slots[sid].owner.load(std::memory_order_acquire);
-    if (wid >= 0) g_sampling[wid] = {p.do_sample, p.temperature, p.top_k, p.top_p};
+    if (wid >= 0) {
+      std::lock_guard<std::mutex> lock(g_sampling_mu);
+      g_sampling[wid] = {p.do_sample, p.temperature, p.top_k, p.top_p};
+    }
   });
 }
 
@@ -1153,6 +1159,7 @@ struct AggHooks {
     s.temperature = static_cast<float>(c.x_key >> 1) / 10000.0f;
     s.top_k = static_cast<int>(c.y0_key);
     s.top_p = static_cast<float>(c.y1_key) / 10000.0f;
+    std::lock_guard<std::mutex> lock(g_sampling_mu);
     g_sampling[c.worker_id] = s;
   }
   void validate(int op, int layer, const std::vector<DrainedCmd>& cmds, std::vector<int>* bad) {
