@@ -104,8 +104,8 @@ int g_round_algo = kAlgoAuto;
 int g_round_splits = 0;
 std::map<int, SamplingState> g_sampling;  // worker_id -> params
 std::mutex g_sampling_mu;                 // the loop thread and in-process setters both touch it
-uint64_t g_sample_seed = 0;                // LM-head sampling: uniforms from (seed, offset, row)
-uint64_t g_sample_offset = 0;              // advanced by every sampling LM-head round
+std::atomic<uint64_t> g_sample_seed{0};    // LM-head sampling: uniforms from (seed, offset, row)
+std::atomic<uint64_t> g_sample_offset{0};  // advanced by every sampling LM-head round
 
 // Column-sharded base weights over two GPUs (one process per GPU; the
 // variant of the multi-GPU configuration with an NVLink all-gather of the
@@ -280,8 +280,8 @@ int run_round(int op, int layer, const std::vector<RoundCmd>& cmds, cudaStream_t
       any = any || q.do_sample != 0;
     }
     if (!any) return launch_argmax_rows(g_logits, n, g_vocab, g_vocab, outs, stream);
-    return launch_sample_rows(g_logits, n, g_vocab, g_vocab, params, nullptr, g_sample_seed, g_sample_offset++,
-                              outs, stream);
+    return launch_sample_rows(g_logits, n, g_vocab, g_vocab, params, nullptr, g_sample_seed.load(),
+                              g_sample_offset.fetch_add(1), outs, stream);
   }
   if (layer < 0 || layer >= g_num_layers)
     return set_error(SWL_ERR_ARG, "round: layer_idx %d out of range [0, %d)", layer, g_num_layers);
@@ -865,8 +865,8 @@ SWL_EXPORT int swl_agg_set_worker_sampling(int worker_id, int do_sample, float t
 
 // Seed of the LM-head sampling; the draw offset restarts at 0.
 SWL_EXPORT int swl_agg_set_sampling_seed(uint64_t seed) {
-  g_sample_seed = seed;
-  g_sample_offset = 0;
+  g_sample_seed.store(seed);
+  g_sample_offset.store(0);
   return SWL_OK;
 }
 
