@@ -637,7 +637,8 @@ class SlotGroup:
         (`capture` / `replay`). Its `rows` / `tokens` arguments have one
         entry per active slot, in `active` order; `set_context` and
         `set_adapter` still take group indices. Closing the view only drops
-        its graph."""
+        its graph; a view (and its graph) is usable only while its group is
+        open, since it launches on the group's buffers."""
         if self._subset is not None:
             raise ValueError("a subset of a subset view")
         if not self.fused:
