@@ -82,6 +82,9 @@ def parse():
                     help="prefill rows per prefill slot per step (16 = the reference's max_seq_per_step)")
     ap.add_argument("--shard", action="store_true",
                     help="column-sharded base weights over 2 GPUs (one slot group; torchrun, --gpus 2)")
+    ap.add_argument("--profile-layers", type=int, default=0, metavar="N",
+                    help="print N per-step [LAYER_PROFILE] lines (the reference worker's PROFILE_LAYERS format) "
+                         "for the decode workload and exit")
     ap.add_argument("--profile-attention", action="store_true",
                     help="run only --steps paged-attention launches over one layer's KV (small ncu case)")
     return ap.parse_args()
@@ -770,6 +773,30 @@ def mixed_arm(args):
     return 0
 
 
+def profile_layers_arm(args):
+    """The decode workload (--slots, --ctx-lo/--ctx-hi, --layers, --vocab)
+    stepped eagerly with a CUDA event after every launch; prints one
+    [LAYER_PROFILE] line per step (SlotGroup.profile_step)."""
+    import dataclasses
+    import torch
+    from swarmlora_b200.engine import LLAMA_3_1_8B, SlotGroup, random_adapter, random_base
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = dataclasses.replace(LLAMA_3_1_8B, layers=args.layers, vocab=args.vocab)
+    n = args.slots
+    g = torch.Generator().manual_seed(1234)
+    ctx = [int(c) for c in torch.randint(args.ctx_lo, args.ctx_hi + 1, (n,), generator=g)]
+    base = random_base(cfg, seed=1, device=dev)
+    adapters = [random_adapter(cfg, seed=100 + i, device=dev) for i in range(n)]
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=args.profile_layers + 8, device=0, seed=0)
+    grp.tokens.copy_(torch.randint(0, cfg.vocab, (n,), generator=g))
+    grp.profile_step(print_line=False)  # kernel attributes, first-launch costs
+    for _ in range(args.profile_layers):
+        grp.profile_step(print_line=True)
+    grp.close()
+    return 0
+
+
 def churn_arm(args):
     """The churn configuration on one GPU: a seeded trace of Poisson arrivals
     (8/s), lognormal prompts and outputs, Zipf adapter ids over a pool of 500
@@ -847,6 +874,8 @@ def churn_arm(args):
 
 def main():
     args = parse()
+    if args.profile_layers:
+        return profile_layers_arm(args)
     if args.churn:
         return churn_arm(args)
     if args.mixed:
