@@ -10,6 +10,11 @@
 // sampling parameters first) and leaving after different token counts, one worker that stops mid-token (evicted by the barrier
 // timeout), one that submits a command under another worker's id (evicted
 // by validation). Exit status 0 and "protocol stress ok" on success.
+#include <signal.h>
+#include <sys/mman.h>
+#include <sys/wait.h>
+#include <unistd.h>
+
 #include <atomic>
 #include <chrono>
 #include <cstdio>
@@ -46,8 +51,13 @@ constexpr int kOpsPerToken = 1 + 4 * kLayers + 1;
 constexpr int kStall = 3;  // stops submitting mid-token
 constexpr int kRogue = 6;  // submits one command under another worker's id
 
-uint64_t g_in[kMaxSlots];   // a worker's input of the current op (plain data)
-uint64_t g_out[kMaxSlots];  // the round's output for the slot (plain data)
+// A worker's input of the current op and the round's output for its slot
+// (plain data); in the process mode they live in a shared mapping.
+uint64_t g_in_local[kMaxSlots], g_out_local[kMaxSlots];
+uint64_t* g_in = g_in_local;
+uint64_t* g_out = g_out_local;
+constexpr int kVictim = 5;  // process mode: dies by SIGKILL mid-token
+bool g_processes = false;
 std::atomic<int> g_failures{0};
 std::atomic<int> g_rounds{0};
 std::atomic<int> g_evicted_seen{0};
@@ -135,6 +145,7 @@ void worker(int slot, int tokens, int join_delay_ms) {
         std::this_thread::yield();
       if (rc != SWL_OK) return fail("submit failed", slot);
       swl_q_slot_signal_ready(slot);
+      if (g_processes && slot == kVictim && t == 2 && k == 4) raise(SIGKILL);  // the fault driver's kill
       int64_t e = 0;
       if (swl_q_wait_for_epoch(e0, 5000, &e) != SWL_OK) return fail("epoch did not move", slot);
       if (is_evicted(slot)) {
@@ -152,7 +163,51 @@ void worker(int slot, int tokens, int join_delay_ms) {
 
 }  // namespace
 
-int main() {
+// Process mode: the workers are forked processes sharing the queue segment
+// (inherited mapping) and a shared page for the slot data; kVictim kills
+// itself after signalling ready mid-token, as the reference's fault driver
+// (security_eval/common/fault_driver.py) kills a worker; the aggregator must
+// evict it after the barrier timeout and every other worker must finish.
+int run_processes(ControlBlock* ctrl, Command* ring, HostHooks& hooks, const ProtocolTimes& times) {
+  void* shared = mmap(nullptr, 2 * sizeof(uint64_t) * kMaxSlots, PROT_READ | PROT_WRITE, MAP_SHARED | MAP_ANONYMOUS,
+                      -1, 0);
+  if (shared == MAP_FAILED) return 2;
+  g_in = static_cast<uint64_t*>(shared);
+  g_out = g_in + kMaxSlots;
+  std::vector<pid_t> pids;
+  for (int s = 0; s < kWorkers; ++s) {
+    if (s == kStall || s == kRogue) continue;  // this mode tests the kill alone
+    pid_t pid = fork();
+    if (pid == 0) {
+      worker(s, 12 + 2 * (s % 3), (s % 3) * 10);
+      _exit(g_failures.load() ? 1 : 0);
+    }
+    pids.push_back(pid);
+  }
+  int loop_status = -99;
+  const auto t0 = std::chrono::steady_clock::now();
+  std::thread agg([&] { loop_status = run_main_loop(ctrl, ring, swl_q_capacity(), kOpsPerToken, hooks, times); });
+  int killed = 0, ok = 0;
+  for (pid_t pid : pids) {
+    int st = 0;
+    waitpid(pid, &st, 0);
+    if (WIFSIGNALED(st) && WTERMSIG(st) == SIGKILL) ++killed;
+    else if (WIFEXITED(st) && WEXITSTATUS(st) == 0) ++ok;
+    else fail("a surviving worker failed", -1);
+  }
+  const double secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  swl_q_set_quit(1);
+  agg.join();
+  if (loop_status != 0) fail("main loop returned an error", -1);
+  if (killed != 1) fail("expected exactly one killed worker", -1);
+  if (ctrl->evicted_slot_mask.test(kVictim) == false) fail("the killed worker's slot was not evicted", kVictim);
+  if (g_failures.load()) return 1;
+  printf("protocol stress ok: processes, %d survived, 1 killed and evicted, %.2f s\n", ok, secs);
+  return 0;
+}
+
+int main(int argc, char** argv) {
+  g_processes = argc > 1 && std::string(argv[1]) == "--processes";
   char name[128];
   if (swl_q_create(256, 256, name, sizeof(name)) != SWL_OK || swl_q_init_batch_control(kWorkers) != SWL_OK) {
     fprintf(stderr, "queue setup failed: %s\n", last_error());
@@ -167,6 +222,11 @@ int main() {
   ProtocolTimes times;
   times.evict_after = std::chrono::milliseconds(100);
   times.leave_every = std::chrono::milliseconds(2);
+  if (g_processes) {
+    const int rc = run_processes(ctrl, ring, hooks, times);
+    swl_q_close();
+    return rc;
+  }
   int loop_status = -99;
   std::thread agg([&] { loop_status = run_main_loop(ctrl, ring, swl_q_capacity(), kOpsPerToken, hooks, times); });
   std::vector<std::thread> ws;
