@@ -161,6 +161,9 @@ class SlotGroup:
                  prefetch=(), prefetch_cap: int = 80 << 20, qkv_rope_fused: bool = False):
         self.cfg = cfg
         self.fused = fused
+        if fused and cfg.hidden != 4096:
+            raise ValueError(f"the fused step's RMSNorm epilogue is built for hidden 4096 (got {cfg.hidden}); "
+                             "use fused=False for other sizes")
         # qkv_rope_fused: the QKV round carries the RoPE epilogue (one launch
         # instead of two; measured 3.5 us per layer slower than the separate
         # epilogue kernel at 28 slots, so off by default)
