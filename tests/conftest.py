@@ -18,9 +18,11 @@ def pytest_configure(config):
 # no-allocation entry points last; file order within each group (a run that
 # stops at its first failure then reports the core results first).
 _LATE = ("test_shard_gpu.py", "test_worker_process_gpu.py", "test_donor_gpu.py", "test_checkpoint_gpu.py")
-_LATE_TESTS = {"test_subset_view_steps_only_its_slots", "test_profile_step_reports_the_reference_line",
+_LATE_TESTS = {"test_mixed_step_device_tokens_and_graph_replay", "test_subset_view_steps_only_its_slots",
+               "test_profile_step_reports_the_reference_line",
                "test_config2_full_size_step_properties", "test_sampled_tokens_follow_the_reference_rule",
-               "test_sampling_without_uniforms_is_seeded", "test_lm_head_round_samples_with_each_workers_state"}
+               "test_sampling_without_uniforms_is_seeded", "test_lm_head_round_samples_with_each_workers_state",
+               "test_main_loop_serves_two_workers[sampling]"}
 _LAST = ("test_zz_no_alloc.py",)
 
 
@@ -31,7 +33,8 @@ def pytest_collection_modifyitems(config, items):
             return (2, 0)
         if name in _LATE:
             return (1, 1 + _LATE.index(name))
-        return (1, 0) if getattr(item, "originalname", item.name) in _LATE_TESTS else (0, 0)
+        late = item.name in _LATE_TESTS or getattr(item, "originalname", item.name) in _LATE_TESTS
+        return (1, 0) if late else (0, 0)
     items[:] = [it for _, it in sorted(enumerate(items), key=lambda p: (*key(p[1]), p[0]))]
 
 

@@ -258,28 +258,8 @@ def test_mixed_prefill_and_decode_step(native, cuda):
         g = torch.Generator().manual_seed(9)
         toks = [torch.randint(0, cfg.vocab, (r,), generator=g).tolist() for r in rows]
         stream = torch.cuda.current_stream()
-        kc0 = [k.clone() for k in grp.k_cache]
-        vc0 = [v.clone() for v in grp.v_cache]
-        # one-row slots pass None: their row is the slot's last output, on the device
-        grp.tokens.copy_(torch.tensor([t[0] for t in toks]))
-        grp.enqueue_step(stream, rows=rows, tokens=[None if r == 1 else t for t, r in zip(toks, rows)])
+        grp.enqueue_step(stream, rows=rows, tokens=toks)
         torch.cuda.synchronize()
-        # the same mixed step from a CUDA graph of the row pattern (token ids
-        # staged in tok_in) gives bit-identical tokens, hidden rows and caches
-        eager = (grp.tokens.clone(), grp.h_rows.clone(), [k.clone() for k in grp.k_cache],
-                 [v.clone() for v in grp.v_cache], grp.seqlens.clone())
-        grp.capture(rows=rows)
-        for l in range(cfg.layers):
-            grp.k_cache[l].copy_(kc0[l])
-            grp.v_cache[l].copy_(vc0[l])
-        grp.reset_positions()
-        for i, t in enumerate(toks):
-            grp.tok_in[i, :len(t)].copy_(torch.tensor(t))
-        grp.replay()
-        torch.cuda.synchronize()
-        assert torch.equal(grp.tokens, eager[0]) and torch.equal(grp.seqlens, eager[4])
-        assert all(torch.equal(grp.h_rows[i, :r], eager[1][i, :r]) for i, r in enumerate(rows))
-        assert all(torch.equal(a, b) for a, b in zip(grp.k_cache + grp.v_cache, eager[2] + eager[3]))
         want, final, logits, h_last = decode_step(cfg, base_c, ad_c, kc, vc, bts, list(ctx), toks)
         got_h = torch.stack([grp.h_rows[i, r - 1] for i, r in enumerate(rows)])
         assert_close(got_h, h_last, "mixed step: last row's last-layer hidden", atol_rms=ATOL_RMS_MULTILAYER)
@@ -449,5 +429,54 @@ def test_config2_full_size_step_properties(native, cuda):
         torch.cuda.synchronize()
         assert torch.equal(grp.tokens, eager[0]) and torch.equal(grp.h, eager[1])
         assert all(torch.equal(a, b) for a, b in zip(grp.k_cache + grp.v_cache, kn + vn))
+    finally:
+        grp.close()
+
+
+def test_mixed_step_device_tokens_and_graph_replay(native, cuda):
+    """A mixed step whose one-row slots pass None (their row is the slot's
+    last output, read on the device) equals the step with the ids given,
+    and the same step from a CUDA graph of the row pattern (ids staged in
+    tok_in) is bit-identical: tokens, hidden rows, positions and caches."""
+    from swarmlora_b200.engine import ModelConfig, SlotGroup, random_adapter, random_base
+    cfg = ModelConfig(layers=2, vocab=4096)
+    ctx = [0, 20, 31, 100, 7]
+    rows = [16, 1, 5, 1, 3]
+    base = random_base(cfg, seed=3, device=cuda, norm_noise=0.1)
+    adapters = [random_adapter(cfg, seed=80 + i, device=cuda) if i != 1 else None for i in range(len(ctx))]
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=32, seed=8)
+    try:
+        g = torch.Generator().manual_seed(9)
+        toks = [torch.randint(0, cfg.vocab, (r,), generator=g).tolist() for r in rows]
+        stream = torch.cuda.current_stream()
+        kc0 = [k.clone() for k in grp.k_cache]
+        vc0 = [v.clone() for v in grp.v_cache]
+
+        def restore():
+            for l in range(cfg.layers):
+                grp.k_cache[l].copy_(kc0[l])
+                grp.v_cache[l].copy_(vc0[l])
+            grp.reset_positions()
+        grp.enqueue_step(stream, rows=rows, tokens=toks)
+        torch.cuda.synchronize()
+        given = (grp.tokens.clone(), grp.h_rows.clone(), [k.clone() for k in grp.k_cache],
+                 [v.clone() for v in grp.v_cache], grp.seqlens.clone())
+
+        def same(what):
+            assert torch.equal(grp.tokens, given[0]) and torch.equal(grp.seqlens, given[4]), what
+            assert all(torch.equal(grp.h_rows[i, :r], given[1][i, :r]) for i, r in enumerate(rows)), what
+            assert all(torch.equal(a, b) for a, b in zip(grp.k_cache + grp.v_cache, given[2] + given[3])), what
+        restore()
+        grp.tokens.copy_(torch.tensor([t[0] for t in toks]))
+        grp.enqueue_step(stream, rows=rows, tokens=[None if r == 1 else t for t, r in zip(toks, rows)])
+        torch.cuda.synchronize()
+        same("one-row slots' tokens read on the device")
+        grp.capture(rows=rows)
+        restore()
+        for i, t in enumerate(toks):
+            grp.tok_in[i, :len(t)].copy_(torch.tensor(t))
+        grp.replay()
+        torch.cuda.synchronize()
+        same("graph replay of the row pattern")
     finally:
         grp.close()

@@ -4,8 +4,8 @@ ring and epoch barrier (ext_ipc_queue) and the slot buffers
 (ext_unified_barrier), each worker issuing one token's ops in the reference
 worker's order (worker_sync.py:1274-1425: embed, QKV, O, Gate+Up, Down, LM
 head; epoch captured before slot_signal_ready). Every round's output is
-checked against the CPU oracle; one worker's LM head samples (top_k = 1,
-posted before its join), the other's is greedy."""
+checked against the CPU oracle; in the sampling variant one worker's LM
+head samples (top_k = 1, posted before its join), the other's is greedy."""
 import threading
 
 import pytest
@@ -18,7 +18,8 @@ pytestmark = pytest.mark.gpu
 BF = torch.bfloat16
 
 
-def test_main_loop_serves_two_workers(native, cuda):
+@pytest.mark.parametrize("sampling", [False, True], ids=["greedy", "sampling"])
+def test_main_loop_serves_two_workers(native, cuda, sampling):
     from swarmlora_b200 import ext_aggregator as agg
     from swarmlora_b200 import ext_ipc_queue as extq
     from swarmlora_b200 import ext_unified_barrier as ub
@@ -49,10 +50,11 @@ def test_main_loop_serves_two_workers(native, cuda):
         a_in, a_out = agg.slot_buffers(c["slot_id"])
         ub.attach_slot(c["slot_id"], a_in, a_out, c["input_buffer_size"], c["output_buffer_size"])
         slots.append((c["slot_id"], wid))
-    # the second worker posts sampling with top_k = 1 before it joins: its
-    # LM-head round goes through the sampling kernel and keeps only the
-    # maximum (worker_sync.py posts its request's parameters this way)
-    extq.slot_set_pending_sampling(slots[1][0], True, 1.0, 1, 1.0)
+    if sampling:
+        # the second worker posts sampling with top_k = 1 before it joins: its
+        # LM-head round goes through the sampling kernel and keeps only the
+        # maximum (worker_sync.py posts its request's parameters this way)
+        extq.slot_set_pending_sampling(slots[1][0], True, 1.0, 1, 1.0)
     for s, _ in slots:  # both join before the loop starts: they activate together
         extq.slot_signal_join(s)
 
