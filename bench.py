@@ -826,9 +826,10 @@ def churn_arm(args):
     loader, pool_dir = None, None
     if args.churn_from_disk:  # every adapter the trace uses, as a bf16 PEFT directory
         import shutil
-        import tempfile
         from swarmlora_b200.adapters import AdapterLoader, save_adapter
-        pool_dir = tempfile.mkdtemp(prefix="swl_adapter_pool_")
+        pool_dir = str(ROOT / "_build" / f"adapter_pool_{os.getpid()}")  # inside the checkout (ignored by git)
+        shutil.rmtree(pool_dir, ignore_errors=True)
+        os.makedirs(pool_dir)
         for aid in sorted({r.adapter for r in trace}):
             save_adapter(os.path.join(pool_dir, f"lora-{aid}"),
                          random_adapter(cfg, seed=10_000 + aid, device=dev, rank=int(ranks[aid])),
