@@ -456,15 +456,19 @@ class SlotGroup:
             full[i] = x
         return full
 
-    def _advance_of(self, row_counts) -> torch.Tensor:
-        """Device copy of a row pattern (the per-slot position advance), made
-        once per pattern outside any graph capture."""
+    def _advance_of(self, row_counts, keep: bool = False) -> torch.Tensor:
+        """Device copy of a row pattern (the per-slot position advance). A
+        captured graph reads its copy on every replay, so `capture` makes it
+        beforehand and keeps it (keep=True); an eager step uses a temporary
+        (its memory returns to the stream's pool once the add has run)."""
         key = tuple(int(x) for x in row_counts)
         t = self._advance.get(key)
         if t is None:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("a new row pattern inside a graph capture: pass it to capture(rows=...)")
-            t = self._advance[key] = torch.tensor(key, dtype=torch.int32, device=self.dev)
+            t = torch.tensor(key, dtype=torch.int32, device=self.dev)
+            if keep:
+                self._advance[key] = t
         return t
 
     def _enqueue_unfused(self, stream: torch.cuda.Stream) -> None:
@@ -587,7 +591,7 @@ class SlotGroup:
             if len(rows) != self.n or any(x < 1 or x > self.max_rows for x in rows) or not self.fused:
                 raise ValueError(f"rows: one count per slot in 1..{self.max_rows} (fused sequence)")
         if self._subset is not None or (rows is not None and len(set(rows)) > 1):
-            self._advance_of(self._full_pattern(rows))
+            self._advance_of(self._full_pattern(rows), keep=True)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=s):
             if rows is None:
