@@ -17,6 +17,39 @@ pytestmark = pytest.mark.gpu
 BF = torch.bfloat16
 
 
+def test_loaders_on_the_device_equal_their_cpu_loads(native, cuda, scratch):
+    """The adapter and checkpoint loaders through the pinned staging buffer
+    and the asynchronous host-to-device copies (the staging buffer reused
+    across tensors and across loads) give exactly what they give on the CPU."""
+    from pathlib import Path
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from swarmlora_b200 import adapters as ad
+    from swarmlora_b200.checkpoint import load_base
+    from swarmlora_b200.engine import ModelConfig
+    golden = Path(__file__).resolve().parent / "golden"
+    tiny = ModelConfig(hidden=64, inter=96, layers=2, hq=2, hkv=1, head_dim=32, vocab=128)
+    loader = ad.AdapterLoader(tiny, cuda)
+    for name in ("adapter_r4", "adapter_r8_partial", "adapter_r4"):
+        on_dev, cfg_d = loader.load(str(golden / name))
+        on_cpu, cfg_c = ad.load_adapter(str(golden / name), tiny, "cpu")
+        assert cfg_d == cfg_c
+        for l in range(tiny.layers):
+            for p in ad.MODULES:
+                for a, b in zip(on_dev[l][p], on_cpu[l][p]):
+                    assert a.is_cuda and torch.equal(a.cpu(), b), (name, l, p)
+    hf = LlamaConfig(hidden_size=64, intermediate_size=96, num_attention_heads=2, num_key_value_heads=1,
+                     head_dim=32, num_hidden_layers=2, vocab_size=128, tie_word_embeddings=False)
+    LlamaForCausalLM(hf).to(BF).save_pretrained(str(scratch / "tiny"), safe_serialization=True,
+                                                max_shard_size="20KB")
+    dev_base, _ = load_base(str(scratch / "tiny"), cuda)
+    cpu_base, _ = load_base(str(scratch / "tiny"), "cpu")
+    for field in ("q", "k", "v", "o", "gate", "up", "down", "in_norm", "post_norm"):
+        for a, b in zip(getattr(dev_base, field), getattr(cpu_base, field)):
+            assert a.is_cuda and torch.equal(a.cpu(), b), field
+    for field in ("final_norm", "embed", "lm_head"):
+        assert torch.equal(getattr(dev_base, field).cpu(), getattr(cpu_base, field)), field
+
+
 def test_engine_matches_hf_llama_from_a_checkpoint(native, cuda, scratch):
     from transformers import LlamaConfig, LlamaForCausalLM
     from swarmlora_b200.checkpoint import load_base
@@ -73,36 +106,3 @@ def test_engine_matches_hf_llama_from_a_checkpoint(native, cuda, scratch):
         assert len(seq) > len(prompt) + 3
     finally:
         grp.close()
-
-
-def test_loaders_on_the_device_equal_their_cpu_loads(native, cuda, scratch):
-    """The adapter and checkpoint loaders through the pinned staging buffer
-    and the asynchronous host-to-device copies (the staging buffer reused
-    across tensors and across loads) give exactly what they give on the CPU."""
-    from pathlib import Path
-    from transformers import LlamaConfig, LlamaForCausalLM
-    from swarmlora_b200 import adapters as ad
-    from swarmlora_b200.checkpoint import load_base
-    from swarmlora_b200.engine import ModelConfig
-    golden = Path(__file__).resolve().parent / "golden"
-    tiny = ModelConfig(hidden=64, inter=96, layers=2, hq=2, hkv=1, head_dim=32, vocab=128)
-    loader = ad.AdapterLoader(tiny, cuda)
-    for name in ("adapter_r4", "adapter_r8_partial", "adapter_r4"):
-        on_dev, cfg_d = loader.load(str(golden / name))
-        on_cpu, cfg_c = ad.load_adapter(str(golden / name), tiny, "cpu")
-        assert cfg_d == cfg_c
-        for l in range(tiny.layers):
-            for p in ad.MODULES:
-                for a, b in zip(on_dev[l][p], on_cpu[l][p]):
-                    assert a.is_cuda and torch.equal(a.cpu(), b), (name, l, p)
-    hf = LlamaConfig(hidden_size=64, intermediate_size=96, num_attention_heads=2, num_key_value_heads=1,
-                     head_dim=32, num_hidden_layers=2, vocab_size=128, tie_word_embeddings=False)
-    LlamaForCausalLM(hf).to(BF).save_pretrained(str(scratch / "tiny"), safe_serialization=True,
-                                                max_shard_size="20KB")
-    dev_base, _ = load_base(str(scratch / "tiny"), cuda)
-    cpu_base, _ = load_base(str(scratch / "tiny"), "cpu")
-    for field in ("q", "k", "v", "o", "gate", "up", "down", "in_norm", "post_norm"):
-        for a, b in zip(getattr(dev_base, field), getattr(cpu_base, field)):
-            assert a.is_cuda and torch.equal(a.cpu(), b), field
-    for field in ("final_norm", "embed", "lm_head"):
-        assert torch.equal(getattr(dev_base, field).cpu(), getattr(cpu_base, field)), field
