@@ -56,3 +56,19 @@ def test_errors_are_reported_without_gpu(native):
     assert lib.swl_agg_claim_slot(1, None, None, None, None, None) != 0
     assert "not initialized" in native.last_error()
     assert lib.swl_agg_get_slot_owner(0) == -1
+
+
+def test_sampling_and_donor_entry_points_check_arguments(native):
+    """swl_sample_rows, swl_agg_set_worker_sampling and the donor export
+    refuse bad arguments with a message, before any device work."""
+    import ctypes as C
+    lib = native.lib()
+    p = (native.Sampling * 2)()
+    out = C.c_void_p(0x1000)
+    assert lib.swl_sample_rows(C.c_void_p(0x1000), 200, 10, 10, p, None, 0, 0, out, None) != 0  # too many rows
+    assert "sample" in native.last_error()
+    assert lib.swl_sample_rows(C.c_void_p(0x1000), 2, 10, 5, p, None, 0, 0, out, None) != 0  # ld < vocab
+    assert lib.swl_sample_rows(None, 2, 10, 10, p, None, 0, 0, out, None) != 0  # no logits
+    assert lib.swl_agg_set_worker_sampling(-1, 1, 1.0, 0, 1.0) != 0
+    assert "worker_id" in native.last_error()
+    assert lib.swl_agg_set_sampling_seed(7) == 0
