@@ -58,9 +58,9 @@ def test_errors_are_reported_without_gpu(native):
     assert lib.swl_agg_get_slot_owner(0) == -1
 
 
-def test_sampling_and_donor_entry_points_check_arguments(native):
-    """swl_sample_rows, swl_agg_set_worker_sampling and the donor export
-    refuse bad arguments with a message, before any device work."""
+def test_sampling_entry_points_check_arguments(native):
+    """swl_sample_rows and swl_agg_set_worker_sampling refuse bad arguments
+    with a message, before any device work."""
     import ctypes as C
     lib = native.lib()
     p = (native.Sampling * 2)()
