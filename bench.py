@@ -765,7 +765,9 @@ def mixed_arm(args):
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None,
                      "algorithmic_bytes": rounds[dom]["bytes"], "peak_source": peak_kind},
-        "gpu_launches": grp.launches_per_step() * args.steps,
+        # the mixed step advances its positions with a torch add, not this
+        # library's advance kernel
+        "gpu_launches": (grp.launches_per_step() - 1) * args.steps,
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)
