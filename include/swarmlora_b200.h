@@ -344,13 +344,20 @@ int swl_paged_attention(int nseg, const int* rows, const void* const* block_tabl
  * that overlap on the GPU corrupt each other. Nothing in it needs to start at
  * zero. The first call on a device looks up the array's address (this may
  * load the library's code onto the device): make it before any stream
- * capture begins. */
+ * capture begins. The address is cached per device for the life of the
+ * device's primary context; after cudaDeviceReset call
+ * swl_noalloc_forget_device with that device current. */
 #define SWL_NOALLOC_ATTN_SCRATCH_FLOATS 1048576
 int swl_paged_attention_noalloc(int nseg, const int* rows, const void* const* block_tables,
                                 const void* const* k_cache, const void* const* v_cache,
                                 const void* const* seqlens, void* const* out, int64_t out_stride,
                                 int hq, int hkv, int head_dim, int page, float scale, int max_len,
                                 const void* q_rot, void* stream);
+/* Forgets the current device's cached address of the no-allocation scratch
+ * array, so the next swl_paged_attention_noalloc looks it up again (needed
+ * only after the device's primary context was destroyed, e.g. by
+ * cudaDeviceReset). No counterpart in the reference. */
+int swl_noalloc_forget_device(void);
 /* swl_paged_attention + the O projection's LoRA shrink on its output. */
 int swl_paged_attention_shrink(int nseg, const int* rows, const void* const* block_tables,
                                const void* const* k_cache, const void* const* v_cache,

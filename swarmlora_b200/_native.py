@@ -122,6 +122,7 @@ SIGNATURES: dict[str, tuple] = {
                                    _i32, _f32, _i32, _p, _p, _p]),
     "swl_paged_attention_noalloc": (_i32, [_i32, _pi32, _pp, _pp, _pp, _pp, _pp, _i64, _i32, _i32,
                                            _i32, _i32, _f32, _i32, _p, _p]),
+    "swl_noalloc_forget_device": (_i32, []),
     "swl_rms_norm": (_i32, [_i32, _pi32, _pp, _i64, _pp, _i64, _p, _i64, _f32, _p]),
     "swl_copy_rows": (_i32, [_i32, _pp, _pp, _pi64, _p]),
     "swl_paged_attention_shrink": (_i32, [_i32, _pi32, _pp, _pp, _pp, _pp, _pp, _i64, _i32, _i32, _i32,

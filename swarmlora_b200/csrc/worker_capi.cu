@@ -361,7 +361,10 @@ SWL_EXPORT int swl_advance_i32(int* p, int n, int delta, void* stream) {
 // The first call on a device looks up the array's device address
 // (cudaGetSymbolAddress, which may load this part of the library onto the
 // device) and caches it; later calls only launch. Make that first call before
-// any stream capture begins.
+// any stream capture begins. The cached address belongs to the device's
+// primary context: after cudaDeviceReset (or anything else that destroys and
+// recreates that context) call swl_noalloc_forget_device so that the next
+// call looks the address up again.
 namespace {
 constexpr int64_t kNoAllocPartFloats = int64_t{1} << 20;
 constexpr int kNoAllocMaxDevices = 64;
@@ -393,6 +396,17 @@ int noalloc_scratch(float** out) {
 }
 }  // namespace
 
+// Drops the cached scratch address of the current device (after a device
+// reset); the array itself stays as compiled.
+SWL_EXPORT int swl_noalloc_forget_device(void) {
+  int dev = 0;
+  SWL_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return SWL_OK;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  g_noalloc_part[dev].store(nullptr, std::memory_order_release);
+  return SWL_OK;
+}
+
 // swl_paged_attention with the same arguments minus `part`; the partials live
 // in the library's static per-device array described above.
 SWL_EXPORT int swl_paged_attention_noalloc(int nseg, const int* rows, const void* const* block_tables,
@@ -403,7 +417,8 @@ SWL_EXPORT int swl_paged_attention_noalloc(int nseg, const int* rows, const void
   AttnTable t;
   SWL_TRY(fill_attn(&t, nseg, rows, nullptr, block_tables, const_cast<void* const*>(k_cache),
                     const_cast<void* const*>(v_cache), seqlens, out));
-  if (hkv <= 0) return set_error(SWL_ERR_ARG, "paged_attention_noalloc: hkv must be positive");
+  if (hq <= 0 || hkv <= 0)
+    return set_error(SWL_ERR_ARG, "paged_attention_noalloc: hq and hkv must be positive");
   const int64_t need = attention_part_floats(t.seg.total_rows, hq,
                                              attention_splits(t.seg.total_rows, hkv, max_len));
   if (need > kNoAllocPartFloats)

@@ -843,8 +843,8 @@ int launch_attention_stages(const AttnTable& tab, const AttnParams& p, int grid,
 int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream_t stream,
                            const ShrinkSide* shrink) {
   if (tab.seg.total_rows <= 0) return SWL_OK;
-  if (p.head_dim != kD || p.page != kPageTok || p.hkv <= 0 || p.hkv > kAttnMaxHkv || p.hq % p.hkv ||
-      p.hq / p.hkv > 8)
+  if (p.head_dim != kD || p.page != kPageTok || p.hq <= 0 || p.hkv <= 0 || p.hkv > kAttnMaxHkv ||
+      p.hq % p.hkv || p.hq / p.hkv > 8)
     return set_error(SWL_ERR_ARG, "attention: head_dim 128, page 16, 1..%d kv heads, at most 8 query heads per kv head",
                      kAttnMaxHkv);
   if (tab.seg.total_rows > kAttnMaxRows)

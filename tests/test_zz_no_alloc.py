@@ -82,3 +82,10 @@ def test_noalloc_attention_rejects_oversize_launch(native):
                                          None)
     assert st != 0
     assert "static scratch holds 1048576" in native.last_error()
+    # a non-positive head count is refused before the scratch size is computed
+    for bad_hq in (0, -8):
+        st = lib.swl_paged_attention_noalloc(n, native.i32_array([r] * n), fake, fake, fake, fake, fake,
+                                             hq * D, bad_hq, hkv, D, PAGE, 0.1, 64, C.c_void_p(0x1000),
+                                             None)
+        assert st != 0
+        assert "hq and hkv must be positive" in native.last_error()
