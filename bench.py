@@ -85,6 +85,10 @@ def parse():
     ap.add_argument("--profile-layers", type=int, default=0, metavar="N",
                     help="print N per-step [LAYER_PROFILE] lines (the reference worker's PROFILE_LAYERS format) "
                          "for the decode workload and exit")
+    ap.add_argument("--protocol", default="28",
+                    help="worker-client counts (comma separated) for the decode through the drop-in protocol "
+                         "(aggregator main loop + native worker clients over the shared-memory ring), each "
+                         "with event, host (the reference's) and device-published completion; 'off' skips it")
     ap.add_argument("--profile-attention", action="store_true",
                     help="run only --steps paged-attention launches over one layer's KV (small ncu case)")
     return ap.parse_args()
@@ -356,6 +360,43 @@ def round_phase(grp, cfg, reps=3, rows=None):
     return out
 
 
+def protocol_phase(grp, args, variants, rounds=None):
+    """Decode through the drop-in protocol: the aggregator's main loop
+    serving native worker clients (swarmlora_b200.protocol) that request
+    every round through the shared-memory ring and epoch barrier, as the
+    reference's workers do. `variants`: (workers, completion, input_ready).
+    Returns one dict per variant: tok/s over the timed tokens (host clock of
+    the slowest client, from each token's first launch to its last round's
+    epoch), and per-round times."""
+    import statistics
+    import torch
+    from swarmlora_b200.protocol import ProtocolRun
+    n = grp.n
+    ops = 1 + 4 * grp.cfg.layers + 1
+    out = []
+    for workers, completion, input_ready in variants:
+        grp.reset_positions()
+        torch.cuda.synchronize()
+        run = ProtocolRun(grp, workers=workers, completion=completion, input_ready=input_ready)
+        try:
+            res = run.run(args.warmup + args.steps)
+        finally:
+            run.close()
+        timed = res["token_s"][args.warmup:]
+        tok_s = n * len(timed) / sum(timed)
+        entry = {"workers": workers, "slots_per_worker": round(n / workers, 2), "completion": completion,
+                 "input_ready": input_ready, "tok_s": round(tok_s, 2),
+                 "ms_per_token": round(1e3 * sum(timed) / len(timed), 3),
+                 "ms_per_token_p50": round(1e3 * statistics.median(timed), 3),
+                 "us_per_round_e2e": round(1e6 * sum(timed) / len(timed) / ops, 2)}
+        if rounds:
+            entry["us_per_round_kernels"] = round(
+                (sum(v["us"] for v in rounds.values()) * grp.cfg.layers) / (4 * grp.cfg.layers), 2)
+        out.append(entry)
+    grp.reset_positions()
+    return out
+
+
 def our_arm(args):
     import torch
     world, rank, local = dist_setup(args.gpus)
@@ -453,6 +494,13 @@ def our_arm(args):
     #       python bench.py --profile-round gate_up --steps 3 --warmup 1
     ncu_traffic = {("gate_up", 28): 235_135_744 + 3_593_216}
     rounds = round_phase(grp, cfg)
+    proto = None
+    if args.protocol != "off" and world == 1:
+        variants = []
+        for w in (int(x) for x in args.protocol.split(",")):
+            w = min(max(1, w), n)
+            variants += [(w, "event", "event"), (w, "host", "sync"), (w, "device", "flag")]
+        proto = protocol_phase(grp, args, variants, rounds)
     peak, peak_kind = measured_peaks()
     dom = max(rounds, key=lambda k: rounds[k]["us"])
     achieved = rounds[dom]["bytes"] / rounds[dom]["us"] / 1e3
@@ -493,6 +541,10 @@ def our_arm(args):
             "gpu_launches": launches,
             "clocks": clk,
         }
+        if proto:
+            # the same decode through the drop-in protocol: the reference's
+            # deployment shape (main loop + worker clients over the shm ring)
+            line["e2e_protocol"] = proto
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)

@@ -164,6 +164,29 @@ int swl_agg_execute_round(int op, int layer, int n, const int* slot_ids, const i
                           const int64_t* bx, const int64_t* tx, void* stream);
 /* aggregator_main_loop_slots (ext_aggregator.cpp:1024-1210); blocking. */
 int swl_agg_main_loop_slots(int num_slots, int dtype_code);
+/* How the main loop completes a round (not in the reference). 0: it
+ * synchronizes the round's stream, then bumps barrier_done_epoch on the host
+ * (ext_aggregator.cpp:1196-1202). 1: the control block is registered as
+ * mapped host memory and a device store after the round's kernels bumps the
+ * epoch; the loop goes on without waiting (workers see the epoch as soon as
+ * the round has finished on the GPU). Needs swl_agg_init_queue first;
+ * mapping a new queue resets the mode to 0. */
+int swl_agg_set_completion_mode(int mode);
+int swl_agg_completion_mode(void);
+/* Event completion (mode 2 of swl_agg_set_completion_mode; not in the
+ * reference): each slot's worker records an event after the work that
+ * writes the slot's round input and then sets its ready bit; the round's
+ * stream waits for those events, the round event is recorded after the
+ * round's kernels and the host bumps the epoch at once; a worker that sees
+ * the epoch makes its stream wait for the round event before reading the
+ * outputs. A slot without an input event is refused under mode 2. The round
+ * event: its IPC handle (64 bytes) for workers in other processes, or the
+ * cudaEvent_t for workers in this process. A slot's input event: from the
+ * worker's IPC handle (NULL / 0 = none), or a cudaEvent_t of this process. */
+int swl_agg_round_event_handle(unsigned char* out, size_t len);
+int swl_agg_round_event(void** event);
+int swl_agg_set_slot_input_event(int slot_id, const unsigned char* handle, size_t len);
+int swl_agg_set_slot_input_event_local(int slot_id, void* event);
 /* The QKV round of `layer` fused with the RoPE epilogue (swl_fused_qkv_rope's
  * arguments; table entry i belongs to command i): each round tile is one head
  * and adds its LoRA delta, applies NeoX RoPE and writes rotated q to q_rot
@@ -401,6 +424,40 @@ int swl_fused_silu_splits(int64_t inter);
 int swl_copy_rows(int n, const void* const* src, void* const* dst, const int64_t* bytes,
                   void* stream);
 int swl_advance_i32(int* p, int n, int delta, void* stream);
+
+/* ======================================================================
+ * Worker client of the slot protocol — the reference worker's per-token
+ * loop (worker_sync.py:1274-1425) and its round requests
+ * (BatchedAggregatorOps.*_submit_all / barrier_sync, worker_sync.py:230-389)
+ * for the slots one client owns, from one host thread, with this library's
+ * fused worker kernels between the rounds (slot outputs read in place, the
+ * next round's input written straight into the slot input). Each round:
+ * the input is known written (input mode 0: cudaStreamSynchronize, as
+ * prepare_input_slot; 1: a device-written host flag; 2: an event recorded
+ * for the aggregator's event completion), the epoch is captured, one command
+ * per slot is submitted, the ready bits are set, the client waits for the
+ * epoch (mode 2: then its stream waits for the round event). Uses this process's queue mapping (swl_q_create or
+ * swl_q_open); the slots must have joined and be active.
+ * ==================================================================== */
+int swl_wc_create(int nslots, const int* slot_ids, const int* worker_ids, int layers, int hidden,
+                  int inter, int hq, int hkv, int head_dim, int page, int rank, float eps,
+                  float scaling, int max_len, void** out);
+int swl_wc_set_buffers(void* handle, void* const* slot_in, void* const* slot_out,
+                       void* const* h_rows, void* const* tokens, const void* const* block_tables,
+                       const void* const* seqlens, int* seqlen_base, void* q_rot, float* part,
+                       float* ws_qkv, float* ws_o, float* ws_gu, float* ws_dn,
+                       const void* cos_sin, const void* final_norm);
+int swl_wc_set_layer(void* handle, int layer, const void* in_norm, const void* post_norm,
+                     void* const* k_cache, void* const* v_cache, const void* const* A_qkv,
+                     const void* const* B_qkv, const void* const* A_o, const void* const* B_o,
+                     const void* const* A_gu, const void* const* B_gu, const void* const* A_dn,
+                     const void* const* B_dn);
+int swl_wc_configure(void* handle, int input_mode, int64_t timeout_ms, void* history);
+/* Runs `tokens` decode tokens (blocking); token_ns[t] = token t's host wall
+ * time in ns, or NULL. */
+int swl_wc_run(void* handle, int tokens, int64_t* token_ns);
+int64_t swl_wc_rounds(void* handle);
+int swl_wc_destroy(void* handle);
 
 #ifdef __cplusplus
 }

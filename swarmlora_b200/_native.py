@@ -89,6 +89,12 @@ SIGNATURES: dict[str, tuple] = {
     "swl_agg_shard_connect": (_i32, [_p, _i32]),
     "swl_agg_shard_end": (_i32, []),
     "swl_agg_main_loop_slots": (_i32, [_i32, _i32]),
+    "swl_agg_set_completion_mode": (_i32, [_i32]),
+    "swl_agg_completion_mode": (_i32, []),
+    "swl_agg_round_event_handle": (_i32, [C.c_char_p, _sz]),
+    "swl_agg_round_event": (_i32, [C.POINTER(C.c_void_p)]),
+    "swl_agg_set_slot_input_event": (_i32, [_i32, C.c_char_p, _sz]),
+    "swl_agg_set_slot_input_event_local": (_i32, [_i32, _p]),
     # ---- ext_unified_barrier
     "swl_ub_init_worker_slot_manager": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "swl_ub_open_slot": (_i32, [_i32, C.c_char_p, _sz, C.c_char_p, _sz, _sz, _sz]),
@@ -137,6 +143,14 @@ SIGNATURES: dict[str, tuple] = {
     "swl_fused_norm_splits": (_i32, [_i32]),
     "swl_fused_silu_splits": (_i32, [_i64]),
     "swl_advance_i32": (_i32, [_p, _i32, _i32, _p]),
+    "swl_wc_create": (_i32, [_i32, _pi32, _pi32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _f32,
+                             _i32, C.POINTER(C.c_void_p)]),
+    "swl_wc_set_buffers": (_i32, [_p, _pp, _pp, _pp, _pp, _pp, _pp, _p, _p, _p, _p, _p, _p, _p, _p, _p]),
+    "swl_wc_set_layer": (_i32, [_p, _i32, _p, _p, _pp, _pp, _pp, _pp, _pp, _pp, _pp, _pp, _pp, _pp]),
+    "swl_wc_configure": (_i32, [_p, _i32, _i64, _p]),
+    "swl_wc_run": (_i32, [_p, _i32, _pi64]),
+    "swl_wc_rounds": (_i64, [_p]),
+    "swl_wc_destroy": (_i32, [_p]),
 }
 
 _lib = None

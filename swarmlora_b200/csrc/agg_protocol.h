@@ -86,11 +86,20 @@ inline int wait_for_slots(ControlBlock* ctrl, Mask128& active, const ProtocolTim
   }
 }
 
-// aggregator_signal_done_slots (ext_aggregator.cpp:981-987).
-inline void signal_done(ControlBlock* ctrl) {
+// First half of aggregator_signal_done_slots (ext_aggregator.cpp:981-987):
+// the round's ready state (count and the active slots' ready bits) is reset.
+// A worker sets its next ready bit only after it has seen the epoch move, so
+// resetting before the epoch is published (by the host below, or by the
+// device once the round's kernels have finished) never loses a ready bit.
+inline void clear_ready(ControlBlock* ctrl) {
   ctrl->slot_ready_count.store(0, std::memory_order_release);
   Mask128 active = ctrl->active_slot_mask.load();
   ctrl->per_slot_ready_mask.and_with(~active);
+}
+
+// aggregator_signal_done_slots (ext_aggregator.cpp:981-987).
+inline void signal_done(ControlBlock* ctrl) {
+  clear_ready(ctrl);
   ctrl->barrier_done_epoch.fetch_add(1, std::memory_order_release);
 }
 
@@ -157,7 +166,19 @@ inline bool drain_commands(ControlBlock* ctrl, Command* ring, int capacity, cons
 // aggregator_main_loop_slots (ext_aggregator.cpp:1024-1210). Joins and
 // leaves are applied at token boundaries; each token is ops_per_token
 // rounds: wait for every active slot's ready bit, drain one command per
-// slot, run the round, signal the epoch. Hooks:
+// slot, run the round, signal the epoch.
+//
+// Completion. With h.deferred_epoch() false the host signals each round
+// after h.round returns (the reference: the round has finished, the host
+// bumps the epoch). With it true the loop clears the ready state first and
+// passes h.round the epoch value that completes the round; the hook
+// arranges for that value to be stored into barrier_done_epoch once the
+// round's results are in place (a device write after the round's kernels)
+// and returns at once, so the host goes on to wait for the next round's
+// ready bits while the round runs. The loop keeps the last value it handed
+// out; before the host itself signals (quit, a failed drain, a sampling-only
+// round) it calls h.flush(), which must return only once every handed-out
+// value has been stored. Hooks:
 //   void on_membership(const Mask128& active, const Mask128& joins)
 //       after a token boundary's joins / leaves are applied;
 //   void on_sampling(const DrainedCmd& c)   for each set-sampling command;
@@ -165,7 +186,12 @@ inline bool drain_commands(ControlBlock* ctrl, Command* ring, int capacity, cons
 //                 std::vector<int>* bad)     slots whose commands are refused
 //                                            (evicted; the round runs without them);
 //   int round(int op, int layer, const std::vector<DrainedCmd>& cmds,
-//             const std::vector<int>& bad)   0 or a failure status, which ends the loop.
+//             const std::vector<int>& bad, int64_t epoch)
+//                                            0 or a failure status, which ends the loop;
+//                                            `epoch` is the value to publish (deferred
+//                                            completion) or 0;
+//   bool deferred_epoch()                    see Completion above;
+//   void flush()                             every handed-out epoch stored.
 // Returns 0 when the quit flag ends the loop.
 template <class Hooks>
 int run_main_loop(ControlBlock* ctrl, Command* ring, int capacity, int ops_per_token, Hooks& h,
@@ -174,12 +200,23 @@ int run_main_loop(ControlBlock* ctrl, Command* ring, int capacity, int ops_per_t
   std::vector<DrainedCmd> cmds;
   std::vector<int> bad;
   cmds.reserve(kMaxSlots);
+  // last epoch value handed to the hooks (deferred completion)
+  int64_t handed = ctrl->barrier_done_epoch.load(std::memory_order_acquire);
+  auto host_signal = [&] {
+    h.flush();
+    signal_done(ctrl);
+    handed = ctrl->barrier_done_epoch.load(std::memory_order_acquire);
+  };
   while (ctrl->quit_flag.load(std::memory_order_acquire) == 0) {
     Mask128 leaves, joins;
     if (!ctrl->pending_slot_leaves.load().empty()) leaves = ctrl->pending_slot_leaves.take_all();
     if (!leaves.empty()) active = active & ~leaves;
     if (!ctrl->pending_slot_joins.load().empty()) joins = ctrl->pending_slot_joins.take_all();
     if (!joins.empty()) active = active | joins;
+    // A joining worker reads the epoch once it sees itself active and waits
+    // for it to move: every round's epoch must be stored before then, or a
+    // late store would release its first wait before its round ran.
+    if (!joins.empty() && h.deferred_epoch()) h.flush();
     int N = active.count();
     ctrl->active_slot_mask.store(active);
     ctrl->active_slot_count.store(N);
@@ -191,14 +228,14 @@ int run_main_loop(ControlBlock* ctrl, Command* ring, int capacity, int ops_per_t
     for (int op_idx = 0; op_idx < ops_per_token; ++op_idx) {
       int got = wait_for_slots(ctrl, active, t);
       if (got < 0) {
-        signal_done(ctrl);
+        host_signal();
         break;
       }
       if (got == 0) break;
       N = got;
       cmds.clear();
       if (!drain_commands(ctrl, ring, capacity, active, N, &cmds, t)) {
-        signal_done(ctrl);
+        host_signal();
         break;
       }
       if (cmds.empty()) continue;
@@ -206,17 +243,28 @@ int run_main_loop(ControlBlock* ctrl, Command* ring, int capacity, int ops_per_t
       for (const DrainedCmd& c : cmds)
         if (c.op_type == kOpSetSampling) h.on_sampling(c);
       if (op == kOpSetSampling) {
-        signal_done(ctrl);
+        host_signal();
         continue;
       }
       bad.clear();
       h.validate(op, layer, cmds, &bad);
       if (!bad.empty()) evict_slots(ctrl, bad, active);
-      const int st = h.round(op, layer, cmds, bad);
-      signal_done(ctrl);
-      if (st != 0) return st;  // device state is unknown; stop like the reference does
+      int st;
+      if (h.deferred_epoch()) {
+        clear_ready(ctrl);
+        st = h.round(op, layer, cmds, bad, ++handed);
+        if (st != 0) {
+          host_signal();  // publish what the failed round would have, so no worker waits on it
+          return st;
+        }
+      } else {
+        st = h.round(op, layer, cmds, bad, 0);
+        signal_done(ctrl);
+        if (st != 0) return st;  // device state is unknown; stop like the reference does
+      }
     }
   }
+  h.flush();
   return 0;
 }
 

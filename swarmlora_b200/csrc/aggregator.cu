@@ -19,6 +19,7 @@
 #include <sys/mman.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <array>
 #include <chrono>
 #include <cstring>
@@ -45,6 +46,10 @@ struct Slot {
   void* out = nullptr;
   cudaIpcMemHandle_t in_handle;
   cudaIpcMemHandle_t out_handle;
+  // event completion: the worker's event recorded after the work that
+  // writes the slot's round input (opened from an IPC handle: owned here)
+  cudaEvent_t input_event = nullptr;
+  bool input_event_owned = false;
 };
 
 struct Pool {
@@ -445,6 +450,9 @@ SWL_EXPORT int swl_agg_release_slot(int slot_id, int worker_id) {
   cudaError_t e = cudaStreamSynchronize(st);
   cudaStreamDestroy(st);
   if (e != cudaSuccess) return set_error(SWL_ERR_CUDA, "release_slot: %s", cudaGetErrorString(e));
+  if (s.input_event && s.input_event_owned) cudaEventDestroy(s.input_event);
+  s.input_event = nullptr;
+  s.input_event_owned = false;
   g_pool.free_w[slot_id >> 6].fetch_or(1ull << (slot_id & 63), std::memory_order_release);
   g_pool.active_w[slot_id >> 6].fetch_and(~(1ull << (slot_id & 63)), std::memory_order_release);
   return SWL_OK;
@@ -496,6 +504,9 @@ SWL_EXPORT int swl_agg_cleanup_slot_pool(void) {
     if (s.in) cudaFree(s.in);
     if (s.out) cudaFree(s.out);
     s.in = s.out = nullptr;
+    if (s.input_event && s.input_event_owned) cudaEventDestroy(s.input_event);
+    s.input_event = nullptr;
+    s.input_event_owned = false;
     s.owner.store(-1);
   }
   g_pool.initialized = false;
@@ -834,6 +845,153 @@ SWL_EXPORT int swl_agg_import_weights(const swl_weight_ipc* recs, int count, con
   return SWL_OK;
 }
 
+// ===== device-published round completion =======================================
+//
+// Completion mode 0 (the reference, ext_aggregator.cpp:1196-1202): after a
+// round's launches the main loop synchronizes the stream, then bumps the
+// epoch on the host. Mode 1: the control block is registered with CUDA as
+// mapped host memory, and after the round's kernels the loop enqueues a
+// one-thread kernel that stores the round's epoch into barrier_done_epoch;
+// the loop does not wait, so the workers see the epoch as soon as the round
+// has finished on the GPU while the host already waits for the next round's
+// ready bits (agg_protocol.h, deferred completion).
+namespace {
+int g_completion_mode = 0;
+void* g_ctrl_registered = nullptr;  // the mapping registered with cudaHostRegister
+size_t g_ctrl_registered_bytes = 0;
+int64_t* g_epoch_dev = nullptr;     // device address of barrier_done_epoch
+
+// Launched in stream order without programmatic serialization: it starts
+// after every earlier kernel on the stream has completed.
+__global__ void publish_epoch_kernel(int64_t* epoch, int64_t value) {
+  __threadfence_system();
+  asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(epoch), "l"(value) : "memory");
+}
+
+void unregister_ctrl() {
+  if (g_ctrl_registered) {
+    cudaHostUnregister(g_ctrl_registered);
+    cudaGetLastError();
+  }
+  g_ctrl_registered = nullptr;
+  g_ctrl_registered_bytes = 0;
+  g_epoch_dev = nullptr;
+}
+
+int register_ctrl() {
+  if (!g_ctrl) return set_error(SWL_ERR_STATE, "completion mode: aggregator queue not initialized");
+  if (g_ctrl_registered == g_ctrl && g_epoch_dev) return SWL_OK;
+  unregister_ctrl();
+  SWL_CUDA_TRY(cudaSetDevice(g_device));
+  const size_t page = static_cast<size_t>(sysconf(_SC_PAGESIZE));
+  const size_t len = (g_map_bytes + page - 1) / page * page;  // the mapping starts on a page
+  cudaError_t e = cudaHostRegister(g_ctrl, len, cudaHostRegisterMapped | cudaHostRegisterPortable);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(SWL_ERR_CUDA, "completion mode: registering the control block failed: %s",
+                     cudaGetErrorString(e));
+  }
+  void* d = nullptr;
+  e = cudaHostGetDevicePointer(&d, &g_ctrl->barrier_done_epoch, 0);
+  if (e != cudaSuccess || !d) {
+    cudaHostUnregister(g_ctrl);
+    cudaGetLastError();
+    return set_error(SWL_ERR_CUDA, "completion mode: no device address for the control block: %s",
+                     cudaGetErrorString(e));
+  }
+  g_ctrl_registered = g_ctrl;
+  g_ctrl_registered_bytes = len;
+  g_epoch_dev = static_cast<int64_t*>(d);
+  return SWL_OK;
+}
+}  // namespace
+
+// Event completion (mode 2). Every slot's worker records a CUDA event after
+// the work that writes the slot's round input and only then sets its ready
+// bit; the round's stream waits for those events, the round's kernels are
+// enqueued, the round event is recorded after them, and the host bumps the
+// epoch at once. A worker that sees the epoch makes its stream wait for the
+// round event before it reads the outputs. Neither side's host waits for the
+// GPU; the GPU orders the work by stream-level event dependencies. Only for
+// workers that follow this (swl_wc_* clients, or a worker that registers
+// its input event and waits for the round event).
+namespace {
+cudaEvent_t g_round_event = nullptr;
+
+int ensure_round_event() {
+  if (g_round_event) return SWL_OK;
+  SWL_CUDA_TRY(cudaSetDevice(g_device));
+  SWL_CUDA_TRY(cudaEventCreateWithFlags(&g_round_event, cudaEventDisableTiming | cudaEventInterprocess));
+  return SWL_OK;
+}
+
+int slot_for_event(int slot_id, Slot** out) {
+  if (!g_pool.initialized || slot_id < 0 || slot_id >= g_pool.num_slots)
+    return set_error(SWL_ERR_ARG, "input event: invalid slot %d", slot_id);
+  *out = &g_pool.slots[slot_id];
+  if ((*out)->input_event && (*out)->input_event_owned) cudaEventDestroy((*out)->input_event);
+  (*out)->input_event = nullptr;
+  (*out)->input_event_owned = false;
+  return SWL_OK;
+}
+}  // namespace
+
+// The round event's IPC handle (64 bytes), for workers in other processes
+// (cudaIpcOpenEventHandle).
+SWL_EXPORT int swl_agg_round_event_handle(unsigned char* out, size_t len) {
+  if (!out || len < sizeof(cudaIpcEventHandle_t)) return set_error(SWL_ERR_ARG, "round event: 64-byte buffer needed");
+  SWL_TRY(ensure_round_event());
+  cudaIpcEventHandle_t h;
+  SWL_CUDA_TRY(cudaIpcGetEventHandle(&h, g_round_event));
+  memcpy(out, &h, sizeof(h));
+  return SWL_OK;
+}
+
+// The round event itself (cudaEvent_t), for workers in this process.
+SWL_EXPORT int swl_agg_round_event(void** event) {
+  if (!event) return set_error(SWL_ERR_ARG, "round event: null pointer");
+  SWL_TRY(ensure_round_event());
+  *event = g_round_event;
+  return SWL_OK;
+}
+
+// A slot's input event from its worker's IPC handle (a worker in another
+// process), or (len 0, handle NULL) none.
+SWL_EXPORT int swl_agg_set_slot_input_event(int slot_id, const unsigned char* handle, size_t len) {
+  Slot* s = nullptr;
+  SWL_TRY(slot_for_event(slot_id, &s));
+  if (!handle || len == 0) return SWL_OK;
+  if (len != sizeof(cudaIpcEventHandle_t)) return set_error(SWL_ERR_ARG, "input event: handle of 64 bytes expected");
+  cudaIpcEventHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  SWL_CUDA_TRY(cudaSetDevice(g_device));
+  SWL_CUDA_TRY(cudaIpcOpenEventHandle(&s->input_event, h));
+  s->input_event_owned = true;
+  return SWL_OK;
+}
+
+// A slot's input event created in this process (not owned; NULL = none).
+SWL_EXPORT int swl_agg_set_slot_input_event_local(int slot_id, void* event) {
+  Slot* s = nullptr;
+  SWL_TRY(slot_for_event(slot_id, &s));
+  s->input_event = static_cast<cudaEvent_t>(event);
+  return SWL_OK;
+}
+
+// 0: the host signals each round after a stream sync (the reference);
+// 1: the device publishes each round's epoch (needs the queue mapped by
+// swl_agg_init_queue; registers it); 2: event completion (above). Takes
+// effect at the next main loop.
+SWL_EXPORT int swl_agg_set_completion_mode(int mode) {
+  if (mode < 0 || mode > 2) return set_error(SWL_ERR_ARG, "completion mode must be 0, 1 or 2");
+  if (mode == 1) SWL_TRY(register_ctrl());
+  if (mode == 2) SWL_TRY(ensure_round_event());
+  g_completion_mode = mode;
+  return SWL_OK;
+}
+
+SWL_EXPORT int swl_agg_completion_mode(void) { return g_completion_mode; }
+
 // ext_aggregator.cpp:427-459 init_aggregator_queue: map the queue segment
 // created by ext_ipc_queue.create_queue (this module's own view).
 SWL_EXPORT int swl_agg_init_queue(const char* shm_name, int capacity) {
@@ -845,6 +1003,8 @@ SWL_EXPORT int swl_agg_init_queue(const char* shm_name, int capacity) {
   void* p = mmap(nullptr, bytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
   close(fd);
   if (p == MAP_FAILED) return set_error(SWL_ERR_SYS, "Failed to mmap shared memory");
+  unregister_ctrl();
+  g_completion_mode = 0;  // a new segment starts with host completion
   if (g_ctrl) munmap(g_ctrl, g_map_bytes);
   g_ctrl = static_cast<ControlBlock*>(p);
   g_ring = reinterpret_cast<Command*>(static_cast<char*>(p) + sizeof(ControlBlock));
@@ -1170,10 +1330,54 @@ struct AggHooks {
     std::string why;
     ::validate(all.data(), static_cast<int>(all.size()), in_row, out_row, &good, bad, &why);
     if (!why.empty()) fprintf(stderr, "[swl aggregator] dropping commands: %s\n", why.c_str());
+    if (g_completion_mode == 2) {
+      // event completion reads a slot's input only after its worker's event;
+      // a slot without one cannot be ordered, so its command is refused
+      size_t k = 0;
+      for (const RoundCmd& c : good) {
+        if (g_pool.slots[c.slot_id].input_event) {
+          good[k++] = c;
+        } else {
+          bad->push_back(c.slot_id);
+          fprintf(stderr, "[swl aggregator] slot %d has no input event under event completion; evicted\n",
+                  c.slot_id);
+        }
+      }
+      good.resize(k);
+    }
   }
-  int round(int op, int layer, const std::vector<DrainedCmd>&, const std::vector<int>&) {
+  bool deferred = false;  // device-published completion (mode 1)
+  bool events = false;    // event completion (mode 2)
+  std::vector<cudaEvent_t> waits;
+  bool deferred_epoch() const { return deferred; }
+  void flush() {
+    if (deferred || events) cudaStreamSynchronize(g_stream);
+  }
+  int round(int op, int layer, const std::vector<DrainedCmd>&, const std::vector<int>&, int64_t epoch) {
+    if (events) {
+      waits.clear();
+      for (const RoundCmd& c : good) {
+        cudaEvent_t e = g_pool.slots[c.slot_id].input_event;
+        if (std::find(waits.begin(), waits.end(), e) == waits.end()) waits.push_back(e);
+      }
+      for (cudaEvent_t e : waits) {
+        const cudaError_t err = cudaStreamWaitEvent(g_stream, e, 0);
+        if (err != cudaSuccess) {
+          set_error(SWL_ERR_CUDA, "round: waiting for a worker's input event: %s", cudaGetErrorString(err));
+          fprintf(stderr, "[swl aggregator] %s\n", last_error());
+          return SWL_ERR_CUDA;
+        }
+      }
+    }
     int st = run_round(op, layer, good, g_stream);
-    if (st == SWL_OK) {
+    if (st == SWL_OK && events) {
+      const cudaError_t e = cudaEventRecord(g_round_event, g_stream);
+      if (e != cudaSuccess) st = set_error(SWL_ERR_CUDA, "round: recording the round event: %s", cudaGetErrorString(e));
+    } else if (st == SWL_OK && deferred) {
+      publish_epoch_kernel<<<1, 1, 0, g_stream>>>(g_epoch_dev, epoch);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) st = set_error(SWL_ERR_CUDA, "round: publishing the epoch: %s", cudaGetErrorString(e));
+    } else if (st == SWL_OK) {
       cudaError_t e = cudaStreamSynchronize(g_stream);
       if (e != cudaSuccess) st = set_error(SWL_ERR_CUDA, "round: %s", cudaGetErrorString(e));
     }
@@ -1196,5 +1400,17 @@ SWL_EXPORT int swl_agg_main_loop_slots(int num_slots, int dtype_code) {
   SWL_CUDA_TRY(cudaSetDevice(g_device));
   SWL_TRY(ensure_stream());
   AggHooks hooks;
-  return run_main_loop(g_ctrl, g_ring, g_capacity, 1 + g_num_layers * 4 + 1, hooks);
+  if (g_completion_mode == 1) {
+    SWL_TRY(register_ctrl());
+    hooks.deferred = true;
+  } else if (g_completion_mode == 2) {
+    SWL_TRY(ensure_round_event());
+    hooks.events = true;
+  }
+  const int st = run_main_loop(g_ctrl, g_ring, g_capacity, 1 + g_num_layers * 4 + 1, hooks);
+  if (st == SWL_OK && (hooks.deferred || hooks.events)) {
+    cudaError_t e = cudaStreamSynchronize(g_stream);
+    if (e != cudaSuccess) return set_error(SWL_ERR_CUDA, "main loop: %s", cudaGetErrorString(e));
+  }
+  return st;
 }

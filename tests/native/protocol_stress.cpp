@@ -9,7 +9,11 @@
 // Scenarios: workers joining at different times (half of them posting
 // sampling parameters first) and leaving after different token counts, one worker that stops mid-token (evicted by the barrier
 // timeout), one that submits a command under another worker's id (evicted
-// by validation). Exit status 0 and "protocol stress ok" on success.
+// by validation). With --deferred the rounds complete the way the library's
+// device-published completion does: the loop clears the ready state, hands
+// the round's epoch to a publisher thread (standing in for the device) and
+// goes on; the publisher stores it after a short random delay. Exit status
+// 0 and "protocol stress ok" on success.
 #include <signal.h>
 #include <sys/mman.h>
 #include <sys/wait.h>
@@ -17,6 +21,9 @@
 
 #include <atomic>
 #include <chrono>
+#include <condition_variable>
+#include <deque>
+#include <mutex>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -89,9 +96,66 @@ bool is_evicted(int s) { return swl_q_is_slot_evicted(s) == 1; }
 
 std::atomic<int> g_sampling_taken{0};
 
+// Stores handed-out epochs into the control block after a short delay, in
+// order, as the device does after a round's kernels.
+struct Publisher {
+  ControlBlock* ctrl = nullptr;
+  std::mutex mu;
+  std::condition_variable cv;
+  std::deque<int64_t> todo;
+  int64_t stored = 0;
+  bool stop = false;
+  std::thread th;
+  void start(ControlBlock* c) {
+    ctrl = c;
+    stored = c->barrier_done_epoch.load();
+    th = std::thread([this] { run(); });
+  }
+  void run() {
+    unsigned seed = 12345;
+    std::unique_lock<std::mutex> lk(mu);
+    for (;;) {
+      cv.wait(lk, [this] { return stop || !todo.empty(); });
+      if (todo.empty()) return;
+      const int64_t v = todo.front();
+      lk.unlock();
+      seed = seed * 1103515245u + 12345u;
+      std::this_thread::sleep_for(std::chrono::microseconds((seed >> 16) % 50));
+      ctrl->barrier_done_epoch.store(v, std::memory_order_release);
+      lk.lock();
+      todo.pop_front();
+      stored = v;
+      cv.notify_all();
+    }
+  }
+  void publish(int64_t v) {
+    std::lock_guard<std::mutex> lk(mu);
+    if (v <= stored || (!todo.empty() && v <= todo.back())) fail("epochs handed out of order", -1);
+    todo.push_back(v);
+    cv.notify_all();
+  }
+  void flush() {
+    std::unique_lock<std::mutex> lk(mu);
+    cv.wait(lk, [this] { return todo.empty(); });
+  }
+  void finish() {
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      stop = true;
+      cv.notify_all();
+    }
+    th.join();
+  }
+};
+
 struct HostHooks {
   std::vector<int> owner;  // slot -> worker id
   ControlBlock* ctrl = nullptr;
+  Publisher* pub = nullptr;  // deferred completion
+  bool deferred_epoch() const { return pub != nullptr; }
+  void flush() {
+    if (pub) pub->flush();
+  }
   void on_membership(const Mask128&, const Mask128& joins) {
     take_pending_sampling(ctrl, joins, [](int sid, const PendingSampling& p) {
       // the joining worker posted temperature 0.5 + slot and top_k = slot
@@ -105,7 +169,10 @@ struct HostHooks {
     for (const DrainedCmd& c : cmds)
       if (c.worker_id != owner[c.slot_id] || c.rows != 1) bad->push_back(c.slot_id);
   }
-  int round(int op, int layer, const std::vector<DrainedCmd>& cmds, const std::vector<int>& bad) {
+  int round(int op, int layer, const std::vector<DrainedCmd>& cmds, const std::vector<int>& bad, int64_t epoch) {
+    if (pub && !ctrl->per_slot_ready_mask.load().empty() &&
+        !(ctrl->per_slot_ready_mask.load() & ctrl->active_slot_mask.load()).empty())
+      fail("ready bits of the round still set when it runs", -1);
     for (const DrainedCmd& c : cmds) {
       if (c.op_type != op || c.layer_idx != layer) fail("round mixes ops", c.slot_id);
       bool refused = false;
@@ -115,6 +182,7 @@ struct HostHooks {
       g_out[c.slot_id] = c.x_key + 1;
     }
     g_rounds.fetch_add(1);
+    if (pub) pub->publish(epoch);
     return 0;
   }
 };
@@ -208,6 +276,7 @@ int run_processes(ControlBlock* ctrl, Command* ring, HostHooks& hooks, const Pro
 
 int main(int argc, char** argv) {
   g_processes = argc > 1 && std::string(argv[1]) == "--processes";
+  const bool deferred = argc > 1 && std::string(argv[1]) == "--deferred";
   char name[128];
   if (swl_q_create(256, 256, name, sizeof(name)) != SWL_OK || swl_q_init_batch_control(kWorkers) != SWL_OK) {
     fprintf(stderr, "queue setup failed: %s\n", last_error());
@@ -227,6 +296,11 @@ int main(int argc, char** argv) {
     swl_q_close();
     return rc;
   }
+  Publisher pub;
+  if (deferred) {
+    pub.start(ctrl);
+    hooks.pub = &pub;
+  }
   int loop_status = -99;
   std::thread agg([&] { loop_status = run_main_loop(ctrl, ring, swl_q_capacity(), kOpsPerToken, hooks, times); });
   std::vector<std::thread> ws;
@@ -234,11 +308,16 @@ int main(int argc, char** argv) {
   for (auto& w : ws) w.join();
   swl_q_set_quit(1);
   agg.join();
+  if (deferred) {
+    if (!pub.todo.empty()) fail("the loop returned with epochs still to store", -1);
+    pub.finish();
+  }
   swl_q_close();
   if (loop_status != 0) fail("main loop returned an error", -1);
   if (g_evicted_seen.load() != 2) fail("expected exactly the stalled and the rogue slot evicted", -1);
   if (g_sampling_taken.load() != (kWorkers + 1) / 2) fail("every posted sampling state taken once", -1);
   if (g_failures.load()) return 1;
-  printf("protocol stress ok: %d rounds, %d workers, 2 evicted\n", g_rounds.load(), kWorkers);
+  printf("protocol stress ok: %d rounds, %d workers, 2 evicted%s\n", g_rounds.load(), kWorkers,
+         deferred ? ", epochs published by a deferred publisher" : "");
   return 0;
 }
