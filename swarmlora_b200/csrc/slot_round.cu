@@ -18,6 +18,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -53,17 +54,24 @@ struct NoEpi {
   int unused;
 };
 
-template <int BN>
+// Tile of BN token rows and a ring of STAGES K-blocks (each a 128 x 64 W
+// tile and a BN x 64 token tile).
+template <int BN, int STAGES>
 struct TcCfg {
-  static constexpr int kStages = BN == 32 ? 4 : (BN == 64 ? 4 : (BN == 128 ? 6 : 4));
+  static constexpr int kStages = STAGES;
   static constexpr int kXStageBytes = BN * 128;
   static constexpr int kPipeBytes = kStages * (kWStageBytes + kXStageBytes);
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kPipeBytes + 256 + BN * 24;
   // per-row tables of the fused QKV/RoPE epilogue: slot, position, page, t[32]
   static constexpr int kRopeBytes = BN * (3 * 4 + 32 * 4);
-  static constexpr int kTmemCols = BN;
+  // TMEM columns are allocated in powers of two, at least 32
+  static constexpr int kTmemCols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "MMA N of a 128-row tile: 16..256 in steps of 16");
   static_assert(BN * kBlockW * 4 <= kPipeBytes, "epilogue tile must fit in pipeline smem");
 };
+
+// Launch-time flags of the tensor-core round.
+constexpr int kFlagGatherSpin = 1;  // gather warps poll the free-stage barrier without sleeping
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
@@ -103,15 +111,14 @@ __device__ __forceinline__ int slot_of_row(const SlotTable& tab, int gr) {
   return lo;
 }
 
-template <int BN, class Ex>
+template <int BN, int STAGES, class Ex>
 __global__ void __launch_bounds__(kThreads, 1)
     slot_round_tc_kernel(const __grid_constant__ CUtensorMap wmap,
                          const __grid_constant__ SlotTable tab, const RoundShape shape,
-                         int splits, const __grid_constant__ Ex ex) {
+                         int splits, int flags, const __grid_constant__ Ex ex) {
   constexpr bool kShard = std::is_same<Ex, ShardArgs>::value;
   constexpr bool kRope = std::is_same<Ex, QkvRopeEpi>::value;
-  using Cfg = TcCfg<BN>;
-  constexpr int STAGES = Cfg::kStages;
+  using Cfg = TcCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -253,7 +260,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < nk; ++i) {
       const int s = i % STAGES;
       const uint32_t ph = (i / STAGES) & 1;
-      if (!ptx::mbar_wait_sleep(&empty[s], ph ^ 1, err, kErrWaitEmptyX, kWaitTimeoutNs, 64)) break;
+      const bool freed = (flags & kFlagGatherSpin)
+                             ? ptx::mbar_wait(&empty[s], ph ^ 1, err, kErrWaitEmptyX, kWaitTimeoutNs)
+                             : ptx::mbar_wait_sleep(&empty[s], ph ^ 1, err, kErrWaitEmptyX, kWaitTimeoutNs, 64);
+      if (!freed) break;
       const int64_t k0 = static_cast<int64_t>(kb_begin + i) * kBlockK;
       const uint32_t xs = ptx::smem_addr(x_st + s * Cfg::kXStageBytes);
       for (int c = t; c < BN * 8; c += kGatherThreads) {
@@ -510,16 +520,21 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-template <int BN, class Ex>
+// Tuning of the tensor-core round (swl_round_tune): the tile used for 65..128
+// token rows, and the launch flags.
+std::atomic<int> g_tile_variant{0};
+std::atomic<int> g_round_flags{0};
+
+template <int BN, int STAGES, class Ex>
 int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& map, int splits,
               const Ex& ex, cudaStream_t stream) {
-  using Cfg = TcCfg<BN>;
+  using Cfg = TcCfg<BN, STAGES>;
   constexpr bool kShard = std::is_same<Ex, ShardArgs>::value;
   constexpr int smem_bytes = Cfg::kSmemBytes + (std::is_same<Ex, QkvRopeEpi>::value ? Cfg::kRopeBytes : 0);
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(slot_round_tc_kernel<BN, Ex>,
+    attr_err = cudaFuncSetAttribute(slot_round_tc_kernel<BN, STAGES, Ex>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   });
   if (attr_err != cudaSuccess)
@@ -533,7 +548,8 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
     // Largest power-of-two cluster (<= 8) that keeps the grid within the
     // resident CTA capacity and at least 8 K-blocks per split. Clusters whose
     // size does not divide the SMs of a GPC (3, 5, 6) schedule poorly.
-    const int per_sm = BN <= 64 ? 2 : 1;
+    // resident CTAs per SM by shared memory (228 KB per SM, 1 KB reserved per CTA), at most 2
+    const int per_sm = std::max(1, std::min(2, (228 * 1024) / (smem_bytes + 1024)));
     const int cap = sm_count() * per_sm;
     const int base = std::max(1, n_tiles * m_chunks);
     splits = 1;
@@ -542,11 +558,33 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
   }
   splits = std::max(1, std::min(splits, std::min(8, nkb)));
 
-  SWL_CUDA_TRY(launch_kernel(slot_round_tc_kernel<BN, Ex>,
+  SWL_CUDA_TRY(launch_kernel(slot_round_tc_kernel<BN, STAGES, Ex>,
                              dim3(static_cast<unsigned>(n_tiles * splits), static_cast<unsigned>(m_chunks), 1),
                              dim3(kThreads, 1, 1), smem_bytes, stream, static_cast<unsigned>(splits),
-                             map, tab, shape, splits, ex));
+                             map, tab, shape, splits, g_round_flags.load(std::memory_order_relaxed), ex));
   return SWL_OK;
+}
+
+// The tile for a round of m token rows: 32 or 64 rows (4-stage rings, two
+// CTAs per SM); 65..128 rows by the tuning (default 128 rows, 6 stages, one
+// CTA per SM); above 128, 256-row chunks.
+template <class Ex>
+int launch_tc_any(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& map, int splits,
+                  const Ex& ex, cudaStream_t stream) {
+  const int m = std::max(1, tab.total_rows);
+  if (m <= 32) return launch_tc<32, 4>(tab, shape, map, splits, ex, stream);
+  if (m <= 64) return launch_tc<64, 4>(tab, shape, map, splits, ex, stream);
+  if (m <= 128) {
+    switch (g_tile_variant.load(std::memory_order_relaxed)) {
+      case 1: if (m <= 96) return launch_tc<96, 3>(tab, shape, map, splits, ex, stream); break;
+      case 2: if (m <= 96) return launch_tc<96, 4>(tab, shape, map, splits, ex, stream); break;
+      case 3: return launch_tc<128, 3>(tab, shape, map, splits, ex, stream);
+      case 4: return launch_tc<128, 4>(tab, shape, map, splits, ex, stream);
+      default: break;
+    }
+    return launch_tc<128, 6>(tab, shape, map, splits, ex, stream);
+  }
+  return launch_tc<256, 4>(tab, shape, map, splits, ex, stream);
 }
 
 }  // namespace
@@ -593,10 +631,7 @@ int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void*
     return launch_slot_round_streamk(tab, shape, *tmap, stream);
   }
   const NoEpi none{0};
-  if (m <= 32) return launch_tc<32>(tab, shape, *tmap, splits, none, stream);
-  if (m <= 64) return launch_tc<64>(tab, shape, *tmap, splits, none, stream);
-  if (m <= 128) return launch_tc<128>(tab, shape, *tmap, splits, none, stream);
-  return launch_tc<256>(tab, shape, *tmap, splits, none, stream);
+  return launch_tc_any(tab, shape, *tmap, splits, none, stream);
 }
 
 int launch_slot_round_qkv_rope(const SlotTable& tab, const RoundShape& shape, const void* W,
@@ -624,8 +659,8 @@ int launch_slot_round_qkv_rope(const SlotTable& tab, const RoundShape& shape, co
     SWL_TRY(encode_weight_tmap(&local, W, shape.N, shape.K));
     tmap = &local;
   }
-  if (tab.total_rows <= 32) return launch_tc<32>(tab, shape, *tmap, splits, epi, stream);
-  return launch_tc<64>(tab, shape, *tmap, splits, epi, stream);
+  if (tab.total_rows <= 32) return launch_tc<32, 4>(tab, shape, *tmap, splits, epi, stream);
+  return launch_tc<64, 4>(tab, shape, *tmap, splits, epi, stream);
 }
 
 int launch_slot_round_shard(const SlotTable& tab, const RoundShape& shape, const void* W,
@@ -649,10 +684,8 @@ int launch_slot_round_shard(const SlotTable& tab, const RoundShape& shape, const
     SWL_TRY(encode_weight_tmap(&local, W, shape.N, shape.K));
     tmap = &local;
   }
-  if (m <= 32) return launch_tc<32>(tab, shape, *tmap, splits, sh, stream);
-  if (m <= 64) return launch_tc<64>(tab, shape, *tmap, splits, sh, stream);
-  if (m <= 128) return launch_tc<128>(tab, shape, *tmap, splits, sh, stream);
-  return launch_tc<256>(tab, shape, *tmap, splits, sh, stream);
+  (void)m;
+  return launch_tc_any(tab, shape, *tmap, splits, sh, stream);
 }
 
 int read_and_clear_device_error(unsigned int* code) {
@@ -711,6 +744,18 @@ SWL_EXPORT int swl_slot_gemm(const void* W, int64_t N, int64_t K, const void* bi
 SWL_EXPORT int swl_round_device_error(unsigned int* code) {
   if (!code) return set_error(SWL_ERR_ARG, "null code pointer");
   return read_and_clear_device_error(code);
+}
+
+// Tuning of the tensor-core round: tile_variant picks the tile for 65..128
+// token rows (0 default = 128 rows x 6 stages; 1 = 96 x 3 and 2 = 96 x 4 up
+// to 96 rows; 3 = 128 x 3; 4 = 128 x 4); flags bit 0 makes the gather warps
+// poll the free-stage barrier without sleeping.
+SWL_EXPORT int swl_round_tune(int tile_variant, int flags) {
+  if (tile_variant < 0 || tile_variant > 4 || (flags & ~kFlagGatherSpin))
+    return set_error(SWL_ERR_ARG, "round tuning: tile_variant 0..4, flags bit 0");
+  g_tile_variant.store(tile_variant);
+  g_round_flags.store(flags);
+  return SWL_OK;
 }
 
 // Tuning: persistent CTAs per SM of the stream-K round (1: 9-stage pipeline,
