@@ -321,11 +321,11 @@ int swl_round_device_error(unsigned int* code);
 /* Tuning of the stream-K round (algo 3). */
 int swl_round_set_streamk_ctas_per_sm(int n);
 int swl_round_set_streamk_ctas(int n);
-/* Tuning of the tensor-core round: the tile for 65..128 token rows
- * (0 = 128 rows x 6 stages; 1 / 2 = 96 rows x 3 / 4 stages up to 96 rows;
- * 3 / 4 = 128 rows x 3 / 4 stages) and flags (bit 0: the gather warps poll
- * without sleeping). */
-int swl_round_tune(int tile_variant, int flags);
+/* Tuning of the tensor-core round: rounds of up to max_rows token rows (32,
+ * 64, 96, 128; 0 = above 128) use a tile of bn rows with a ring of `stages`
+ * K-blocks (bn 0 = the default); flags bit 0: the gather warps poll without
+ * sleeping. */
+int swl_round_tune(int max_rows, int bn, int stages, int flags);
 
 /* LoRA shrink (model_builder.py:258-262 x @ fused_A; worker_sync.py:305/375
  * lora_A): ws[split][row][R] fp32 partials of x @ A, A[i] = [K, R] or NULL. */

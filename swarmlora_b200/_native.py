@@ -116,7 +116,7 @@ SIGNATURES: dict[str, tuple] = {
     "swl_round_device_error": (_i32, [_pu32]),
     "swl_round_set_streamk_ctas_per_sm": (_i32, [_i32]),
     "swl_round_set_streamk_ctas": (_i32, [_i32]),
-    "swl_round_tune": (_i32, [_i32, _i32]),
+    "swl_round_tune": (_i32, [_i32, _i32, _i32, _i32]),
     # ---- worker kernels
     "swl_lora_shrink": (_i32, [_i32, _pi32, _pp, _i64, _pp, _i64, _i32, _i32, _p, _p]),
     "swl_lora_expand": (_i32, [_i32, _pi32, _pp, _i64, _pp, _pp, _i64, _pp, _i64, _i64, _i32,

@@ -520,10 +520,25 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-// Tuning of the tensor-core round (swl_round_tune): the tile used for 65..128
-// token rows, and the launch flags.
-std::atomic<int> g_tile_variant{0};
+// Tuning of the tensor-core round (swl_round_tune): the (tile rows, stages)
+// used for each class of round row counts, and the launch flags.
+constexpr int kRowClasses = 5;                  // <= 32, <= 64, <= 96, <= 128, more
+constexpr int kClassRows[kRowClasses] = {32, 64, 96, 128, 1 << 30};
+// Defaults from sweeps on B200 (CUDA graphs of launches over weights beyond
+// L2): more CTA pipelines per SM beat deeper rings at the same bytes in flight.
+// Per class (32-row decode: 4 stages at 2 CTAs/SM; 96 and 128 rows: 3
+// stages at 2 CTAs/SM instead of 6 stages at one, M = 88 Gate+Up 103.7 ->
+// 53.0 us; above 128 rows 256-row chunks of 3 stages).
+constexpr int kDefaultTile[kRowClasses][2] = {{32, 4}, {64, 4}, {96, 3}, {128, 3}, {256, 3}};
+std::atomic<int> g_tile_bn[kRowClasses] = {{0}, {0}, {0}, {0}, {0}};
+std::atomic<int> g_tile_stages[kRowClasses] = {{0}, {0}, {0}, {0}, {0}};
 std::atomic<int> g_round_flags{0};
+
+int row_class(int m) {
+  int c = 0;
+  while (c < kRowClasses - 1 && m > kClassRows[c]) ++c;
+  return c;
+}
 
 template <int BN, int STAGES, class Ex>
 int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& map, int splits,
@@ -548,8 +563,8 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
     // Largest power-of-two cluster (<= 8) that keeps the grid within the
     // resident CTA capacity and at least 8 K-blocks per split. Clusters whose
     // size does not divide the SMs of a GPC (3, 5, 6) schedule poorly.
-    // resident CTAs per SM by shared memory (228 KB per SM, 1 KB reserved per CTA), at most 2
-    const int per_sm = std::max(1, std::min(2, (228 * 1024) / (smem_bytes + 1024)));
+    // resident CTAs per SM by shared memory (228 KB per SM, 1 KB reserved per CTA), at most 4
+    const int per_sm = std::max(1, std::min(4, (228 * 1024) / (smem_bytes + 1024)));
     const int cap = sm_count() * per_sm;
     const int base = std::max(1, n_tiles * m_chunks);
     splits = 1;
@@ -565,26 +580,36 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
   return SWL_OK;
 }
 
-// The tile for a round of m token rows: 32 or 64 rows (4-stage rings, two
-// CTAs per SM); 65..128 rows by the tuning (default 128 rows, 6 stages, one
-// CTA per SM); above 128, 256-row chunks.
+// Supported (tile rows, stages) pairs; the tile must cover the round's rows
+// (rows above a tile of 256 are split into 256-row chunks).
+#define SWL_ROUND_TILES(X) \
+  X(32, 2) X(32, 3) X(32, 4) X(64, 2) X(64, 3) X(64, 4) X(96, 2) X(96, 3) X(96, 4) X(128, 2) X(128, 3) \
+  X(128, 4) X(128, 6) X(256, 3) X(256, 4)
+
+bool tile_supported(int bn, int stages) {
+#define SWL_TILE_CASE(B, S) if (bn == B && stages == S) return true;
+  SWL_ROUND_TILES(SWL_TILE_CASE)
+#undef SWL_TILE_CASE
+  return false;
+}
+
+// The tile for a round of m token rows: the tuned (or default) pair of its
+// row class.
 template <class Ex>
 int launch_tc_any(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& map, int splits,
                   const Ex& ex, cudaStream_t stream) {
   const int m = std::max(1, tab.total_rows);
-  if (m <= 32) return launch_tc<32, 4>(tab, shape, map, splits, ex, stream);
-  if (m <= 64) return launch_tc<64, 4>(tab, shape, map, splits, ex, stream);
-  if (m <= 128) {
-    switch (g_tile_variant.load(std::memory_order_relaxed)) {
-      case 1: if (m <= 96) return launch_tc<96, 3>(tab, shape, map, splits, ex, stream); break;
-      case 2: if (m <= 96) return launch_tc<96, 4>(tab, shape, map, splits, ex, stream); break;
-      case 3: return launch_tc<128, 3>(tab, shape, map, splits, ex, stream);
-      case 4: return launch_tc<128, 4>(tab, shape, map, splits, ex, stream);
-      default: break;
-    }
-    return launch_tc<128, 6>(tab, shape, map, splits, ex, stream);
+  const int c = row_class(m);
+  int bn = g_tile_bn[c].load(std::memory_order_relaxed), stages = g_tile_stages[c].load(std::memory_order_relaxed);
+  if (bn == 0 || (bn < m && bn < 256)) {
+    bn = kDefaultTile[c][0];
+    stages = kDefaultTile[c][1];
   }
-  return launch_tc<256, 4>(tab, shape, map, splits, ex, stream);
+#define SWL_TILE_CASE(B, S) \
+  if (bn == B && stages == S) return launch_tc<B, S>(tab, shape, map, splits, ex, stream);
+  SWL_ROUND_TILES(SWL_TILE_CASE)
+#undef SWL_TILE_CASE
+  return set_error(SWL_ERR_ARG, "slot round: no tile %d x %d stages", bn, stages);
 }
 
 }  // namespace
@@ -746,14 +771,24 @@ SWL_EXPORT int swl_round_device_error(unsigned int* code) {
   return read_and_clear_device_error(code);
 }
 
-// Tuning of the tensor-core round: tile_variant picks the tile for 65..128
-// token rows (0 default = 128 rows x 6 stages; 1 = 96 x 3 and 2 = 96 x 4 up
-// to 96 rows; 3 = 128 x 3; 4 = 128 x 4); flags bit 0 makes the gather warps
-// poll the free-stage barrier without sleeping.
-SWL_EXPORT int swl_round_tune(int tile_variant, int flags) {
-  if (tile_variant < 0 || tile_variant > 4 || (flags & ~kFlagGatherSpin))
-    return set_error(SWL_ERR_ARG, "round tuning: tile_variant 0..4, flags bit 0");
-  g_tile_variant.store(tile_variant);
+// Tuning of the tensor-core round: for rounds of up to `max_rows` token rows
+// (32, 64, 96, 128, or 0 = above 128), tile `bn` rows with a ring of
+// `stages` K-blocks (bn = 0 restores the default of that class; the tile
+// must hold the class's rows, except 256-row chunks above 128). flags bit 0
+// makes the gather warps poll the free-stage barrier without sleeping.
+SWL_EXPORT int swl_round_tune(int max_rows, int bn, int stages, int flags) {
+  int c = -1;
+  for (int i = 0; i < kRowClasses - 1; ++i)
+    if (max_rows == kClassRows[i]) c = i;
+  if (max_rows == 0) c = kRowClasses - 1;
+  if (c < 0) return set_error(SWL_ERR_ARG, "round tuning: max_rows 32, 64, 96, 128 or 0");
+  if (flags & ~kFlagGatherSpin) return set_error(SWL_ERR_ARG, "round tuning: flags bit 0 only");
+  if (bn != 0 && (!tile_supported(bn, stages) || (c < kRowClasses - 1 && bn < kClassRows[c]) ||
+                  (c == kRowClasses - 1 && bn != 256)))
+    return set_error(SWL_ERR_ARG, "round tuning: tile %d x %d stages not built or too small for %d rows", bn,
+                     stages, max_rows);
+  g_tile_bn[c].store(bn);
+  g_tile_stages[c].store(bn ? stages : 0);
   g_round_flags.store(flags);
   return SWL_OK;
 }
