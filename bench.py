@@ -69,6 +69,8 @@ def parse():
                     help="round kernel for --profile-round: 0 auto, 1 cluster split-K, 3 stream-K")
     ap.add_argument("--attn-chunk-pages", type=int, default=0, help="attention pages per chunk (0 = auto)")
     ap.add_argument("--attn-stages", type=int, default=0, help="attention page-ring depth 2..4 (0 = auto)")
+    ap.add_argument("--attn-groups", type=int, default=0,
+                    help="attention kv head groups 1/2/4/8: CTAs sharing one page's heads (0 = auto)")
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch every kernel fully serialized (no programmatic dependent launch)")
     ap.add_argument("--churn", type=float, default=0.0, metavar="SECONDS",
@@ -436,7 +438,7 @@ def our_arm(args):
     import swarmlora_b200
     swarmlora_b200.set_pdl(not args.no_pdl)
     from swarmlora_b200 import worker_ops as _wo
-    _wo.attention_tune(args.attn_chunk_pages, args.attn_stages)
+    _wo.attention_tune(args.attn_chunk_pages, args.attn_stages, args.attn_groups)
     if args.checkpoint:
         from swarmlora_b200.checkpoint import load_base
         base, cfg = load_base(args.checkpoint, dev)
@@ -614,7 +616,7 @@ def profile_attention(args):
     import torch
     from swarmlora_b200 import worker_ops as wo
     from swarmlora_b200.engine import LLAMA_3_1_8B as cfg
-    wo.attention_tune(args.attn_chunk_pages, args.attn_stages)
+    wo.attention_tune(args.attn_chunk_pages, args.attn_stages, args.attn_groups)
     dev = torch.device("cuda:0")
     n = args.slots
     g = torch.Generator(device=dev).manual_seed(0)

@@ -324,7 +324,10 @@ int swl_round_set_streamk_ctas(int n);
 /* Tuning of the tensor-core round: rounds of up to max_rows token rows (32,
  * 64, 96, 128; 0 = above 128) use a tile of bn rows with a ring of `stages`
  * K-blocks (bn 0 = the default); flags bit 0: the gather warps poll without
- * sleeping. */
+ * sleeping; bit 1: split-K sums reduced through a per-device global-memory
+ * workspace instead of across a thread-block cluster (then rounds with
+ * split-K on one device share that workspace and must run in stream order,
+ * never concurrently). */
 int swl_round_tune(int max_rows, int bn, int stages, int flags);
 
 /* LoRA shrink (model_builder.py:258-262 x @ fused_A; worker_sync.py:305/375
@@ -344,9 +347,11 @@ int swl_rope_append(int nseg, const int* rows, const void* const* qkv, int64_t q
                     const void* const* block_tables, void* const* k_cache, void* const* v_cache,
                     const void* const* seqlens, int hq, int hkv, int head_dim, int page,
                     const void* cos_sin, int max_pos, void* q_rot, void* stream);
-/* Tuning of the attention launch: pages per context chunk and page-ring
- * depth (2..4); 0 = automatic. A launch option, no counterpart in the reference. */
-int swl_attention_tune(int chunk_pages, int stages);
+/* Tuning of the attention launch: pages per context chunk, page-ring depth
+ * (2..4) and kv head groups (1, 2, 4, 8: CTAs that share one page's heads,
+ * each holding its group's slices); 0 = automatic. A launch option, no
+ * counterpart in the reference. */
+int swl_attention_tune(int chunk_pages, int stages, int groups);
 /* fp32 scratch floats swl_paged_attention needs in `part`. */
 int64_t swl_attention_part_floats(int total_rows, int hq, int hkv, int max_len);
 /* Causal GQA attention over paged KV (flash_attn_with_kvcache semantics,

@@ -71,7 +71,8 @@ struct TcCfg {
 };
 
 // Launch-time flags of the tensor-core round.
-constexpr int kFlagGatherSpin = 1;  // gather warps poll the free-stage barrier without sleeping
+constexpr int kFlagGatherSpin = 1;    // gather warps poll the free-stage barrier without sleeping
+constexpr int kFlagGlobalSplit = 2;   // split-K reduced through global memory instead of across a cluster
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
@@ -115,7 +116,7 @@ template <int BN, int STAGES, class Ex>
 __global__ void __launch_bounds__(kThreads, 1)
     slot_round_tc_kernel(const __grid_constant__ CUtensorMap wmap,
                          const __grid_constant__ SlotTable tab, const RoundShape shape,
-                         int splits, int flags, const __grid_constant__ Ex ex) {
+                         int splits, int flags, const SplitWs sws, const __grid_constant__ Ex ex) {
   constexpr bool kShard = std::is_same<Ex, ShardArgs>::value;
   constexpr bool kRope = std::is_same<Ex, QkvRopeEpi>::value;
   using Cfg = TcCfg<BN, STAGES>;
@@ -136,9 +137,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* rope_page = rope_pos + BN;
   float* rope_t = reinterpret_cast<float*>(rope_page + BN);  // [BN][32]
   __shared__ int shard_ok;
+  __shared__ int split_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int rank = splits > 1 ? static_cast<int>(ptx::cluster_rank()) : 0;
+  // split-K across a cluster (DSMEM reduction) or through global memory
+  const bool gsplit = splits > 1 && sws.part != nullptr;
+  const bool csplit = splits > 1 && !gsplit;
+  const int rank = gsplit ? static_cast<int>(blockIdx.x) % splits
+                          : (splits > 1 ? static_cast<int>(ptx::cluster_rank()) : 0);
   const int n0 = (blockIdx.x / splits) * kBlockW;
   const int chunk_row0 = blockIdx.y * BN;
   const int chunk_rows = min(BN, tab.total_rows - chunk_row0);
@@ -334,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int e = tid; e < BN * kBlockW; e += kThreads) P[e] = 0.f;
   }
   ptx::tc_fence_before();
-  if (splits > 1) ptx::cluster_sync();
+  if (csplit) ptx::cluster_sync();
   else __syncthreads();
 
   // Sharded round: the peer may still read its previous round's outputs
@@ -347,9 +353,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   const uint32_t pbase = ptx::smem_addr(P);
+  // Split-K through global memory: this split's partial tile goes to the
+  // workspace; only the last split of the tile to arrive goes on, and it
+  // reads every split's partial (including its own) back from L2.
+  const int tile_id = static_cast<int>(blockIdx.y) * static_cast<int>(gridDim.x / splits) +
+                      static_cast<int>(blockIdx.x) / splits;
+  const float* gpart = gsplit ? sws.part + static_cast<int64_t>(tile_id) * splits * (BN * kBlockW) : nullptr;
+  bool emit = true;
+  if (gsplit) {
+    float4* mine = reinterpret_cast<float4*>(sws.part + (static_cast<int64_t>(tile_id) * splits + rank) *
+                                                            (BN * kBlockW));
+    const float4* src = reinterpret_cast<const float4*>(P);
+    for (int e = tid; e < chunk_rows * (kBlockW / 4); e += kThreads) mine[e] = src[e];
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) split_last = atomicAdd(sws.count + tile_id, 1) == splits - 1;
+    __syncthreads();
+    emit = split_last != 0;
+    __threadfence();
+  }
   // the K-split sum of the 4 outputs at (row r, column c) of the tile
   auto reduce4 = [&](int r, int c) -> float4 {
     const uint32_t off = static_cast<uint32_t>((r * kBlockW + c) * 4);
+    if (gsplit) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < splits; ++p) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(gpart + static_cast<int64_t>(p) * (BN * kBlockW) +
+                                                                 r * kBlockW + c));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      return acc;
+    }
     if (splits == 1) return *reinterpret_cast<const float4*>(P + r * kBlockW + c);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int p = 0; p < splits; ++p) {
@@ -407,29 +444,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
-  // Each CTA of the cluster reduces an equal share of the tile's 4-float groups.
-  const int groups = kRope ? 0 : chunk_rows * (kBlockW / 4);
-  const int g_begin = static_cast<int>(static_cast<int64_t>(rank) * groups / splits);
-  const int g_end = static_cast<int>(static_cast<int64_t>(rank + 1) * groups / splits);
+  // Each CTA of the cluster reduces an equal share of the tile's 4-float
+  // groups; through global memory the last split to arrive reduces them all.
+  const int groups = (kRope || !emit) ? 0 : chunk_rows * (kBlockW / 4);
+  const int g_begin = csplit ? static_cast<int>(static_cast<int64_t>(rank) * groups / splits) : 0;
+  const int g_end = csplit ? static_cast<int>(static_cast<int64_t>(rank + 1) * groups / splits) : groups;
   for (int g = g_begin + tid; g < g_end; g += kThreads) {
     const int r = g >> 5;
     const int c = (g & 31) * 4;
     const int64_t n = n0 + c;
     if (n >= shape.N) continue;
-    const uint32_t off = static_cast<uint32_t>((r * kBlockW + c) * 4);
-    float4 acc;
-    if (splits > 1) {
-      acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int p = 0; p < splits; ++p) {
-        const float4 v = ptx::ld_cluster_f4(ptx::map_peer(pbase + off, p));
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
-    } else {
-      acc = *reinterpret_cast<const float4*>(P + r * kBlockW + c);
-    }
+    float4 acc = reduce4(r, c);
     if (shape.bias) {
       acc.x += __bfloat162float(shape.bias[n]);
       acc.y += __bfloat162float(shape.bias[n + 1]);
@@ -445,16 +470,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (kShard && to_peer) *reinterpret_cast<uint2*>(row_peer[r] + n) = packed;
   }
 
+  // The tile's arrival counter starts at zero for the next launch (which, in
+  // stream order, reaches it only after this launch has completed).
+  if (gsplit && emit && tid == 0) sws.count[tile_id] = 0;
   // Done reading the peers' P; they may still read ours, so the CTA waits
   // for the whole cluster before it exits (TMEM was last read before the
   // barrier above, so it is released in between).
-  if (splits > 1) ptx::cluster_arrive();
+  if (csplit) ptx::cluster_arrive();
   else __syncthreads();
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, Cfg::kTmemCols);
   }
-  if (splits > 1) ptx::cluster_wait();
+  if (csplit) ptx::cluster_wait();
 
   if constexpr (kShard) {
     // Every thread's peer stores are visible system-wide before its CTA
@@ -573,10 +601,29 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
   }
   splits = std::max(1, std::min(splits, std::min(8, nkb)));
 
+  // Split-K through global memory when tuned on (not for the fused RoPE
+  // epilogue): no cluster, every CTA of the grid resident at once, but the
+  // last split of a tile reads all partials back alone; measured slower than
+  // the cluster reduction on the decode shapes (O at M = 28: 14.1 vs 10.3 us,
+  // Down 26.9 vs 23.5 us), so the cluster reduction is the default.
+  const int flags = g_round_flags.load(std::memory_order_relaxed);
+  SplitWs sws{nullptr, nullptr};
+  if (splits > 1 && !std::is_same<Ex, QkvRopeEpi>::value && (flags & kFlagGlobalSplit)) {
+    const size_t need = static_cast<size_t>(n_tiles) * m_chunks * splits * BN * kBlockW;
+    const int tiles = n_tiles * m_chunks;
+    if (splitk_workspace(&sws, need, tiles) != SWL_OK) {
+      sws = SplitWs{nullptr, nullptr};
+      cudaStreamCaptureStatus cap = cudaStreamCaptureStatusActive;
+      if (cudaStreamIsCapturing(stream, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone &&
+          ensure_streamk_workspace() == SWL_OK && splitk_workspace(&sws, need, tiles) != SWL_OK)
+        sws = SplitWs{nullptr, nullptr};
+    }
+  }
   SWL_CUDA_TRY(launch_kernel(slot_round_tc_kernel<BN, STAGES, Ex>,
                              dim3(static_cast<unsigned>(n_tiles * splits), static_cast<unsigned>(m_chunks), 1),
-                             dim3(kThreads, 1, 1), smem_bytes, stream, static_cast<unsigned>(splits),
-                             map, tab, shape, splits, g_round_flags.load(std::memory_order_relaxed), ex));
+                             dim3(kThreads, 1, 1), smem_bytes, stream,
+                             sws.part ? 1u : static_cast<unsigned>(splits), map, tab, shape, splits, flags, sws,
+                             ex));
   return SWL_OK;
 }
 
@@ -775,14 +822,16 @@ SWL_EXPORT int swl_round_device_error(unsigned int* code) {
 // (32, 64, 96, 128, or 0 = above 128), tile `bn` rows with a ring of
 // `stages` K-blocks (bn = 0 restores the default of that class; the tile
 // must hold the class's rows, except 256-row chunks above 128). flags bit 0
-// makes the gather warps poll the free-stage barrier without sleeping.
+// makes the gather warps poll the free-stage barrier without sleeping; bit 1
+// reduces split-K partial sums through the global-memory workspace instead
+// of across a thread-block cluster (DSMEM).
 SWL_EXPORT int swl_round_tune(int max_rows, int bn, int stages, int flags) {
   int c = -1;
   for (int i = 0; i < kRowClasses - 1; ++i)
     if (max_rows == kClassRows[i]) c = i;
   if (max_rows == 0) c = kRowClasses - 1;
   if (c < 0) return set_error(SWL_ERR_ARG, "round tuning: max_rows 32, 64, 96, 128 or 0");
-  if (flags & ~kFlagGatherSpin) return set_error(SWL_ERR_ARG, "round tuning: flags bit 0 only");
+  if (flags & ~(kFlagGatherSpin | kFlagGlobalSplit)) return set_error(SWL_ERR_ARG, "round tuning: flags bits 0-1 only");
   if (bn != 0 && (!tile_supported(bn, stages) || (c < kRowClasses - 1 && bn < kClassRows[c]) ||
                   (c == kRowClasses - 1 && bn != 256)))
     return set_error(SWL_ERR_ARG, "round tuning: tile %d x %d stages not built or too small for %d rows", bn,

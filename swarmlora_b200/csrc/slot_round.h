@@ -80,6 +80,22 @@ struct QkvRopeEpi {
 // in shared memory next to the pipeline).
 constexpr int kQkvRopeMaxRows = 64;
 
+// Split-K through global memory (no thread-block cluster): split s of tile t
+// writes its fp32 partial tile to part[(t * splits + s) * tile_floats] and
+// counts itself in count[t]; the last of a tile's splits to arrive sums the
+// partials in split order (the same order as the cluster reduction, so the
+// results are bit-identical to it), writes the outputs and resets count[t].
+// part == nullptr selects the cluster reduction.
+struct SplitWs {
+  float* part;
+  int* count;
+};
+
+// The per-device split-K workspace (inside the stream-K workspace, allocated
+// with the slot pool or on first use outside a stream capture): room for
+// `floats` partial values and `tiles` counters, or SWL_ERR_STATE.
+int splitk_workspace(SplitWs* out, size_t floats, int tiles);
+
 enum RoundAlgo : int {
   kAlgoAuto = 0,        // cluster split-K (measured faster than stream-K on B200)
   kAlgoTensorCore = 1,  // tcgen05 + TMA, K split across a thread-block cluster (DSMEM reduce)

@@ -371,6 +371,22 @@ int ensure_streamk_workspace() {
   return SWL_OK;
 }
 
+// The split-K workspace of the tensor-core round shares the stream-K buffer
+// (the two never run at once: both are launched in stream order) and uses
+// the upper half of its counters.
+int splitk_workspace(SplitWs* out, size_t floats, int tiles) {
+  int dev = 0;
+  SWL_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 16) return set_error(SWL_ERR_ARG, "split-K: device ordinal out of range");
+  Workspace& w = g_ws[dev];
+  if (!w.ws) return set_error(SWL_ERR_STATE, "split-K: workspace not allocated");
+  const int half = w.counters_n / 2;
+  if (floats > w.ws_floats || tiles > half) return set_error(SWL_ERR_STATE, "split-K: workspace too small");
+  out->part = w.ws;
+  out->count = w.counters + half;
+  return SWL_OK;
+}
+
 // Resets the arrival counters (after a round reported a bounded-wait timeout,
 // a tile may have been left half-counted). Synchronous.
 int reset_streamk_counters() {

@@ -129,10 +129,11 @@ SWL_EXPORT int64_t swl_attention_part_floats(int total_rows, int hq, int hkv, in
   return attention_part_floats(total_rows, hq, attention_splits(total_rows, hkv, max_len));
 }
 
-// Tuning knob of the attention launch: pages per context chunk and depth of
-// the page ring (2..4); 0 restores the automatic choice.
-SWL_EXPORT int swl_attention_tune(int chunk_pages, int stages) {
-  return set_attention_tuning(chunk_pages, stages);
+// Tuning knob of the attention launch: pages per context chunk, depth of
+// the page ring (2..4) and kv head groups (1, 2, 4, 8: CTAs sharing one
+// page's heads); 0 restores the automatic choice.
+SWL_EXPORT int swl_attention_tune(int chunk_pages, int stages, int groups) {
+  return set_attention_tuning(chunk_pages, stages, groups);
 }
 
 // Causal GQA attention of each new token over its slot's paged cache

@@ -272,9 +272,11 @@ constexpr int kMinUnits = 8;                             // pages per CTA at lea
 constexpr int kAttnSmemMax = 227 * 1024 - 4096;          // dynamic ring budget
 constexpr uint64_t kAttnWaitNs = 2000000000ull;
 
-// Tuning overrides (0 = automatic): minimum pages per CTA and ring depth.
+// Tuning overrides (0 = automatic): minimum pages per CTA, ring depth, kv
+// head groups per page (CTAs sharing one page's heads).
 std::atomic<int> g_attn_min_units{0};
 std::atomic<int> g_attn_stages{0};
+std::atomic<int> g_attn_groups{0};
 
 __host__ __device__ __forceinline__ int attn_row_bytes(int hkv) { return hkv * kD * 2 + 16; }
 __host__ __device__ __forceinline__ int attn_stage_bytes(int hq, int hkv) {
@@ -324,10 +326,13 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   __shared__ int pre[kAttnMaxRows + 1];  // page prefix over rows
   __shared__ int keys[kAttnMaxRows];     // keys (causal length) of each row
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the kv heads are split into gridDim.y groups; this CTA's group is
+  // blockIdx.y and it holds only that group's slices of each page
   const int hkv = p.hkv, G = p.hq / p.hkv;
-  const int row_bytes = attn_row_bytes(hkv);
+  const int hkv_c = hkv / static_cast<int>(gridDim.y);
+  const int row_bytes = attn_row_bytes(hkv_c);
   const int kv_bytes = kPageTok * row_bytes;
-  const int stage_bytes = attn_stage_bytes(p.hq, hkv);
+  const int stage_bytes = attn_stage_bytes(hkv_c * G, hkv_c);
 
   // Page prefix over the rows (every CTA derives the same unit stream). The
   // context lengths and block tables are not written by the launch just
@@ -376,10 +381,10 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   }
   const int t_start = static_cast<int>(u0 - pre[r_start]);
 
-  const int kvh = warp;
+  const int kvh = static_cast<int>(blockIdx.y) * hkv_c + warp;  // this warp's kv head
   const uint32_t sm0 = ptx::smem_addr(att_dyn);
-  const uint32_t head_off = kvh * kD * 2;
-  const uint32_t q_off = 2 * kv_bytes + kvh * G * kD * 2;  // this head group's query rows in a stage
+  const uint32_t head_off = warp * kD * 2;
+  const uint32_t q_off = 2 * kv_bytes + warp * G * kD * 2;  // this head's query rows in a stage
 
   // ---- loads: this warp's slice of unit (lr, lt) into stage `st` ----
   const int ld_tok = lane >> 4, ld_ch = lane & 15;  // token parity and 16-byte chunk of this lane
@@ -390,7 +395,7 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   int next_page = idle ? 0 : tab.block_table[lsg][lt];
   ptx::grid_dep_wait();
   ptx::grid_dep_launch();
-  if (blockIdx.x == 0 && warp == 0) {
+  if (blockIdx.x == 0 && blockIdx.y == 0 && warp == 0) {
     int* hdr = reinterpret_cast<int*>(part);
     if (lane == 0) hdr[0] = static_cast<int>(W);
     for (int r = lane; r <= rows; r += 32) hdr[1 + r] = pre[r];
@@ -823,7 +828,7 @@ int sm_count_attn() {
 }
 
 template <int S>
-int launch_attention_stages(const AttnTable& tab, const AttnParams& p, int grid, size_t smem,
+int launch_attention_stages(const AttnTable& tab, const AttnParams& p, int grid, int groups, size_t smem,
                             const AttnSplit& sp, cudaStream_t stream) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
@@ -833,8 +838,8 @@ int launch_attention_stages(const AttnTable& tab, const AttnParams& p, int grid,
   });
   if (attr_err != cudaSuccess)
     return set_error(SWL_ERR_CUDA, "attention: smem attribute: %s", cudaGetErrorString(attr_err));
-  SWL_CUDA_TRY(launch_kernel(paged_attention_kernel<S>, dim3(grid), dim3(p.hkv * 32), smem, stream, 1,
-                             tab, p, sp.chunks, sp.chunk_pages, p.part));
+  SWL_CUDA_TRY(launch_kernel(paged_attention_kernel<S>, dim3(grid, groups), dim3(p.hkv / groups * 32), smem,
+                             stream, 1, tab, p, sp.chunks, sp.chunk_pages, p.part));
   return SWL_OK;
 }
 
@@ -856,7 +861,12 @@ int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream
       return set_error(SWL_ERR_ARG, "attention: KV caches must be 16-byte aligned");
   if (!p.part) return set_error(SWL_ERR_ARG, "attention: missing partial scratch");
   const AttnSplit sp = attention_split(tab.seg.total_rows, p.hkv, p.max_len);
-  const int stage_bytes = attn_stage_bytes(p.hq, p.hkv);
+  // kv head groups: CTAs that share a page's heads (each holds only its
+  // group's slices, so a smaller ring per CTA and more CTAs per SM)
+  const int og = g_attn_groups.load(std::memory_order_relaxed);
+  int groups = og > 0 ? og : 1;
+  while (groups > 1 && p.hkv % groups) --groups;
+  const int stage_bytes = attn_stage_bytes(p.hq / groups, p.hkv / groups);
   // two page stages per warp by default (one in flight while one is
   // consumed): the 148 KB ring lets a CTA sit beside the RoPE epilogue's
   // CTAs; deeper rings (tuning) measured no faster in the decode step
@@ -870,9 +880,9 @@ int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream
   const int grid = static_cast<int>(std::max<int64_t>(
       1, std::min<int64_t>((units_max + sp.chunk_pages - 1) / sp.chunk_pages, sm_count_attn())));
   switch (stages) {
-    case 2: SWL_TRY(launch_attention_stages<2>(tab, p, grid, smem, sp, stream)); break;
-    case 3: SWL_TRY(launch_attention_stages<3>(tab, p, grid, smem, sp, stream)); break;
-    default: SWL_TRY(launch_attention_stages<4>(tab, p, grid, smem, sp, stream)); break;
+    case 2: SWL_TRY(launch_attention_stages<2>(tab, p, grid, groups, smem, sp, stream)); break;
+    case 3: SWL_TRY(launch_attention_stages<3>(tab, p, grid, groups, smem, sp, stream)); break;
+    default: SWL_TRY(launch_attention_stages<4>(tab, p, grid, groups, smem, sp, stream)); break;
   }
   ShrinkSide none;
   if (!shrink) {
@@ -896,11 +906,14 @@ int launch_rms_norm(const NormTable& tab, const __nv_bfloat16* w, int64_t hidden
   return SWL_OK;
 }
 
-int set_attention_tuning(int chunk_pages, int stages) {
-  if (chunk_pages < 0 || chunk_pages > 4096 || (stages != 0 && (stages < 2 || stages > kAttnStagesMax)))
-    return set_error(SWL_ERR_ARG, "attention tuning: chunk_pages 0..4096, stages 0 or 2..%d", kAttnStagesMax);
+int set_attention_tuning(int chunk_pages, int stages, int groups) {
+  if (chunk_pages < 0 || chunk_pages > 4096 || (stages != 0 && (stages < 2 || stages > kAttnStagesMax)) ||
+      (groups != 0 && groups != 1 && groups != 2 && groups != 4 && groups != 8))
+    return set_error(SWL_ERR_ARG, "attention tuning: chunk_pages 0..4096, stages 0 or 2..%d, groups 0/1/2/4/8",
+                     kAttnStagesMax);
   g_attn_min_units.store(chunk_pages);
   g_attn_stages.store(stages);
+  g_attn_groups.store(groups);
   return SWL_OK;
 }
 

@@ -158,10 +158,10 @@ def rope_append(qkvs, block_tables, k_caches, v_caches, seqlens, q_rot, cos_sin,
                                 int(cos_sin.shape[0]), q_rot.data_ptr(), _stream(stream)))
 
 
-def attention_tune(chunk_pages: int = 0, stages: int = 0) -> None:
-    """Pages per context chunk and page-ring depth of the attention launch
-    (0 = automatic)."""
-    check(lib().swl_attention_tune(chunk_pages, stages))
+def attention_tune(chunk_pages: int = 0, stages: int = 0, groups: int = 0) -> None:
+    """Pages per context chunk, page-ring depth and kv head groups (CTAs that
+    share one page's heads) of the attention launch (0 = automatic)."""
+    check(lib().swl_attention_tune(chunk_pages, stages, groups))
 
 
 def attention_part_floats(total_rows: int, hq: int, hkv: int, max_len: int) -> int:

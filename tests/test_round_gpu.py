@@ -92,6 +92,30 @@ def test_explicit_splits(native, cuda, splits):
     _check(W, xs, b, outs, f"splits={splits}")
 
 
+@pytest.mark.parametrize("name,rows,splits", [("o", [1] * 28, 8), ("down", [1] * 28, 0), ("qkv", [1] * 88, 0),
+                                               ("o", [2, 1, 5, 0, 9], 3), ("down", [1] * 28, 5)])
+def test_global_split_matches_cluster_split(native, cuda, name, rows, splits):
+    """Split-K reduced through the global-memory workspace (tuning flag) and
+    across a thread-block cluster (the default) give bit-identical outputs (both sum
+    the splits' fp32 partials in split order), and repeated launches agree
+    (the per-tile arrival counters reset themselves); both against the
+    oracle."""
+    from swarmlora_b200._native import check, lib
+    N, K = SHAPES[name]
+    W, xs, b = _case(N, K, rows, seed=N + len(rows) + splits)
+    try:
+        cluster = _run(W, xs, b, algo=1, splits=splits)
+        check(lib().swl_round_tune(32, 0, 0, 2))  # flags are global; the tile stays the default
+        glob = _run(W, xs, b, algo=1, splits=splits)
+        again = _run(W, xs, b, algo=1, splits=splits)
+    finally:
+        check(lib().swl_round_tune(32, 0, 0, 0))
+    _check(W, xs, b, glob, f"{name} rows={len(rows)} global split-K")
+    for i, (c, g2, a) in enumerate(zip(cluster, glob, again)):
+        assert torch.equal(c, g2), f"slot {i}: global split-K differs from the cluster reduction"
+        assert torch.equal(g2, a), f"slot {i}: global split-K is not repeatable"
+
+
 def test_bias_and_down_shape_ragged(native, cuda):
     W, xs, b = _case(H, I, [2, 1, 5], seed=11, with_bias=True)
     outs = _run(W, xs, b, algo=1)

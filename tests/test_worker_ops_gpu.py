@@ -184,6 +184,44 @@ def test_rope_append_attention(native, cuda, ctx, rows):
     _attn_case(ctx, rows, seed=sum(ctx) + len(rows))
 
 
+@pytest.mark.parametrize("stages,groups", [(3, 2), (2, 2), (4, 4), (2, 8)])
+def test_attention_head_groups_match_one_group(native, cuda, stages, groups):
+    """CTAs that share a page's kv heads (each holding its group's slices,
+    a smaller ring per CTA) give bit for bit the one-group result: every
+    head still streams the same pages in the same order."""
+    from swarmlora_b200 import worker_ops as wo
+    g = _g(77)
+    ctx, rows = [1000, 3, 513, 77, 0, 300], [1, 1, 1, 4, 16, 1]
+    n, page = len(ctx), 16
+    max_len = max(c + r for c, r in zip(ctx, rows))
+    pages_per = (max_len + page - 1) // page + 1
+    perm = torch.randperm(n * pages_per, generator=g).tolist()
+    bts = [torch.tensor(perm[i * pages_per:(i + 1) * pages_per], dtype=torch.int32, device=DEV) for i in range(n)]
+    kd = torch.randn(n * pages_per, page, HKV, D, generator=g).to(BF).to(DEV)
+    vd = torch.randn(n * pages_per, page, HKV, D, generator=g).to(BF).to(DEV)
+    sls = [torch.tensor([c], dtype=torch.int32, device=DEV) for c in ctx]
+    total = sum(rows)
+    q_rot = torch.randn(total, HQ * D, generator=g).to(BF).to(DEV)
+    part = torch.empty(max(1, wo.attention_part_floats(total, HQ, HKV, max_len)), dtype=torch.float32, device=DEV)
+    scale = 1.0 / math.sqrt(D)
+
+    def run():
+        outs = [torch.full((r, HQ * D), float("nan"), dtype=BF, device=DEV) for r in rows]
+        wo.paged_attention(rows, bts, [kd] * n, [vd] * n, sls, outs, q_rot, part, HQ, HKV, max_len, scale)
+        torch.cuda.synchronize()
+        return [o.cpu() for o in outs]
+    try:
+        wo.attention_tune(0, 2, 1)
+        want = run()
+        wo.attention_tune(0, stages, groups)
+        got = run()
+    finally:
+        wo.attention_tune(0, 0, 0)
+    for i in range(n):
+        assert torch.isfinite(want[i].float()).all()
+        assert torch.equal(got[i], want[i]), f"slot {i}: {groups} head groups x {stages} stages differ"
+
+
 def test_rope_matches_hf_rotary(native, cuda):
     """The oracle's llama3 inv_freq equals HF LlamaRotaryEmbedding's for Llama-3.1."""
     from transformers import LlamaConfig
