@@ -65,10 +65,15 @@ def parse():
                          "(for ncu --profile-from-start off)")
     ap.add_argument("--profile-round", choices=["qkv", "o", "gate_up", "down"], default=None,
                     help="run only --steps launches of one round kind at M=--slots (small ncu case)")
+    ap.add_argument("--round-rows", type=int, default=1,
+                    help="token rows per slot for --profile-round (M = slots x rows; a prefill-packed round)")
     ap.add_argument("--round-algo", type=int, default=0,
                     help="round kernel for --profile-round: 0 auto, 1 cluster split-K, 3 stream-K")
     ap.add_argument("--attn-chunk-pages", type=int, default=0, help="attention pages per chunk (0 = auto)")
     ap.add_argument("--attn-stages", type=int, default=0, help="attention page-ring depth 2..4 (0 = auto)")
+    ap.add_argument("--round-flags", type=int, default=0,
+                    help="round kernel flags (swl_round_tune): 1 gather spin, 2 global-memory split-K, "
+                         "4 L2 prefetch of the W tiles beyond the ring")
     ap.add_argument("--attn-groups", type=int, default=0,
                     help="attention kv head groups 1/2/4/8: CTAs sharing one page's heads (0 = auto)")
     ap.add_argument("--no-pdl", action="store_true",
@@ -439,6 +444,9 @@ def our_arm(args):
     swarmlora_b200.set_pdl(not args.no_pdl)
     from swarmlora_b200 import worker_ops as _wo
     _wo.attention_tune(args.attn_chunk_pages, args.attn_stages, args.attn_groups)
+    if args.round_flags:
+        from swarmlora_b200._native import check as _check, lib as _lib
+        _check(_lib().swl_round_tune(32, 0, 0, args.round_flags))
     if args.checkpoint:
         from swarmlora_b200.checkpoint import load_base
         base, cfg = load_base(args.checkpoint, dev)
@@ -592,19 +600,25 @@ def profile_round(args):
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(0)
     W = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-    ins = [torch.randn(16, K, generator=g, device=dev).to(torch.bfloat16)[:1] for _ in range(args.slots)]
-    outs = [torch.empty(16, N, dtype=torch.bfloat16, device=dev) for _ in range(args.slots)]
+    rows = max(1, args.round_rows)
+    ins = [torch.randn(max(16, rows), K, generator=g, device=dev).to(torch.bfloat16)[:rows] for _ in range(args.slots)]
+    outs = [torch.empty(max(16, rows), N, dtype=torch.bfloat16, device=dev) for _ in range(args.slots)]
     for _ in range(args.warmup):
         slot_gemm(W, ins, outs, algo=args.round_algo)
     torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
+    times = []
     for _ in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
         slot_gemm(W, ins, outs, algo=args.round_algo)
-    b.record()
-    b.synchronize()
-    print(json.dumps({"profile_round": args.profile_round, "M": args.slots, "N": N, "K": K,
-                      "launches": args.steps, "us_per_launch_incl_host": a.elapsed_time(b) * 1e3 / args.steps}))
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    M = args.slots * rows
+    us = min(times)
+    print(json.dumps({"profile_round": args.profile_round, "M": M, "N": N, "K": K, "launches": args.steps,
+                      "us_per_launch_best": round(us, 2), "us_per_launch_all": [round(t, 1) for t in times],
+                      "tflops_best": round(2 * M * N * K / us / 1e6, 1)}))
     return 0
 
 

@@ -327,7 +327,13 @@ int swl_round_set_streamk_ctas(int n);
  * sleeping; bit 1: split-K sums reduced through a per-device global-memory
  * workspace instead of across a thread-block cluster (then rounds with
  * split-K on one device share that workspace and must run in stream order,
- * never concurrently). */
+ * never concurrently); bit 2: before its dependency wait each CTA prefetches
+ * into L2 the W tiles its ring cannot hold (up to 12 K-blocks); bits 0-2
+ * apply to every class. Bit 3 (with bn != 0): the class's token rows are
+ * packed into a per-device staging copy by a launch ahead of the round,
+ * which then loads its token tiles by TMA (default above 128 rows, and for
+ * the large weights from 65 rows); such rounds on one device share the
+ * staging copy and run in stream order. */
 int swl_round_tune(int max_rows, int bn, int stages, int flags);
 
 /* LoRA shrink (model_builder.py:258-262 x @ fused_A; worker_sync.py:305/375

@@ -51,6 +51,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                "r"(bytes)
                : "memory");
 }
+// Adds `bytes` to the barrier's expected transaction count without arriving
+// (the phase cannot complete before a later arrive).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -147,6 +153,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_
       "hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
+}
+// Prefetch of a 2-D tile of a tensor map into L2 (no shared memory, no
+// completion to wait for). c0 is the innermost coordinate.
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1)
+               : "memory");
 }
 // 1-D bulk copy global -> this CTA's shared memory through the TMA engine,
 // completing `bytes` of transaction on `bar` (addresses 16-byte aligned,

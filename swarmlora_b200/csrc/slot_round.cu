@@ -18,6 +18,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
 #include <atomic>
 #include <mutex>
 #include <type_traits>
@@ -73,6 +74,9 @@ struct TcCfg {
 // Launch-time flags of the tensor-core round.
 constexpr int kFlagGatherSpin = 1;    // gather warps poll the free-stage barrier without sleeping
 constexpr int kFlagGlobalSplit = 2;   // split-K reduced through global memory instead of across a cluster
+constexpr int kFlagPrefetchRest = 4;  // before the dependency wait, prefetch the rest of the CTA's W tiles into L2
+constexpr int kFlagStagedX = 8;       // token tiles by TMA from a packed staging copy (set per launch)
+constexpr int kPrefetchRestMax = 12;  // at most this many K-blocks per CTA (the small rounds)
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
@@ -114,7 +118,7 @@ __device__ __forceinline__ int slot_of_row(const SlotTable& tab, int gr) {
 
 template <int BN, int STAGES, class Ex>
 __global__ void __launch_bounds__(kThreads, 1)
-    slot_round_tc_kernel(const __grid_constant__ CUtensorMap wmap,
+    slot_round_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                          const __grid_constant__ SlotTable tab, const RoundShape shape,
                          int splits, int flags, const SplitWs sws, const __grid_constant__ Ex ex) {
   constexpr bool kShard = std::is_same<Ex, ShardArgs>::value;
@@ -184,14 +188,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (kShard) row_peer[r] = ppeer;
   }
 
+  // Staged tokens: the chunk's token rows were packed into one [M, K] copy
+  // by the launch just ahead, and the TMA warp loads each token tile with the
+  // weight tile (the gather warps idle); otherwise the gather warps copy each
+  // row from its slot buffer.
+  const bool staged = (flags & kFlagStagedX) != 0;
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      ptx::mbar_init(&full[s], 1 + kGatherThreads);
+      ptx::mbar_init(&full[s], staged ? 1 : 1 + kGatherThreads);
       ptx::mbar_init(&empty[s], 1);
     }
     ptx::mbar_init(accf, 1);
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&wmap);
+    if (staged) ptx::prefetch_tmap(&xmap);
   }
   if (warp == 1) {
     ptx::tmem_alloc(tmem_holder, Cfg::kTmemCols);
@@ -208,9 +218,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     const uint64_t pol = ptx::policy_evict_first();
     for (int i = 0; i < npre; ++i) {
-      ptx::mbar_arrive_expect_tx(&full[i], kWStageBytes);
+      // staged: the stage completes only with the token tile's arrival below
+      if (staged) ptx::mbar_expect_tx(&full[i], kWStageBytes);
+      else ptx::mbar_arrive_expect_tx(&full[i], kWStageBytes);
       ptx::tma_load_2d(w_st + i * kWStageBytes, &wmap, &full[i], (kb_begin + i) * kBlockK, n0, pol);
     }
+    // the tiles that do not fit in the ring move into L2 now, while the
+    // kernel ahead still runs (small rounds only: the bytes stay in L2)
+    if ((flags & kFlagPrefetchRest) && nk - npre <= kPrefetchRestMax)
+      for (int i = npre; i < nk; ++i) ptx::tma_prefetch_2d(&wmap, (kb_begin + i) * kBlockK, n0);
   }
   ptx::grid_dep_wait();
   ptx::grid_dep_launch();
@@ -227,13 +243,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol = ptx::policy_evict_first();
+      const uint64_t pol_x = ptx::policy_evict_last();  // every CTA of the chunk reads the token tiles
+      if (staged)
+        for (int i = 0; i < npre; ++i) {
+          ptx::mbar_arrive_expect_tx(&full[i], Cfg::kXStageBytes);
+          ptx::tma_load_2d(x_st + i * Cfg::kXStageBytes, &xmap, &full[i], (kb_begin + i) * kBlockK, chunk_row0,
+                           pol_x);
+        }
       for (int i = npre; i < nk; ++i) {
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1;
         if (!ptx::mbar_wait(&empty[s], ph ^ 1, err, kErrWaitEmptyW, kWaitTimeoutNs)) break;
-        ptx::mbar_arrive_expect_tx(&full[s], kWStageBytes);
+        ptx::mbar_arrive_expect_tx(&full[s], kWStageBytes + (staged ? Cfg::kXStageBytes : 0));
         ptx::tma_load_2d(w_st + s * kWStageBytes, &wmap, &full[s], (kb_begin + i) * kBlockK, n0,
                          pol);
+        if (staged)
+          ptx::tma_load_2d(x_st + s * Cfg::kXStageBytes, &xmap, &full[s], (kb_begin + i) * kBlockK, chunk_row0,
+                           pol_x);
       }
     }
   } else if (warp == 1) {
@@ -263,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // its eight 16-byte pieces are stored XOR-swizzled by (r & 7) as the
     // 128B-swizzle canonical layout requires. Rows past the chunk are zeros.
     const int t = tid - 2 * 32;
-    for (int i = 0; i < nk; ++i) {
+    for (int i = 0; i < (staged ? 0 : nk); ++i) {
       const int s = i % STAGES;
       const uint32_t ph = (i / STAGES) & 1;
       const bool freed = (flags & kFlagGatherSpin)
@@ -560,7 +586,66 @@ constexpr int kClassRows[kRowClasses] = {32, 64, 96, 128, 1 << 30};
 constexpr int kDefaultTile[kRowClasses][2] = {{32, 4}, {64, 4}, {96, 3}, {128, 3}, {256, 3}};
 std::atomic<int> g_tile_bn[kRowClasses] = {{0}, {0}, {0}, {0}, {0}};
 std::atomic<int> g_tile_stages[kRowClasses] = {{0}, {0}, {0}, {0}, {0}};
+// Token tiles staged (packed copy, loaded by TMA) per class by default when
+// the weight has at least this many elements (-1: never): measured on B200,
+// staging pays above 128 rows for every round (Gate+Up at M = 200: 188 -> 90
+// us; Down at M = 512: 156 -> 73 us), and at 65..128 rows for the large
+// weights only (Gate+Up at M = 88: 56 -> 51 us; O at M = 88: 15.3 -> 17.3
+// us, the packing launch costing more than it saves).
+constexpr int64_t kDefaultStagedMinElems[kRowClasses] = {-1, -1, int64_t{1} << 26, int64_t{1} << 25, 0};
+std::atomic<int> g_tile_staged[kRowClasses] = {{-1}, {-1}, {-1}, {-1}, {-1}};
 std::atomic<int> g_round_flags{0};
+
+// ---- staged token rows ------------------------------------------------------------------
+// A launch ahead of the round packs the round's token rows into one [M, K]
+// bf16 buffer per device, so the round loads its token tiles by TMA (the same
+// 128B-swizzled layout the gather warps write) instead of by per-row copies.
+struct Staging {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+Staging g_stage[16];
+std::mutex g_stage_mu;
+constexpr size_t kStageMaxBytes = size_t{256} << 20;
+
+// The device's staging buffer with room for `bytes`, grown outside stream
+// captures (growing waits for the device); nullptr when it cannot be had.
+void* staging_buffer(size_t bytes, cudaStream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16 || bytes > kStageMaxBytes) return nullptr;
+  std::lock_guard<std::mutex> lk(g_stage_mu);
+  Staging& st = g_stage[dev];
+  if (st.bytes >= bytes) return st.p;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusActive;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
+  const size_t want = std::max(bytes, size_t{16} << 20);
+  if (st.p) {
+    if (cudaDeviceSynchronize() != cudaSuccess) return nullptr;
+    cudaFree(st.p);
+    st.p = nullptr;
+    st.bytes = 0;
+  }
+  if (cudaMalloc(&st.p, want) != cudaSuccess) {
+    cudaGetLastError();
+    st.p = nullptr;
+    return nullptr;
+  }
+  st.bytes = want;
+  return st.p;
+}
+
+// Row gr of the round -> row gr of the staging copy (16-byte vectors).
+__global__ void stage_rows_kernel(const __grid_constant__ SlotTable tab, int64_t in_stride, int64_t K,
+                                  __nv_bfloat16* __restrict__ out) {
+  ptx::grid_dep_wait();
+  ptx::grid_dep_launch();
+  const int gr = blockIdx.x;
+  const int s = slot_of_row(tab, gr);
+  const int64_t local = gr - tab.row_start[s];
+  const uint4* src = reinterpret_cast<const uint4*>(tab.in[s] + local * in_stride);
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(gr) * K);
+  for (int64_t k = threadIdx.x; k < K / 8; k += blockDim.x) dst[k] = src[k];
+}
 
 int row_class(int m) {
   int c = 0;
@@ -568,9 +653,25 @@ int row_class(int m) {
   return c;
 }
 
+// The packed token rows [rows, K] bf16, box 64 x box_rows, 128B swizzle:
+// rows past `rows` read as zeros.
+int encode_token_tmap(CUtensorMap* map, const void* X, int64_t rows, int64_t K, int box_rows) {
+  auto enc = tmap_encoder();
+  if (!enc) return set_error(SWL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBlockK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(X), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(SWL_ERR_CUDA, "token tensor map: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return SWL_OK;
+}
+
 template <int BN, int STAGES, class Ex>
 int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& map, int splits,
-              const Ex& ex, cudaStream_t stream) {
+              const Ex& ex, cudaStream_t stream, const void* staged = nullptr) {
   using Cfg = TcCfg<BN, STAGES>;
   constexpr bool kShard = std::is_same<Ex, ShardArgs>::value;
   constexpr int smem_bytes = Cfg::kSmemBytes + (std::is_same<Ex, QkvRopeEpi>::value ? Cfg::kRopeBytes : 0);
@@ -606,7 +707,13 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
   // last split of a tile reads all partials back alone; measured slower than
   // the cluster reduction on the decode shapes (O at M = 28: 14.1 vs 10.3 us,
   // Down 26.9 vs 23.5 us), so the cluster reduction is the default.
-  const int flags = g_round_flags.load(std::memory_order_relaxed);
+  int flags = g_round_flags.load(std::memory_order_relaxed);
+  CUtensorMap xmap;
+  memset(&xmap, 0, sizeof(xmap));
+  if (staged) {
+    SWL_TRY(encode_token_tmap(&xmap, staged, tab.total_rows, shape.K, BN));
+    flags |= kFlagStagedX;
+  }
   SplitWs sws{nullptr, nullptr};
   if (splits > 1 && !std::is_same<Ex, QkvRopeEpi>::value && (flags & kFlagGlobalSplit)) {
     const size_t need = static_cast<size_t>(n_tiles) * m_chunks * splits * BN * kBlockW;
@@ -622,8 +729,8 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
   SWL_CUDA_TRY(launch_kernel(slot_round_tc_kernel<BN, STAGES, Ex>,
                              dim3(static_cast<unsigned>(n_tiles * splits), static_cast<unsigned>(m_chunks), 1),
                              dim3(kThreads, 1, 1), smem_bytes, stream,
-                             sws.part ? 1u : static_cast<unsigned>(splits), map, tab, shape, splits, flags, sws,
-                             ex));
+                             sws.part ? 1u : static_cast<unsigned>(splits), map, xmap, tab, shape, splits, flags,
+                             sws, ex));
   return SWL_OK;
 }
 
@@ -652,8 +759,20 @@ int launch_tc_any(const SlotTable& tab, const RoundShape& shape, const CUtensorM
     bn = kDefaultTile[c][0];
     stages = kDefaultTile[c][1];
   }
+  // staged token rows (plain rounds only): pack them, then the round
+  const int st_set = g_tile_staged[c].load(std::memory_order_relaxed);
+  const int64_t min_elems = kDefaultStagedMinElems[c];
+  const bool want_staged = std::is_same<Ex, NoEpi>::value && tab.total_rows > 0 &&
+                           (st_set >= 0 ? st_set != 0 : (min_elems >= 0 && shape.N * shape.K >= min_elems));
+  void* staged = nullptr;
+  if (want_staged) {
+    staged = staging_buffer(static_cast<size_t>(tab.total_rows) * shape.K * 2, stream);
+    if (staged)
+      SWL_CUDA_TRY(launch_kernel(stage_rows_kernel, dim3(static_cast<unsigned>(tab.total_rows)), dim3(256), 0, stream,
+                                 1, tab, shape.in_stride, shape.K, static_cast<__nv_bfloat16*>(staged)));
+  }
 #define SWL_TILE_CASE(B, S) \
-  if (bn == B && stages == S) return launch_tc<B, S>(tab, shape, map, splits, ex, stream);
+  if (bn == B && stages == S) return launch_tc<B, S>(tab, shape, map, splits, ex, stream, staged);
   SWL_ROUND_TILES(SWL_TILE_CASE)
 #undef SWL_TILE_CASE
   return set_error(SWL_ERR_ARG, "slot round: no tile %d x %d stages", bn, stages);
@@ -824,21 +943,27 @@ SWL_EXPORT int swl_round_device_error(unsigned int* code) {
 // must hold the class's rows, except 256-row chunks above 128). flags bit 0
 // makes the gather warps poll the free-stage barrier without sleeping; bit 1
 // reduces split-K partial sums through the global-memory workspace instead
-// of across a thread-block cluster (DSMEM).
+// of across a thread-block cluster (DSMEM); bit 2 prefetches into L2, before
+// the dependency wait, the W tiles of a CTA that do not fit in its ring (up
+// to 12 K-blocks). Bits 0-2 apply to every class. Bit 3 (with bn != 0) packs
+// the class's token rows into a staging copy that the round loads by TMA;
+// bn = 0 restores the class's default tile and staging.
 SWL_EXPORT int swl_round_tune(int max_rows, int bn, int stages, int flags) {
   int c = -1;
   for (int i = 0; i < kRowClasses - 1; ++i)
     if (max_rows == kClassRows[i]) c = i;
   if (max_rows == 0) c = kRowClasses - 1;
   if (c < 0) return set_error(SWL_ERR_ARG, "round tuning: max_rows 32, 64, 96, 128 or 0");
-  if (flags & ~(kFlagGatherSpin | kFlagGlobalSplit)) return set_error(SWL_ERR_ARG, "round tuning: flags bits 0-1 only");
+  if (flags & ~(kFlagGatherSpin | kFlagGlobalSplit | kFlagPrefetchRest | kFlagStagedX))
+    return set_error(SWL_ERR_ARG, "round tuning: flags bits 0-3 only");
   if (bn != 0 && (!tile_supported(bn, stages) || (c < kRowClasses - 1 && bn < kClassRows[c]) ||
                   (c == kRowClasses - 1 && bn != 256)))
     return set_error(SWL_ERR_ARG, "round tuning: tile %d x %d stages not built or too small for %d rows", bn,
                      stages, max_rows);
   g_tile_bn[c].store(bn);
   g_tile_stages[c].store(bn ? stages : 0);
-  g_round_flags.store(flags);
+  g_tile_staged[c].store(bn ? ((flags & kFlagStagedX) ? 1 : 0) : -1);
+  g_round_flags.store(flags & ~kFlagStagedX);
   return SWL_OK;
 }
 
