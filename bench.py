@@ -95,7 +95,8 @@ def parse():
     ap.add_argument("--protocol", default="28",
                     help="worker-client counts (comma separated) for the decode through the drop-in protocol "
                          "(aggregator main loop + native worker clients over the shared-memory ring), each "
-                         "with event, host (the reference's) and device-published completion; 'off' skips it")
+                         "with event completion (with and without per-segment graphs) and host completion "
+                         "(the reference's); 'off' skips it")
     ap.add_argument("--profile-attention", action="store_true",
                     help="run only --steps paged-attention launches over one layer's KV (small ncu case)")
     return ap.parse_args()
@@ -399,7 +400,7 @@ def protocol_phase(grp, args, variants, rounds=None):
     """Decode through the drop-in protocol: the aggregator's main loop
     serving native worker clients (swarmlora_b200.protocol) that request
     every round through the shared-memory ring and epoch barrier, as the
-    reference's workers do. `variants`: (workers, completion, input_ready).
+    reference's workers do. `variants`: (workers, completion, input_ready, per-segment graphs).
     Returns one dict per variant: tok/s over the timed tokens (host clock of
     the slowest client, from each token's first launch to its last round's
     epoch), and per-round times."""
@@ -409,10 +410,10 @@ def protocol_phase(grp, args, variants, rounds=None):
     n = grp.n
     ops = 1 + 4 * grp.cfg.layers + 1
     out = []
-    for workers, completion, input_ready in variants:
+    for workers, completion, input_ready, graphs in variants:
         grp.reset_positions()
         torch.cuda.synchronize()
-        run = ProtocolRun(grp, workers=workers, completion=completion, input_ready=input_ready)
+        run = ProtocolRun(grp, workers=workers, completion=completion, input_ready=input_ready, graphs=graphs)
         try:
             res = run.run(args.warmup + args.steps)
         finally:
@@ -420,7 +421,7 @@ def protocol_phase(grp, args, variants, rounds=None):
         timed = res["token_s"][args.warmup:]
         tok_s = n * len(timed) / sum(timed)
         entry = {"workers": workers, "slots_per_worker": round(n / workers, 2), "completion": completion,
-                 "input_ready": input_ready, "tok_s": round(tok_s, 2),
+                 "input_ready": input_ready, "segment_graphs": graphs, "tok_s": round(tok_s, 2),
                  "ms_per_token": round(1e3 * sum(timed) / len(timed), 3),
                  "ms_per_token_p50": round(1e3 * statistics.median(timed), 3),
                  "us_per_round_e2e": round(1e6 * sum(timed) / len(timed) / ops, 2)}
@@ -537,7 +538,7 @@ def our_arm(args):
         variants = []
         for w in (int(x) for x in args.protocol.split(",")):
             w = min(max(1, w), n)
-            variants += [(w, "event", "event"), (w, "host", "sync"), (w, "device", "flag")]
+            variants += [(w, "event", "event", True), (w, "event", "event", False), (w, "host", "sync", False)]
         proto = protocol_phase(grp, args, variants, rounds)
     peak, peak_kind = measured_peaks()
     dom = max(rounds, key=lambda k: rounds[k]["us"])

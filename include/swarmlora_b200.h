@@ -472,6 +472,10 @@ int swl_wc_configure(void* handle, int input_mode, int64_t timeout_ms, void* his
 /* Runs `tokens` decode tokens (blocking); token_ns[t] = token t's host wall
  * time in ns, or NULL. */
 int swl_wc_run(void* handle, int tokens, int64_t* token_ns);
+/* Input mode 2 only: 1 = capture the launches between each pair of rounds
+ * into one CUDA graph (external event wait / record nodes at its ends), after
+ * the client's first eager token; 0 = launch them one by one. */
+int swl_wc_use_graphs(void* handle, int on);
 int64_t swl_wc_rounds(void* handle);
 int swl_wc_destroy(void* handle);
 

@@ -151,6 +151,7 @@ SIGNATURES: dict[str, tuple] = {
     "swl_wc_configure": (_i32, [_p, _i32, _i64, _p]),
     "swl_wc_run": (_i32, [_p, _i32, _pi64]),
     "swl_wc_rounds": (_i64, [_p]),
+    "swl_wc_use_graphs": (_i32, [_p, _i32]),
     "swl_wc_destroy": (_i32, [_p]),
 }
 

@@ -73,6 +73,8 @@ struct WorkerClient {
   int input_mode = 0;
   cudaEvent_t input_event = nullptr;  // mode 2: recorded after each round's input
   cudaEvent_t round_event = nullptr;  // mode 2: the aggregator's, recorded after each round
+  bool use_graphs = false;            // mode 2: one CUDA graph per segment between rounds
+  std::vector<cudaGraphExec_t> graphs;
   uint32_t* flag_host = nullptr;
   uint32_t* flag_dev = nullptr;
   uint32_t flag_seq = 0;
@@ -127,10 +129,34 @@ int wait_input_written(WorkerClient* c) {
   return SWL_OK;
 }
 
+// Rounds of one token: EMBED, per layer QKV / O / Gate+Up / Down, LM_HEAD.
+int rounds_per_token(const WorkerClient* c) { return 4 * c->layers + 2; }
+
+void round_of(const WorkerClient* c, int i, int* op, int* layer, int64_t* dx) {
+  if (i == 0) {
+    *op = kOpEmbed, *layer = 0, *dx = c->hidden;
+    return;
+  }
+  if (i == rounds_per_token(c) - 1) {
+    *op = kOpLmHead, *layer = 0, *dx = c->hidden;
+    return;
+  }
+  const int l = (i - 1) / 4;
+  *layer = l;
+  switch ((i - 1) % 4) {
+    case 0: *op = kOpQkvFused, *dx = c->hidden; break;
+    case 1: *op = kOpOProj, *dx = static_cast<int64_t>(c->hq) * c->head_dim; break;
+    case 2: *op = kOpGateUpFused, *dx = c->hidden; break;
+    default: *op = kOpDownProj, *dx = c->inter; break;
+  }
+}
+
 // One round through the protocol (BatchedAggregatorOps.*_submit_all +
-// barrier_sync, worker_sync.py:250-389), for every slot of the client.
-int protocol_round(WorkerClient* c, int op, int layer, int64_t dx) {
-  SWL_TRY(wait_input_written(c));
+// barrier_sync, worker_sync.py:250-389), for every slot of the client. With
+// `launched` the segment just enqueued already ends with the input event
+// and the next one starts by waiting for the round event (per-segment graphs).
+int protocol_round(WorkerClient* c, int op, int layer, int64_t dx, bool launched = false) {
+  if (!launched) SWL_TRY(wait_input_written(c));
   const int64_t e0 = swl_q_get_barrier_done_epoch();
   for (int i = 0; i < c->n; ++i) {
     int st;
@@ -146,15 +172,17 @@ int protocol_round(WorkerClient* c, int op, int layer, int64_t dx) {
     if (swl_q_is_slot_evicted(c->slot_ids[i]))
       return set_error(SWL_ERR_STATE, "worker client: slot %d evicted by the aggregator", c->slot_ids[i]);
   // the round is enqueued, not finished: order the reads of its outputs after it
-  if (c->input_mode == 2) SWL_CUDA_TRY(cudaStreamWaitEvent(c->stream, c->round_event, 0));
+  if (c->input_mode == 2 && !launched) SWL_CUDA_TRY(cudaStreamWaitEvent(c->stream, c->round_event, 0));
   ++c->rounds_done;
   return SWL_OK;
 }
 
-// One decode token for every slot of the client: the reference worker's
-// per-token sequence, with the fused epilogues of this library between the
-// rounds (the same launches as the in-process engine's step).
-int run_token(WorkerClient* c, int t) {
+// The launches between round i - 1 and round i of a token (segment 0: before
+// the EMBED round; segment rounds_per_token: after the LM head), with this
+// library's fused epilogues: the same sequence as the in-process engine's
+// step. The epilogues read each round's output in place and write the next
+// round's input straight into the slot input buffers.
+int enqueue_segment(WorkerClient* c, int i, int t) {
   const int n = c->n;
   const int H = c->hidden, I = c->inter, D = c->head_dim, r = c->rank;
   const int64_t qkv_n = static_cast<int64_t>(c->hq + 2 * c->hkv) * D;
@@ -163,44 +191,102 @@ int run_token(WorkerClient* c, int t) {
   void* const* out = c->slot_out.data();
   void* const* in = c->slot_in.data();
   void* const* h = c->h_rows.data();
-  SWL_TRY(swl_copy_rows(n, c->tokens.data(), in, c->tok_bytes.data(), st));
-  SWL_TRY(protocol_round(c, kOpEmbed, 0, H));
-  SWL_TRY(swl_fused_resid_norm_shrink(n, rows, out, H, nullptr, 0, 0.f, nullptr, 0, 0, h, H, c->L[0].in_norm, H,
-                                      c->eps, in, H, c->L[0].A_qkv.data(), 3 * r, c->ws_qkv, nullptr, 0, st));
-  for (int l = 0; l < c->layers; ++l) {
-    const WcLayer& w = c->L[l];
-    SWL_TRY(protocol_round(c, kOpQkvFused, l, H));
-    SWL_TRY(swl_fused_qkv_rope(n, rows, out, qkv_n, w.B_qkv.data(), r, c->ws_qkv, c->norm_splits,
-                               c->block_tables.data(), w.k_cache.data(), w.v_cache.data(), c->seqlens.data(), c->hq,
-                               c->hkv, D, c->page, c->cos_sin, c->q_rot, nullptr, 0, st));
-    SWL_TRY(swl_paged_attention_shrink(n, rows, c->block_tables.data(), w.k_cache.data(), w.v_cache.data(),
-                                       c->seqlens.data(), in,
-                                       static_cast<int64_t>(c->hq) * D, c->hq, c->hkv, D, c->page,
-                                       1.0f / sqrtf(static_cast<float>(D)), c->max_len, c->q_rot, c->part,
-                                       w.A_o.data(), r, c->ws_o, nullptr, 0, st));
-    SWL_TRY(protocol_round(c, kOpOProj, l, static_cast<int64_t>(c->hq) * D));
-    SWL_TRY(swl_fused_resid_norm_shrink(n, rows, out, H, w.B_o.data(), r, c->scaling, c->ws_o, c->hq, 1, h, H,
-                                        w.post_norm, H, c->eps, in, H, w.A_gu.data(), 2 * r, c->ws_gu, nullptr, 0,
-                                        st));
-    SWL_TRY(protocol_round(c, kOpGateUpFused, l, H));
-    SWL_TRY(swl_fused_gu_silu_shrink(n, rows, out, 2 * static_cast<int64_t>(I), w.B_gu.data(), r, c->ws_gu,
-                                     c->norm_splits, I, in, I, w.A_dn.data(), r, c->ws_dn, nullptr, 0, st));
-    SWL_TRY(protocol_round(c, kOpDownProj, l, I));
-    const bool last = l == c->layers - 1;
-    SWL_TRY(swl_fused_resid_norm_shrink(n, rows, out, H, w.B_dn.data(), r, c->scaling, c->ws_dn, c->dn_splits, 1, h,
-                                        H, last ? c->final_norm : c->L[l + 1].in_norm, H, c->eps, in, H,
-                                        last ? nullptr : c->L[l + 1].A_qkv.data(), 3 * r, c->ws_qkv, nullptr, 0,
-                                        st));
+  const int R = rounds_per_token(c);
+  if (i == 0) return swl_copy_rows(n, c->tokens.data(), in, c->tok_bytes.data(), st);
+  if (i == 1)
+    return swl_fused_resid_norm_shrink(n, rows, out, H, nullptr, 0, 0.f, nullptr, 0, 0, h, H, c->L[0].in_norm, H,
+                                       c->eps, in, H, c->L[0].A_qkv.data(), 3 * r, c->ws_qkv, nullptr, 0, st);
+  if (i == R) {
+    SWL_TRY(swl_copy_rows(n, out, c->tokens.data(), c->tok_bytes.data(), st));
+    if (c->history) {
+      std::vector<void*> dst(n);
+      for (int k = 0; k < n; ++k) dst[k] = static_cast<int64_t*>(c->history) + static_cast<int64_t>(t) * n + k;
+      SWL_TRY(swl_copy_rows(n, out, dst.data(), c->tok_bytes.data(), st));
+    }
+    return swl_advance_i32(c->seqlen_base, n, 1, st);
   }
-  SWL_TRY(protocol_round(c, kOpLmHead, 0, H));
-  SWL_TRY(swl_copy_rows(n, out, c->tokens.data(), c->tok_bytes.data(), st));
-  if (c->history) {
-    std::vector<void*> dst(n);
-    for (int i = 0; i < n; ++i) dst[i] = static_cast<int64_t*>(c->history) + static_cast<int64_t>(t) * n + i;
-    SWL_TRY(swl_copy_rows(n, out, dst.data(), c->tok_bytes.data(), st));
+  const int l = (i - 2) / 4;  // the layer of the round just finished
+  const WcLayer& w = c->L[l];
+  switch ((i - 2) % 4) {
+    case 0:  // after QKV: LoRA expand + RoPE + K/V append, attention -> O input
+      SWL_TRY(swl_fused_qkv_rope(n, rows, out, qkv_n, w.B_qkv.data(), r, c->ws_qkv, c->norm_splits,
+                                 c->block_tables.data(), w.k_cache.data(), w.v_cache.data(), c->seqlens.data(), c->hq,
+                                 c->hkv, D, c->page, c->cos_sin, c->q_rot, nullptr, 0, st));
+      return swl_paged_attention_shrink(n, rows, c->block_tables.data(), w.k_cache.data(), w.v_cache.data(),
+                                        c->seqlens.data(), in, static_cast<int64_t>(c->hq) * D, c->hq, c->hkv, D,
+                                        c->page, 1.0f / sqrtf(static_cast<float>(D)), c->max_len, c->q_rot, c->part,
+                                        w.A_o.data(), r, c->ws_o, nullptr, 0, st);
+    case 1:  // after O: LoRA expand, + residual, RMSNorm -> Gate+Up input
+      return swl_fused_resid_norm_shrink(n, rows, out, H, w.B_o.data(), r, c->scaling, c->ws_o, c->hq, 1, h, H,
+                                         w.post_norm, H, c->eps, in, H, w.A_gu.data(), 2 * r, c->ws_gu, nullptr, 0,
+                                         st);
+    case 2:  // after Gate+Up: LoRA expand, SiLU * up -> Down input
+      return swl_fused_gu_silu_shrink(n, rows, out, 2 * static_cast<int64_t>(I), w.B_gu.data(), r, c->ws_gu,
+                                      c->norm_splits, I, in, I, w.A_dn.data(), r, c->ws_dn, nullptr, 0, st);
+    default: {  // after Down: LoRA expand, + residual, next RMSNorm -> next QKV (or LM-head) input
+      const bool last = l == c->layers - 1;
+      return swl_fused_resid_norm_shrink(n, rows, out, H, w.B_dn.data(), r, c->scaling, c->ws_dn, c->dn_splits, 1,
+                                         h, H, last ? c->final_norm : c->L[l + 1].in_norm, H, c->eps, in, H,
+                                         last ? nullptr : c->L[l + 1].A_qkv.data(), 3 * r, c->ws_qkv, nullptr, 0,
+                                         st);
+    }
   }
-  SWL_TRY(swl_advance_i32(c->seqlen_base, n, 1, st));
+}
+
+void drop_graphs(WorkerClient* c) {
+  for (cudaGraphExec_t g : c->graphs)
+    if (g) cudaGraphExecDestroy(g);
+  c->graphs.clear();
+}
+
+// Event mode with graphs: segments 0 .. rounds_per_token - 1 captured once,
+// each as [wait for the round event] + launches + [record the input event]
+// (segment 0 has no wait: it follows the token-end launches on the stream).
+int build_graphs(WorkerClient* c) {
+  drop_graphs(c);
+  const int R = rounds_per_token(c);
+  c->graphs.assign(R, nullptr);
+  for (int i = 0; i < R; ++i) {
+    cudaGraph_t g = nullptr;
+    SWL_CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    int st = SWL_OK;
+    if (i > 0 && cudaStreamWaitEvent(c->stream, c->round_event, cudaEventWaitExternal) != cudaSuccess)
+      st = set_error(SWL_ERR_CUDA, "worker client: capturing the round-event wait");
+    if (st == SWL_OK) st = enqueue_segment(c, i, 0);
+    if (st == SWL_OK && cudaEventRecordWithFlags(c->input_event, c->stream, cudaEventRecordExternal) != cudaSuccess)
+      st = set_error(SWL_ERR_CUDA, "worker client: capturing the input-event record");
+    const cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (st != SWL_OK || e != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      drop_graphs(c);
+      return st != SWL_OK ? st : set_error(SWL_ERR_CUDA, "worker client: capture: %s", cudaGetErrorString(e));
+    }
+    const cudaError_t ie = cudaGraphInstantiate(&c->graphs[i], g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) {
+      drop_graphs(c);
+      return set_error(SWL_ERR_CUDA, "worker client: instantiating a segment graph: %s", cudaGetErrorString(ie));
+    }
+  }
   return SWL_OK;
+}
+
+// One decode token for every slot of the client: the reference worker's
+// per-token sequence, segment by segment, each round through the protocol.
+int run_token(WorkerClient* c, int t) {
+  const int R = rounds_per_token(c);
+  const bool graphed = !c->graphs.empty();
+  for (int i = 0; i < R; ++i) {
+    int op, layer;
+    int64_t dx;
+    round_of(c, i, &op, &layer, &dx);
+    if (graphed) SWL_CUDA_TRY(cudaGraphLaunch(c->graphs[i], c->stream));
+    else SWL_TRY(enqueue_segment(c, i, t));
+    SWL_TRY(protocol_round(c, op, layer, dx, graphed));
+  }
+  // token end: the stream waits for the LM-head round before reading its picks
+  if (graphed) SWL_CUDA_TRY(cudaStreamWaitEvent(c->stream, c->round_event, 0));
+  return enqueue_segment(c, R, t);
 }
 
 }  // namespace
@@ -338,6 +424,7 @@ SWL_EXPORT int swl_wc_configure(void* handle, int input_mode, int64_t timeout_ms
   } else if (c->input_mode == 2) {
     for (int i = 0; i < c->n; ++i) swl_agg_set_slot_input_event_local(c->slot_ids[i], nullptr);
   }
+  if (input_mode != 2) drop_graphs(c);
   c->input_mode = input_mode;
   c->timeout_ms = timeout_ms;
   c->history = history;
@@ -354,6 +441,9 @@ SWL_EXPORT int swl_wc_run(void* handle, int tokens, int64_t* token_ns) {
   SWL_TRY(check_client(c));
   if (tokens < 0) return set_error(SWL_ERR_ARG, "worker client: negative token count");
   for (int t = 0; t < tokens; ++t) {
+    // per-segment graphs are captured after one eager token (which sets the
+    // kernels' attributes outside any capture)
+    if (c->use_graphs && c->input_mode == 2 && c->graphs.empty() && c->rounds_done > 0) SWL_TRY(build_graphs(c));
     const auto t0 = std::chrono::steady_clock::now();
     SWL_TRY(run_token(c, t));
     if (token_ns)
@@ -369,9 +459,21 @@ SWL_EXPORT int64_t swl_wc_rounds(void* handle) {
   return c ? c->rounds_done : 0;
 }
 
+// Event mode (input mode 2) only: 1 captures the launches between each pair
+// of rounds into one CUDA graph (one launch per round instead of several),
+// after the client's first eager token; 0 launches them one by one.
+SWL_EXPORT int swl_wc_use_graphs(void* handle, int on) {
+  auto* c = static_cast<WorkerClient*>(handle);
+  if (!c) return set_error(SWL_ERR_ARG, "worker client: null handle");
+  c->use_graphs = on != 0;
+  if (!c->use_graphs) drop_graphs(c);
+  return SWL_OK;
+}
+
 SWL_EXPORT int swl_wc_destroy(void* handle) {
   auto* c = static_cast<WorkerClient*>(handle);
   if (!c) return SWL_OK;
+  drop_graphs(c);
   if (c->stream) {
     cudaStreamSynchronize(c->stream);
     cudaStreamDestroy(c->stream);

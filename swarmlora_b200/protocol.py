@@ -23,7 +23,10 @@ prepare_input_slot) or from a device-written host flag ("flag"). "event"
 a client records an event after writing its inputs and sets its ready bits
 at once, the aggregator's stream waits for those events, and the epoch
 moves as soon as the round is enqueued; the client's stream then waits for
-the round's event. No host thread waits for the GPU inside a token.
+the round's event. No host thread waits for the GPU inside a token. With
+`graphs` (event completion only) each client captures the launches between
+two rounds, event wait and record included, into one CUDA graph after its
+first token, so a round costs each client one launch.
 """
 from __future__ import annotations
 
@@ -41,7 +44,7 @@ from ._native import check, i32_array, lib, ptr_array
 
 class ProtocolRun:
     def __init__(self, grp, workers: int, completion: str = "device", input_ready: str = "flag",
-                 timeout_ms: int = 30000, capacity: int = 512):
+                 timeout_ms: int = 30000, capacity: int = 512, graphs: bool = False):
         if (completion, input_ready) not in (("host", "sync"), ("host", "flag"), ("device", "sync"),
                                              ("device", "flag"), ("event", "event")):
             raise ValueError("completion 'host' or 'device' with input_ready 'sync' or 'flag', "
@@ -106,6 +109,11 @@ class ProtocolRun:
                                          lay["kc"], lay["vc"], lay["A_qkv"], lay["B_qkv"], lay["A_o"], lay["B_o"],
                                          lay["A_gu"], lay["B_gu"], lay["A_dn"], lay["B_dn"]))
             check(L.swl_wc_configure(h, self._input_mode(input_ready), timeout_ms, None))
+            if graphs:
+                if completion != "event":
+                    raise ValueError("per-segment graphs need event completion")
+                check(L.swl_wc_use_graphs(h, 1))
+        self.graphs = bool(graphs)
         self.timeout_ms = timeout_ms
         self._loop = None
         self._loop_err = []

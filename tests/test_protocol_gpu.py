@@ -4,8 +4,9 @@ clients that request every round through the shared-memory ring and epoch
 barrier (worker_sync.py:230-389, 1274-1425), one host thread per client.
 
 * one client owning every slot (device-published completion with a flag
-  input wait, and event completion): the same launches as the in-process
-  engine's step, so tokens and hidden rows are bit-identical to it;
+  input wait, event completion, event completion with per-segment graphs):
+  the same launches as the in-process engine's step, so tokens and hidden
+  rows are bit-identical to it;
 * one client per two slots (the reference's host completion with a
   stream-sync input wait, and event completion): tokens and last-layer
   hidden rows against the CPU oracle (attention splits its work by the
@@ -49,8 +50,9 @@ def _group(cuda):
     return cfg, base, adapters, ctx, grp
 
 
-@pytest.mark.parametrize("completion,input_ready", [("device", "flag"), ("event", "event")])
-def test_one_client_matches_the_engine_bit_for_bit(native, cuda, completion, input_ready):
+@pytest.mark.parametrize("completion,input_ready,graphs", [("device", "flag", False), ("event", "event", False),
+                                                            ("event", "event", True)])
+def test_one_client_matches_the_engine_bit_for_bit(native, cuda, completion, input_ready, graphs):
     from swarmlora_b200.protocol import ProtocolRun
     cfg, base, adapters, ctx, grp = _group(cuda)
     try:
@@ -70,7 +72,7 @@ def test_one_client_matches_the_engine_bit_for_bit(native, cuda, completion, inp
             grp.v_cache[l].copy_(v0[l])
         grp.reset_positions()
         grp.tokens.copy_(first)
-        run = ProtocolRun(grp, workers=1, completion=completion, input_ready=input_ready)
+        run = ProtocolRun(grp, workers=1, completion=completion, input_ready=input_ready, graphs=graphs)
         try:
             got = run.run(3, record=True)
         finally:
@@ -86,8 +88,9 @@ def test_one_client_matches_the_engine_bit_for_bit(native, cuda, completion, inp
         grp.close()
 
 
-@pytest.mark.parametrize("completion,input_ready", [("host", "sync"), ("event", "event")])
-def test_clients_of_two_slots_match_the_oracle(native, cuda, completion, input_ready):
+@pytest.mark.parametrize("completion,input_ready,graphs", [("host", "sync", False), ("event", "event", False),
+                                                            ("event", "event", True)])
+def test_clients_of_two_slots_match_the_oracle(native, cuda, completion, input_ready, graphs):
     from swarmlora_b200.protocol import ProtocolRun
     cfg, base, adapters, ctx, grp = _group(cuda)
     try:
@@ -97,7 +100,7 @@ def test_clients_of_two_slots_match_the_oracle(native, cuda, completion, input_r
         bts = [t.tolist() for t in grp.block_tables]
         tokens = [5, 4095, 17, 0, 1234, 77]
         grp.tokens.copy_(torch.tensor(tokens))
-        run = ProtocolRun(grp, workers=3, completion=completion, input_ready=input_ready)
+        run = ProtocolRun(grp, workers=3, completion=completion, input_ready=input_ready, graphs=graphs)
         try:  # all tokens in one go: the aggregator evicts a slot not ready within 500 ms
             got = run.run(3, record=True)
         finally:
