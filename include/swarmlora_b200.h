@@ -183,6 +183,11 @@ int swl_agg_completion_mode(void);
  * event: its IPC handle (64 bytes) for workers in other processes, or the
  * cudaEvent_t for workers in this process. A slot's input event: from the
  * worker's IPC handle (NULL / 0 = none), or a cudaEvent_t of this process. */
+/* Under event completion, 1 = replay each (op, layer) round from a CUDA
+ * graph holding the input-event waits, the round's kernels and the round
+ * event's record, captured when the same slots send the same rows a second
+ * time (the LM-head round always runs eagerly); 0 = launch each round. */
+int swl_agg_set_round_graphs(int on);
 int swl_agg_round_event_handle(unsigned char* out, size_t len);
 int swl_agg_round_event(void** event);
 int swl_agg_set_slot_input_event(int slot_id, const unsigned char* handle, size_t len);

@@ -91,6 +91,7 @@ SIGNATURES: dict[str, tuple] = {
     "swl_agg_main_loop_slots": (_i32, [_i32, _i32]),
     "swl_agg_set_completion_mode": (_i32, [_i32]),
     "swl_agg_completion_mode": (_i32, []),
+    "swl_agg_set_round_graphs": (_i32, [_i32]),
     "swl_agg_round_event_handle": (_i32, [C.c_char_p, _sz]),
     "swl_agg_round_event": (_i32, [C.POINTER(C.c_void_p)]),
     "swl_agg_set_slot_input_event": (_i32, [_i32, C.c_char_p, _sz]),

@@ -857,6 +857,7 @@ SWL_EXPORT int swl_agg_import_weights(const swl_weight_ipc* recs, int count, con
 // ready bits (agg_protocol.h, deferred completion).
 namespace {
 int g_completion_mode = 0;
+bool g_round_graphs = false;
 void* g_ctrl_registered = nullptr;  // the mapping registered with cudaHostRegister
 size_t g_ctrl_registered_bytes = 0;
 int64_t* g_epoch_dev = nullptr;     // device address of barrier_done_epoch
@@ -991,6 +992,15 @@ SWL_EXPORT int swl_agg_set_completion_mode(int mode) {
 }
 
 SWL_EXPORT int swl_agg_completion_mode(void) { return g_completion_mode; }
+
+// Under event completion: 1 replays each (op, layer) round from a CUDA graph
+// (the input-event waits, the round's kernels and the round event's record),
+// captured when the same slots send the same rows a second time; the LM-head
+// round always runs eagerly. Takes effect at the next main loop.
+SWL_EXPORT int swl_agg_set_round_graphs(int on) {
+  g_round_graphs = on != 0;
+  return SWL_OK;
+}
 
 // ext_aggregator.cpp:427-459 init_aggregator_queue: map the queue segment
 // created by ext_ipc_queue.create_queue (this module's own view).
@@ -1348,10 +1358,61 @@ struct AggHooks {
   }
   bool deferred = false;  // device-published completion (mode 1)
   bool events = false;    // event completion (mode 2)
+  bool graphs = false;    // event completion: replay each (op, layer) round from a CUDA graph
   std::vector<cudaEvent_t> waits;
+  // A round's graph: the waits for its slots' input events, its kernels, the
+  // round event's record; valid while the same slots send the same rows
+  // with the same events (the steady state of decode).
+  struct RoundGraph {
+    std::vector<int> slots;
+    std::vector<int64_t> rows;
+    std::vector<cudaEvent_t> events;
+    int seen = 0;  // eager runs of this command set (capture after the first)
+    cudaGraphExec_t exec = nullptr;
+  };
+  std::map<std::pair<int, int>, RoundGraph> graph_cache;
+  ~AggHooks() {
+    for (auto& kv : graph_cache)
+      if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+  }
   bool deferred_epoch() const { return deferred; }
   void flush() {
     if (deferred || events) cudaStreamSynchronize(g_stream);
+  }
+  // The cached graph of this round if it matches the commands, capturing it
+  // when the same command set comes a second time; nullptr = run eagerly.
+  // The LM-head round is not cached: its sampling draws move every token.
+  cudaGraphExec_t round_graph(int op, int layer) {
+    if (!graphs || op == kOpLmHead) return nullptr;
+    RoundGraph& g = graph_cache[{op, layer}];
+    bool same = g.slots.size() == good.size() && g.events == waits;
+    for (size_t i = 0; same && i < good.size(); ++i)
+      same = g.slots[i] == good[i].slot_id && g.rows[i] == good[i].rows;
+    if (!same) {
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+      g = RoundGraph();
+      for (const RoundCmd& c : good) {
+        g.slots.push_back(c.slot_id);
+        g.rows.push_back(c.rows);
+      }
+      g.events = waits;
+    }
+    if (g.exec) return g.exec;
+    if (g.seen++ == 0) return nullptr;  // the first run sets the kernels' attributes outside any capture
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(g_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    bool ok = true;
+    for (cudaEvent_t e : waits) ok = ok && cudaStreamWaitEvent(g_stream, e, cudaEventWaitExternal) == cudaSuccess;
+    ok = ok && run_round(op, layer, good, g_stream) == SWL_OK;
+    ok = ok && cudaEventRecordWithFlags(g_round_event, g_stream, cudaEventRecordExternal) == cudaSuccess;
+    const bool ended = cudaStreamEndCapture(g_stream, &graph) == cudaSuccess;
+    if (ok && ended && graph && cudaGraphInstantiate(&g.exec, graph, 0) != cudaSuccess) g.exec = nullptr;
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return g.exec;
   }
   int round(int op, int layer, const std::vector<DrainedCmd>&, const std::vector<int>&, int64_t epoch) {
     if (events) {
@@ -1359,6 +1420,13 @@ struct AggHooks {
       for (const RoundCmd& c : good) {
         cudaEvent_t e = g_pool.slots[c.slot_id].input_event;
         if (std::find(waits.begin(), waits.end(), e) == waits.end()) waits.push_back(e);
+      }
+      if (cudaGraphExec_t exec = round_graph(op, layer)) {
+        const cudaError_t e = cudaGraphLaunch(exec, g_stream);
+        if (e == cudaSuccess) return SWL_OK;
+        set_error(SWL_ERR_CUDA, "round: replaying the round graph: %s", cudaGetErrorString(e));
+        fprintf(stderr, "[swl aggregator] %s\n", last_error());
+        return SWL_ERR_CUDA;
       }
       for (cudaEvent_t e : waits) {
         const cudaError_t err = cudaStreamWaitEvent(g_stream, e, 0);
@@ -1406,6 +1474,7 @@ SWL_EXPORT int swl_agg_main_loop_slots(int num_slots, int dtype_code) {
   } else if (g_completion_mode == 2) {
     SWL_TRY(ensure_round_event());
     hooks.events = true;
+    hooks.graphs = g_round_graphs;
   }
   const int st = run_main_loop(g_ctrl, g_ring, g_capacity, 1 + g_num_layers * 4 + 1, hooks);
   if (st == SWL_OK && (hooks.deferred || hooks.events)) {

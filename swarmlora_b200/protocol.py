@@ -26,7 +26,9 @@ moves as soon as the round is enqueued; the client's stream then waits for
 the round's event. No host thread waits for the GPU inside a token. With
 `graphs` (event completion only) each client captures the launches between
 two rounds, event wait and record included, into one CUDA graph after its
-first token, so a round costs each client one launch.
+first token, and the aggregator replays each round (its input-event waits,
+kernels and round-event record) from a graph once the same command set
+repeats, so a round costs each client and the aggregator one launch.
 """
 from __future__ import annotations
 
@@ -64,6 +66,8 @@ class ProtocolRun:
         agg.init_aggregator_queue(info["shm_name"], capacity)
         extq.init_batch_control(n)
         check(L.swl_agg_set_completion_mode({"host": 0, "device": 1, "event": 2}[completion]))
+        # with graphs, the aggregator also replays each round from a graph
+        check(L.swl_agg_set_round_graphs(1 if graphs else 0))
         # contiguous slot ranges, as even as possible
         bounds = [round(i * n / workers) for i in range(workers + 1)]
         self.ranges = [(bounds[i], bounds[i + 1]) for i in range(workers)]
@@ -191,5 +195,6 @@ class ProtocolRun:
         self.handles = []
         if getattr(self, "_queue_open", False):
             check(L.swl_agg_set_completion_mode(0))
+            check(L.swl_agg_set_round_graphs(0))
             extq.close_queue()
             self._queue_open = False
