@@ -120,3 +120,62 @@ def test_clients_of_two_slots_match_the_oracle(native, cuda, completion, input_r
         assert grp.seqlens.cpu().tolist() == seq
     finally:
         grp.close()
+
+
+def test_stalled_client_is_evicted_and_the_other_finishes(native, cuda):
+    """Event completion with graphs: one of two clients runs one token and
+    stops (its worker process died between tokens, as far as the aggregator
+    can tell); the aggregator evicts its slots after the barrier timeout and
+    the other client's remaining tokens still match the oracle."""
+    import ctypes as C
+    import threading
+    from swarmlora_b200._native import lib
+    from swarmlora_b200 import ext_ipc_queue as extq
+    from swarmlora_b200.protocol import ProtocolRun
+    cfg, base, adapters, ctx, grp = _group(cuda)
+    try:
+        base_c, ad_c = _cpu(base), _cpu(adapters)
+        kc = [k.cpu() for k in grp.k_cache]
+        vc = [v.cpu() for v in grp.v_cache]
+        bts = [t.tolist() for t in grp.block_tables]
+        tokens = [5, 4095, 17, 0, 1234, 77]
+        grp.tokens.copy_(torch.tensor(tokens))
+        run = ProtocolRun(grp, workers=2, completion="event", input_ready="event", graphs=True)
+        try:
+            run._start_loop()
+            L = lib()
+            hist = torch.zeros(3, 3, dtype=torch.int64, device=cuda)
+            L.swl_wc_configure(run.handles[1], 2, 30000, C.c_void_p(hist.data_ptr()))
+            L.swl_wc_configure(run.handles[0], 2, 30000, None)
+            status = {}
+
+            def client(i, n):
+                status[i] = L.swl_wc_run(run.handles[i], n, None)
+            t0 = threading.Thread(target=client, args=(0, 1))
+            t1 = threading.Thread(target=client, args=(1, 3))
+            t0.start()
+            t1.start()
+            t0.join(timeout=60)
+            t1.join(timeout=60)
+            assert status == {0: 0, 1: 0}, status
+            gone = [extq.is_slot_evicted(grp.slot_ids[i]) for i in range(6)]
+            assert gone == [True] * 3 + [False] * 3, gone
+        finally:
+            run.close()
+        # the surviving slots (3..5) against the oracle over their three tokens
+        seq = list(ctx)
+        picks = hist.cpu()
+        for step in range(3):
+            want, _, logits, h_last = decode_step(cfg, base_c, ad_c, kc, vc, bts, seq, tokens)
+            for j, i in enumerate(range(3, 6)):
+                g = int(picks[step, j])
+                if g != int(want[i]):
+                    lg = logits[i].float()
+                    assert lg[g] >= lg.max() - BF_ULP * lg.max().abs(), f"step {step} slot {i}: {g} != {int(want[i])}"
+            # slots 0..2 stopped after the first token: the oracle keeps them
+            # decoding, their rows do not touch the others'
+            tokens = [int(x) for x in want.tolist()[:3]] + [int(picks[step, j]) for j in range(3)]
+            seq = [s + 1 for s in seq]
+        assert_close(grp.h[3:], h_last[3:], "surviving slots' last-layer hidden", atol_rms=ATOL_RMS_MULTILAYER)
+    finally:
+        grp.close()
