@@ -160,9 +160,15 @@ int protocol_round(WorkerClient* c, int op, int layer, int64_t dx, bool launched
   const int64_t e0 = swl_q_get_barrier_done_epoch();
   for (int i = 0; i < c->n; ++i) {
     int st;
+    const auto t0 = std::chrono::steady_clock::now();
     while ((st = swl_q_submit_slot_command(op, layer, c->slot_ids[i], c->worker_ids[i], 1, c->rows[i], dx, 0, 0,
-                                           0, 0, 0)) == SWL_ERR_FULL)
+                                           0, 0, 0)) == SWL_ERR_FULL) {
+      // the ring drains as the aggregator takes commands; give up with the client's time limit
+      if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(c->timeout_ms))
+        return set_error(SWL_ERR_TIMEOUT, "worker client: command ring stayed full for %lld ms",
+                         static_cast<long long>(c->timeout_ms));
       std::this_thread::yield();
+    }
     SWL_TRY(st);
   }
   for (int i = 0; i < c->n; ++i) SWL_TRY(swl_q_slot_signal_ready(c->slot_ids[i]));
