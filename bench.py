@@ -752,7 +752,9 @@ def mixed_arm(args):
     each step first stages the prefill chunks' token ids into the group's
     token buffer. value = new tokens (prefill + decode) per second; e2e adds
     the chunks' ids from pinned host memory and reads the next tokens back
-    every step. Prints one JSON line."""
+    every step. Each prefill slot starts at a seeded chunk boundary inside
+    its prompt (its prefix already in the cache), so the prefixes attended to
+    spread over the prompt lengths. Prints one JSON line."""
     import dataclasses
     import torch
     import swarmlora_b200
@@ -771,14 +773,18 @@ def mixed_arm(args):
     steps_total = args.warmup + args.steps
     base = random_base(cfg, seed=1, device=dev)
     adapters = [random_adapter(cfg, seed=300 + i, device=dev) for i in range(n)]
-    grp = SlotGroup(cfg, base, adapters, [0] * n_pf + dec_ctx,
+    # each prefill slot starts at a seeded chunk boundary inside its prompt, so
+    # the prefixes its rows attend to cover the prompt lengths as a steady
+    # stream of prefilling requests does (not only their first chunks)
+    offs = [chunk * int(torch.randint(0, (p_len - chunk) // chunk + 1, (1,), generator=g)) for p_len in prompts]
+    grp = SlotGroup(cfg, base, adapters, offs + dec_ctx,
                     max_new=max(max(prompts), 2 * steps_total + 8), device=0, seed=0)
     rows = [chunk] * n_pf + [1] * n_dec
     ids = torch.randint(0, cfg.vocab, (n_pf, max(prompts)), generator=g)
     ids_dev = ids.to(dev)
     grp.tokens.copy_(torch.randint(0, cfg.vocab, (n,), generator=g))
     stream = torch.cuda.Stream(dev)
-    done = [0] * n_pf  # prefilled tokens of each prefill slot's current prompt
+    done = list(offs)  # prefilled tokens of each prefill slot's current prompt
 
     def stage(host_ids=None):
         """Token ids of the next step into tok_in (decode rows: last outputs)."""
@@ -846,7 +852,8 @@ def mixed_arm(args):
         "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights, adapters, prompts)",
         "config": {"workload": f"BASELINE config 3: {cfg.layers} layers, vocab {cfg.vocab}; 4 slots prefilling "
-                               f"prompts U[512,2048] in {chunk}-row chunks + 24 decode slots at ctx U[256,2048], "
+                               f"prompts U[512,2048] in {chunk}-row chunks (each from a seeded point inside its "
+                               f"prompt) + 24 decode slots at ctx U[256,2048], "
                                f"{new_rows} rows per round, distinct r=16 adapters",
                    "prefill_tok_s": round(n_pf * chunk * args.steps / (ms / 1e3), 2),
                    "decode_tok_s": round(n_dec * args.steps / (ms / 1e3), 2),
