@@ -363,6 +363,10 @@ int swl_rope_append(int nseg, const int* rows, const void* const* qkv, int64_t q
  * each holding its group's slices); 0 = automatic. A launch option, no
  * counterpart in the reference. */
 int swl_attention_tune(int chunk_pages, int stages, int groups);
+/* 1 (default): two consecutive rows of one slot (a prefill chunk) share each
+ * page read, their query heads filling the MMA's columns together; 0: every
+ * row reads its pages alone. A launch option, no counterpart in the reference. */
+int swl_attention_pairing(int on);
 /* fp32 scratch floats swl_paged_attention needs in `part`. */
 int64_t swl_attention_part_floats(int total_rows, int hq, int hkv, int max_len);
 /* Causal GQA attention over paged KV (flash_attn_with_kvcache semantics,

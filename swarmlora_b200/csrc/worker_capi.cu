@@ -136,6 +136,10 @@ SWL_EXPORT int swl_attention_tune(int chunk_pages, int stages, int groups) {
   return set_attention_tuning(chunk_pages, stages, groups);
 }
 
+// 1 (default): two consecutive rows of a slot share each page read when a
+// launch has slots with several rows; 0: every row reads its pages alone.
+SWL_EXPORT int swl_attention_pairing(int on) { return set_attention_pairing(on); }
+
 // Causal GQA attention of each new token over its slot's paged cache
 // (flash_attn_with_kvcache semantics, worker_sync.py:196-203): token t of
 // slot i attends to cache positions 0 .. *seqlens[i] + t. max_len bounds

@@ -269,7 +269,7 @@ constexpr int kAttnStagesMax = 4;
 constexpr int kAttnMaxHkv = 8;
 constexpr int kAttnMaxRows = 256;
 constexpr int kMinUnits = 8;                             // pages per CTA at least
-constexpr int kAttnSmemMax = 227 * 1024 - 4096;          // dynamic ring budget
+constexpr int kAttnSmemMax = 227 * 1024 - 8192;          // dynamic ring budget (static tables take ~5 KB)
 constexpr uint64_t kAttnWaitNs = 2000000000ull;
 
 // Tuning overrides (0 = automatic): minimum pages per CTA, ring depth, kv
@@ -277,15 +277,19 @@ constexpr uint64_t kAttnWaitNs = 2000000000ull;
 std::atomic<int> g_attn_min_units{0};
 std::atomic<int> g_attn_stages{0};
 std::atomic<int> g_attn_groups{0};
+std::atomic<int> g_attn_no_pair{0};  // tuning: never pair a slot's rows
 
 __host__ __device__ __forceinline__ int attn_row_bytes(int hkv) { return hkv * kD * 2 + 16; }
-__host__ __device__ __forceinline__ int attn_stage_bytes(int hq, int hkv) {
-  return 2 * kPageTok * attn_row_bytes(hkv) + hq * kD * 2;
+// One page stage: K and V token rows of the CTA's kv heads, and the query
+// rows of `qrows` token rows (a group) for its query heads.
+__host__ __device__ __forceinline__ int attn_stage_bytes(int hq, int hkv, int qrows = 1) {
+  return 2 * kPageTok * attn_row_bytes(hkv) + qrows * hq * kD * 2;
 }
 
 // The partial scratch starts with a header the combine step reads: [0] units
-// per CTA, [1 + r] page prefix of row r (r = 0..rows), padded to 32 floats.
-__host__ __device__ __forceinline__ int64_t attn_hdr_floats(int rows) { return (rows + 2 + 31) / 32 * 32; }
+// per CTA, [1 + 2r] and [2 + 2r] the page prefix at the start and the end of
+// row r's group (r = 0..rows-1), padded to 32 floats.
+__host__ __device__ __forceinline__ int64_t attn_hdr_floats(int rows) { return (2 * rows + 1 + 31) / 32 * 32; }
 
 // Units per CTA: at least min_units, and enough that `grid` CTAs cover all.
 __device__ __forceinline__ int64_t attn_units_per_cta(int64_t total, int grid, int min_units) {
@@ -321,10 +325,13 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 template <int kStages>
 __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
     paged_attention_kernel(const __grid_constant__ AttnTable tab, const AttnParams p, int max_pieces,
-                           int min_units, float* __restrict__ part) {
+                           int min_units, int pair, float* __restrict__ part) {
   extern __shared__ __align__(128) uint8_t att_dyn[];
-  __shared__ int pre[kAttnMaxRows + 1];  // page prefix over rows
+  __shared__ int pre[kAttnMaxRows + 1];  // page prefix over groups
   __shared__ int keys[kAttnMaxRows];     // keys (causal length) of each row
+  __shared__ int gfirst[kAttnMaxRows];   // first row of each group
+  __shared__ int gcount[kAttnMaxRows];   // rows of each group (1 or 2)
+  __shared__ int rgroup[kAttnMaxRows];   // group of each row
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // the kv heads are split into gridDim.y groups; this CTA's group is
   // blockIdx.y and it holds only that group's slices of each page
@@ -332,7 +339,10 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   const int hkv_c = hkv / static_cast<int>(gridDim.y);
   const int row_bytes = attn_row_bytes(hkv_c);
   const int kv_bytes = kPageTok * row_bytes;
-  const int stage_bytes = attn_stage_bytes(hkv_c * G, hkv_c);
+  // pair: two consecutive rows of a slot share each page read (their query
+  // heads fill the MMA's 8 columns: column = 4 * row-in-group + head)
+  const int qrows = pair ? 2 : 1;
+  const int stage_bytes = attn_stage_bytes(hkv_c * G, hkv_c, qrows);
 
   // Page prefix over the rows (every CTA derives the same unit stream). The
   // context lengths and block tables are not written by the launch just
@@ -340,38 +350,62 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   // prefix, this CTA's range and its first page id are set up before
   // waiting for it.
   const int rows = tab.seg.total_rows;
+  __shared__ int ngroups_sh;
   if (warp == 0) {
-    int carry = 0;
+    // rows -> keys and groups (a group starts at every row, or with pairing
+    // at every other row of a slot)
+    int gcarry = 0;
     for (int r0 = 0; r0 < rows; r0 += 32) {
       const int r = r0 + lane;
-      int v = 0;
+      bool start = false;
+      int n_in = 1;
       if (r < rows) {
         const int sg = seg_of_row(tab.seg, r);
-        const int L = *tab.seqlen[sg] + (r - tab.seg.row_start[sg]) + 1;
-        keys[r] = L;
-        v = (L + kPageTok - 1) / kPageTok;
+        const int local = r - tab.seg.row_start[sg];
+        keys[r] = *tab.seqlen[sg] + local + 1;
+        start = !pair || (local & 1) == 0;
+        if (pair && start && r + 1 < tab.seg.row_start[sg + 1]) n_in = 2;
       }
+      const unsigned m = __ballot_sync(0xffffffffu, start);
+      const int gi = gcarry + __popc(m & ((1u << lane) - 1u));
+      if (start) {
+        gfirst[gi] = r;
+        gcount[gi] = n_in;
+        rgroup[r] = gi;
+        if (n_in == 2) rgroup[r + 1] = gi;
+      }
+      gcarry += __popc(m);
+    }
+    if (lane == 0) ngroups_sh = gcarry;
+    __syncwarp();
+    // page prefix over groups: a group has the pages of its last row
+    int carry = 0;
+    for (int j0 = 0; j0 < gcarry; j0 += 32) {
+      const int j = j0 + lane;
+      int v = 0;
+      if (j < gcarry) v = (keys[gfirst[j] + gcount[j] - 1] + kPageTok - 1) / kPageTok;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += y;
       }
-      if (r < rows) pre[r + 1] = carry + v;
+      if (j < gcarry) pre[j + 1] = carry + v;
       carry += __shfl_sync(0xffffffffu, v, 31);
     }
     if (lane == 0) pre[0] = 0;
   }
   __syncthreads();
-  const int64_t total = pre[rows];
+  const int ngroups = ngroups_sh;
+  const int64_t total = pre[ngroups];
   const int64_t W = attn_units_per_cta(total, gridDim.x, min_units);
   float* const recs = part + attn_hdr_floats(rows);
   const int64_t u0 = static_cast<int64_t>(blockIdx.x) * W;
   const int64_t u1 = min(total, u0 + W);
   const bool idle = u0 >= u1;
   const int nunits = idle ? 0 : static_cast<int>(u1 - u0);
-  int r_start;
+  int r_start;  // the first group of this CTA's range
   {
-    int lo = 0, hi = rows - 1;
+    int lo = 0, hi = ngroups - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
       if (pre[mid] <= u0) lo = mid;
@@ -384,27 +418,31 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   const int kvh = static_cast<int>(blockIdx.y) * hkv_c + warp;  // this warp's kv head
   const uint32_t sm0 = ptx::smem_addr(att_dyn);
   const uint32_t head_off = warp * kD * 2;
-  const uint32_t q_off = 2 * kv_bytes + warp * G * kD * 2;  // this head's query rows in a stage
+  const uint32_t q_off = 2 * kv_bytes + warp * qrows * G * kD * 2;  // this head's query rows in a stage
 
   // ---- loads: this warp's slice of unit (lr, lt) into stage `st` ----
   const int ld_tok = lane >> 4, ld_ch = lane & 15;  // token parity and 16-byte chunk of this lane
   // load position (row lr, page lt), its slot, and its page id fetched one
   // unit ahead so the copies of a page never wait on the block-table read
-  int lr = r_start, lt = t_start;
-  int lsg = seg_of_row(tab.seg, lr);
+  int lr = r_start, lt = t_start;  // load position: group lr, page lt
+  int lsg = idle ? 0 : seg_of_row(tab.seg, gfirst[lr]);
   int next_page = idle ? 0 : tab.block_table[lsg][lt];
   ptx::grid_dep_wait();
   ptx::grid_dep_launch();
   if (blockIdx.x == 0 && blockIdx.y == 0 && warp == 0) {
     int* hdr = reinterpret_cast<int*>(part);
     if (lane == 0) hdr[0] = static_cast<int>(W);
-    for (int r = lane; r <= rows; r += 32) hdr[1 + r] = pre[r];
+    for (int r = lane; r < rows; r += 32) {
+      hdr[1 + 2 * r] = pre[rgroup[r]];
+      hdr[2 + 2 * r] = pre[rgroup[r] + 1];
+    }
   }
   if (idle) return;
   auto issue = [&](int j) {
     const int st = j % kStages;
     const uint32_t ss = sm0 + st * stage_bytes;
-    const int live = min(kPageTok, keys[lr] - lt * kPageTok);
+    const int glast = gfirst[lr] + gcount[lr] - 1;  // the group's longest row
+    const int live = min(kPageTok, keys[glast] - lt * kPageTok);
     const int64_t page = next_page;
     const int64_t e0 = ((page * p.page + ld_tok) * hkv + kvh) * kD + ld_ch * 8;  // element offset, token ld_tok
     const __nv_bfloat16* kp = tab.k_cache[lsg] + e0;
@@ -420,13 +458,19 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
                        ok ? 16u : 0u);
     }
     if (j == 0 || lt == 0) {
-      const char* qp = reinterpret_cast<const char*>(p.q_rot + (static_cast<int64_t>(lr) * p.hq + kvh * G) * kD);
-      for (int e = lane; e < G * kD * 2 / 16; e += 32) ptx::cp_async_16(ss + q_off + e * 16, qp + e * 16, 16u);
+      // the group's query rows (a missing second row reads as zeros)
+      for (int ri = 0; ri < qrows; ++ri) {
+        const bool have = ri < gcount[lr];
+        const char* qp = reinterpret_cast<const char*>(
+            p.q_rot + (static_cast<int64_t>(gfirst[lr] + (have ? ri : 0)) * p.hq + kvh * G) * kD);
+        for (int e = lane; e < G * kD * 2 / 16; e += 32)
+          ptx::cp_async_16(ss + q_off + (ri * G * kD * 2) + e * 16, qp + e * 16, have ? 16u : 0u);
+      }
     }
     if (++lt == pre[lr + 1] - pre[lr]) {
       lt = 0;
       ++lr;
-      if (lr < rows) lsg = seg_of_row(tab.seg, lr);
+      if (lr < ngroups) lsg = seg_of_row(tab.seg, gfirst[lr]);
     }
     if (j + 1 < nunits) next_page = tab.block_table[lsg][lt];
   };
@@ -451,16 +495,21 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
     const int st = j % kStages;
     const uint32_t ss = sm0 + st * stage_bytes;
     const int tiles = pre[r + 1] - pre[r];
-    const int L = keys[r];
+    // causal length of this thread's columns (2c, 2c+1: row c >> 1 of the group)
+    const int my_ri = pair ? (c >> 1) : 0;
+    const int L = (pair && my_ri >= gcount[r]) ? 0 : keys[gfirst[r] + my_ri];
     if (j == 0 || t == 0) {
-      // new piece: Q^T as the B operand (k = dims, n = query head g < G),
+      // new piece: Q^T as the B operand (k = dims, n = column g: query head
+      // g & 3 of the group's row g >> 2 with pairing, head g without),
       // fresh softmax state
       const uint8_t* qs = att_dyn + st * stage_bytes + q_off;
-      const bool real = g < G;
+      const int q_ri = pair ? (g >> 2) : 0, q_h = pair ? (g & 3) : g;
+      const bool real = q_h < G && q_ri < qrows;
+      const int q_col = q_ri * G + q_h;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        qb[ks][0] = real ? *reinterpret_cast<const uint32_t*>(qs + (g * kD + ks * 16 + 2 * c) * 2) : 0u;
-        qb[ks][1] = real ? *reinterpret_cast<const uint32_t*>(qs + (g * kD + ks * 16 + 8 + 2 * c) * 2) : 0u;
+        qb[ks][0] = real ? *reinterpret_cast<const uint32_t*>(qs + (q_col * kD + ks * 16 + 2 * c) * 2) : 0u;
+        qb[ks][1] = real ? *reinterpret_cast<const uint32_t*>(qs + (q_col * kD + ks * 16 + 8 + 2 * c) * 2) : 0u;
       }
       m0 = m1 = -INFINITY;
       l0 = l1 = 0.f;
@@ -548,9 +597,11 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
       if (piece < max_pieces) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          const int hg = 2 * c + hh;
-          if (hg >= G) continue;
-          float* rec = recs + ((static_cast<int64_t>(r) * p.hq + kvh * G + hg) * max_pieces + piece) * (kD + 2);
+          const int col = 2 * c + hh;
+          const int ri = pair ? (col >> 2) : 0, hg = pair ? (col & 3) : col;
+          if (hg >= G || ri >= gcount[r]) continue;
+          const int64_t row = gfirst[r] + ri;
+          float* rec = recs + ((row * p.hq + kvh * G + hg) * max_pieces + piece) * (kD + 2);
           if (g == 0) {
             rec[0] = hh ? m1 : m0;
             rec[1] = hh ? lt1 : lt0;
@@ -610,7 +661,7 @@ __global__ void __launch_bounds__(128) attention_combine_kernel(const __grid_con
     lv[i] = in ? rec[i * (kD + 2) + 1] : 0.f;
     ov[i] = in ? rec[i * (kD + 2) + 2 + d] : 0.f;
   }
-  const int W = hdr[0], p0 = hdr[1 + gr], p1 = hdr[2 + gr];
+  const int W = hdr[0], p0 = hdr[1 + 2 * gr], p1 = hdr[2 + 2 * gr];
   const int nch = min((p1 - 1) / W - p0 / W + 1, max_pieces);
   float M = -INFINITY, lsum = 0.f, acc = 0.f;
   if (nch <= kBatch) {
@@ -828,7 +879,7 @@ int sm_count_attn() {
 }
 
 template <int S>
-int launch_attention_stages(const AttnTable& tab, const AttnParams& p, int grid, int groups, size_t smem,
+int launch_attention_stages(const AttnTable& tab, const AttnParams& p, int grid, int groups, int pair, size_t smem,
                             const AttnSplit& sp, cudaStream_t stream) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
@@ -839,7 +890,7 @@ int launch_attention_stages(const AttnTable& tab, const AttnParams& p, int grid,
   if (attr_err != cudaSuccess)
     return set_error(SWL_ERR_CUDA, "attention: smem attribute: %s", cudaGetErrorString(attr_err));
   SWL_CUDA_TRY(launch_kernel(paged_attention_kernel<S>, dim3(grid, groups), dim3(p.hkv / groups * 32), smem,
-                             stream, 1, tab, p, sp.chunks, sp.chunk_pages, p.part));
+                             stream, 1, tab, p, sp.chunks, sp.chunk_pages, pair, p.part));
   return SWL_OK;
 }
 
@@ -866,7 +917,13 @@ int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream
   const int og = g_attn_groups.load(std::memory_order_relaxed);
   int groups = og > 0 ? og : 1;
   while (groups > 1 && p.hkv % groups) --groups;
-  const int stage_bytes = attn_stage_bytes(p.hq / groups, p.hkv / groups);
+  // rows of one slot are paired (one page read for both) when a slot has
+  // several rows and two rows' query heads fit the MMA's 8 columns
+  int max_seg_rows = 0;
+  for (int i = 0; i < tab.seg.nseg; ++i)
+    max_seg_rows = std::max(max_seg_rows, tab.seg.row_start[i + 1] - tab.seg.row_start[i]);
+  const int pair = (max_seg_rows >= 2 && p.hq / p.hkv <= 4 && !g_attn_no_pair.load(std::memory_order_relaxed)) ? 1 : 0;
+  const int stage_bytes = attn_stage_bytes(p.hq / groups, p.hkv / groups, pair ? 2 : 1);
   // two page stages per warp by default (one in flight while one is
   // consumed): the 148 KB ring lets a CTA sit beside the RoPE epilogue's
   // CTAs; deeper rings (tuning) measured no faster in the decode step
@@ -880,9 +937,9 @@ int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream
   const int grid = static_cast<int>(std::max<int64_t>(
       1, std::min<int64_t>((units_max + sp.chunk_pages - 1) / sp.chunk_pages, sm_count_attn())));
   switch (stages) {
-    case 2: SWL_TRY(launch_attention_stages<2>(tab, p, grid, groups, smem, sp, stream)); break;
-    case 3: SWL_TRY(launch_attention_stages<3>(tab, p, grid, groups, smem, sp, stream)); break;
-    default: SWL_TRY(launch_attention_stages<4>(tab, p, grid, groups, smem, sp, stream)); break;
+    case 2: SWL_TRY(launch_attention_stages<2>(tab, p, grid, groups, pair, smem, sp, stream)); break;
+    case 3: SWL_TRY(launch_attention_stages<3>(tab, p, grid, groups, pair, smem, sp, stream)); break;
+    default: SWL_TRY(launch_attention_stages<4>(tab, p, grid, groups, pair, smem, sp, stream)); break;
   }
   ShrinkSide none;
   if (!shrink) {
@@ -903,6 +960,11 @@ int launch_rms_norm(const NormTable& tab, const __nv_bfloat16* w, int64_t hidden
   if (hidden % 8) return set_error(SWL_ERR_ARG, "rms_norm: hidden must be a multiple of 8");
   SWL_CUDA_TRY(launch_kernel(rms_norm_kernel, dim3(tab.seg.total_rows), dim3(256), 0, stream, 1, tab, w, hidden, eps,
                              x_stride, out_stride));
+  return SWL_OK;
+}
+
+int set_attention_pairing(int on) {
+  g_attn_no_pair.store(on ? 0 : 1);
   return SWL_OK;
 }
 

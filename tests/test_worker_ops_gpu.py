@@ -184,6 +184,20 @@ def test_rope_append_attention(native, cuda, ctx, rows):
     _attn_case(ctx, rows, seed=sum(ctx) + len(rows))
 
 
+@pytest.mark.parametrize("ctx,rows", [([0, 40, 7, 300], [16, 15, 1, 2]), ([1000, 16, 0], [3, 16, 16])])
+@pytest.mark.parametrize("pairing", [1, 0])
+def test_attention_row_pairs_and_single_rows(native, cuda, ctx, rows, pairing):
+    """Prefill chunks (several rows of one slot, even and odd counts) beside
+    decode rows: with two rows of a slot sharing each page read and with
+    every row reading alone, against the oracle."""
+    from swarmlora_b200._native import check, lib
+    try:
+        check(lib().swl_attention_pairing(pairing))
+        _attn_case(ctx, rows, seed=sum(ctx) + 3 * len(rows) + pairing)
+    finally:
+        check(lib().swl_attention_pairing(1))
+
+
 @pytest.mark.parametrize("stages,groups", [(3, 2), (2, 2), (4, 4), (2, 8)])
 def test_attention_head_groups_match_one_group(native, cuda, stages, groups):
     """CTAs that share a page's kv heads (each holding its group's slices,
