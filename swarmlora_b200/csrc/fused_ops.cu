@@ -298,13 +298,15 @@ __global__ void __launch_bounds__(norm_threads(CL)) resid_norm_shrink_kernel(con
     ss_part = a;
   }
   ptx::cluster_sync();
-  float total = 0.f;
+  // every CTA's part is loaded first (one round trip), then summed in order
   const uint32_t my = static_cast<uint32_t>(__cvta_generic_to_shared(&ss_part));
-  for (int r = 0; r < kCluster; ++r) {
-    float pv;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(ptx::map_peer(my, r)) : "memory");
-    total += pv;
-  }
+  float pv[kCluster];
+#pragma unroll
+  for (int r = 0; r < kCluster; ++r)
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv[r]) : "r"(ptx::map_peer(my, r)) : "memory");
+  float total = 0.f;
+#pragma unroll
+  for (int r = 0; r < kCluster; ++r) total += pv[r];
   ptx::cluster_arrive();  // done with the peers' ss_part; waited for before exit
   const float inv = rsqrtf(total / static_cast<float>(p.hidden) + p.eps);
   __nv_bfloat16* xo = tab.x_out[s] + local * p.x_stride;

@@ -398,30 +398,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     emit = split_last != 0;
     __threadfence();
   }
-  // the K-split sum of the 4 outputs at (row r, column c) of the tile
+  // the K-split sum of the 4 outputs at (row r, column c) of the tile: every
+  // split's partial is loaded first (up to 8 loads in flight, one round trip
+  // to the peers or L2), then summed in split order
   auto reduce4 = [&](int r, int c) -> float4 {
     const uint32_t off = static_cast<uint32_t>((r * kBlockW + c) * 4);
-    if (gsplit) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int p = 0; p < splits; ++p) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(gpart + static_cast<int64_t>(p) * (BN * kBlockW) +
-                                                                 r * kBlockW + c));
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
-      return acc;
-    }
-    if (splits == 1) return *reinterpret_cast<const float4*>(P + r * kBlockW + c);
+    if (!gsplit && splits == 1) return *reinterpret_cast<const float4*>(P + r * kBlockW + c);
+    float4 v[8];
+#pragma unroll
+    for (int p = 0; p < 8; ++p)
+      if (p < splits)
+        v[p] = gsplit ? __ldcg(reinterpret_cast<const float4*>(gpart + static_cast<int64_t>(p) * (BN * kBlockW) +
+                                                                r * kBlockW + c))
+                      : ptx::ld_cluster_f4(ptx::map_peer(pbase + off, p));
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p = 0; p < splits; ++p) {
-      const float4 v = ptx::ld_cluster_f4(ptx::map_peer(pbase + off, p));
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
-    }
+#pragma unroll
+    for (int p = 0; p < 8; ++p)
+      if (p < splits) {
+        acc.x += v[p].x;
+        acc.y += v[p].y;
+        acc.z += v[p].z;
+        acc.w += v[p].w;
+      }
     return acc;
   };
   if constexpr (kRope) {
