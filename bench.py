@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--round-flags", type=int, default=0,
                     help="round kernel flags (swl_round_tune): 1 gather spin, 2 global-memory split-K, "
                          "4 L2 prefetch of the W tiles beyond the ring")
+    ap.add_argument("--round-tile", default="",
+                    help="decode-class round tile as ROWSxSTAGES, e.g. 32x4 (swl_round_tune; default: automatic)")
     ap.add_argument("--attn-groups", type=int, default=0,
                     help="attention kv head groups 1/2/4/8: CTAs sharing one page's heads (0 = auto)")
     ap.add_argument("--no-pdl", action="store_true",
@@ -274,6 +276,20 @@ def cpu_layer_sample(n_slots, seed=0, ctx_lo=CTX_LO, ctx_hi=CTX_HI):
         last = torch.cat([ref.rms_norm(v, w_in) for v in h], 0).float()
         return (last @ W_lm[0].t()).argmax(-1)
 
+    def round_us(m, reps=3):
+        """Mean microseconds of one round of each op type (cat -> x @ W^T ->
+        split) over m one-row slots."""
+        out = {}
+        for name, W in (("qkv", Wqkv), ("o", Wo), ("gate_up", Wgu), ("down", Wd)):
+            xl = [torch.randn(1, W.shape[1]).to(bf) for _ in range(m)]
+            mm(xl, W)
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                mm(xl, W)
+            out[name] = round((time.perf_counter() - t0) / reps * 1e6, 1)
+        return out
+
+    full_step.round_us = round_us
     return step, full_step
 
 
@@ -312,7 +328,11 @@ def cpu_baseline(n_slots, seconds_budget=20.0, ctx_lo=CTX_LO, ctx_hi=CTX_HI):
         full_step()
         times.append(time.perf_counter() - t0)
     t_step = sum(times) / len(times)
+    # the per-round metric on the same cores: M = the slots (one row each) and
+    # M = 4 (the reference's CPU-runnable one-layer configuration)
+    rounds = {"m%d" % m: full_step.round_us(m) for m in (n_slots, 4)}
     return {"value": round(n_slots / t_step, 4), "unit": UNIT, "cores": threads, "cpu": cpu_model(),
+            "us_per_round": rounds,
             "kind": "port",
             "sample": f"{len(times)} whole decode steps of {n_slots} slots at ctx U[{ctx_lo},{ctx_hi}] "
                       f"(32 layer passes: 4 rounds + LoRA + RoPE + paged attention + norms; one layer's "
@@ -341,6 +361,7 @@ def reference_arm(args):
         times.append(time.perf_counter() - t0)
     t_step = sum(times) / len(times)
     value = args.slots / t_step
+    rounds = {"m%d" % m: full_step.round_us(m) for m in (args.slots, 4)}
     sample = (f"{args.steps} whole decode steps of {args.slots} slots (32 layer passes with one layer's weights "
               f"reused + LM-head GEMV + argmax) on {threads} threads")
     line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "impl": "reference",
@@ -350,7 +371,7 @@ def reference_arm(args):
             "config": {"workload": workload_string(args.slots, args.ctx_lo, args.ctx_hi),
                        "slots": args.slots, "layers": 32, "vocab": 128256, "sample": sample},
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "cpu": cpu_model(),
-                             "kind": "port", "sample": sample},
+                             "kind": "port", "sample": sample, "us_per_round": rounds},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -445,9 +466,10 @@ def our_arm(args):
     swarmlora_b200.set_pdl(not args.no_pdl)
     from swarmlora_b200 import worker_ops as _wo
     _wo.attention_tune(args.attn_chunk_pages, args.attn_stages, args.attn_groups)
-    if args.round_flags:
+    if args.round_flags or args.round_tile:
         from swarmlora_b200._native import check as _check, lib as _lib
-        _check(_lib().swl_round_tune(32, 0, 0, args.round_flags))
+        bn, st = (int(x) for x in args.round_tile.split("x")) if args.round_tile else (0, 0)
+        _check(_lib().swl_round_tune(32, bn, st, args.round_flags))
     if args.checkpoint:
         from swarmlora_b200.checkpoint import load_base
         base, cfg = load_base(args.checkpoint, dev)
