@@ -184,6 +184,18 @@ def test_rope_append_attention(native, cuda, ctx, rows):
     _attn_case(ctx, rows, seed=sum(ctx) + len(rows))
 
 
+@pytest.mark.parametrize("ctx,rows", [
+    ([4000, 1024, 2047, 3000, 1], [1, 1, 1, 1, 1]),  # the long-context configuration's range
+    ([4000], [1]),  # one long row: 250 pages split over more pieces than the combine loads at once
+    ([2000, 3040], [16, 16]),  # prefill chunks far into their prompts
+])
+def test_attention_long_contexts_and_many_pieces(native, cuda, ctx, rows):
+    """Contexts up to 4000 tokens (the configurations with U[1024,4096] and
+    U[256,2048] contexts), including a row whose pages are split over more
+    pieces than the combine step reads in its first batch."""
+    _attn_case(ctx, rows, seed=sum(ctx) + 7 * len(rows))
+
+
 @pytest.mark.parametrize("ctx,rows", [([0, 40, 7, 300], [16, 15, 1, 2]), ([1000, 16, 0], [3, 16, 16])])
 @pytest.mark.parametrize("pairing", [1, 0])
 def test_attention_row_pairs_and_single_rows(native, cuda, ctx, rows, pairing):
