@@ -382,6 +382,44 @@ def test_profile_step_reports_the_reference_line(native, cuda, capsys):
         grp.close()
 
 
+def test_engine_long_contexts_32_slots_match_oracle(native, cuda):
+    """The long-context configuration's shape (32 slots with their own
+    rank-16 adapters, contexts U[1024, 4096]) at 2 layers: two decode steps
+    against the CPU oracle (last-layer hidden state, LM-head input, greedy
+    tokens). Rounds of M = 32 and attention rows of 64 to 256 pages."""
+    from swarmlora_b200.engine import ModelConfig, SlotGroup, random_adapter, random_base
+    cfg = ModelConfig(layers=2, vocab=4096)
+    n = 32
+    g = torch.Generator().manual_seed(2024)
+    ctx = [int(c) for c in torch.randint(1024, 4091, (n,), generator=g)]
+    base = random_base(cfg, seed=5, device=cuda, norm_noise=0.1)
+    adapters = [random_adapter(cfg, seed=50 + i, device=cuda) for i in range(n)]
+    grp = SlotGroup(cfg, base, adapters, ctx, max_new=4, seed=9)
+    try:
+        base_c, ad_c = _cpu(base), _cpu(adapters)
+        kc = [k.cpu() for k in grp.k_cache]
+        vc = [v.cpu() for v in grp.v_cache]
+        bts = [t.tolist() for t in grp.block_tables]
+        tokens = torch.randint(0, cfg.vocab, (n,), generator=g).tolist()
+        grp.tokens.copy_(torch.tensor(tokens))
+        seq = list(ctx)
+        stream = torch.cuda.current_stream()
+        for step in range(2):
+            grp.enqueue_step(stream)
+            torch.cuda.synchronize()
+            got = grp.tokens.cpu()
+            want, final, logits, h_last = decode_step(cfg, base_c, ad_c, kc, vc, bts, seq, tokens)
+            assert_close(grp.h, h_last, f"step {step} last-layer hidden", atol_rms=ATOL_RMS_MULTILAYER)
+            assert_close(grp.read_slot_rows("in", cfg.hidden), final, f"step {step} LM-head input",
+                         atol_rms=ATOL_RMS_MULTILAYER)
+            _check_tokens(got, want, logits, f"step {step}")
+            tokens = got.tolist()
+            seq = [x + 1 for x in seq]
+        assert grp.seqlens.cpu().tolist() == seq
+    finally:
+        grp.close()
+
+
 def test_config2_full_size_step_properties(native, cuda):
     """BASELINE config 2 at its full size (32 layers, vocabulary 128256, 28
     slots with their own rank-16 adapters, contexts U[256, 1024]), checked
