@@ -18,6 +18,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdint>
 #include <cstring>
 #include <atomic>
 #include <mutex>
@@ -687,16 +688,27 @@ int launch_tc(const SlotTable& tab, const RoundShape& shape, const CUtensorMap& 
   const int m_chunks = std::max(kShard ? 1 : 0, (tab.total_rows + BN - 1) / BN);
   const int nkb = static_cast<int>((shape.K + kBlockK - 1) / kBlockK);
   if (splits <= 0) {
-    // Largest power-of-two cluster (<= 8) that keeps the grid within the
-    // resident CTA capacity and at least 8 K-blocks per split. Clusters whose
-    // size does not divide the SMs of a GPC (3, 5, 6) schedule poorly.
+    // The split that minimises the K-blocks of the busiest SM (its CTAs x
+    // K-blocks per CTA), among cluster sizes that schedule well (1, 2, 4, 5,
+    // 8; 3, 6 and 7 measured slow), with the grid within the resident CTA
+    // capacity and at least 8 K-blocks per split; ties go to more splits.
+    // Decode at M = 28: O and Down take 8, QKV 5 (13.1 vs 13.8 us with 4).
     // resident CTAs per SM by shared memory (228 KB per SM, 1 KB reserved per CTA), at most 4
     const int per_sm = std::max(1, std::min(4, (228 * 1024) / (smem_bytes + 1024)));
-    const int cap = sm_count() * per_sm;
+    const int sms = sm_count();
+    const int cap = sms * per_sm;
     const int base = std::max(1, n_tiles * m_chunks);
     splits = 1;
-    for (int s = 2; s <= 8; s *= 2)
-      if (base * s <= cap && nkb / s >= 8) splits = s;
+    int64_t best = INT64_MAX;
+    for (int s : {1, 2, 4, 5, 8}) {
+      if (s > 1 && (base * s > cap || nkb / s < 8)) continue;
+      const int64_t ctas = static_cast<int64_t>(base) * s;
+      const int64_t cost = ((ctas + sms - 1) / sms) * ((nkb + s - 1) / s);
+      if (cost <= best) {
+        best = cost;
+        splits = s;
+      }
+    }
   }
   splits = std::max(1, std::min(splits, std::min(8, nkb)));
 
