@@ -76,6 +76,8 @@ def parse():
                          "4 L2 prefetch of the W tiles beyond the ring")
     ap.add_argument("--round-tile", default="",
                     help="decode-class round tile as ROWSxSTAGES, e.g. 32x4 (swl_round_tune; default: automatic)")
+    ap.add_argument("--attn-lane-copies", action="store_true",
+                    help="attention K/V pages by per-lane cp.async copies instead of TMA")
     ap.add_argument("--attn-groups", type=int, default=0,
                     help="attention kv head groups 1/2/4/8: CTAs sharing one page's heads (0 = auto)")
     ap.add_argument("--no-pdl", action="store_true",
@@ -466,6 +468,7 @@ def our_arm(args):
     swarmlora_b200.set_pdl(not args.no_pdl)
     from swarmlora_b200 import worker_ops as _wo
     _wo.attention_tune(args.attn_chunk_pages, args.attn_stages, args.attn_groups)
+    _wo.attention_tma(not args.attn_lane_copies)
     if args.round_flags or args.round_tile:
         from swarmlora_b200._native import check as _check, lib as _lib
         bn, st = (int(x) for x in args.round_tile.split("x")) if args.round_tile else (0, 0)
@@ -654,6 +657,7 @@ def profile_attention(args):
     from swarmlora_b200 import worker_ops as wo
     from swarmlora_b200.engine import LLAMA_3_1_8B as cfg
     wo.attention_tune(args.attn_chunk_pages, args.attn_stages, args.attn_groups)
+    wo.attention_tma(not args.attn_lane_copies)
     dev = torch.device("cuda:0")
     n = args.slots
     g = torch.Generator(device=dev).manual_seed(0)

@@ -367,6 +367,11 @@ int swl_attention_tune(int chunk_pages, int stages, int groups);
  * page read, their query heads filling the MMA's columns together; 0: every
  * row reads its pages alone. A launch option, no counterpart in the reference. */
 int swl_attention_pairing(int on);
+/* 1 (default): the attention kernel loads its K/V pages with TMA (one lane
+ * per warp issues its kv head's 128B-swizzled halves) when every row's pages
+ * lie in one cache allocation; 0: per-lane cp.async copies always. A launch
+ * option, no counterpart in the reference. */
+int swl_attention_tma(int on);
 /* fp32 scratch floats swl_paged_attention needs in `part`. */
 int64_t swl_attention_part_floats(int total_rows, int hq, int hkv, int max_len);
 /* Causal GQA attention over paged KV (flash_attn_with_kvcache semantics,

@@ -127,6 +127,7 @@ SIGNATURES: dict[str, tuple] = {
     "swl_attention_part_floats": (_i64, [_i32, _i32, _i32, _i32]),
     "swl_attention_tune": (_i32, [_i32, _i32, _i32]),
     "swl_attention_pairing": (_i32, [_i32]),
+    "swl_attention_tma": (_i32, [_i32]),
     "swl_paged_attention": (_i32, [_i32, _pi32, _pp, _pp, _pp, _pp, _pp, _i64, _i32, _i32, _i32,
                                    _i32, _f32, _i32, _p, _p, _p]),
     "swl_paged_attention_noalloc": (_i32, [_i32, _pi32, _pp, _pp, _pp, _pp, _pp, _i64, _i32, _i32,

@@ -648,7 +648,7 @@ PFN_cuMemGetAddressRange_v3020 address_range_fn() {
 }
 
 // The allocation holding `p`: its base and size.
-int allocation_of(const void* p, char** base, size_t* size) {
+int swl::allocation_of(const void* p, char** base, size_t* size) {
   auto fn = address_range_fn();
   if (!fn) return set_error(SWL_ERR_CUDA, "cuMemGetAddressRange is unavailable");
   CUdeviceptr b = 0;

@@ -9,6 +9,7 @@
 // std::runtime_error (ipc_types.h:223-229 CUDA_RT_CHECK).
 #pragma once
 
+#include <cstddef>
 #include <cstdint>
 #include <cstdio>
 #include <cstdarg>
@@ -30,6 +31,9 @@ namespace swl {
 // Sets the calling thread's last-error message and returns `code`.
 int set_error(int code, const char* fmt, ...);
 const char* last_error();
+// The device allocation holding `p` (its base and size); defined with the
+// aggregator's allocation bookkeeping.
+int allocation_of(const void* p, char** base, size_t* size);
 
 }  // namespace swl
 

@@ -154,6 +154,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
 }
+// 3-D tiled bulk tensor load into this CTA's shared memory (shared-memory
+// address `dst`), completing on `bar` (no multicast). c0 is innermost.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
+      : "memory");
+}
 // Prefetch of a 2-D tile of a tensor map into L2 (no shared memory, no
 // completion to wait for). c0 is the innermost coordinate.
 __device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int c0, int c1) {

@@ -806,6 +806,22 @@ int encode_weight_tmap(CUtensorMap* map, const void* W, int64_t N, int64_t K) {
   return SWL_OK;
 }
 
+int encode_kv_page_tmap(CUtensorMap* map, const void* cache, int64_t tokens, int hkv) {
+  auto enc = tmap_encoder();
+  if (!enc) return set_error(SWL_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(cache) & 15) != 0 || hkv <= 0 || tokens < 16 || tokens > (int64_t{1} << 31))
+    return set_error(SWL_ERR_ARG, "KV tensor map: bad cache base, head count or extent");
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(hkv), static_cast<cuuint64_t>(tokens)};
+  cuuint64_t strides[2] = {128 * 2, static_cast<cuuint64_t>(hkv) * 128 * 2};
+  cuuint32_t box[3] = {64, 1, 16};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(cache), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(SWL_ERR_CUDA, "KV tensor map: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return SWL_OK;
+}
+
 int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void* W,
                       const CUtensorMap* tmap, int algo, int splits, cudaStream_t stream) {
   if (tab.nslots <= 0 || tab.total_rows <= 0) return SWL_OK;  // nothing to do

@@ -107,6 +107,11 @@ enum RoundAlgo : int {
 // 128-byte swizzle). Returns SWL_OK or an error status.
 int encode_weight_tmap(CUtensorMap* map, const void* W, int64_t N, int64_t K);
 
+// Encodes the TMA descriptor of a paged KV cache, viewed as [tokens][hkv][128]
+// bf16 with `tokens` rows (pages x page tokens): box 64 dims x 1 head x 16
+// tokens, 128-byte swizzle (one kv head's half of a page per load).
+int encode_kv_page_tmap(CUtensorMap* map, const void* cache, int64_t tokens, int hkv);
+
 // Launches one round on `stream`. `tmap` may be nullptr (encoded on the fly).
 // `splits` <= 0 picks the split-K factor automatically.
 int launch_slot_round(const SlotTable& tab, const RoundShape& shape, const void* W,

@@ -140,6 +140,10 @@ SWL_EXPORT int swl_attention_tune(int chunk_pages, int stages, int groups) {
 // launch has slots with several rows; 0: every row reads its pages alone.
 SWL_EXPORT int swl_attention_pairing(int on) { return set_attention_pairing(on); }
 
+// 1 (default): K/V pages loaded by TMA when every row's pages lie in one
+// cache allocation; 0: per-lane copies always.
+SWL_EXPORT int swl_attention_tma(int on) { return set_attention_tma(on); }
+
 // Causal GQA attention of each new token over its slot's paged cache
 // (flash_attn_with_kvcache semantics, worker_sync.py:196-203): token t of
 // slot i attends to cache positions 0 .. *seqlens[i] + t. max_len bounds

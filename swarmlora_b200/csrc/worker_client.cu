@@ -245,49 +245,55 @@ void drop_graphs(WorkerClient* c) {
   c->graphs.clear();
 }
 
-// Event mode with graphs: segments 0 .. rounds_per_token - 1 captured once,
-// each as [wait for the round event] + launches + [record the input event]
+// Event mode with graphs: segment i (0 .. rounds_per_token - 1) captured
+// once, as [wait for the round event] + launches + [record the input event]
 // (segment 0 has no wait: it follows the token-end launches on the stream).
-int build_graphs(WorkerClient* c) {
-  drop_graphs(c);
+// Each segment is captured just before its first graphed launch, so a round
+// waits for one capture, not the aggregator for a whole token's worth (which
+// could outlast its barrier's eviction time).
+int build_graph(WorkerClient* c, int i) {
   const int R = rounds_per_token(c);
-  c->graphs.assign(R, nullptr);
-  for (int i = 0; i < R; ++i) {
-    cudaGraph_t g = nullptr;
-    SWL_CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    int st = SWL_OK;
-    if (i > 0 && cudaStreamWaitEvent(c->stream, c->round_event, cudaEventWaitExternal) != cudaSuccess)
-      st = set_error(SWL_ERR_CUDA, "worker client: capturing the round-event wait");
-    if (st == SWL_OK) st = enqueue_segment(c, i, 0);
-    if (st == SWL_OK && cudaEventRecordWithFlags(c->input_event, c->stream, cudaEventRecordExternal) != cudaSuccess)
-      st = set_error(SWL_ERR_CUDA, "worker client: capturing the input-event record");
-    const cudaError_t e = cudaStreamEndCapture(c->stream, &g);
-    if (st != SWL_OK || e != cudaSuccess) {
-      if (g) cudaGraphDestroy(g);
-      drop_graphs(c);
-      return st != SWL_OK ? st : set_error(SWL_ERR_CUDA, "worker client: capture: %s", cudaGetErrorString(e));
-    }
-    const cudaError_t ie = cudaGraphInstantiate(&c->graphs[i], g, 0);
-    cudaGraphDestroy(g);
-    if (ie != cudaSuccess) {
-      drop_graphs(c);
-      return set_error(SWL_ERR_CUDA, "worker client: instantiating a segment graph: %s", cudaGetErrorString(ie));
-    }
+  if (static_cast<int>(c->graphs.size()) != R) c->graphs.assign(R, nullptr);
+  cudaGraph_t g = nullptr;
+  SWL_CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  int st = SWL_OK;
+  if (i > 0 && cudaStreamWaitEvent(c->stream, c->round_event, cudaEventWaitExternal) != cudaSuccess)
+    st = set_error(SWL_ERR_CUDA, "worker client: capturing the round-event wait");
+  if (st == SWL_OK) st = enqueue_segment(c, i, 0);
+  if (st == SWL_OK && cudaEventRecordWithFlags(c->input_event, c->stream, cudaEventRecordExternal) != cudaSuccess)
+    st = set_error(SWL_ERR_CUDA, "worker client: capturing the input-event record");
+  const cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+  if (st != SWL_OK || e != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return st != SWL_OK ? st : set_error(SWL_ERR_CUDA, "worker client: capture: %s", cudaGetErrorString(e));
+  }
+  const cudaError_t ie = cudaGraphInstantiate(&c->graphs[i], g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) {
+    c->graphs[i] = nullptr;
+    return set_error(SWL_ERR_CUDA, "worker client: instantiating a segment graph: %s", cudaGetErrorString(ie));
   }
   return SWL_OK;
 }
 
 // One decode token for every slot of the client: the reference worker's
 // per-token sequence, segment by segment, each round through the protocol.
+// With graphs, every token after the first (eager) one launches each
+// segment as its graph (the first eager token sets the kernels' attributes
+// outside any capture).
 int run_token(WorkerClient* c, int t) {
   const int R = rounds_per_token(c);
-  const bool graphed = !c->graphs.empty();
+  const bool graphed = c->use_graphs && c->input_mode == 2 && c->rounds_done > 0;
   for (int i = 0; i < R; ++i) {
     int op, layer;
     int64_t dx;
     round_of(c, i, &op, &layer, &dx);
-    if (graphed) SWL_CUDA_TRY(cudaGraphLaunch(c->graphs[i], c->stream));
-    else SWL_TRY(enqueue_segment(c, i, t));
+    if (graphed) {
+      if (static_cast<int>(c->graphs.size()) != R || !c->graphs[i]) SWL_TRY(build_graph(c, i));
+      SWL_CUDA_TRY(cudaGraphLaunch(c->graphs[i], c->stream));
+    } else {
+      SWL_TRY(enqueue_segment(c, i, t));
+    }
     SWL_TRY(protocol_round(c, op, layer, dx, graphed));
   }
   // token end: the stream waits for the LM-head round before reading its picks
@@ -447,9 +453,6 @@ SWL_EXPORT int swl_wc_run(void* handle, int tokens, int64_t* token_ns) {
   SWL_TRY(check_client(c));
   if (tokens < 0) return set_error(SWL_ERR_ARG, "worker client: negative token count");
   for (int t = 0; t < tokens; ++t) {
-    // per-segment graphs are captured after one eager token (which sets the
-    // kernels' attributes outside any capture)
-    if (c->use_graphs && c->input_mode == 2 && c->graphs.empty() && c->rounds_done > 0) SWL_TRY(build_graphs(c));
     const auto t0 = std::chrono::steady_clock::now();
     SWL_TRY(run_token(c, t));
     if (token_ns)

@@ -20,11 +20,13 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstring>
 #include <mutex>
 
 #include "common.h"
 #include "launch.h"
 #include "ptx.cuh"
+#include "slot_round.h"
 #include "worker_ops.h"
 
 namespace swl {
@@ -278,12 +280,21 @@ std::atomic<int> g_attn_min_units{0};
 std::atomic<int> g_attn_stages{0};
 std::atomic<int> g_attn_groups{0};
 std::atomic<int> g_attn_no_pair{0};  // tuning: never pair a slot's rows
+std::atomic<int> g_attn_tma{1};      // K/V pages by TMA where every row's pages share one cache
 
 __host__ __device__ __forceinline__ int attn_row_bytes(int hkv) { return hkv * kD * 2 + 16; }
 // One page stage: K and V token rows of the CTA's kv heads, and the query
 // rows of `qrows` token rows (a group) for its query heads.
 __host__ __device__ __forceinline__ int attn_stage_bytes(int hq, int hkv, int qrows = 1) {
   return 2 * kPageTok * attn_row_bytes(hkv) + qrows * hq * kD * 2;
+}
+
+// TMA layout of one warp's share of a page stage: its kv head's K then V
+// slice of the page, each as two 128B-swizzled [16 tokens][64 dims] halves
+// (2 KB each), then the query rows (dense), padded to 1024 bytes so every
+// warp's halves start on the 1024-byte boundary the swizzle pattern needs.
+__host__ __device__ __forceinline__ int attn_tma_warp_bytes(int G, int qrows = 1) {
+  return 4 * kPageTok * 128 + (qrows * G * kD * 2 + 1023) / 1024 * 1024;
 }
 
 // The partial scratch starts with a header the combine step reads: [0] units
@@ -322,11 +333,17 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-template <int kStages>
+template <int kStages, bool kTma>
 __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
     paged_attention_kernel(const __grid_constant__ AttnTable tab, const AttnParams p, int max_pieces,
-                           int min_units, int pair, float* __restrict__ part) {
-  extern __shared__ __align__(128) uint8_t att_dyn[];
+                           int min_units, int pair, float* __restrict__ part,
+                           const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ __align__(128) uint8_t att_dyn_raw[];
+  // the TMA path's swizzled halves sit on 1024-byte boundaries
+  uint8_t* const att_dyn =
+      kTma ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(att_dyn_raw) + 1023) & ~uintptr_t(1023))
+           : att_dyn_raw;
+  __shared__ __align__(8) uint64_t tbar[kAttnMaxHkv][kAttnStagesMax];  // TMA: one per (warp, stage)
   __shared__ int pre[kAttnMaxRows + 1];  // page prefix over groups
   __shared__ int keys[kAttnMaxRows];     // keys (causal length) of each row
   __shared__ int gfirst[kAttnMaxRows];   // first row of each group
@@ -342,7 +359,12 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   // pair: two consecutive rows of a slot share each page read (their query
   // heads fill the MMA's 8 columns: column = 4 * row-in-group + head)
   const int qrows = pair ? 2 : 1;
-  const int stage_bytes = attn_stage_bytes(hkv_c * G, hkv_c, qrows);
+  const int wblk = attn_tma_warp_bytes(G, qrows);
+  const int stage_bytes = kTma ? hkv_c * wblk : attn_stage_bytes(hkv_c * G, hkv_c, qrows);
+  if (kTma && lane == 0) {
+    for (int st = 0; st < kStages; ++st) ptx::mbar_init(&tbar[warp][st], 1);
+    ptx::fence_mbar_init();
+  }
 
   // Page prefix over the rows (every CTA derives the same unit stream). The
   // context lengths and block tables are not written by the launch just
@@ -444,27 +466,63 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
     const int glast = gfirst[lr] + gcount[lr] - 1;  // the group's longest row
     const int live = min(kPageTok, keys[glast] - lt * kPageTok);
     const int64_t page = next_page;
-    const int64_t e0 = ((page * p.page + ld_tok) * hkv + kvh) * kD + ld_ch * 8;  // element offset, token ld_tok
-    const __nv_bfloat16* kp = tab.k_cache[lsg] + e0;
-    const __nv_bfloat16* vp = tab.v_cache[lsg] + e0;
-    const int64_t tstep = 2 * hkv * kD;  // two tokens
+    if constexpr (kTma) {
+      // one lane issues the warp's K and V halves (4 boxes) and, at a new
+      // piece, the group's query rows; a missing second row reads as zeros
+      uint8_t* wb = att_dyn + st * stage_bytes + warp * wblk;
+      const bool newq = j == 0 || lt == 0;
+      uint32_t qbytes = 0;
+      if (newq)
+        for (int ri = 0; ri < qrows; ++ri) {
+          if (ri < gcount[lr]) {
+            qbytes += G * kD * 2;
+          } else {
+            uint4* z = reinterpret_cast<uint4*>(wb + 4 * kPageTok * 128 + ri * G * kD * 2);
+            for (int e = lane; e < G * kD * 2 / 16; e += 32) z[e] = make_uint4(0u, 0u, 0u, 0u);
+            ptx::fence_proxy_async_smem();  // before a later copy into the same bytes
+          }
+        }
+      __syncwarp();
+      if (lane == 0) {
+        ptx::fence_proxy_async_smem();
+        uint64_t* bar = &tbar[warp][st];
+        ptx::mbar_arrive_expect_tx(bar, 4 * kPageTok * 128 + qbytes);
+        const int tok0 = static_cast<int>(page * p.page);
+        const uint32_t ws = ptx::smem_addr(wb);
+        ptx::tma_load_3d(ws, &kmap, bar, 0, kvh, tok0);
+        ptx::tma_load_3d(ws + kPageTok * 128, &kmap, bar, 64, kvh, tok0);
+        ptx::tma_load_3d(ws + 2 * kPageTok * 128, &vmap, bar, 0, kvh, tok0);
+        ptx::tma_load_3d(ws + 3 * kPageTok * 128, &vmap, bar, 64, kvh, tok0);
+        if (newq)
+          for (int ri = 0; ri < qrows && ri < gcount[lr]; ++ri)
+            ptx::bulk_load(wb + 4 * kPageTok * 128 + ri * G * kD * 2,
+                           p.q_rot + (static_cast<int64_t>(gfirst[lr] + ri) * p.hq + kvh * G) * kD,
+                           static_cast<uint32_t>(G * kD * 2), bar);
+      }
+      (void)live;
+    } else {
+      const int64_t e0 = ((page * p.page + ld_tok) * hkv + kvh) * kD + ld_ch * 8;  // element offset, token ld_tok
+      const __nv_bfloat16* kp = tab.k_cache[lsg] + e0;
+      const __nv_bfloat16* vp = tab.v_cache[lsg] + e0;
+      const int64_t tstep = 2 * hkv * kD;  // two tokens
 #pragma unroll
-    for (int i = 0; i < kPageTok / 2; ++i) {
-      const int tok = ld_tok + 2 * i;
-      const bool ok = tok < live;
-      const uint32_t d = ss + tok * row_bytes + head_off + ld_ch * 16;
-      ptx::cp_async_16(d, ok ? static_cast<const void*>(kp + i * tstep) : static_cast<const void*>(kp), ok ? 16u : 0u);
-      ptx::cp_async_16(d + kv_bytes, ok ? static_cast<const void*>(vp + i * tstep) : static_cast<const void*>(vp),
-                       ok ? 16u : 0u);
-    }
-    if (j == 0 || lt == 0) {
-      // the group's query rows (a missing second row reads as zeros)
-      for (int ri = 0; ri < qrows; ++ri) {
-        const bool have = ri < gcount[lr];
-        const char* qp = reinterpret_cast<const char*>(
-            p.q_rot + (static_cast<int64_t>(gfirst[lr] + (have ? ri : 0)) * p.hq + kvh * G) * kD);
-        for (int e = lane; e < G * kD * 2 / 16; e += 32)
-          ptx::cp_async_16(ss + q_off + (ri * G * kD * 2) + e * 16, qp + e * 16, have ? 16u : 0u);
+      for (int i = 0; i < kPageTok / 2; ++i) {
+        const int tok = ld_tok + 2 * i;
+        const bool ok = tok < live;
+        const uint32_t d = ss + tok * row_bytes + head_off + ld_ch * 16;
+        ptx::cp_async_16(d, ok ? static_cast<const void*>(kp + i * tstep) : static_cast<const void*>(kp), ok ? 16u : 0u);
+        ptx::cp_async_16(d + kv_bytes, ok ? static_cast<const void*>(vp + i * tstep) : static_cast<const void*>(vp),
+                         ok ? 16u : 0u);
+      }
+      if (j == 0 || lt == 0) {
+        // the group's query rows (a missing second row reads as zeros)
+        for (int ri = 0; ri < qrows; ++ri) {
+          const bool have = ri < gcount[lr];
+          const char* qp = reinterpret_cast<const char*>(
+              p.q_rot + (static_cast<int64_t>(gfirst[lr] + (have ? ri : 0)) * p.hq + kvh * G) * kD);
+          for (int e = lane; e < G * kD * 2 / 16; e += 32)
+            ptx::cp_async_16(ss + q_off + (ri * G * kD * 2) + e * 16, qp + e * 16, have ? 16u : 0u);
+        }
       }
     }
     if (++lt == pre[lr + 1] - pre[lr]) {
@@ -488,13 +546,30 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
   float o[8][4];                                            // O^T tiles: dims 16mt + (g, g+8) x heads (2c, 2c+1)
   int r = r_start, t = t_start;
   for (int j = 0; j < nunits; ++j) {
-    ptx::cp_async_wait_group<kStages - 2>();
-    __syncwarp();
-    if (j + kStages - 1 < nunits) issue(j + kStages - 1);
-    ptx::cp_async_commit();
     const int st = j % kStages;
     const uint32_t ss = sm0 + st * stage_bytes;
     const int tiles = pre[r + 1] - pre[r];
+    if constexpr (kTma) {
+      ptx::mbar_wait(&tbar[warp][st], (j / kStages) & 1, nullptr, 0, kAttnWaitNs);
+      // V token rows past the group's causal end: zeros (the page may hold
+      // stale values there; their weights are 0, but 0 * NaN is not)
+      const int live = min(kPageTok, keys[gfirst[r] + gcount[r] - 1] - t * kPageTok);
+      if (live < kPageTok) {
+        uint4* v0 = reinterpret_cast<uint4*>(att_dyn + st * stage_bytes + warp * wblk + 2 * kPageTok * 128);
+        for (int e = lane; e < 2 * (kPageTok - live) * 8; e += 32) {
+          const int half = e / ((kPageTok - live) * 8), rem = e % ((kPageTok - live) * 8);
+          v0[half * kPageTok * 8 + (live + rem / 8) * 8 + rem % 8] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        ptx::fence_proxy_async_smem();  // before a later copy into the same bytes
+      }
+      __syncwarp();
+      if (j + kStages - 1 < nunits) issue(j + kStages - 1);
+    } else {
+      ptx::cp_async_wait_group<kStages - 2>();
+      __syncwarp();
+      if (j + kStages - 1 < nunits) issue(j + kStages - 1);
+      ptx::cp_async_commit();
+    }
     // causal length of this thread's columns (2c, 2c+1: row c >> 1 of the group)
     const int my_ri = pair ? (c >> 1) : 0;
     const int L = (pair && my_ri >= gcount[r]) ? 0 : keys[gfirst[r] + my_ri];
@@ -502,7 +577,7 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
       // new piece: Q^T as the B operand (k = dims, n = column g: query head
       // g & 3 of the group's row g >> 2 with pairing, head g without),
       // fresh softmax state
-      const uint8_t* qs = att_dyn + st * stage_bytes + q_off;
+      const uint8_t* qs = att_dyn + st * stage_bytes + (kTma ? warp * wblk + 4 * kPageTok * 128 : q_off);
       const int q_ri = pair ? (g >> 2) : 0, q_h = pair ? (g & 3) : g;
       const bool real = q_h < G && q_ri < qrows;
       const int q_col = q_ri * G + q_h;
@@ -521,11 +596,15 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
     {
       const int tok = (mi & 1) * 8 + r8;
       const uint32_t a_row = ss + tok * row_bytes + head_off + (mi >> 1) * 16;
+      // TMA layout: 16-byte chunk c of token row `tok` of a 64-dim half sits
+      // at chunk c ^ (tok & 7) (128-byte swizzle)
+      const uint32_t kb = ss + warp * wblk + tok * 128;
+      auto kaddr = [&](int ch) { return kb + (ch >> 3) * (kPageTok * 128) + (((ch & 7) ^ (tok & 7)) << 4); };
 #pragma unroll
       for (int ks = 0; ks < 8; ks += 2) {
         uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-        ldsm_x4(a_row + ks * 32, a0, a1, a2, a3);
-        ldsm_x4(a_row + ks * 32 + 32, b0, b1, b2, b3);
+        ldsm_x4(kTma ? kaddr(ks * 2 + (mi >> 1)) : a_row + ks * 32, a0, a1, a2, a3);
+        ldsm_x4(kTma ? kaddr(ks * 2 + 2 + (mi >> 1)) : a_row + ks * 32 + 32, b0, b1, b2, b3);
         mma_bf16_16816(sa, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
         mma_bf16_16816(sb, b0, b1, b2, b3, qb[ks + 1][0], qb[ks + 1][1]);
       }
@@ -578,10 +657,12 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
     {
       const int tok = (mi >> 1) * 8 + r8;
       const uint32_t a_row = ss + kv_bytes + tok * row_bytes + head_off + (mi & 1) * 16;
+      const uint32_t vb = ss + warp * wblk + 2 * kPageTok * 128 + tok * 128;
+      auto vaddr = [&](int ch) { return vb + (ch >> 3) * (kPageTok * 128) + (((ch & 7) ^ (tok & 7)) << 4); };
 #pragma unroll
       for (int mt = 0; mt < 8; ++mt) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4_trans(a_row + mt * 32, a0, a1, a2, a3);
+        ldsm_x4_trans(kTma ? vaddr(mt * 2 + (mi & 1)) : a_row + mt * 32, a0, a1, a2, a3);
         mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
       }
     }
@@ -620,7 +701,7 @@ __global__ void __launch_bounds__(kAttnMaxHkv * 32, 1)
       ++r;
     }
   }
-  ptx::cp_async_wait_all();
+  if constexpr (!kTma) ptx::cp_async_wait_all();
 }
 
 // Merges the pieces of one (row, head): O = sum_j 2^(m_j - M) o_j /
@@ -878,20 +959,38 @@ int sm_count_attn() {
   return n > 0 ? n : 148;
 }
 
-template <int S>
+template <int S, bool Tma>
 int launch_attention_stages(const AttnTable& tab, const AttnParams& p, int grid, int groups, int pair, size_t smem,
-                            const AttnSplit& sp, cudaStream_t stream) {
+                            const AttnSplit& sp, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                            cudaStream_t stream) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(paged_attention_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_err = cudaFuncSetAttribute(paged_attention_kernel<S, Tma>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     kAttnSmemMax);
   });
   if (attr_err != cudaSuccess)
     return set_error(SWL_ERR_CUDA, "attention: smem attribute: %s", cudaGetErrorString(attr_err));
-  SWL_CUDA_TRY(launch_kernel(paged_attention_kernel<S>, dim3(grid, groups), dim3(p.hkv / groups * 32), smem,
-                             stream, 1, tab, p, sp.chunks, sp.chunk_pages, pair, p.part));
+  SWL_CUDA_TRY(launch_kernel(paged_attention_kernel<S, Tma>, dim3(grid, groups), dim3(p.hkv / groups * 32), smem,
+                             stream, 1, tab, p, sp.chunks, sp.chunk_pages, pair, p.part, kmap, vmap));
   return SWL_OK;
+}
+
+// The TMA path: every row's K (and V) pages lie in one cache allocation,
+// whose extent bounds the tensor map. Returns false when the slots use
+// different caches (the per-lane copies then load each slot's own pages).
+bool attention_tmaps(const AttnTable& tab, const AttnParams& p, CUtensorMap* kmap, CUtensorMap* vmap) {
+  for (int i = 1; i < tab.seg.nseg; ++i)
+    if (tab.k_cache[i] != tab.k_cache[0] || tab.v_cache[i] != tab.v_cache[0]) return false;
+  const int64_t row = static_cast<int64_t>(p.hkv) * kD * 2;  // bytes per token row
+  char *kb = nullptr, *vb = nullptr;
+  size_t kn = 0, vn = 0;
+  if (allocation_of(tab.k_cache[0], &kb, &kn) != SWL_OK || allocation_of(tab.v_cache[0], &vb, &vn) != SWL_OK)
+    return false;
+  const int64_t kt = (kb + kn - reinterpret_cast<const char*>(tab.k_cache[0])) / row;
+  const int64_t vt = (vb + vn - reinterpret_cast<const char*>(tab.v_cache[0])) / row;
+  return encode_kv_page_tmap(kmap, tab.k_cache[0], kt, p.hkv) == SWL_OK &&
+         encode_kv_page_tmap(vmap, tab.v_cache[0], vt, p.hkv) == SWL_OK;
 }
 
 }  // namespace
@@ -923,24 +1022,39 @@ int launch_paged_attention(const AttnTable& tab, const AttnParams& p, cudaStream
   for (int i = 0; i < tab.seg.nseg; ++i)
     max_seg_rows = std::max(max_seg_rows, tab.seg.row_start[i + 1] - tab.seg.row_start[i]);
   const int pair = (max_seg_rows >= 2 && p.hq / p.hkv <= 4 && !g_attn_no_pair.load(std::memory_order_relaxed)) ? 1 : 0;
-  const int stage_bytes = attn_stage_bytes(p.hq / groups, p.hkv / groups, pair ? 2 : 1);
-  // two page stages per warp by default (one in flight while one is
-  // consumed): the 148 KB ring lets a CTA sit beside the RoPE epilogue's
-  // CTAs; deeper rings (tuning) measured no faster in the decode step
+  // K/V pages by TMA (one lane per warp issues its kv head's 128B-swizzled
+  // halves) when every row's pages lie in one cache; else per-lane copies
+  CUtensorMap kmap, vmap;
+  memset(&kmap, 0, sizeof(kmap));
+  memset(&vmap, 0, sizeof(vmap));
+  const bool tma = g_attn_tma.load(std::memory_order_relaxed) != 0 && attention_tmaps(tab, p, &kmap, &vmap);
+  const int G = p.hq / p.hkv;
+  const int stage_bytes = tma ? p.hkv / groups * attn_tma_warp_bytes(G, pair ? 2 : 1)
+                              : attn_stage_bytes(p.hq / groups, p.hkv / groups, pair ? 2 : 1);
+  // Page stages per warp by default: with per-lane copies two (one in flight
+  // while one is consumed; the 148 KB ring lets a CTA sit beside the RoPE
+  // epilogue's CTAs; deeper rings measured no faster); with TMA three
+  // (216 KB: 18.0 vs 18.5 us with two at the decode shape, and 1% faster
+  // whole steps at contexts U[1024, 4096])
   const int o = g_attn_stages.load(std::memory_order_relaxed);
-  const int stages = std::min(std::min(kAttnStagesMax, kAttnSmemMax / stage_bytes), o > 0 ? o : 2);
+  const int budget = kAttnSmemMax - (tma ? 1024 : 0);  // TMA: 1024-byte alignment slack
+  const int stages = std::min(std::min(kAttnStagesMax, budget / stage_bytes), o > 0 ? o : (tma ? 3 : 2));
   if (stages < 2) return set_error(SWL_ERR_ARG, "attention: page stage of %d bytes too large", stage_bytes);
-  const size_t smem = static_cast<size_t>(stages) * stage_bytes;
+  const size_t smem = static_cast<size_t>(stages) * stage_bytes + (tma ? 1024 : 0);
   // one CTA per SM, but no more CTAs than the units can keep busy
   const int64_t units_max =
       static_cast<int64_t>(tab.seg.total_rows) * ((p.max_len + kPageTok - 1) / kPageTok);
   const int grid = static_cast<int>(std::max<int64_t>(
       1, std::min<int64_t>((units_max + sp.chunk_pages - 1) / sp.chunk_pages, sm_count_attn())));
+#define SWL_ATTN_LAUNCH(S)                                                                                 \
+  (tma ? launch_attention_stages<S, true>(tab, p, grid, groups, pair, smem, sp, kmap, vmap, stream)          \
+       : launch_attention_stages<S, false>(tab, p, grid, groups, pair, smem, sp, kmap, vmap, stream))
   switch (stages) {
-    case 2: SWL_TRY(launch_attention_stages<2>(tab, p, grid, groups, pair, smem, sp, stream)); break;
-    case 3: SWL_TRY(launch_attention_stages<3>(tab, p, grid, groups, pair, smem, sp, stream)); break;
-    default: SWL_TRY(launch_attention_stages<4>(tab, p, grid, groups, pair, smem, sp, stream)); break;
+    case 2: SWL_TRY(SWL_ATTN_LAUNCH(2)); break;
+    case 3: SWL_TRY(SWL_ATTN_LAUNCH(3)); break;
+    default: SWL_TRY(SWL_ATTN_LAUNCH(4)); break;
   }
+#undef SWL_ATTN_LAUNCH
   ShrinkSide none;
   if (!shrink) {
     for (int i = 0; i < kMaxSlots; ++i) none.A[i] = nullptr;
@@ -965,6 +1079,11 @@ int launch_rms_norm(const NormTable& tab, const __nv_bfloat16* w, int64_t hidden
 
 int set_attention_pairing(int on) {
   g_attn_no_pair.store(on ? 0 : 1);
+  return SWL_OK;
+}
+
+int set_attention_tma(int on) {
+  g_attn_tma.store(on ? 1 : 0);
   return SWL_OK;
 }
 

@@ -86,6 +86,7 @@ int attention_splits(int total_rows, int hkv, int max_len);
 // Overrides of the chunk size (pages) and page-ring depth; 0 = automatic.
 int set_attention_tuning(int chunk_pages, int stages, int groups);
 int set_attention_pairing(int on);
+int set_attention_tma(int on);
 int64_t attention_part_floats(int total_rows, int hq, int splits);
 
 // RMSNorm over rows.

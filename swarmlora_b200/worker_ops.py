@@ -164,6 +164,12 @@ def attention_tune(chunk_pages: int = 0, stages: int = 0, groups: int = 0) -> No
     check(lib().swl_attention_tune(chunk_pages, stages, groups))
 
 
+def attention_tma(on: bool = True) -> None:
+    """K/V pages by TMA (default, when every row's pages share one cache
+    allocation) or by per-lane copies."""
+    check(lib().swl_attention_tma(1 if on else 0))
+
+
 def attention_part_floats(total_rows: int, hq: int, hkv: int, max_len: int) -> int:
     return int(lib().swl_attention_part_floats(total_rows, hq, hkv, max_len))
 

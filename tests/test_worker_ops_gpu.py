@@ -173,6 +173,7 @@ def _attn_case(ctx, rows, seed, page=16):
     assert torch.equal(vd.cpu(), vc_ref), "V cache append differs"
     for i in range(n):
         assert_close(outs[i], want[i], f"attention slot {i} ctx {ctx[i]} rows {rows[i]}")
+    return [o.cpu() for o in outs]
 
 
 @pytest.mark.parametrize("ctx,rows", [
@@ -182,6 +183,31 @@ def _attn_case(ctx, rows, seed, page=16):
 ])
 def test_rope_append_attention(native, cuda, ctx, rows):
     _attn_case(ctx, rows, seed=sum(ctx) + len(rows))
+
+
+@pytest.mark.parametrize("ctx,rows,groups", [
+    ([127, 0, 15, 16, 300, 1000], [1, 1, 1, 1, 1, 1], 0),  # decode rows, partial and empty last pages
+    ([0, 40, 7, 300], [16, 15, 1, 2], 0),  # prefill chunks: rows paired on one page read
+    ([1000, 3, 513, 77], [1, 4, 1, 16], 2),  # kv head groups split across CTAs
+    ([4000, 33], [1, 3], 0),
+])
+def test_attention_tma_pages_match_lane_copies(native, cuda, ctx, rows, groups):
+    """K/V pages loaded by TMA (one lane per warp, 128B-swizzled halves,
+    the query rows by bulk copy, stale V rows past the causal end zeroed)
+    and by per-lane cp.async copies give bit-identical outputs (the same
+    values reach the same MMAs in the same order); against the oracle too."""
+    from swarmlora_b200._native import check, lib
+    try:
+        check(lib().swl_attention_tune(0, 0, groups))
+        check(lib().swl_attention_tma(1))
+        tma = _attn_case(ctx, rows, seed=sum(ctx) + 11 * len(rows))
+        check(lib().swl_attention_tma(0))
+        copies = _attn_case(ctx, rows, seed=sum(ctx) + 11 * len(rows))
+    finally:
+        check(lib().swl_attention_tma(1))
+        check(lib().swl_attention_tune(0, 0, 0))
+    for i, (a, b) in enumerate(zip(tma, copies)):
+        assert torch.equal(a, b), f"slot {i}: TMA pages differ from lane copies"
 
 
 @pytest.mark.parametrize("ctx,rows", [
