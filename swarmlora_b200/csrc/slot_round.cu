@@ -500,8 +500,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (gsplit && emit && tid == 0) sws.count[tile_id] = 0;
   // Done reading the peers' P; they may still read ours, so the CTA waits
   // for the whole cluster before it exits (TMEM was last read before the
-  // barrier above, so it is released in between).
-  if (csplit) ptx::cluster_arrive();
+  // barrier above, so it is released in between). Every value read from a
+  // peer went into a store above, so those reads are complete: the arrive
+  // needs no release ordering (which would wait for the output stores).
+  if (csplit) ptx::cluster_arrive_relaxed();
   else __syncthreads();
   if (warp == 1) {
     ptx::tc_fence_after();
