@@ -556,7 +556,7 @@ def our_arm(args):
     # launch at this workload, from the capture
     #   ncu --set full --clock-control none -k regex:slot_round -s 1 -c 1 \
     #       python bench.py --profile-round gate_up --steps 3 --warmup 1
-    ncu_traffic = {("gate_up", 28): 235_135_744 + 3_593_216}
+    ncu_traffic = {("gate_up", 28): 235_173_376 + 4_176_640}
     rounds = round_phase(grp, cfg)
     proto = None
     if args.protocol != "off" and world == 1:
