@@ -39,6 +39,12 @@ sys.path.insert(0, str(ROOT))
 METRIC = "decode tok/s/GPU (Llama-3.1-8B shape, N=28 slots)"
 UNIT = "tok/s"
 N_SLOTS = 28
+
+
+def metric_for(slots: int) -> str:
+    """The headline metric's name with the run's slot count (the headline
+    configuration runs 28)."""
+    return METRIC if slots == N_SLOTS else METRIC.replace("N=28", f"N={slots}")
 CTX_LO, CTX_HI = 256, 1024
 MAX_NEW = 160
 
@@ -366,7 +372,7 @@ def reference_arm(args):
     rounds = {"m%d" % m: full_step.round_us(m) for m in (args.slots, 4)}
     sample = (f"{args.steps} whole decode steps of {args.slots} slots (32 layer passes with one layer's weights "
               f"reused + LM-head GEMV + argmax) on {threads} threads")
-    line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "impl": "reference",
+    line = {"metric": metric_for(args.slots), "value": round(value, 4), "unit": UNIT, "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t_step * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -580,7 +586,7 @@ def our_arm(args):
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "metric": metric_for(args.slots), "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": ("base weights from " + os.path.basename(os.path.normpath(args.checkpoint))
@@ -753,7 +759,7 @@ def shard_arm(args):
     dist.all_gather_object(both, toks.tolist())
     if rank == 0:
         print(json.dumps({
-            "metric": METRIC + " (column-sharded base weights, one group on 2 GPUs)",
+            "metric": metric_for(args.slots) + " (column-sharded base weights, one group on 2 GPUs)",
             "value": round(n * args.steps / (ms_max / 1e3), 2), "unit": UNIT, "n_gpus": 2,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
             "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
