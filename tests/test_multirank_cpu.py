@@ -87,3 +87,10 @@ def test_reference_arm_runs_on_rank_zero_only():
     line = json.loads(out0.strip().splitlines()[-1])
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "port"
+    assert line["metric"] == "decode tok/s/GPU (Llama-3.1-8B shape, N=4 slots)"
+
+
+def test_metric_names_the_headline_configuration_and_other_slot_counts():
+    import bench
+    assert bench.metric_for(28) == "decode tok/s/GPU (Llama-3.1-8B shape, N=28 slots)"
+    assert bench.metric_for(32) == "decode tok/s/GPU (Llama-3.1-8B shape, N=32 slots)"
