@@ -63,7 +63,8 @@ def test_decode_round_28_slots(native, cuda, name, algo):
 
 
 @pytest.mark.parametrize("rows", [[1], [3, 0, 16, 1, 7], [16] * 4 + [1] * 24,
-                                  [16] * 8 + [1] * 40, [64, 64, 64, 64, 44, 1]])
+                                  [16] * 8 + [1] * 40, [64, 64, 64, 64, 44, 1],
+                                  [1] * 128])  # the slot table's maximum
 def test_ragged_rows(native, cuda, rows):
     N, K = 4096, 4096
     W, xs, b = _case(N, K, rows, seed=sum(rows))
